@@ -1,0 +1,427 @@
+#!/usr/bin/env python
+"""Benchmark of the Qwen3-MoE layer hot path (BASELINE.json metric: MoE-layer tokens/s and the
+fraction of the HBM roofline), one JSON line on stdout.
+
+Workload ("C2"): a Qwen3-30B-A3B-shaped MoE layer at decode batch T
+(default 64): hidden 2048, 128 experts, top-8 renormalised, moe_intermediate 768, gate/up Q4_K,
+down Q6_K, weights ~N(0, 0.02) before quantisation, router f32 ~N(0, 0.02), activations ~N(0, 1).
+A step is one pass over the MoE layers of a 48-layer model (48 distinct, resident layers of that
+shape, the same T tokens into each), so every step streams ~48 x the distinct-expert bytes through
+HBM (far above the 126 MB L2).  `value` = layer-tokens per second (T x layers x steps / time),
+device-resident inputs, the 48 layer calls replayed as one CUDA graph.  `e2e` = the same through
+the C-ABI calls from the host, per step the T x H f32 input copied host->device from pinned memory
+and the last layer's output read back.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
+
+--impl reference times the CPU oracle (the stand-in for ggml's CPU mul_mat_id path, which is not
+present in the reference tree) on the host cores, one layer call per step.
+Under torchrun (N > 1) every rank runs an independent replica (weak scaling); rank 0 prints.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, I, E, K_USED = 2048, 768, 128, 8
+Q4K, Q6K = 12, 14
+EXPERT_BYTES = 2 * I * (H // 256) * 144 + H * (I // 256) * 210  # 3,059,712
+GATE_UP_BYTES = 2 * I * (H // 256) * 144                          # 1,769,472
+DOWN_BYTES = H * (I // 256) * 210                                 # 1,290,240
+ROUTER_BYTES = E * H * 4                                          # 1,048,576
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--tokens", type=int, default=64)
+    p.add_argument("--layers", type=int, default=48)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--seed", type=int, default=20261201)
+    p.add_argument("--cpu-sample-s", type=float, default=15.0)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--sweep", action="store_true", help="also time T in {1,4,16,64}")
+    return p.parse_args()
+
+
+def workload(args, n_gpus):
+    return {"workload": "C2 Qwen3-30B-A3B MoE layer, decode", "tokens_per_layer_call": args.tokens,
+            "n_embd": H, "n_ff": I, "n_expert": E, "n_expert_used": K_USED,
+            "types": "gate/up Q4_K, down Q6_K (this repo's quantiser)", "layers_per_step": args.layers,
+            "l2": "inputs larger than L2: 48 distinct resident layers rotated each step",
+            "parallelism": f"replicas x{n_gpus}" if n_gpus > 1 else "single GPU", "seed": args.seed}
+
+
+# ---------------------------------------------------------------------------------------- clocks
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        rows = []
+        for line in open(self.path):
+            f = [c.strip() for c in line.split(",")]
+            if len(f) >= 9 and f[1].isdigit():
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [int(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": int(statistics.median(sm)), "sm_max_mhz": int(rows[0][2]), "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None,
+                "reasons": reasons}
+
+
+# ---------------------------------------------------------------------------------------- ours
+def make_layers(torch, moe, n_layers, seed, device):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    layers = []
+    for _ in range(n_layers):
+        rw = torch.randn((E, H), generator=g, device=device) * 0.02
+        gate = moe.quantize(Q4K, torch.randn((E, I, H), generator=g, device=device) * 0.02)
+        up = moe.quantize(Q4K, torch.randn((E, I, H), generator=g, device=device) * 0.02)
+        down = moe.quantize(Q6K, torch.randn((E, H, I), generator=g, device=device) * 0.02)
+        layers.append((rw, moe.ExpertWeights(gate, up, down)))
+    torch.cuda.synchronize()
+    return layers
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import tetraeder_b200 as tb
+    from tetraeder_b200 import moe
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    T, L = args.tokens, args.layers
+    layers = make_layers(torch, moe, L, args.seed + 7919 * rank, dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed + 1 + rank)
+    x_dev = torch.randn((T, H), generator=gen, device=dev)
+    x_host = x_dev.cpu().pin_memory()
+    out_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=Q6K, max_tokens=T, device=local_rank)
+    outs = [torch.empty((T, H), device=dev) for _ in range(L)]
+    ids = [torch.empty((T, K_USED), dtype=torch.int32, device=dev) for _ in range(L)]
+    ws = [torch.empty((T, K_USED), dtype=torch.float32, device=dev) for _ in range(L)]
+
+    def one_step(x):
+        for li, (rw, wts) in enumerate(layers):
+            layer.moe_ffn(x, wts, router_w=rw, out=outs[li], ids_out=ids[li], w_out=ws[li])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # eager warm-up (sets kernel attributes), checks the device flag
+    one_step(x_dev)
+    layer.check()
+    # one CUDA graph for the 48 layer calls
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        one_step(x_dev)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=s):
+            one_step(x_dev)
+    torch.cuda.synchronize()
+
+    def timed(fn, K, W):
+        for _ in range(W):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(K):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1))
+
+    with Clocks(local_rank) as clk:
+        ms = timed(graph.replay, args.steps, max(args.warmup, 3))
+    clocks = clk.summary()
+    layer.check()
+    units = world * args.steps * L * T
+    value = units / (ms / 1e3)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        one_step(x_dev)
+        out_host.copy_(outs[-1], non_blocking=True)
+
+    e2e_ms = timed(e2e_step, args.steps, max(args.warmup, 3))
+    e2e_value = units / (e2e_ms / 1e3)
+
+    # distinct experts per layer (the D of the roofline bytes)
+    distinct = [int(torch.unique(ids[li]).numel()) for li in range(L)]
+
+    # per-kernel device time of the same workload (events around each kernel)
+    layer.profile(True)
+    for _ in range(2):
+        for li, (rw, wts) in enumerate(layers):
+            layer.moe_ffn(x_dev, wts, router_w=rw, out=outs[li], ids_out=ids[li], w_out=ws[li])
+            prof = layer.profile_collect()
+    layer.profile(False)
+    n_calls = 2 * L
+    phase_ms = {k: v[0] / v[1] for k, v in prof.items()}
+    total_phase = sum(v[0] for v in prof.values())
+    shares = {k: round(v[0] / total_phase, 4) for k, v in prof.items()}
+    d_mean = sum(distinct) / L
+    gate_up_bytes = d_mean * GATE_UP_BYTES + T * (H + H // 256 * 4 + H // 16 * 2) + T * K_USED * I * 4
+    down_bytes = d_mean * DOWN_BYTES + T * K_USED * (I + I // 256 * 4 + I // 16 * 2) + T * K_USED * H * 4
+    peaks = load_peaks()
+    dom = max(("gate_up", "down"), key=lambda k: prof.get(k, (0, 1))[0])
+    dom_bytes = gate_up_bytes if dom == "gate_up" else down_bytes
+    achieved = dom_bytes / (phase_ms[dom] / 1e3) / 1e9
+    layer_bytes = d_mean * EXPERT_BYTES + ROUTER_BYTES + T * H * 8
+    layer_ms = ms / (args.steps * L)
+    roofline = {"bound": "hbm", "kernel": f"gemv_kernel ({dom})", "achieved": round(achieved, 1),
+                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "peak_source": peaks["source"], "traffic": traffic_from_profiles(dom),
+                "algorithmic_bytes_per_launch": int(dom_bytes), "avg_launch_us": round(phase_ms[dom] * 1e3, 2)}
+    layer_roof = {"bytes_per_layer_call": int(layer_bytes), "distinct_experts_mean": round(d_mean, 2),
+                  "us_per_layer_call": round(layer_ms * 1e3, 2),
+                  "achieved_gbs": round(layer_bytes / (layer_ms / 1e3) / 1e9, 1),
+                  "frac": round(layer_bytes / (layer_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+                  "kernel_us": {k: round(v * 1e3, 2) for k, v in phase_ms.items()}, "kernel_share": shares}
+    launches_per_call = sum(v[1] for v in prof.values()) / n_calls
+    result = {
+        "metric": "moe_layer_tokens_per_s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 (Q8_K activations x Q4_K/Q6_K weights, dp4a, f32 scales)", "data": "synthetic",
+        "config": workload(args, world), "roofline": roofline, "layer_roofline": layer_roof,
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
+                "d2h_bytes_per_step": T * H * 4, "ms_per_step": round(e2e_ms / args.steps, 4),
+                "path": "tmoe_layer C-ABI calls (ctypes) x 48 + pinned H2D/D2H"},
+        "gpu_launches": int(launches_per_call * L * args.steps), "clocks": clocks,
+    }
+    if args.sweep and rank == 0:
+        result["sweep"] = sweep_tokens(torch, tb, layers, dev)
+    del graph
+    return result
+
+
+def sweep_tokens(torch, tb, layers, dev):
+    """tokens/s and layer roofline fraction at T in {1, 4, 16, 64} (graph of 48 layer calls)."""
+    peaks = load_peaks()
+    res = {}
+    for T in (1, 4, 16, 64):
+        layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=Q6K, max_tokens=T,
+                            device=dev.index)
+        x = torch.randn((T, H), device=dev)
+        out = torch.empty((T, H), device=dev)
+        ids = [torch.empty((T, K_USED), dtype=torch.int32, device=dev) for _ in layers]
+
+        def step():
+            for li, (rw, wts) in enumerate(layers):
+                layer.moe_ffn(x, wts, router_w=rw, out=out, ids_out=ids[li])
+        step()
+        s = torch.cuda.Stream(device=dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            step()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=s):
+                step()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 20
+        e0.record()
+        for _ in range(n):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (n * len(layers))
+        d = sum(int(torch.unique(i).numel()) for i in ids) / len(layers)
+        by = d * EXPERT_BYTES + ROUTER_BYTES + T * H * 8
+        res[str(T)] = {"tokens_per_s": round(T / (ms / 1e3), 1), "us_per_layer": round(ms * 1e3, 2),
+                       "distinct_experts": round(d, 2), "hbm_frac": round(by / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)}
+        del g
+        layer.close()
+    return res
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d.get("bf16_tflops"), "source": "measured (MEASURED_PEAKS.json)"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback (profiling recipe)"}
+
+
+def traffic_from_profiles(kernel):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "gemv_decode_c2.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith(f"traffic_bytes_per_launch[{kernel}]:"):
+            try:
+                return int(float(line.split(":", 1)[1].strip()))
+            except ValueError:
+                return None
+    return None
+
+
+# ---------------------------------------------------------------------------------------- CPU
+def host_layer(seed, T):
+    """One C2 layer on the host, quantised with the oracle's fit (the same algorithm as the device
+    quantiser)."""
+    import oracle as O
+    rng = np.random.default_rng(seed)
+    gate = O.quantize(O.TYPE_Q4_K, (rng.standard_normal((E, I, H), dtype=np.float32) * 0.02))
+    up = O.quantize(O.TYPE_Q4_K, (rng.standard_normal((E, I, H), dtype=np.float32) * 0.02))
+    down = O.quantize(O.TYPE_Q6_K, (rng.standard_normal((E, H, I), dtype=np.float32) * 0.02))
+    rw = (rng.standard_normal((E, H), dtype=np.float32) * 0.02)
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    return gate, up, down, rw, x
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(args):
+    import oracle as O
+    O.build()
+    T = args.tokens
+    gate, up, down, rw, x = host_layer(args.seed, T)
+    threads = cpu_threads()
+    t0 = time.perf_counter()
+    O.layer(x, K_USED, gate, up, down, H, I, E, router_w=rw, down_type=O.TYPE_Q6_K, nthreads=threads)
+    first = time.perf_counter() - t0
+    n = max(1, int(args.cpu_sample_s / max(first, 1e-3)))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        O.layer(x, K_USED, gate, up, down, H, I, E, router_w=rw, down_type=O.TYPE_Q6_K, nthreads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": round(n * T / dt, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n} C2 layer calls of T={T} tokens (router, Q8_K expert dots, combine), one layer's weights"}
+
+
+def run_reference(args):
+    """The reference arm: the CPU oracle (stand-in for ggml's CPU mul_mat_id path) on the host cores,
+    one C2 layer call of T tokens per step, wall-clock timed."""
+    import oracle as O
+    O.build()
+    T = args.tokens
+    gate, up, down, rw, x = host_layer(args.seed, T)
+    threads = cpu_threads()
+    for _ in range(args.warmup):
+        O.layer(x, K_USED, gate, up, down, H, I, E, router_w=rw, down_type=O.TYPE_Q6_K, nthreads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.layer(x, K_USED, gate, up, down, H, I, E, router_w=rw, down_type=O.TYPE_Q6_K, nthreads=threads)
+    dt = time.perf_counter() - t0
+    value = args.steps * T / dt
+    sample = f"{args.steps} C2 layer calls of T={T} tokens, one layer's weights, {threads} threads"
+    return {"metric": "moe_layer_tokens_per_s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 (Q8_K activations x Q4_K/Q6_K weights)", "data": "synthetic",
+            "config": workload(args, 1), "impl": "reference",
+            "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "ggml's CPU mul_mat_id (llama.cpp b12426) is not in the reference tree and cannot be built "
+                    "here; the oracle/ C restatement of its semantics is timed instead"}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        print(json.dumps(run_reference(args)), flush=True)
+        return 0
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    res = run_ours(args, rank, world, local_rank)
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_baseline(args)
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

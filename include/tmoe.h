@@ -1,0 +1,174 @@
+/*
+ * tmoe.h -- C ABI of the B200-native Qwen3-MoE layer hot path (router -> dispatch ->
+ * Q4_K/Q6_K SwiGLU experts -> weighted combine, optional expert parallelism).
+ *
+ * The entry points replace, for the MoE layer of Tetraeder's own Qwen3-MoE builder
+ * (`--engine moe`), the ggml graph ops that crates/ggml-sys forwards today.  Paths below are
+ * relative to the tetraeder project root:
+ *
+ *   tmoe_mul_mat_id   <- Context::mul_mat_id            crates/ggml-sys/src/ggml/context.rs:322-336
+ *   tmoe_route        <- router()                       crates/model/src/qwen3moe.rs:2871-2890
+ *                        (soft_max :279, argsort_top_k :290, get_rows :231, sum_rows,
+ *                         clamp, div of context.rs)
+ *   tmoe_experts      <- weighted_experts() + sum_experts()
+ *                                                       crates/model/src/qwen3moe.rs:2899-2923
+ *   tmoe_layer        <- moe_ffn() / the router+experts window of build_step
+ *                                                       crates/model/src/qwen3moe.rs:2892-2896
+ *   tmoe_map_ids      <- the EP id remap get_rows(map, ids)
+ *                                                       crates/model/src/qwen3moe_shard.rs:1043-1050
+ *   tmoe_ep_*         <- the EP combine b.reduce -> Executor::all_reduce -> Comm::all_reduce
+ *                        crates/model/src/qwen3moe_shard.rs:1051-1056,
+ *                        crates/executor/src/exec.rs:326-351, crates/ggml-sys/src/comm.rs:69-87
+ *
+ * Conventions (the same as ggml's, so a binding passes ggml tensor data pointers through):
+ *   - tensors are row-major with ne[0] fastest; an expert weight tensor is
+ *     [ne0 = K, ne1 = N rows, ne2 = experts or slots], row r of expert e at byte
+ *     e*nb2 + r*nb1.  gate/up are [H, I, E], down is [I, H, E];
+ *   - type ids are ggml's: 12 = Q4_K, 14 = Q6_K;
+ *   - ids are int32 [T][k] (token-major); an id < 0 means "no expert": nothing is read and the
+ *     row is exactly zero (patches/0004-cuda-mul-mat-id-skip-negative.patch:1-10);
+ *   - every pointer argument of a compute call is a device pointer; `stream` is a cudaStream_t
+ *     (NULL = the legacy default stream).  Calls are stream-ordered and do not block the host.
+ *
+ * Errors: every call returns TMOE_OK (0) or a negative TMOE_E* code and never aborts; the
+ * message is kept per handle (tmoe_last_error).  Device-side faults of the kernels' own bounded
+ * waits are latched in a device flag and reported by tmoe_check().
+ * Threading: a handle is used from one host thread at a time (one handle per model thread,
+ * like the reference's non-Send builder).  Workspace is owned by the handle, sized at create.
+ */
+#ifndef TMOE_H
+#define TMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TMOE_API __attribute__((visibility("default")))
+#else
+#define TMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TMOE_OK 0
+#define TMOE_E_INVALID -1   /* bad argument or shape */
+#define TMOE_E_CUDA -2      /* a CUDA runtime call failed */
+#define TMOE_E_NOMEM -3     /* device allocation failed */
+#define TMOE_E_UNSUPPORTED -4
+#define TMOE_E_DEVICE -5    /* a kernel reported an error (timeout of a bounded wait) */
+#define TMOE_E_COMM -6      /* NCCL failure */
+
+#define TMOE_TYPE_Q4_K 12
+#define TMOE_TYPE_Q6_K 14
+
+typedef struct tmoe_handle tmoe_handle;
+
+typedef struct {
+    int32_t n_embd;        /* H */
+    int32_t n_ff;          /* I, moe_intermediate */
+    int32_t n_expert;      /* E, router width (global expert count) */
+    int32_t n_expert_used; /* k */
+    int32_t gate_type;     /* ggml type ids */
+    int32_t up_type;
+    int32_t down_type;
+    int32_t max_tokens;    /* T the workspace is sized for */
+    int32_t device;        /* CUDA ordinal */
+    float rms_eps;         /* rms_norm epsilon of the router's ffn_norm */
+} tmoe_config;
+
+/* Stacked or slot expert tensors, device pointers into caller-owned buffers (never copied). */
+typedef struct {
+    const void *gate;
+    const void *up;
+    const void *down;
+    size_t gate_nb1, gate_nb2; /* row and expert strides in bytes */
+    size_t up_nb1, up_nb2;
+    size_t down_nb1, down_nb2;
+    int32_t n_slots; /* experts (or slots) in the tensors; ids must be < n_slots */
+} tmoe_expert_tensors;
+
+/* Returns the ABI version (major * 100 + minor). */
+TMOE_API int tmoe_version(void);
+
+TMOE_API int tmoe_create(const tmoe_config *cfg, tmoe_handle **out);
+TMOE_API void tmoe_destroy(tmoe_handle *h);
+/* Message of the last failed call on this handle ("" if none).  NULL handle: the last
+ * create failure of this thread. */
+TMOE_API const char *tmoe_last_error(const tmoe_handle *h);
+/* Synchronises `stream`, then reads and clears the device error flag. */
+TMOE_API int tmoe_check(tmoe_handle *h, void *stream);
+
+/* ggml mul_mat_id: out[t][j][:] = W[ids[t][j]] . b[t][b1 == 1 ? 0 : j][:]  (f32 [T][n_used][N]).
+ * W: [K, N, n_w] of `type` (Q4_K or Q6_K, K % 256 == 0) with strides nb1/nb2;
+ * b: f32 [T][b1][K], b1 == 1 or n_used; activations go through Q8_K as on ggml's CPU path. */
+TMOE_API int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1,
+                    size_t nb2, int64_t K, int64_t N, int64_t n_w, const float *b, int64_t b1,
+                    const int32_t *ids, int64_t n_used, int64_t T, float *out);
+
+/* router(): optional xn = rms_norm(x, eps) * norm_w (use_norm != 0; norm_w may be NULL),
+ * logits = router_w . xn (router_w f32 [E][H], the ggml [H, E] gate_inp) or the given
+ * `logits` f32 [T][E] when router_w is NULL; probs = softmax; ids = top-k (descending, ties to
+ * the lower index); w = sel / clamp(sum sel, 6.1035156e-5).  ids_out int32 [T][k], w_out f32
+ * [T][k]; xn_out f32 [T][H] and logits_out f32 [T][E] may be NULL. */
+TMOE_API int tmoe_route(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t use_norm,
+               const float *norm_w, const float *router_w, const float *logits, int32_t *ids_out,
+               float *w_out, float *xn_out, float *logits_out);
+
+/* weighted_experts() + sum_experts(): out[t] = sum_j w[t][j] * down(silu(gate xn_t) * up xn_t)
+ * over the choices j in order; ids are slot ids of `wts` (< 0: no contribution). */
+TMOE_API int tmoe_experts(tmoe_handle *h, void *stream, const float *xn, int64_t T, const int32_t *ids,
+                 const float *w, const tmoe_expert_tensors *wts, float *out);
+
+/* route + (optional id map) + experts in one call.  id_map int32 [E] (device) maps global
+ * expert ids to slots of `wts` or -1 (NULL: identity).  ids_out / w_out may be NULL. */
+TMOE_API int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t use_norm,
+               const float *norm_w, const float *router_w, const float *logits,
+               const int32_t *id_map, const tmoe_expert_tensors *wts, float *out,
+               int32_t *ids_out, float *w_out);
+
+/* ids' = table[ids] for ids in [0, n_table), else -1 (the EP expert_map lookup). */
+TMOE_API int tmoe_map_ids(tmoe_handle *h, void *stream, const int32_t *ids, int64_t n,
+                 const int32_t *table, int64_t n_table, int32_t *out);
+
+/* The per-expert dispatch of `ids` int32 [T][k] over n_slots experts (a4 of the path, the row
+ * mapping of ggml's mul_mat_id): counts[n_slots], offsets[n_slots + 1] and perm[] holding, for
+ * each expert in increasing order, its pair indices t*k + j in increasing order (token-major,
+ * choice-minor: crates/model/src/qwen3moe.rs:2126-2150 group_pairs).  Ids outside
+ * [0, n_slots) are skipped; perm must hold T*k entries (offsets[n_slots] are written). */
+TMOE_API int tmoe_dispatch(tmoe_handle *h, void *stream, const int32_t *ids, int64_t T,
+                           int32_t n_slots, int32_t *counts, int32_t *offsets, int32_t *perm);
+
+/* quant::quantize (crates/ggml-sys/src/quant.rs:52) for Q4_K / Q6_K on the device: nrows x ncols
+ * f32 (ncols % 256 == 0) -> nrows * row_size bytes.  This library's own fit of the formats, not
+ * ggml's search; the bytes are deterministic.  Errors: tmoe_last_error(NULL). */
+TMOE_API int tmoe_quantize(int32_t type, const float *x, int64_t nrows, int64_t ncols, void *out,
+                           void *stream);
+/* quant::to_f32 (crates/ggml-sys/src/quant.rs:19) for Q4_K / Q6_K: n values (n % 256 == 0). */
+TMOE_API int tmoe_dequantize(int32_t type, const void *in, int64_t n, float *out, void *stream);
+
+/* Per-kernel device timing of this handle's calls (the StepProfile phase timers of
+ * crates/model/src/qwen3moe.rs:69-107, narrowed to the layer's kernels).  While enabled, every
+ * kernel launch is bracketed by CUDA events on its stream; tmoe_profile_collect synchronises,
+ * adds the elapsed times to per-phase totals and writes the totals (ms) and launch counts to
+ * arrays of TMOE_N_PHASES entries (either may be NULL).  Enabling resets the totals.  At most
+ * 64 launches are recorded between two collects.  Phase ids: */
+#define TMOE_PHASE_RMS_NORM 0
+#define TMOE_PHASE_ROUTER_LOGITS 1
+#define TMOE_PHASE_TOPK 2
+#define TMOE_PHASE_MAP_IDS 3
+#define TMOE_PHASE_DISPATCH 4
+#define TMOE_PHASE_QUANT_X 5
+#define TMOE_PHASE_GATE_UP 6
+#define TMOE_PHASE_QUANT_ACT 7
+#define TMOE_PHASE_DOWN 8
+#define TMOE_PHASE_COMBINE 9
+#define TMOE_N_PHASES 10
+TMOE_API int tmoe_profile_enable(tmoe_handle *h, int32_t enable);
+TMOE_API int tmoe_profile_collect(tmoe_handle *h, double *ms_out, int64_t *count_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TMOE_H */

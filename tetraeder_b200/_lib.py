@@ -1,0 +1,93 @@
+"""ctypes binding of libtmoe.so (include/tmoe.h).  No fallback: if the library is missing or
+cannot load, every call raises."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libtmoe.so")
+HEADER = os.path.join(HERE, "..", "include", "tmoe.h")
+
+TMOE_OK = 0
+ERRORS = {-1: "TMOE_E_INVALID", -2: "TMOE_E_CUDA", -3: "TMOE_E_NOMEM", -4: "TMOE_E_UNSUPPORTED",
+          -5: "TMOE_E_DEVICE", -6: "TMOE_E_COMM"}
+TYPE_Q4_K, TYPE_Q6_K = 12, 14
+
+
+class TmoeError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class Config(C.Structure):
+    _fields_ = [("n_embd", C.c_int32), ("n_ff", C.c_int32), ("n_expert", C.c_int32),
+                ("n_expert_used", C.c_int32), ("gate_type", C.c_int32), ("up_type", C.c_int32),
+                ("down_type", C.c_int32), ("max_tokens", C.c_int32), ("device", C.c_int32),
+                ("rms_eps", C.c_float)]
+
+
+class ExpertTensors(C.Structure):
+    _fields_ = [("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p),
+                ("gate_nb1", C.c_size_t), ("gate_nb2", C.c_size_t),
+                ("up_nb1", C.c_size_t), ("up_nb2", C.c_size_t),
+                ("down_nb1", C.c_size_t), ("down_nb2", C.c_size_t),
+                ("n_slots", C.c_int32)]
+
+
+P = C.c_void_p
+I32, I64 = C.c_int32, C.c_int64
+SIGNATURES = {
+    "tmoe_version": ([], C.c_int),
+    "tmoe_create": ([C.POINTER(Config), C.POINTER(C.c_void_p)], C.c_int),
+    "tmoe_destroy": ([P], None),
+    "tmoe_last_error": ([P], C.c_char_p),
+    "tmoe_check": ([P, P], C.c_int),
+    "tmoe_mul_mat_id": ([P, P, I32, P, C.c_size_t, C.c_size_t, I64, I64, I64, P, I64, P, I64, I64, P],
+                        C.c_int),
+    "tmoe_route": ([P, P, P, I64, I32, P, P, P, P, P, P, P], C.c_int),
+    "tmoe_experts": ([P, P, P, I64, P, P, C.POINTER(ExpertTensors), P], C.c_int),
+    "tmoe_layer": ([P, P, P, I64, I32, P, P, P, P, C.POINTER(ExpertTensors), P, P, P], C.c_int),
+    "tmoe_map_ids": ([P, P, P, I64, P, I64, P], C.c_int),
+    "tmoe_dispatch": ([P, P, P, I64, I32, P, P, P], C.c_int),
+    "tmoe_quantize": ([I32, P, I64, I64, P, P], C.c_int),
+    "tmoe_dequantize": ([I32, P, I64, P, P], C.c_int),
+    "tmoe_profile_enable": ([P, I32], C.c_int),
+    "tmoe_profile_collect": ([P, P, P], C.c_int),
+}
+PHASES = ["rms_norm", "router_logits", "topk", "map_ids", "dispatch", "quant_x", "gate_up", "quant_act",
+          "down", "combine"]
+
+_lib = None
+
+
+def header_symbols() -> list[str]:
+    """Every function the C ABI header declares."""
+    with open(HEADER) as f:
+        text = f.read()
+    return re.findall(r"TMOE_API\s+[\w\s\*]+?\b(tmoe_\w+)\s*\(", text)
+
+
+def load():
+    """Loads libtmoe.so (building it first if it is absent and nvcc is here)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        from . import build as _build
+        _build.build()
+    lib = C.CDLL(LIB_PATH)
+    for name, (args, res) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = lib
+    return lib
+
+
+def check(rc: int, handle=None):
+    if rc != TMOE_OK:
+        msg = load().tmoe_last_error(handle)
+        raise TmoeError(rc, msg.decode() if msg else "")

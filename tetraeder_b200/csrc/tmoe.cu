@@ -1,0 +1,549 @@
+// C ABI of the MoE layer hot path (include/tmoe.h): handle, workspace and the launch sequences
+// route -> dispatch -> gate/up (+SwiGLU) -> Q8_K of the activation -> down -> combine.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/tmoe.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace {
+
+constexpr int kMaxSlots = 1024;
+thread_local std::string g_create_error;
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+struct tmoe_handle {
+    tmoe_config cfg{};
+    int sm_count = 0;
+    void *ws = nullptr;
+    size_t ws_bytes = 0;
+    // routing
+    float *logits = nullptr;
+    int32_t *ids = nullptr;
+    float *w = nullptr;
+    int32_t *mapped = nullptr;
+    int32_t *counts = nullptr, *offsets = nullptr, *perm = nullptr, *active = nullptr, *n_active = nullptr;
+    // activations
+    float *xn = nullptr;
+    int8_t *xq = nullptr;
+    float *xd = nullptr;
+    int16_t *xb = nullptr;
+    float *act = nullptr;
+    int8_t *aq = nullptr;
+    float *ad = nullptr;
+    int16_t *ab = nullptr;
+    float *dout = nullptr;
+    int *err = nullptr;
+    // growable scratch of tmoe_mul_mat_id
+    void *op_ws = nullptr;
+    size_t op_ws_bytes = 0;
+    std::string last_error;
+    // per-kernel timing (tmoe_profile_*)
+    struct Prof {
+        bool on = false;
+        static constexpr int kRing = 128;
+        cudaEvent_t ev[kRing] = {};
+        int phase[kRing / 2] = {};
+        int n = 0;  // events recorded since the last collect
+        double ms[TMOE_N_PHASES] = {};
+        int64_t count[TMOE_N_PHASES] = {};
+    } prof;
+};
+
+namespace {
+
+int fail(tmoe_handle *h, int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    if (h)
+        h->last_error = buf;
+    else
+        g_create_error = buf;
+    return code;
+}
+
+int cuda_fail(tmoe_handle *h, cudaError_t e, const char *what) {
+    return fail(h, TMOE_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+// Brackets one kernel launch with timing events when profiling is on.
+struct PhaseMark {
+    tmoe_handle *h;
+    cudaStream_t st;
+    int slot = -1;
+    PhaseMark(tmoe_handle *h_, cudaStream_t st_, int phase) : h(h_), st(st_) {
+        auto &p = h->prof;
+        if (!p.on || p.n + 2 > tmoe_handle::Prof::kRing) return;
+        slot = p.n;
+        p.phase[slot / 2] = phase;
+        cudaEventRecord(p.ev[slot], st);
+        p.n += 2;
+    }
+    ~PhaseMark() {
+        if (slot >= 0) cudaEventRecord(h->prof.ev[slot + 1], st);
+    }
+};
+
+bool is_kquant(int t) { return t == TMOE_TYPE_Q4_K || t == TMOE_TYPE_Q6_K; }
+int wt_of(int t) { return t == TMOE_TYPE_Q4_K ? TMOE_WT_Q4K : TMOE_WT_Q6K; }
+size_t row_size(int t, int64_t K) {
+    return (size_t)(K / TMOE_QK) * (t == TMOE_TYPE_Q4_K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES);
+}
+
+// Carves the workspace out of one allocation; returns the bytes needed when base == nullptr.
+size_t carve(tmoe_handle *h, char *base) {
+    const tmoe_config &c = h->cfg;
+    const size_t T = (size_t)c.max_tokens, k = (size_t)c.n_expert_used, P = T * k;
+    const size_t H = (size_t)c.n_embd, I = (size_t)c.n_ff, E = (size_t)c.n_expert;
+    size_t off = 0;
+    auto take = [&](size_t bytes) -> char * {
+        char *p = base ? base + off : nullptr;
+        off = align_up(off + bytes, 256);
+        return p;
+    };
+    h->logits = (float *)take(T * E * 4);
+    h->ids = (int32_t *)take(P * 4);
+    h->w = (float *)take(P * 4);
+    h->mapped = (int32_t *)take(P * 4);
+    h->counts = (int32_t *)take(kMaxSlots * 4);
+    h->offsets = (int32_t *)take((kMaxSlots + 1) * 4);
+    h->active = (int32_t *)take(kMaxSlots * 4);
+    h->n_active = (int32_t *)take(4);
+    h->perm = (int32_t *)take(P * 4);
+    h->xn = (float *)take(T * H * 4);
+    h->xq = (int8_t *)take(T * H);
+    h->xd = (float *)take(T * (H / 256) * 4);
+    h->xb = (int16_t *)take(T * (H / 16) * 2);
+    h->act = (float *)take(P * I * 4);
+    h->aq = (int8_t *)take(P * I);
+    h->ad = (float *)take(P * (I / 256) * 4);
+    h->ab = (int16_t *)take(P * (I / 16) * 2);
+    h->dout = (float *)take(P * H * 4);
+    h->err = (int *)take(4);
+    return off;
+}
+
+int check_tensors(tmoe_handle *h, const tmoe_expert_tensors *t) {
+    const tmoe_config &c = h->cfg;
+    if (!t || !t->gate || !t->up || !t->down) return fail(h, TMOE_E_INVALID, "expert tensors missing");
+    if (t->n_slots <= 0 || t->n_slots > kMaxSlots)
+        return fail(h, TMOE_E_INVALID, "n_slots %d out of range (1..%d)", t->n_slots, kMaxSlots);
+    const size_t gr = row_size(c.gate_type, c.n_embd), ur = row_size(c.up_type, c.n_embd),
+                 dr = row_size(c.down_type, c.n_ff);
+    if (t->gate_nb1 != gr || t->up_nb1 != ur || t->down_nb1 != dr)
+        return fail(h, TMOE_E_UNSUPPORTED, "expert rows must be contiguous (nb1 == row size)");
+    if (t->gate_nb2 < gr * (size_t)c.n_ff || t->up_nb2 < ur * (size_t)c.n_ff ||
+        t->down_nb2 < dr * (size_t)c.n_embd)
+        return fail(h, TMOE_E_INVALID, "expert stride smaller than one expert");
+    if (((uintptr_t)t->gate | (uintptr_t)t->up | (uintptr_t)t->down) & 15u)
+        return fail(h, TMOE_E_INVALID, "expert tensors must be 16-byte aligned");
+    if ((t->gate_nb2 | t->up_nb2 | t->down_nb2) & 15u)
+        return fail(h, TMOE_E_INVALID, "expert strides must be multiples of 16 bytes");
+    return TMOE_OK;
+}
+
+// a4-a8 on `ids` (already slot ids) and `w`.
+int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, const int32_t *ids,
+                const float *w, const tmoe_expert_tensors *t, float *out) {
+    const tmoe_config &c = h->cfg;
+    const int k = c.n_expert_used, H = c.n_embd, I = c.n_ff;
+    const int64_t P = T * k;
+    cudaError_t e;
+    {
+        PhaseMark pm(h, st, TMOE_PHASE_DISPATCH);
+        e = tmoe::launch_sort_pairs(ids, (int)P, t->n_slots, h->counts, h->offsets, h->perm, h->active,
+                                    h->n_active, h->err, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "sort_pairs");
+    {
+        PhaseMark pm(h, st, TMOE_PHASE_QUANT_X);
+        e = tmoe::launch_quantize_q8k(xn, T, H, nullptr, h->xq, h->xd, h->xb, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "quantize x");
+    const int max_active = (int)(P < t->n_slots ? P : t->n_slots);
+    tmoe::GemvArgs g{};
+    g.w0 = (const uint8_t *)t->gate;
+    g.w1 = (const uint8_t *)t->up;
+    g.nb1_0 = t->gate_nb1, g.nb2_0 = t->gate_nb2, g.nb1_1 = t->up_nb1, g.nb2_1 = t->up_nb2;
+    g.K = H, g.N = I;
+    g.xq = h->xq, g.xd = h->xd, g.xb = h->xb, g.x_div = k;
+    g.perm = h->perm, g.offsets = h->offsets, g.active = h->active, g.n_active = h->n_active;
+    g.out = h->act, g.err = h->err;
+    {
+        PhaseMark pm(h, st, TMOE_PHASE_GATE_UP);
+        e = tmoe::launch_gemv(wt_of(c.gate_type), true, g, max_active, h->sm_count, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "gate/up gemv");
+    {
+        PhaseMark pm(h, st, TMOE_PHASE_QUANT_ACT);
+        e = tmoe::launch_quantize_q8k(h->act, P, I, ids, h->aq, h->ad, h->ab, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "quantize act");
+    tmoe::GemvArgs d{};
+    d.w0 = (const uint8_t *)t->down;
+    d.nb1_0 = t->down_nb1, d.nb2_0 = t->down_nb2;
+    d.K = I, d.N = H;
+    d.xq = h->aq, d.xd = h->ad, d.xb = h->ab, d.x_div = 1;
+    d.perm = h->perm, d.offsets = h->offsets, d.active = h->active, d.n_active = h->n_active;
+    d.out = h->dout, d.err = h->err;
+    {
+        PhaseMark pm(h, st, TMOE_PHASE_DOWN);
+        e = tmoe::launch_gemv(wt_of(c.down_type), false, d, max_active, h->sm_count, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "down gemv");
+    {
+        PhaseMark pm(h, st, TMOE_PHASE_COMBINE);
+        e = tmoe::launch_combine(h->dout, ids, w, T, k, H, t->n_slots, out, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "combine");
+    return TMOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tmoe_version(void) { return 100; }
+
+int tmoe_create(const tmoe_config *cfg, tmoe_handle **out) {
+    if (!cfg || !out) return fail(nullptr, TMOE_E_INVALID, "null argument");
+    *out = nullptr;
+    const tmoe_config &c = *cfg;
+    if (c.n_embd <= 0 || c.n_ff <= 0 || c.n_expert <= 0 || c.n_expert_used <= 0 || c.max_tokens <= 0)
+        return fail(nullptr, TMOE_E_INVALID, "non-positive dimension in config");
+    if (c.n_embd % 256 || c.n_ff % 256)
+        return fail(nullptr, TMOE_E_INVALID, "n_embd and n_ff must be multiples of 256 (K-quant super-blocks)");
+    if (c.n_expert > 256 || c.n_expert_used > 32 || c.n_expert_used > c.n_expert)
+        return fail(nullptr, TMOE_E_INVALID, "n_expert <= 256 and n_expert_used <= min(32, n_expert) required");
+    if (!is_kquant(c.gate_type) || !is_kquant(c.up_type) || !is_kquant(c.down_type))
+        return fail(nullptr, TMOE_E_UNSUPPORTED, "expert types must be Q4_K (12) or Q6_K (14)");
+    if (c.gate_type != c.up_type)
+        return fail(nullptr, TMOE_E_UNSUPPORTED, "gate and up must share a type");
+    if ((int64_t)c.max_tokens * c.n_expert_used > (1 << 30))
+        return fail(nullptr, TMOE_E_INVALID, "max_tokens * n_expert_used too large");
+    DeviceGuard dg(c.device);
+    if (!dg.ok) return fail(nullptr, TMOE_E_CUDA, "cudaSetDevice(%d) failed", c.device);
+    tmoe_handle *h = new tmoe_handle();
+    h->cfg = c;
+    if (cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, c.device) != cudaSuccess) {
+        delete h;
+        return fail(nullptr, TMOE_E_CUDA, "cannot query the SM count");
+    }
+    if (c.n_ff % tmoe::gemv_rows_per_item(wt_of(c.gate_type), true, c.n_embd) ||
+        c.n_embd % tmoe::gemv_rows_per_item(wt_of(c.down_type), false, c.n_ff)) {
+        delete h;
+        return fail(nullptr, TMOE_E_UNSUPPORTED, "row counts must be multiples of the GEMV row tile");
+    }
+    h->ws_bytes = carve(h, nullptr);
+    cudaError_t e = cudaMalloc(&h->ws, h->ws_bytes);
+    if (e != cudaSuccess) {
+        delete h;
+        return fail(nullptr, TMOE_E_NOMEM, "cudaMalloc(%zu) failed: %s", h->ws_bytes, cudaGetErrorString(e));
+    }
+    carve(h, (char *)h->ws);
+    e = cudaMemset(h->err, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        cudaFree(h->ws);
+        delete h;
+        return fail(nullptr, TMOE_E_CUDA, "cudaMemset: %s", cudaGetErrorString(e));
+    }
+    *out = h;
+    return TMOE_OK;
+}
+
+void tmoe_destroy(tmoe_handle *h) {
+    if (!h) return;
+    DeviceGuard dg(h->cfg.device);
+    if (h->ws) cudaFree(h->ws);
+    if (h->op_ws) cudaFree(h->op_ws);
+    for (auto &ev : h->prof.ev)
+        if (ev) cudaEventDestroy(ev);
+    delete h;
+}
+
+const char *tmoe_last_error(const tmoe_handle *h) {
+    return h ? h->last_error.c_str() : g_create_error.c_str();
+}
+
+int tmoe_check(tmoe_handle *h, void *stream) {
+    if (!h) return TMOE_E_INVALID;
+    DeviceGuard dg(h->cfg.device);
+    cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(h, e, "stream synchronize");
+    int flag = 0;
+    if ((e = cudaMemcpy(&flag, h->err, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(h, e, "read error flag");
+    if (flag) {
+        cudaMemset(h->err, 0, sizeof(int));
+        if (flag == TMOE_DEV_ERR_BADID) return fail(h, TMOE_E_INVALID, "an expert id was >= n_slots");
+        return fail(h, TMOE_E_DEVICE, "a kernel gave up on a bounded wait (code %d)", flag);
+    }
+    return TMOE_OK;
+}
+
+int tmoe_route(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t use_norm,
+               const float *norm_w, const float *router_w, const float *logits, int32_t *ids_out,
+               float *w_out, float *xn_out, float *logits_out) {
+    if (!h) return TMOE_E_INVALID;
+    const tmoe_config &c = h->cfg;
+    if (T < 0 || T > c.max_tokens) return fail(h, TMOE_E_INVALID, "T=%lld outside [0, max_tokens]", (long long)T);
+    if (!ids_out || !w_out) return fail(h, TMOE_E_INVALID, "ids_out and w_out are required");
+    if (!router_w && !logits) return fail(h, TMOE_E_INVALID, "need router_w or logits");
+    if ((router_w || use_norm) && !x) return fail(h, TMOE_E_INVALID, "x is required");
+    if (T == 0) return TMOE_OK;
+    DeviceGuard dg(c.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e;
+    const float *xs = x;
+    if (use_norm) {
+        float *dst = xn_out ? xn_out : h->xn;
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_RMS_NORM);
+            e = tmoe::launch_rms_norm(x, norm_w, c.rms_eps, T, c.n_embd, dst, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "rms_norm");
+        xs = dst;
+    } else if (xn_out && x) {
+        if ((e = cudaMemcpyAsync(xn_out, x, sizeof(float) * T * c.n_embd, cudaMemcpyDeviceToDevice, st)) !=
+            cudaSuccess)
+            return cuda_fail(h, e, "copy xn");
+    }
+    const float *lg = logits;
+    if (router_w) {
+        float *dst = logits_out ? logits_out : h->logits;
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_ROUTER_LOGITS);
+            e = tmoe::launch_router_logits(xs, router_w, T, c.n_embd, c.n_expert, dst, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "router logits");
+        lg = dst;
+    } else if (logits_out) {
+        if ((e = cudaMemcpyAsync(logits_out, logits, sizeof(float) * T * c.n_expert, cudaMemcpyDeviceToDevice,
+                                 st)) != cudaSuccess)
+            return cuda_fail(h, e, "copy logits");
+    }
+    {
+        PhaseMark pm(h, st, TMOE_PHASE_TOPK);
+        e = tmoe::launch_softmax_topk(lg, T, c.n_expert, c.n_expert_used, ids_out, w_out, nullptr, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "softmax/top-k");
+    return TMOE_OK;
+}
+
+int tmoe_experts(tmoe_handle *h, void *stream, const float *xn, int64_t T, const int32_t *ids,
+                 const float *w, const tmoe_expert_tensors *wts, float *out) {
+    if (!h) return TMOE_E_INVALID;
+    const tmoe_config &c = h->cfg;
+    if (T < 0 || T > c.max_tokens) return fail(h, TMOE_E_INVALID, "T=%lld outside [0, max_tokens]", (long long)T);
+    if (!xn || !ids || !w || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    int rc = check_tensors(h, wts);
+    if (rc) return rc;
+    if (T == 0) return TMOE_OK;
+    DeviceGuard dg(c.device);
+    return run_experts(h, (cudaStream_t)stream, xn, T, ids, w, wts, out);
+}
+
+int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t use_norm,
+               const float *norm_w, const float *router_w, const float *logits,
+               const int32_t *id_map, const tmoe_expert_tensors *wts, float *out, int32_t *ids_out,
+               float *w_out) {
+    if (!h) return TMOE_E_INVALID;
+    const tmoe_config &c = h->cfg;
+    if (T < 0 || T > c.max_tokens) return fail(h, TMOE_E_INVALID, "T=%lld outside [0, max_tokens]", (long long)T);
+    if (!x || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    int rc = check_tensors(h, wts);
+    if (rc) return rc;
+    if (T == 0) return TMOE_OK;
+    DeviceGuard dg(c.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    int32_t *ids = ids_out ? ids_out : h->ids;
+    float *w = w_out ? w_out : h->w;
+    rc = tmoe_route(h, stream, x, T, use_norm, norm_w, router_w, logits, ids, w, use_norm ? h->xn : nullptr,
+                    nullptr);
+    if (rc) return rc;
+    const float *xn = use_norm ? h->xn : x;
+    const int32_t *used = ids;
+    if (id_map) {
+        cudaError_t e;
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_MAP_IDS);
+            e = tmoe::launch_map_ids(ids, T * c.n_expert_used, id_map, c.n_expert, h->mapped, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "map ids");
+        used = h->mapped;
+    }
+    return run_experts(h, st, xn, T, used, w, wts, out);
+}
+
+int tmoe_map_ids(tmoe_handle *h, void *stream, const int32_t *ids, int64_t n, const int32_t *table,
+                 int64_t n_table, int32_t *out) {
+    if (!h) return TMOE_E_INVALID;
+    if (n < 0 || n_table < 0 || (n > 0 && (!ids || !table || !out)))
+        return fail(h, TMOE_E_INVALID, "bad map_ids arguments");
+    DeviceGuard dg(h->cfg.device);
+    cudaError_t e = tmoe::launch_map_ids(ids, n, table, n_table, out, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(h, e, "map ids");
+    return TMOE_OK;
+}
+
+int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1, size_t nb2,
+                    int64_t K, int64_t N, int64_t n_w, const float *b, int64_t b1, const int32_t *ids,
+                    int64_t n_used, int64_t T, float *out) {
+    if (!h) return TMOE_E_INVALID;
+    if (!is_kquant(type)) return fail(h, TMOE_E_UNSUPPORTED, "mul_mat_id type %d (need Q4_K or Q6_K)", type);
+    if (K <= 0 || K % 256 || N <= 0 || n_w <= 0 || n_w > kMaxSlots || n_used <= 0 || T < 0 ||
+        (b1 != 1 && b1 != n_used))
+        return fail(h, TMOE_E_INVALID, "bad mul_mat_id shape");
+    if (!W || !b || !ids || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    const int wt = wt_of(type);
+    if (nb1 != row_size(type, K)) return fail(h, TMOE_E_UNSUPPORTED, "rows must be contiguous (nb1 == row size)");
+    if (((uintptr_t)W & 15u) || (nb2 & 15u)) return fail(h, TMOE_E_INVALID, "W and nb2 must be 16-byte aligned");
+    if (N % tmoe::gemv_rows_per_item(wt, false, (int)K))
+        return fail(h, TMOE_E_UNSUPPORTED, "N=%lld is not a multiple of the row tile %d", (long long)N,
+                    tmoe::gemv_rows_per_item(wt, false, (int)K));
+    if (T == 0) return TMOE_OK;
+    DeviceGuard dg(h->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t P = T * n_used, rows = T * b1;
+    // scratch: Q8_K of b, sort buffers
+    size_t need = 0;
+    auto lay = [&](size_t bytes) {
+        size_t o = need;
+        need = align_up(need + bytes, 256);
+        return o;
+    };
+    size_t o_q = lay((size_t)rows * K), o_d = lay((size_t)rows * (K / 256) * 4), o_b = lay((size_t)rows * (K / 16) * 2);
+    size_t o_cnt = lay(kMaxSlots * 4), o_off = lay((kMaxSlots + 1) * 4), o_act = lay(kMaxSlots * 4), o_na = lay(4);
+    size_t o_perm = lay((size_t)P * 4);
+    cudaError_t e;
+    if (need > h->op_ws_bytes) {
+        if (h->op_ws) {
+            cudaStreamSynchronize(st);
+            cudaFree(h->op_ws);
+            h->op_ws = nullptr;
+            h->op_ws_bytes = 0;
+        }
+        if ((e = cudaMalloc(&h->op_ws, need)) != cudaSuccess)
+            return fail(h, TMOE_E_NOMEM, "cudaMalloc(%zu): %s", need, cudaGetErrorString(e));
+        h->op_ws_bytes = need;
+    }
+    char *base = (char *)h->op_ws;
+    int8_t *q = (int8_t *)(base + o_q);
+    float *d = (float *)(base + o_d);
+    int16_t *bs = (int16_t *)(base + o_b);
+    int32_t *cnt = (int32_t *)(base + o_cnt), *offs = (int32_t *)(base + o_off), *act = (int32_t *)(base + o_act),
+            *na = (int32_t *)(base + o_na), *perm = (int32_t *)(base + o_perm);
+    if ((e = tmoe::launch_sort_pairs(ids, (int)P, (int)n_w, cnt, offs, perm, act, na, h->err, st)) != cudaSuccess)
+        return cuda_fail(h, e, "sort_pairs");
+    if ((e = tmoe::launch_quantize_q8k(b, rows, (int)K, nullptr, q, d, bs, st)) != cudaSuccess)
+        return cuda_fail(h, e, "quantize b");
+    if ((e = tmoe::launch_zero_invalid_rows(ids, P, (int)n_w, (int)N, out, st)) != cudaSuccess)
+        return cuda_fail(h, e, "zero rows");
+    tmoe::GemvArgs g{};
+    g.w0 = (const uint8_t *)W;
+    g.nb1_0 = nb1, g.nb2_0 = nb2;
+    g.K = (int)K, g.N = (int)N;
+    g.xq = q, g.xd = d, g.xb = bs, g.x_div = b1 == 1 ? (int)n_used : 1;
+    g.perm = perm, g.offsets = offs, g.active = act, g.n_active = na;
+    g.out = out, g.err = h->err;
+    const int max_active = (int)(P < n_w ? P : n_w);
+    if ((e = tmoe::launch_gemv(wt, false, g, max_active, h->sm_count, st)) != cudaSuccess)
+        return cuda_fail(h, e, "mul_mat_id gemv");
+    return TMOE_OK;
+}
+
+int tmoe_dispatch(tmoe_handle *h, void *stream, const int32_t *ids, int64_t T, int32_t n_slots,
+                  int32_t *counts, int32_t *offsets, int32_t *perm) {
+    if (!h) return TMOE_E_INVALID;
+    const tmoe_config &c = h->cfg;
+    if (T < 0 || T > c.max_tokens) return fail(h, TMOE_E_INVALID, "T=%lld outside [0, max_tokens]", (long long)T);
+    if (n_slots <= 0 || n_slots > kMaxSlots) return fail(h, TMOE_E_INVALID, "n_slots %d out of range", n_slots);
+    if (!ids || !counts || !offsets || !perm) return fail(h, TMOE_E_INVALID, "null tensor");
+    DeviceGuard dg(c.device);
+    cudaError_t e = tmoe::launch_sort_pairs(ids, (int)(T * c.n_expert_used), n_slots, counts, offsets, perm,
+                                            h->active, h->n_active, h->err, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(h, e, "sort_pairs");
+    return TMOE_OK;
+}
+
+int tmoe_quantize(int32_t type, const float *x, int64_t nrows, int64_t ncols, void *out, void *stream) {
+    if (!is_kquant(type)) return fail(nullptr, TMOE_E_UNSUPPORTED, "quantize type %d", type);
+    if (nrows < 0 || ncols <= 0 || ncols % 256) return fail(nullptr, TMOE_E_INVALID, "ncols must be a multiple of 256");
+    if (nrows == 0) return TMOE_OK;
+    if (!x || !out) return fail(nullptr, TMOE_E_INVALID, "null tensor");
+    cudaError_t e = tmoe::launch_quantize(wt_of(type), x, nrows * (ncols / 256), (uint8_t *)out, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "quantize");
+    return TMOE_OK;
+}
+
+int tmoe_dequantize(int32_t type, const void *in, int64_t n, float *out, void *stream) {
+    if (!is_kquant(type)) return fail(nullptr, TMOE_E_UNSUPPORTED, "dequantize type %d", type);
+    if (n < 0 || n % 256) return fail(nullptr, TMOE_E_INVALID, "n must be a multiple of 256");
+    if (n == 0) return TMOE_OK;
+    if (!in || !out) return fail(nullptr, TMOE_E_INVALID, "null tensor");
+    cudaError_t e = tmoe::launch_dequantize(wt_of(type), (const uint8_t *)in, n, out, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "dequantize");
+    return TMOE_OK;
+}
+
+int tmoe_profile_enable(tmoe_handle *h, int32_t enable) {
+    if (!h) return TMOE_E_INVALID;
+    DeviceGuard dg(h->cfg.device);
+    auto &p = h->prof;
+    if (enable && !p.ev[0]) {
+        for (auto &ev : p.ev) {
+            cudaError_t e = cudaEventCreate(&ev);
+            if (e != cudaSuccess) return cuda_fail(h, e, "cudaEventCreate");
+        }
+    }
+    p.on = enable != 0;
+    p.n = 0;
+    for (int i = 0; i < TMOE_N_PHASES; i++) p.ms[i] = 0.0, p.count[i] = 0;
+    return TMOE_OK;
+}
+
+int tmoe_profile_collect(tmoe_handle *h, double *ms_out, int64_t *count_out) {
+    if (!h) return TMOE_E_INVALID;
+    DeviceGuard dg(h->cfg.device);
+    auto &p = h->prof;
+    for (int i = 0; i + 1 < p.n; i += 2) {
+        cudaError_t e = cudaEventSynchronize(p.ev[i + 1]);
+        if (e != cudaSuccess) return cuda_fail(h, e, "cudaEventSynchronize");
+        float ms = 0.f;
+        if ((e = cudaEventElapsedTime(&ms, p.ev[i], p.ev[i + 1])) != cudaSuccess)
+            return cuda_fail(h, e, "cudaEventElapsedTime");
+        p.ms[p.phase[i / 2]] += ms;
+        p.count[p.phase[i / 2]] += 1;
+    }
+    p.n = 0;
+    for (int i = 0; i < TMOE_N_PHASES; i++) {
+        if (ms_out) ms_out[i] = p.ms[i];
+        if (count_out) count_out[i] = p.count[i];
+    }
+    return TMOE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,198 @@
+"""Host-side mirror of Tetraeder's MoE-layer operator interface over the C ABI.
+
+The names, argument meanings and error behaviour follow the reference's builder functions and
+ggml ops (paths relative to the tetraeder project root):
+
+  MoeLayer.router            crates/model/src/qwen3moe.rs:2871-2890   router()
+  MoeLayer.weighted_experts  crates/model/src/qwen3moe.rs:2899-2914   weighted_experts() (+ the
+                             sum_experts() fold of :2917-2923, done on device in choice order)
+  MoeLayer.moe_ffn           crates/model/src/qwen3moe.rs:2892-2896   moe_ffn()
+  MoeLayer.mul_mat_id        crates/ggml-sys/src/ggml/context.rs:322-336 Context::mul_mat_id
+  MoeLayer.map_ids           crates/model/src/qwen3moe_shard.rs:1043-1050 get_rows(map, ids)
+
+Tensors are torch CUDA tensors (plumbing only); the computation is the CUDA code of libtmoe.so.
+Where ggml aborts on a bad shape, these raise TmoeError (or ValueError before the call).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import TYPE_Q4_K, TYPE_Q6_K, TmoeError
+
+QK_K = 256
+BLOCK_BYTES = {TYPE_Q4_K: 144, TYPE_Q6_K: 210}
+
+
+def row_size(qtype: int, ncols: int) -> int:
+    if ncols % QK_K:
+        raise ValueError(f"{ncols} columns is not a multiple of {QK_K}")
+    return ncols // QK_K * BLOCK_BYTES[qtype]
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    s = torch.cuda.current_stream() if stream is None else stream
+    return C.c_void_p(s.cuda_stream)
+
+
+@dataclass
+class ExpertWeights:
+    """Stacked (or slot) expert tensors in ggml layout: uint8 [n_slots, rows, row_size]."""
+    gate: torch.Tensor
+    up: torch.Tensor
+    down: torch.Tensor
+
+    def c_struct(self) -> _lib.ExpertTensors:
+        for t in (self.gate, self.up, self.down):
+            if t.dtype != torch.uint8 or t.dim() != 3 or not t.is_cuda or not t.is_contiguous():
+                raise ValueError("expert tensors must be contiguous uint8 CUDA tensors [slots, rows, bytes]")
+        g, u, d = self.gate, self.up, self.down
+        return _lib.ExpertTensors(g.data_ptr(), u.data_ptr(), d.data_ptr(),
+                                  g.shape[2], g.shape[1] * g.shape[2],
+                                  u.shape[2], u.shape[1] * u.shape[2],
+                                  d.shape[2], d.shape[1] * d.shape[2], g.shape[0])
+
+
+def quantize(qtype: int, x: torch.Tensor, stream=None) -> torch.Tensor:
+    """quant::quantize on the device: f32 [..., ncols] -> uint8 [..., row_size(ncols)]."""
+    lib = _lib.load()
+    x = x.contiguous()
+    ncols = x.shape[-1]
+    nrows = x.numel() // ncols
+    out = torch.empty(x.shape[:-1] + (row_size(qtype, ncols),), dtype=torch.uint8, device=x.device)
+    _lib.check(lib.tmoe_quantize(qtype, _ptr(x), nrows, ncols, _ptr(out), _stream(stream)), None)
+    return out
+
+
+def dequantize(qtype: int, data: torch.Tensor, n: int, stream=None) -> torch.Tensor:
+    """quant::to_f32 on the device -> f32 [n]."""
+    lib = _lib.load()
+    out = torch.empty(n, dtype=torch.float32, device=data.device)
+    _lib.check(lib.tmoe_dequantize(qtype, _ptr(data.contiguous()), n, _ptr(out), _stream(stream)), None)
+    return out
+
+
+class MoeLayer:
+    """One handle of the C ABI: H, I, E, k, types and the workspace for `max_tokens`."""
+
+    def __init__(self, n_embd: int, n_ff: int, n_expert: int, n_expert_used: int,
+                 gate_type: int = TYPE_Q4_K, up_type: int = TYPE_Q4_K, down_type: int = TYPE_Q6_K,
+                 max_tokens: int = 64, device: int | None = None, rms_eps: float = 1e-6):
+        if not torch.cuda.is_available():
+            raise RuntimeError("tetraeder_b200 needs a CUDA device (there is no CPU path)")
+        self.lib = _lib.load()
+        dev = torch.cuda.current_device() if device is None else device
+        self.cfg = _lib.Config(n_embd, n_ff, n_expert, n_expert_used, gate_type, up_type, down_type,
+                               max_tokens, dev, rms_eps)
+        h = C.c_void_p()
+        _lib.check(self.lib.tmoe_create(C.byref(self.cfg), C.byref(h)), None)
+        self.h = h
+        self.device = torch.device("cuda", dev)
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.tmoe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- per-kernel timing --------------------------------------------------------------------
+    def profile(self, enable: bool = True):
+        """Brackets every kernel of this handle with CUDA events (resets the totals)."""
+        _lib.check(self.lib.tmoe_profile_enable(self.h, int(enable)), self.h)
+
+    def profile_collect(self) -> dict:
+        """{phase: (total_ms, launches)} accumulated since profile(True)."""
+        n = len(_lib.PHASES)
+        ms = (C.c_double * n)()
+        cnt = (C.c_int64 * n)()
+        _lib.check(self.lib.tmoe_profile_collect(self.h, ms, cnt), self.h)
+        return {name: (ms[i], cnt[i]) for i, name in enumerate(_lib.PHASES) if cnt[i]}
+
+    # -- ops ---------------------------------------------------------------------------------
+    def check(self, stream=None):
+        """Synchronises and raises if a kernel latched a device error."""
+        _lib.check(self.lib.tmoe_check(self.h, _stream(stream)), self.h)
+
+    def router(self, ffn_inp: torch.Tensor, router_w: torch.Tensor | None = None,
+               logits: torch.Tensor | None = None, ffn_norm: torch.Tensor | None = None,
+               use_norm: bool = False, stream=None, want_logits: bool = False):
+        """-> (xn, weights [T, k], ids [T, k]) like router(); xn is None without the norm."""
+        T = ffn_inp.shape[0] if ffn_inp is not None else logits.shape[0]
+        k = self.cfg.n_expert_used
+        ids = torch.empty((T, k), dtype=torch.int32, device=self.device)
+        w = torch.empty((T, k), dtype=torch.float32, device=self.device)
+        xn = torch.empty_like(ffn_inp) if use_norm else None
+        lg = torch.empty((T, self.cfg.n_expert), dtype=torch.float32, device=self.device) if want_logits else None
+        _lib.check(self.lib.tmoe_route(self.h, _stream(stream), _ptr(ffn_inp), T, int(use_norm),
+                                       _ptr(ffn_norm), _ptr(router_w), _ptr(logits), _ptr(ids), _ptr(w),
+                                       _ptr(xn), _ptr(lg)), self.h)
+        return (xn, w, ids, lg) if want_logits else (xn, w, ids)
+
+    def weighted_experts(self, xn: torch.Tensor, ids: torch.Tensor, w: torch.Tensor,
+                         experts: ExpertWeights, out: torch.Tensor | None = None, stream=None):
+        """down(silu(gate xn) * up xn) * w, summed over the choices in order -> [T, H]."""
+        T = xn.shape[0]
+        out = torch.empty((T, self.cfg.n_embd), dtype=torch.float32, device=self.device) if out is None else out
+        st = experts.c_struct()
+        _lib.check(self.lib.tmoe_experts(self.h, _stream(stream), _ptr(xn), T, _ptr(ids), _ptr(w),
+                                         C.byref(st), _ptr(out)), self.h)
+        return out
+
+    def moe_ffn(self, x: torch.Tensor, experts: ExpertWeights, router_w: torch.Tensor | None = None,
+                logits: torch.Tensor | None = None, id_map: torch.Tensor | None = None,
+                ffn_norm: torch.Tensor | None = None, use_norm: bool = False, out=None, ids_out=None,
+                w_out=None, stream=None):
+        """router + (EP id map) + weighted_experts in one C call -> [T, H]."""
+        T = x.shape[0]
+        out = torch.empty((T, self.cfg.n_embd), dtype=torch.float32, device=self.device) if out is None else out
+        st = experts.c_struct()
+        _lib.check(self.lib.tmoe_layer(self.h, _stream(stream), _ptr(x), T, int(use_norm), _ptr(ffn_norm),
+                                       _ptr(router_w), _ptr(logits), _ptr(id_map), C.byref(st), _ptr(out),
+                                       _ptr(ids_out), _ptr(w_out)), self.h)
+        return out
+
+    def mul_mat_id(self, qtype: int, W: torch.Tensor, b: torch.Tensor, ids: torch.Tensor,
+                   out: torch.Tensor | None = None, stream=None):
+        """ggml mul_mat_id: W uint8 [n_w, N, row_size(K)], b f32 [T, b1, K], ids [T, n_used]
+        -> f32 [T, n_used, N]; rows of id -1 are exactly zero."""
+        n_w, N, rs = W.shape
+        T, b1, K = b.shape
+        n_used = ids.shape[1]
+        if rs != row_size(qtype, K):
+            raise ValueError("W row size does not match K")
+        out = torch.empty((T, n_used, N), dtype=torch.float32, device=self.device) if out is None else out
+        _lib.check(self.lib.tmoe_mul_mat_id(self.h, _stream(stream), qtype, _ptr(W), rs, N * rs, K, N, n_w,
+                                            _ptr(b), b1, _ptr(ids), n_used, T, _ptr(out)), self.h)
+        return out
+
+    def dispatch(self, ids: torch.Tensor, n_slots: int, stream=None):
+        """Per-expert pairs of ids [T, k] -> (counts [n_slots], offsets [n_slots+1], perm [T*k]);
+        perm[offsets[n_slots]:] is unused."""
+        T = ids.shape[0]
+        counts = torch.empty(n_slots, dtype=torch.int32, device=self.device)
+        offsets = torch.empty(n_slots + 1, dtype=torch.int32, device=self.device)
+        perm = torch.full((ids.numel(),), -1, dtype=torch.int32, device=self.device)
+        _lib.check(self.lib.tmoe_dispatch(self.h, _stream(stream), _ptr(ids), T, n_slots, _ptr(counts),
+                                          _ptr(offsets), _ptr(perm)), self.h)
+        return counts, offsets, perm
+
+    def map_ids(self, ids: torch.Tensor, table: torch.Tensor, stream=None):
+        out = torch.empty_like(ids)
+        _lib.check(self.lib.tmoe_map_ids(self.h, _stream(stream), _ptr(ids), ids.numel(), _ptr(table),
+                                         table.numel(), _ptr(out)), self.h)
+        return out
+
+
+__all__ = ["MoeLayer", "ExpertWeights", "TmoeError", "TYPE_Q4_K", "TYPE_Q6_K", "row_size", "quantize", "dequantize"]
