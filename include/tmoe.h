@@ -34,7 +34,9 @@
  * message is kept per handle (tmoe_last_error).  Device-side faults of the kernels' own bounded
  * waits are latched in a device flag and reported by tmoe_check().
  * Threading: a handle is used from one host thread at a time (one handle per model thread,
- * like the reference's non-Send builder).  Workspace is owned by the handle, sized at create.
+ * like the reference's non-Send builder).  Workspace is owned by the handle, sized at create,
+ * and shared by its calls: issue a handle's calls on one stream, or order the streams (an event
+ * or a synchronisation) between calls on different ones.
  */
 #ifndef TMOE_H
 #define TMOE_H

@@ -1,0 +1,62 @@
+// Q8_K quantisation of one 256-element block by one warp (ggml quantize_row_q8_K_ref restated):
+// the first element of largest magnitude maps to -127, iscale = -127 / max,
+// q = min(127, round_half_even(iscale * x)), d = 1 / iscale, plus the 16-element block sums.
+// Every use (the standalone kernel and the fused sites) calls this routine, so the bytes agree.
+#pragma once
+
+#include "common.cuh"
+
+namespace tmoe {
+
+// Lane l holds elements 8l .. 8l+7 in v.  Returns the lane's 8 quantised values packed in q
+// (little-endian), the block's d, and s16 = the sum over the lane's 16-element group (lanes 2g
+// and 2g+1 both hold group g's sum).
+__device__ __forceinline__ void q8k_block_warp(const float (&v)[8], uint2 &q, float &d, int &s16) {
+    const int lane = threadIdx.x & 31;
+    float amax = 0.0f, maxv = 0.0f;
+    int idx = 0x7fffffff;
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+        const float ax = fabsf(v[c]);
+        if (ax > amax) {
+            amax = ax;
+            maxv = v[c];
+            idx = 8 * lane + c;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
+        const float ov = __shfl_xor_sync(0xffffffffu, maxv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+        if (oa > amax || (oa == amax && oi < idx)) {
+            amax = oa;
+            maxv = ov;
+            idx = oi;
+        }
+    }
+    int qi[8];
+    d = 0.0f;
+    if (amax == 0.0f) {
+#pragma unroll
+        for (int c = 0; c < 8; c++) qi[c] = 0;
+    } else {
+        const float iscale = __fdiv_rn(-127.0f, maxv);
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            const int t = __float2int_rn(__fmul_rn(iscale, v[c]));
+            qi[c] = t > 127 ? 127 : t;
+        }
+        d = __fdiv_rn(1.0f, iscale);
+    }
+    int s = 0;
+#pragma unroll
+    for (int c = 0; c < 8; c++) s += qi[c];
+    s16 = s + __shfl_xor_sync(0xffffffffu, s, 1);
+    q.x = (uint32_t)(qi[0] & 0xff) | ((uint32_t)(qi[1] & 0xff) << 8) | ((uint32_t)(qi[2] & 0xff) << 16) |
+          ((uint32_t)(qi[3] & 0xff) << 24);
+    q.y = (uint32_t)(qi[4] & 0xff) | ((uint32_t)(qi[5] & 0xff) << 8) | ((uint32_t)(qi[6] & 0xff) << 16) |
+          ((uint32_t)(qi[7] & 0xff) << 24);
+}
+
+}  // namespace tmoe

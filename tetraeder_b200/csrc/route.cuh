@@ -1,0 +1,122 @@
+// Canonical router arithmetic shared by the router kernels (route.cu) and the fused
+// top-k + dispatch kernel (dispatch.cu).  Every floating-point step that feeds the top-k is
+// written with explicit round-to-nearest intrinsics in one fixed order, so that the selected ids
+// are bit-identical with the CPU oracle:
+//   exp:      Cody-Waite reduction by ln 2 and a degree-7 Taylor polynomial (own code);
+//   softmax:  lane l sums e^(x-max) over experts l, l+32, ... then a butterfly over lane
+//             distances 16, 8, 4, 2, 1; p = e / sum (IEEE division);
+//   top-k:    k rounds of a warp argmax under the total order (p descending, index ascending);
+//   weights:  w_j = sel_j / max(sel_0 + sel_1 + ..., 6.1035156e-5) (qwen3moe.rs:2886-2888).
+#pragma once
+
+#include "common.cuh"
+
+namespace tmoe {
+
+__device__ __forceinline__ float exp_canon(float x) {
+    if (x != x) return x;
+    if (x < -87.0f) return 0.0f;
+    if (x > 88.0f) return __int_as_float(0x7f800000);
+    float kf = rintf(__fmul_rn(x, 1.44269504088896341f));
+    float r = __fmaf_rn(kf, -0.693145751953125f, x);
+    r = __fmaf_rn(kf, -1.42860682030941723212e-6f, r);
+    float p = 1.98412698412698412698e-4f;
+    p = __fmaf_rn(p, r, 1.38888888888888888889e-3f);
+    p = __fmaf_rn(p, r, 8.33333333333333333333e-3f);
+    p = __fmaf_rn(p, r, 4.16666666666666666667e-2f);
+    p = __fmaf_rn(p, r, 1.66666666666666666667e-1f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    int ki = static_cast<int>(kf);
+    return __fmul_rn(p, __int_as_float((ki + 127) << 23));
+}
+
+__device__ __forceinline__ float butterfly_f32(float v) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+__device__ __forceinline__ double butterfly_f64(double v) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+// One warp, one token: softmax over the E logits at lg, top-k, renormalised weights.
+// Lane j < k ends with choice j: *id = expert, *wt = weight.  probs may be NULL.
+template <int MAXPER>
+__device__ __forceinline__ void topk_token(const float *__restrict__ lg, int E, int k, float *__restrict__ probs,
+                                           int &id, float &wt) {
+    const int lane = threadIdx.x & 31;
+    float v[MAXPER];
+    float mx = __int_as_float(0xff800000);
+#pragma unroll
+    for (int i = 0; i < MAXPER; i++) {
+        const int e = lane + 32 * i;
+        v[i] = e < E ? lg[e] : __int_as_float(0xff800000);
+        if (e < E && v[i] > mx) mx = v[i];
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float part = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXPER; i++) {
+        const int e = lane + 32 * i;
+        if (e < E) {
+            v[i] = exp_canon(__fsub_rn(v[i], mx));
+            part = __fadd_rn(part, v[i]);
+        } else {
+            v[i] = -1.0f;  // below every probability: never selected
+        }
+    }
+    const float sum = butterfly_f32(part);
+#pragma unroll
+    for (int i = 0; i < MAXPER; i++) {
+        const int e = lane + 32 * i;
+        if (e < E) {
+            v[i] = __fdiv_rn(v[i], sum);
+            if (probs) probs[e] = v[i];
+        }
+    }
+    float sel_mine = 0.0f;
+    int id_mine = -1;
+    for (int j = 0; j < k; j++) {
+        float bp = -2.0f;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < MAXPER; i++) {
+            const int e = lane + 32 * i;
+            if (e < E && v[i] >= 0.0f && (v[i] > bp || (v[i] == bp && e < bi))) {
+                bp = v[i];
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            const float op = __shfl_xor_sync(0xffffffffu, bp, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (op > bp || (op == bp && oi < bi)) {
+                bp = op;
+                bi = oi;
+            }
+        }
+        if ((bi & 31) == lane) {
+#pragma unroll
+            for (int i = 0; i < MAXPER; i++)
+                if (lane + 32 * i == bi) v[i] = -1.0f;
+        }
+        if (lane == j) {
+            sel_mine = bp;
+            id_mine = bi;
+        }
+    }
+    float s = 0.0f;
+    for (int j = 0; j < k; j++) s = __fadd_rn(s, __shfl_sync(0xffffffffu, sel_mine, j));
+    if (!(s >= 6.103515625e-5f)) s = 6.103515625e-5f;
+    id = id_mine;
+    wt = __fdiv_rn(sel_mine, s);
+}
+
+}  // namespace tmoe

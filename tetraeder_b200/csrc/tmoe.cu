@@ -37,9 +37,6 @@ struct tmoe_handle {
     float *xd = nullptr;
     int16_t *xb = nullptr;
     float *act = nullptr;
-    int8_t *aq = nullptr;
-    float *ad = nullptr;
-    int16_t *ab = nullptr;
     float *dout = nullptr;
     int *err = nullptr;
     // growable scratch of tmoe_mul_mat_id
@@ -107,6 +104,8 @@ struct PhaseMark {
     }
 };
 
+bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
 bool is_kquant(int t) { return t == TMOE_TYPE_Q4_K || t == TMOE_TYPE_Q6_K; }
 int wt_of(int t) { return t == TMOE_TYPE_Q4_K ? TMOE_WT_Q4K : TMOE_WT_Q6K; }
 size_t row_size(int t, int64_t K) {
@@ -138,9 +137,6 @@ size_t carve(tmoe_handle *h, char *base) {
     h->xd = (float *)take(T * (H / 256) * 4);
     h->xb = (int16_t *)take(T * (H / 16) * 2);
     h->act = (float *)take(P * I * 4);
-    h->aq = (int8_t *)take(P * I);
-    h->ad = (float *)take(P * (I / 256) * 4);
-    h->ab = (int16_t *)take(P * (I / 16) * 2);
     h->dout = (float *)take(P * H * 4);
     h->err = (int *)take(4);
     return off;
@@ -165,24 +161,30 @@ int check_tensors(tmoe_handle *h, const tmoe_expert_tensors *t) {
     return TMOE_OK;
 }
 
-// a4-a8 on `ids` (already slot ids) and `w`.
-int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, const int32_t *ids,
-                const float *w, const tmoe_expert_tensors *t, float *out) {
+// a4-a8 on `ids` (already slot ids) and `w`.  dispatched: the dispatch buffers (counts, offsets,
+// perm, active) already hold this call's dispatch; x_quantized: h->xq/xd/xb already hold the
+// Q8_K rows of xn.
+int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, const int32_t *ids, const float *w,
+                const tmoe_expert_tensors *t, float *out, bool dispatched, bool x_quantized) {
     const tmoe_config &c = h->cfg;
     const int k = c.n_expert_used, H = c.n_embd, I = c.n_ff;
     const int64_t P = T * k;
     cudaError_t e;
-    {
-        PhaseMark pm(h, st, TMOE_PHASE_DISPATCH);
-        e = tmoe::launch_sort_pairs(ids, (int)P, t->n_slots, h->counts, h->offsets, h->perm, h->active,
-                                    h->n_active, h->err, st);
+    if (!dispatched) {
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_DISPATCH);
+            e = tmoe::launch_sort_pairs(ids, (int)P, t->n_slots, h->counts, h->offsets, h->perm, h->active,
+                                        h->n_active, h->err, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "sort_pairs");
     }
-    if (e != cudaSuccess) return cuda_fail(h, e, "sort_pairs");
-    {
-        PhaseMark pm(h, st, TMOE_PHASE_QUANT_X);
-        e = tmoe::launch_quantize_q8k(xn, T, H, nullptr, h->xq, h->xd, h->xb, st);
+    if (!x_quantized) {
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_QUANT_X);
+            e = tmoe::launch_quantize_q8k(xn, T, H, nullptr, h->xq, h->xd, h->xb, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "quantize x");
     }
-    if (e != cudaSuccess) return cuda_fail(h, e, "quantize x");
     const int max_active = (int)(P < t->n_slots ? P : t->n_slots);
     tmoe::GemvArgs g{};
     g.w0 = (const uint8_t *)t->gate;
@@ -191,23 +193,21 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
     g.K = H, g.N = I;
     g.xq = h->xq, g.xd = h->xd, g.xb = h->xb, g.x_div = k;
     g.perm = h->perm, g.offsets = h->offsets, g.active = h->active, g.n_active = h->n_active;
+    g.n_slots = t->n_slots, g.max_active = max_active, g.n_pairs = (int)P;
     g.out = h->act, g.err = h->err;
     {
         PhaseMark pm(h, st, TMOE_PHASE_GATE_UP);
         e = tmoe::launch_gemv(wt_of(c.gate_type), true, g, max_active, h->sm_count, st);
     }
     if (e != cudaSuccess) return cuda_fail(h, e, "gate/up gemv");
-    {
-        PhaseMark pm(h, st, TMOE_PHASE_QUANT_ACT);
-        e = tmoe::launch_quantize_q8k(h->act, P, I, ids, h->aq, h->ad, h->ab, st);
-    }
-    if (e != cudaSuccess) return cuda_fail(h, e, "quantize act");
+    // down: the f32 activations are quantised to Q8_K while the kernel stages them
     tmoe::GemvArgs d{};
     d.w0 = (const uint8_t *)t->down;
     d.nb1_0 = t->down_nb1, d.nb2_0 = t->down_nb2;
     d.K = I, d.N = H;
-    d.xq = h->aq, d.xd = h->ad, d.xb = h->ab, d.x_div = 1;
+    d.xf = h->act, d.x_div = 1;
     d.perm = h->perm, d.offsets = h->offsets, d.active = h->active, d.n_active = h->n_active;
+    d.n_slots = t->n_slots, d.max_active = max_active, d.n_pairs = (int)P;
     d.out = h->dout, d.err = h->err;
     {
         PhaseMark pm(h, st, TMOE_PHASE_DOWN);
@@ -252,8 +252,8 @@ int tmoe_create(const tmoe_config *cfg, tmoe_handle **out) {
         delete h;
         return fail(nullptr, TMOE_E_CUDA, "cannot query the SM count");
     }
-    if (c.n_ff % tmoe::gemv_rows_per_item(wt_of(c.gate_type), true, c.n_embd) ||
-        c.n_embd % tmoe::gemv_rows_per_item(wt_of(c.down_type), false, c.n_ff)) {
+    if (!tmoe::gemv_rows_per_item(wt_of(c.gate_type), c.n_embd, c.n_ff) ||
+        !tmoe::gemv_rows_per_item(wt_of(c.down_type), c.n_ff, c.n_embd)) {
         delete h;
         return fail(nullptr, TMOE_E_UNSUPPORTED, "row counts must be multiples of the GEMV row tile");
     }
@@ -313,6 +313,8 @@ int tmoe_route(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
     if (!ids_out || !w_out) return fail(h, TMOE_E_INVALID, "ids_out and w_out are required");
     if (!router_w && !logits) return fail(h, TMOE_E_INVALID, "need router_w or logits");
     if ((router_w || use_norm) && !x) return fail(h, TMOE_E_INVALID, "x is required");
+    if (!aligned16(x) || !aligned16(router_w) || !aligned16(xn_out))
+        return fail(h, TMOE_E_INVALID, "x, router_w and xn_out must be 16-byte aligned");
     if (T == 0) return TMOE_OK;
     DeviceGuard dg(c.device);
     cudaStream_t st = (cudaStream_t)stream;
@@ -336,7 +338,7 @@ int tmoe_route(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
         float *dst = logits_out ? logits_out : h->logits;
         {
             PhaseMark pm(h, st, TMOE_PHASE_ROUTER_LOGITS);
-            e = tmoe::launch_router_logits(xs, router_w, T, c.n_embd, c.n_expert, dst, st);
+            e = tmoe::launch_router_logits(xs, router_w, T, c.n_embd, c.n_expert, dst, nullptr, nullptr, nullptr, st);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "router logits");
         lg = dst;
@@ -359,43 +361,84 @@ int tmoe_experts(tmoe_handle *h, void *stream, const float *xn, int64_t T, const
     const tmoe_config &c = h->cfg;
     if (T < 0 || T > c.max_tokens) return fail(h, TMOE_E_INVALID, "T=%lld outside [0, max_tokens]", (long long)T);
     if (!xn || !ids || !w || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    if (!aligned16(xn) || !aligned16(out)) return fail(h, TMOE_E_INVALID, "xn and out must be 16-byte aligned");
     int rc = check_tensors(h, wts);
     if (rc) return rc;
     if (T == 0) return TMOE_OK;
     DeviceGuard dg(c.device);
-    return run_experts(h, (cudaStream_t)stream, xn, T, ids, w, wts, out);
+    return run_experts(h, (cudaStream_t)stream, xn, T, ids, w, wts, out, false, false);
 }
 
-int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t use_norm,
-               const float *norm_w, const float *router_w, const float *logits,
-               const int32_t *id_map, const tmoe_expert_tensors *wts, float *out, int32_t *ids_out,
-               float *w_out) {
+int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t use_norm, const float *norm_w,
+               const float *router_w, const float *logits, const int32_t *id_map, const tmoe_expert_tensors *wts,
+               float *out, int32_t *ids_out, float *w_out) {
     if (!h) return TMOE_E_INVALID;
     const tmoe_config &c = h->cfg;
     if (T < 0 || T > c.max_tokens) return fail(h, TMOE_E_INVALID, "T=%lld outside [0, max_tokens]", (long long)T);
     if (!x || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    if (!router_w && !logits) return fail(h, TMOE_E_INVALID, "need router_w or logits");
+    if (!aligned16(x) || !aligned16(out) || !aligned16(router_w))
+        return fail(h, TMOE_E_INVALID, "x, out and router_w must be 16-byte aligned");
     int rc = check_tensors(h, wts);
     if (rc) return rc;
     if (T == 0) return TMOE_OK;
     DeviceGuard dg(c.device);
     cudaStream_t st = (cudaStream_t)stream;
+    const int k = c.n_expert_used;
     int32_t *ids = ids_out ? ids_out : h->ids;
     float *w = w_out ? w_out : h->w;
-    rc = tmoe_route(h, stream, x, T, use_norm, norm_w, router_w, logits, ids, w, use_norm ? h->xn : nullptr,
-                    nullptr);
-    if (rc) return rc;
-    const float *xn = use_norm ? h->xn : x;
-    const int32_t *used = ids;
-    if (id_map) {
-        cudaError_t e;
+    cudaError_t e;
+    const float *xn = x;
+    if (use_norm) {
         {
-            PhaseMark pm(h, st, TMOE_PHASE_MAP_IDS);
-            e = tmoe::launch_map_ids(ids, T * c.n_expert_used, id_map, c.n_expert, h->mapped, st);
+            PhaseMark pm(h, st, TMOE_PHASE_RMS_NORM);
+            e = tmoe::launch_rms_norm(x, norm_w, c.rms_eps, T, c.n_embd, h->xn, st);
         }
-        if (e != cudaSuccess) return cuda_fail(h, e, "map ids");
-        used = h->mapped;
+        if (e != cudaSuccess) return cuda_fail(h, e, "rms_norm");
+        xn = h->xn;
     }
-    return run_experts(h, st, xn, T, used, w, wts, out);
+    // logits (and, fused, the Q8_K rows of xn)
+    bool x_quantized = false;
+    const float *lg = logits;
+    if (router_w) {
+        x_quantized = tmoe::router_fuses_q8(c.n_embd);
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_ROUTER_LOGITS);
+            e = tmoe::launch_router_logits(xn, router_w, T, c.n_embd, c.n_expert, h->logits,
+                                           x_quantized ? h->xq : nullptr, h->xd, h->xb, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "router logits");
+        lg = h->logits;
+    }
+    const int32_t *used = ids;
+    bool dispatched = false;
+    if (tmoe::route_dispatch_fits(T, k, c.n_expert, wts->n_slots)) {
+        // decode regime: softmax/top-k + id map + dispatch in one kernel
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_TOPK);
+            e = tmoe::launch_route_dispatch(lg, (int)T, c.n_expert, k, id_map, c.n_expert, ids, w, h->mapped,
+                                            wts->n_slots, h->counts, h->offsets, h->perm, h->active, h->n_active,
+                                            h->err, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "route/dispatch");
+        used = h->mapped;
+        dispatched = true;
+    } else {
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_TOPK);
+            e = tmoe::launch_softmax_topk(lg, T, c.n_expert, k, ids, w, nullptr, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "softmax/top-k");
+        if (id_map) {
+            {
+                PhaseMark pm(h, st, TMOE_PHASE_MAP_IDS);
+                e = tmoe::launch_map_ids(ids, T * k, id_map, c.n_expert, h->mapped, st);
+            }
+            if (e != cudaSuccess) return cuda_fail(h, e, "map ids");
+            used = h->mapped;
+        }
+    }
+    return run_experts(h, st, xn, T, used, w, wts, out, dispatched, x_quantized);
 }
 
 int tmoe_map_ids(tmoe_handle *h, void *stream, const int32_t *ids, int64_t n, const int32_t *table,
@@ -418,12 +461,13 @@ int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, s
         (b1 != 1 && b1 != n_used))
         return fail(h, TMOE_E_INVALID, "bad mul_mat_id shape");
     if (!W || !b || !ids || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    if (!aligned16(b)) return fail(h, TMOE_E_INVALID, "b must be 16-byte aligned");
     const int wt = wt_of(type);
     if (nb1 != row_size(type, K)) return fail(h, TMOE_E_UNSUPPORTED, "rows must be contiguous (nb1 == row size)");
     if (((uintptr_t)W & 15u) || (nb2 & 15u)) return fail(h, TMOE_E_INVALID, "W and nb2 must be 16-byte aligned");
-    if (N % tmoe::gemv_rows_per_item(wt, false, (int)K))
-        return fail(h, TMOE_E_UNSUPPORTED, "N=%lld is not a multiple of the row tile %d", (long long)N,
-                    tmoe::gemv_rows_per_item(wt, false, (int)K));
+    if (!tmoe::gemv_rows_per_item(wt, (int)K, (int)N))
+        return fail(h, TMOE_E_UNSUPPORTED, "N=%lld rows per expert fit no GEMV row tile (multiples of 16 or 32)",
+                    (long long)N);
     if (T == 0) return TMOE_OK;
     DeviceGuard dg(h->cfg.device);
     cudaStream_t st = (cudaStream_t)stream;
@@ -467,9 +511,10 @@ int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, s
     g.nb1_0 = nb1, g.nb2_0 = nb2;
     g.K = (int)K, g.N = (int)N;
     g.xq = q, g.xd = d, g.xb = bs, g.x_div = b1 == 1 ? (int)n_used : 1;
-    g.perm = perm, g.offsets = offs, g.active = act, g.n_active = na;
-    g.out = out, g.err = h->err;
     const int max_active = (int)(P < n_w ? P : n_w);
+    g.perm = perm, g.offsets = offs, g.active = act, g.n_active = na;
+    g.n_slots = (int)n_w, g.max_active = max_active, g.n_pairs = (int)P;
+    g.out = out, g.err = h->err;
     if ((e = tmoe::launch_gemv(wt, false, g, max_active, h->sm_count, st)) != cudaSuccess)
         return cuda_fail(h, e, "mul_mat_id gemv");
     return TMOE_OK;
