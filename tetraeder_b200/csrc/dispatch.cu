@@ -23,10 +23,12 @@ constexpr int SORT_WARPS = 32;
 // sh: SORT_WARPS * n_slots + n_slots + 1 ints of shared memory.
 __device__ void sort_pairs_cta(const int32_t *ids, int n_pairs, int n_slots, int32_t *__restrict__ counts,
                                int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
-                               int32_t *__restrict__ active, int32_t *__restrict__ n_active, int *err, int32_t *sh) {
+                               int32_t *__restrict__ active, int32_t *__restrict__ n_active, int *counters,
+                               int n_counters, int *err, int32_t *sh) {
     int32_t *hist = sh;                         // [SORT_WARPS][n_slots]
     int32_t *offs = sh + SORT_WARPS * n_slots;  // [n_slots + 1]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (counters && (int)threadIdx.x < n_counters) counters[threadIdx.x] = 0;  // work counters of the GEMVs
     for (int i = threadIdx.x; i < SORT_WARPS * n_slots; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     int seg = (n_pairs + SORT_WARPS - 1) / SORT_WARPS;
@@ -99,9 +101,10 @@ __device__ void sort_pairs_cta(const int32_t *ids, int n_pairs, int n_slots, int
 __global__ void __launch_bounds__(1024) sort_pairs_kernel(const int32_t *__restrict__ ids, int n_pairs, int n_slots,
                                                           int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
                                                           int32_t *__restrict__ perm, int32_t *__restrict__ active,
-                                                          int32_t *__restrict__ n_active, int *err) {
+                                                          int32_t *__restrict__ n_active, int *counters, int n_counters,
+                                                          int *err) {
     extern __shared__ int32_t sh[];
-    sort_pairs_cta(ids, n_pairs, n_slots, counts, offsets, perm, active, n_active, err, sh);
+    sort_pairs_cta(ids, n_pairs, n_slots, counts, offsets, perm, active, n_active, counters, n_counters, err, sh);
 }
 
 // Decode regime (T*k <= ROUTE_FUSED_MAX_PAIRS): softmax/top-k of every token, the optional EP
@@ -114,7 +117,8 @@ __global__ void __launch_bounds__(1024) route_dispatch_kernel(const float *__res
                                                               int32_t *__restrict__ mapped, int n_slots,
                                                               int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
                                                               int32_t *__restrict__ perm, int32_t *__restrict__ active,
-                                                              int32_t *__restrict__ n_active, int *err) {
+                                                              int32_t *__restrict__ n_active, int *counters,
+                                                              int n_counters, int *err) {
     extern __shared__ int32_t sh[];
     int32_t *sid = sh;  // [T*k] mapped ids
     int32_t *sort_sh = sh + ((T * k + 3) & ~3);
@@ -132,7 +136,7 @@ __global__ void __launch_bounds__(1024) route_dispatch_kernel(const float *__res
         }
     }
     __syncthreads();
-    sort_pairs_cta(sid, T * k, n_slots, counts, offsets, perm, active, n_active, err, sort_sh);
+    sort_pairs_cta(sid, T * k, n_slots, counts, offsets, perm, active, n_active, counters, n_counters, err, sort_sh);
 }
 
 __global__ void map_ids_kernel(const int32_t *__restrict__ ids, int64_t n, const int32_t *__restrict__ table,
@@ -210,12 +214,14 @@ static cudaError_t set_smem_once(KernT kern, size_t smem, int *cache) {
 }
 
 cudaError_t launch_sort_pairs(const int32_t *ids, int n_pairs, int n_slots, int32_t *counts, int32_t *offsets,
-                              int32_t *perm, int32_t *active, int32_t *n_active, int *err, cudaStream_t st) {
+                              int32_t *perm, int32_t *active, int32_t *n_active, int *counters, int n_counters,
+                              int *err, cudaStream_t st) {
     const size_t smem = sort_pairs_smem(n_slots);
     static int cache[64] = {};
     cudaError_t e = set_smem_once(sort_pairs_kernel, smem, cache);
     if (e != cudaSuccess) return e;
-    sort_pairs_kernel<<<1, 1024, smem, st>>>(ids, n_pairs, n_slots, counts, offsets, perm, active, n_active, err);
+    sort_pairs_kernel<<<1, 1024, smem, st>>>(ids, n_pairs, n_slots, counts, offsets, perm, active, n_active, counters,
+                                             n_counters, err);
     return cudaGetLastError();
 }
 
@@ -225,8 +231,8 @@ bool route_dispatch_fits(int64_t T, int k, int E, int n_slots) {
 
 cudaError_t launch_route_dispatch(const float *logits, int T, int E, int k, const int32_t *table, int n_table,
                                   int32_t *ids_out, float *w_out, int32_t *mapped, int n_slots, int32_t *counts,
-                                  int32_t *offsets, int32_t *perm, int32_t *active, int32_t *n_active, int *err,
-                                  cudaStream_t st) {
+                                  int32_t *offsets, int32_t *perm, int32_t *active, int32_t *n_active,
+                                  int *counters, int n_counters, int *err, cudaStream_t st) {
     const size_t smem = sizeof(int32_t) * ((size_t)((T * k + 3) & ~3)) + sort_pairs_smem(n_slots);
     static int cache[4][64] = {};
 #define TMOE_RD(MP, CI)                                                                                        \
@@ -235,7 +241,7 @@ cudaError_t launch_route_dispatch(const float *logits, int T, int E, int k, cons
         if (e != cudaSuccess) return e;                                                                        \
         route_dispatch_kernel<MP><<<1, 1024, smem, st>>>(logits, T, E, k, table, n_table, ids_out, w_out,      \
                                                          mapped, n_slots, counts, offsets, perm, active,      \
-                                                         n_active, err);                                       \
+                                                         n_active, counters, n_counters, err);                 \
     } while (0)
     if (E <= 32)
         TMOE_RD(1, 0);

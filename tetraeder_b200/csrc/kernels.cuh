@@ -10,36 +10,50 @@
 
 namespace tmoe {
 
+// Q8_K rows as the expert GEMV reads them: qs int8 [rows][K], d f32 [rows][K/256], and per
+// super-block the activation sums over the weight type's sub-blocks (32 elements for Q4_K, 16 for
+// Q6_K), split exactly as B = 64 * hi + lo, lo in [0, 64): bl (u8 bytes) / bh (s8 bytes)
+// [rows][K/256][nbw] words, nbw = 2 (Q4_K) or 4 (Q6_K).
+struct Q8Rows {
+    int8_t *qs;
+    float *d;
+    uint32_t *bl, *bh;
+    int wt;  // the consumer's weight type: TMOE_WT_Q4K or TMOE_WT_Q6K
+};
+inline int q8_nbw(int wt) { return wt == TMOE_WT_Q4K ? 2 : 4; }
+
 // route.cu
-cudaError_t launch_rms_norm(const float *x, const float *norm_w, float eps, int64_t T, int H,
-                            float *out, cudaStream_t st);
-// The router logits; when q8_qs != NULL (and router_fuses_q8(H)) also the Q8_K rows of xn.
+cudaError_t launch_rms_norm(const float *x, const float *norm_w, float eps, int64_t T, int H, float *out,
+                            cudaStream_t st);
+// The router logits; with q8 (non-NULL, router_fuses_q8(H)) also the Q8_K rows of xn.
 cudaError_t launch_router_logits(const float *xn, const float *rw, int64_t T, int H, int E, float *logits,
-                                 int8_t *q8_qs, float *q8_d, int16_t *q8_bs, cudaStream_t st);
+                                 const Q8Rows *q8, cudaStream_t st);
 bool router_fuses_q8(int H);
-cudaError_t launch_softmax_topk(const float *logits, int64_t T, int E, int k, int32_t *ids,
-                                float *w, float *probs, cudaStream_t st);
-cudaError_t launch_quantize_q8k(const float *x, int64_t rows, int K, const int32_t *valid,
-                                int8_t *qs, float *d, int16_t *bsums, cudaStream_t st);
+cudaError_t launch_softmax_topk(const float *logits, int64_t T, int E, int k, int32_t *ids, float *w, float *probs,
+                                cudaStream_t st);
+// Q8_K of rows of K f32; rows whose valid entry is negative are skipped (valid may be NULL).
+cudaError_t launch_quantize_q8k(const float *x, int64_t rows, int K, const int32_t *valid, const Q8Rows &out,
+                                cudaStream_t st);
 
 // dispatch.cu
 size_t sort_pairs_smem(int n_slots);
-cudaError_t launch_sort_pairs(const int32_t *ids, int n_pairs, int n_slots, int32_t *counts,
-                              int32_t *offsets, int32_t *perm, int32_t *active, int32_t *n_active,
+// The dispatch also zeroes `counters` (n_counters ints: the GEMV work counters; may be NULL).
+cudaError_t launch_sort_pairs(const int32_t *ids, int n_pairs, int n_slots, int32_t *counts, int32_t *offsets,
+                              int32_t *perm, int32_t *active, int32_t *n_active, int *counters, int n_counters,
                               int *err, cudaStream_t st);
 // Fused softmax/top-k + optional EP map + dispatch for T*k <= ROUTE_FUSED_MAX_PAIRS.
 #define ROUTE_FUSED_MAX_PAIRS 4096
 bool route_dispatch_fits(int64_t T, int k, int E, int n_slots);
 cudaError_t launch_route_dispatch(const float *logits, int T, int E, int k, const int32_t *table, int n_table,
                                   int32_t *ids_out, float *w_out, int32_t *mapped, int n_slots, int32_t *counts,
-                                  int32_t *offsets, int32_t *perm, int32_t *active, int32_t *n_active, int *err,
-                                  cudaStream_t st);
-cudaError_t launch_map_ids(const int32_t *ids, int64_t n, const int32_t *table, int64_t n_table,
-                           int32_t *out, cudaStream_t st);
-cudaError_t launch_zero_invalid_rows(const int32_t *ids, int64_t n_pairs, int n_slots, int N,
-                                     float *out, cudaStream_t st);
-cudaError_t launch_combine(const float *dout, const int32_t *ids, const float *w, int64_t T, int k,
-                           int H, int n_slots, float *out, cudaStream_t st);
+                                  int32_t *offsets, int32_t *perm, int32_t *active, int32_t *n_active,
+                                  int *counters, int n_counters, int *err, cudaStream_t st);
+cudaError_t launch_map_ids(const int32_t *ids, int64_t n, const int32_t *table, int64_t n_table, int32_t *out,
+                           cudaStream_t st);
+cudaError_t launch_zero_invalid_rows(const int32_t *ids, int64_t n_pairs, int n_slots, int N, float *out,
+                                     cudaStream_t st);
+cudaError_t launch_combine(const float *dout, const int32_t *ids, const float *w, int64_t T, int k, int H,
+                           int n_slots, float *out, cudaStream_t st);
 
 // quant.cu
 cudaError_t launch_quantize(int wt, const float *x, int64_t nblocks, uint8_t *out, cudaStream_t st);
@@ -52,28 +66,27 @@ struct GemvArgs {
     size_t nb1_0, nb2_0, nb1_1, nb2_1;
     int K;  // columns, multiple of 256
     int N;  // rows per expert
-    const int8_t *xq;  // Q8_K activations, SoA rows of K
+    // Q8_K activation rows (Q8Rows layout for this weight type); the row of pair p is p / x_div
+    const int8_t *xq;
     const float *xd;
-    const int16_t *xb;
-    const float *xf;   // or f32 activation rows, quantised to Q8_K while staged (xq/xd/xb unused)
-    int x_div;  // activation row of pair p = p / x_div
+    const uint32_t *xbl, *xbh;
+    int x_div;
     const int32_t *perm, *offsets, *active, *n_active;
     int n_slots;     // experts in the weight tensors (active ids are checked against it)
     int max_active;  // the grid was sized for at most this many active experts
     int n_pairs;     // pair rows of perm / out
-    float *out;  // [pairs][N]
+    int *work;       // work counter, zero at launch (the dispatch kernels zero it)
+    float *out;      // [pairs][N]
     int *err;
     // filled by the launcher
     int tiles;
     int n_stages;
     uint32_t stage_bytes;
-    int tokcap;      // activation rows staged in shared memory at a time
     int row_stride;  // shared-memory row (Q4_K) or 8-row group (Q6_K) stride
     int mat_stride;  // shared-memory bytes of one matrix of a stage
 };
 // Rows per work item of the GEMV for K columns and N rows per expert; 0 if N does not fit.
 int gemv_rows_per_item(int wt, int K, int N);
-cudaError_t launch_gemv(int wt, bool gateup, const GemvArgs &a, int max_items, int sm_count,
-                        cudaStream_t st);
+cudaError_t launch_gemv(int wt, bool gateup, const GemvArgs &a, int max_items, int sm_count, cudaStream_t st);
 
 }  // namespace tmoe

@@ -5,6 +5,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace tmoe {
 
@@ -57,6 +58,53 @@ __device__ __forceinline__ void q8k_block_warp(const float (&v)[8], uint2 &q, fl
           ((uint32_t)(qi[3] & 0xff) << 24);
     q.y = (uint32_t)(qi[4] & 0xff) | ((uint32_t)(qi[5] & 0xff) << 8) | ((uint32_t)(qi[6] & 0xff) << 16) |
           ((uint32_t)(qi[7] & 0xff) << 24);
+}
+
+}  // namespace tmoe
+
+namespace tmoe {
+
+// Stores the warp's Q8_K block b of row `row` (from q8k_block_warp) in the Q8Rows layout, with the
+// sub-block sums of the consumer's weight type split into exact low / high bytes.
+__device__ __forceinline__ void q8k_store_warp(const Q8Rows &o, int64_t row, int K, int b, const uint2 &q, float d,
+                                               int s16) {
+    const int lane = threadIdx.x & 31;
+    const int nb = K / TMOE_QK;
+    *reinterpret_cast<uint2 *>(o.qs + row * K + (int64_t)b * TMOE_QK + 8 * lane) = q;
+    if (lane == 0) o.d[row * nb + b] = d;
+    uint32_t lo = 0, hi = 0;
+    if (o.wt == TMOE_WT_Q6K) {  // 16-element sums: lane 2g holds sum g; 4 sums per word
+        if ((lane & 1) == 0) {
+            const int i = (lane >> 1) & 3;
+            lo = (uint32_t)(s16 & 63) << (8 * i);
+            hi = (uint32_t)((s16 >> 6) & 0xff) << (8 * i);
+        }
+        for (int off = 2; off <= 4; off <<= 1) {
+            lo |= __shfl_xor_sync(0xffffffffu, lo, off);
+            hi |= __shfl_xor_sync(0xffffffffu, hi, off);
+        }
+        if ((lane & 7) == 0) {
+            const int64_t w = (row * nb + b) * 4 + (lane >> 3);
+            o.bl[w] = lo;
+            o.bh[w] = hi;
+        }
+    } else {  // 32-element sums: lanes 4g hold sum g after adding the neighbour pair
+        const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);
+        if ((lane & 3) == 0) {
+            const int i = (lane >> 2) & 3;
+            lo = (uint32_t)(s32 & 63) << (8 * i);
+            hi = (uint32_t)((s32 >> 6) & 0xff) << (8 * i);
+        }
+        for (int off = 4; off <= 8; off <<= 1) {
+            lo |= __shfl_xor_sync(0xffffffffu, lo, off);
+            hi |= __shfl_xor_sync(0xffffffffu, hi, off);
+        }
+        if ((lane & 15) == 0) {
+            const int64_t w = (row * nb + b) * 2 + (lane >> 4);
+            o.bl[w] = lo;
+            o.bh[w] = hi;
+        }
+    }
 }
 
 }  // namespace tmoe

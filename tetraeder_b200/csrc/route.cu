@@ -42,16 +42,10 @@ __global__ void rms_norm_kernel(const float *__restrict__ x, const float *__rest
 // expert products), from the same staged rows.
 constexpr int RL_WARPS = 8;
 
-struct Q8Out {
-    int8_t *qs;
-    float *d;
-    int16_t *bs;
-};
-
 template <int TT>
 __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_kernel(const float *__restrict__ xn,
                                                                       const float *__restrict__ rw, int64_t T, int H,
-                                                                      int E, float *__restrict__ logits, Q8Out q8) {
+                                                                      int E, float *__restrict__ logits, Q8Rows q8) {
     extern __shared__ float4 xs4[];  // [TT][H/4]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.x * RL_WARPS + warp;
@@ -74,10 +68,7 @@ __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_kernel(const floa
             float d;
             int s16;
             q8k_block_warp(v, q, d, s16);
-            const int64_t t = t0 + j;
-            *reinterpret_cast<uint2 *>(q8.qs + t * H + b * TMOE_QK + 8 * lane) = q;
-            if ((lane & 1) == 0) q8.bs[t * (H / 16) + b * 16 + lane / 2] = (int16_t)s16;
-            if (lane == 0) q8.d[t * nb + b] = d;
+            q8k_store_warp(q8, t0 + j, H, b, q, d, s16);
         }
     }
     if (e >= E) return;
@@ -143,10 +134,10 @@ __global__ void softmax_topk_kernel(const float *__restrict__ logits, int64_t T,
     }
 }
 
-// Q8_K of rows of K f32: one warp per 256-block.  Output SoA: qs int8 [rows][K], d f32
-// [rows][K/256], bsums int16 [rows][K/16].  Rows whose `valid` entry is negative are skipped.
+// Q8_K of rows of K f32: one warp per 256-block, stored in the Q8Rows layout of the consumer's
+// weight type.  Rows whose `valid` entry is negative are skipped.
 __global__ void quantize_q8k_kernel(const float *__restrict__ x, int64_t rows, int K, const int32_t *__restrict__ valid,
-                                    int8_t *__restrict__ qs, float *__restrict__ d, int16_t *__restrict__ bsums) {
+                                    Q8Rows out) {
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int nb = K / TMOE_QK;
@@ -161,9 +152,7 @@ __global__ void quantize_q8k_kernel(const float *__restrict__ x, int64_t rows, i
     float dd;
     int s16;
     q8k_block_warp(v, q, dd, s16);
-    *reinterpret_cast<uint2 *>(qs + row * K + (int64_t)b * TMOE_QK + 8 * lane) = q;
-    if ((lane & 1) == 0) bsums[row * (K / 16) + (int64_t)b * 16 + lane / 2] = (int16_t)s16;
-    if (lane == 0) d[row * nb + b] = dd;
+    q8k_store_warp(out, row, K, b, q, dd, s16);
 }
 
 // ------------------------------------------------------------------ launchers
@@ -176,7 +165,7 @@ cudaError_t launch_rms_norm(const float *x, const float *norm_w, float eps, int6
 }
 
 cudaError_t launch_router_logits(const float *xn, const float *rw, int64_t T, int H, int E, float *logits,
-                                 int8_t *q8_qs, float *q8_d, int16_t *q8_bs, cudaStream_t st) {
+                                 const Q8Rows *q8, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     constexpr int TT = 8;
     const size_t smem = (size_t)TT * H * 4;
@@ -192,12 +181,11 @@ cudaError_t launch_router_logits(const float *xn, const float *rw, int64_t T, in
             set_bytes[dev] = (int)smem;
         }
         dim3 grid((E + RL_WARPS - 1) / RL_WARPS, (unsigned)((T + TT - 1) / TT));
-        const bool q8 = q8_qs && H % TMOE_QK == 0;
-        router_logits_kernel<TT><<<grid, RL_WARPS * 32, smem, st>>>(xn, rw, T, H, E, logits,
-                                                                   Q8Out{q8 ? q8_qs : nullptr, q8_d, q8_bs});
+        const Q8Rows none{nullptr, nullptr, nullptr, nullptr, 0};
+        router_logits_kernel<TT><<<grid, RL_WARPS * 32, smem, st>>>(xn, rw, T, H, E, logits, q8 ? *q8 : none);
         return cudaGetLastError();
     }
-    if (q8_qs) return cudaErrorInvalidValue;  // the caller quantises separately for such H
+    if (q8) return cudaErrorInvalidValue;  // the caller quantises separately for such H
     const int64_t warps = T * E;
     router_logits_generic_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(xn, rw, T, H, E, logits);
     return cudaGetLastError();
@@ -223,13 +211,13 @@ cudaError_t launch_softmax_topk(const float *logits, int64_t T, int E, int k, in
     return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_q8k(const float *x, int64_t rows, int K, const int32_t *valid, int8_t *qs, float *d,
-                                int16_t *bsums, cudaStream_t st) {
+cudaError_t launch_quantize_q8k(const float *x, int64_t rows, int K, const int32_t *valid, const Q8Rows &out,
+                                cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
     const int64_t warps = rows * (K / TMOE_QK);
     const int per_block = 8;
     quantize_q8k_kernel<<<(unsigned)((warps + per_block - 1) / per_block), per_block * 32, 0, st>>>(x, rows, K, valid,
-                                                                                                    qs, d, bsums);
+                                                                                                    out);
     return cudaGetLastError();
 }
 

@@ -14,6 +14,7 @@
 namespace {
 
 constexpr int kMaxSlots = 1024;
+constexpr int kCounters = 4;
 thread_local std::string g_create_error;
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -31,13 +32,17 @@ struct tmoe_handle {
     float *w = nullptr;
     int32_t *mapped = nullptr;
     int32_t *counts = nullptr, *offsets = nullptr, *perm = nullptr, *active = nullptr, *n_active = nullptr;
-    // activations
+    // activations: Q8_K of the layer input (read by gate/up) and of the SwiGLU output (read by down)
     float *xn = nullptr;
     int8_t *xq = nullptr;
     float *xd = nullptr;
-    int16_t *xb = nullptr;
+    uint32_t *xbl = nullptr, *xbh = nullptr;
     float *act = nullptr;
+    int8_t *aq = nullptr;
+    float *ad = nullptr;
+    uint32_t *abl = nullptr, *abh = nullptr;
     float *dout = nullptr;
+    int *counters = nullptr;  // GEMV work counters
     int *err = nullptr;
     // growable scratch of tmoe_mul_mat_id
     void *op_ws = nullptr;
@@ -132,12 +137,19 @@ size_t carve(tmoe_handle *h, char *base) {
     h->active = (int32_t *)take(kMaxSlots * 4);
     h->n_active = (int32_t *)take(4);
     h->perm = (int32_t *)take(P * 4);
+    const size_t nbg = (size_t)tmoe::q8_nbw(wt_of(c.gate_type)), nbd = (size_t)tmoe::q8_nbw(wt_of(c.down_type));
     h->xn = (float *)take(T * H * 4);
     h->xq = (int8_t *)take(T * H);
     h->xd = (float *)take(T * (H / 256) * 4);
-    h->xb = (int16_t *)take(T * (H / 16) * 2);
+    h->xbl = (uint32_t *)take(T * (H / 256) * nbg * 4);
+    h->xbh = (uint32_t *)take(T * (H / 256) * nbg * 4);
     h->act = (float *)take(P * I * 4);
+    h->aq = (int8_t *)take(P * I);
+    h->ad = (float *)take(P * (I / 256) * 4);
+    h->abl = (uint32_t *)take(P * (I / 256) * nbd * 4);
+    h->abh = (uint32_t *)take(P * (I / 256) * nbd * 4);
     h->dout = (float *)take(P * H * 4);
+    h->counters = (int *)take(kCounters * 4);
     h->err = (int *)take(4);
     return off;
 }
@@ -162,26 +174,27 @@ int check_tensors(tmoe_handle *h, const tmoe_expert_tensors *t) {
 }
 
 // a4-a8 on `ids` (already slot ids) and `w`.  dispatched: the dispatch buffers (counts, offsets,
-// perm, active) already hold this call's dispatch; x_quantized: h->xq/xd/xb already hold the
-// Q8_K rows of xn.
+// perm, active, zeroed work counters) already hold this call's dispatch; x_quantized: the Q8_K
+// rows of xn are already in h->xq/xd/xbl/xbh.
 int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, const int32_t *ids, const float *w,
                 const tmoe_expert_tensors *t, float *out, bool dispatched, bool x_quantized) {
     const tmoe_config &c = h->cfg;
     const int k = c.n_expert_used, H = c.n_embd, I = c.n_ff;
     const int64_t P = T * k;
+    const int wg = wt_of(c.gate_type), wd = wt_of(c.down_type);
     cudaError_t e;
     if (!dispatched) {
         {
             PhaseMark pm(h, st, TMOE_PHASE_DISPATCH);
             e = tmoe::launch_sort_pairs(ids, (int)P, t->n_slots, h->counts, h->offsets, h->perm, h->active,
-                                        h->n_active, h->err, st);
+                                        h->n_active, h->counters, kCounters, h->err, st);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "sort_pairs");
     }
     if (!x_quantized) {
         {
             PhaseMark pm(h, st, TMOE_PHASE_QUANT_X);
-            e = tmoe::launch_quantize_q8k(xn, T, H, nullptr, h->xq, h->xd, h->xb, st);
+            e = tmoe::launch_quantize_q8k(xn, T, H, nullptr, tmoe::Q8Rows{h->xq, h->xd, h->xbl, h->xbh, wg}, st);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "quantize x");
     }
@@ -191,27 +204,31 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
     g.w1 = (const uint8_t *)t->up;
     g.nb1_0 = t->gate_nb1, g.nb2_0 = t->gate_nb2, g.nb1_1 = t->up_nb1, g.nb2_1 = t->up_nb2;
     g.K = H, g.N = I;
-    g.xq = h->xq, g.xd = h->xd, g.xb = h->xb, g.x_div = k;
+    g.xq = h->xq, g.xd = h->xd, g.xbl = h->xbl, g.xbh = h->xbh, g.x_div = k;
     g.perm = h->perm, g.offsets = h->offsets, g.active = h->active, g.n_active = h->n_active;
-    g.n_slots = t->n_slots, g.max_active = max_active, g.n_pairs = (int)P;
+    g.n_slots = t->n_slots, g.max_active = max_active, g.n_pairs = (int)P, g.work = h->counters + 0;
     g.out = h->act, g.err = h->err;
     {
         PhaseMark pm(h, st, TMOE_PHASE_GATE_UP);
-        e = tmoe::launch_gemv(wt_of(c.gate_type), true, g, max_active, h->sm_count, st);
+        e = tmoe::launch_gemv(wg, true, g, max_active, h->sm_count, st);
     }
     if (e != cudaSuccess) return cuda_fail(h, e, "gate/up gemv");
-    // down: the f32 activations are quantised to Q8_K while the kernel stages them
+    {
+        PhaseMark pm(h, st, TMOE_PHASE_QUANT_ACT);
+        e = tmoe::launch_quantize_q8k(h->act, P, I, ids, tmoe::Q8Rows{h->aq, h->ad, h->abl, h->abh, wd}, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "quantize act");
     tmoe::GemvArgs d{};
     d.w0 = (const uint8_t *)t->down;
     d.nb1_0 = t->down_nb1, d.nb2_0 = t->down_nb2;
     d.K = I, d.N = H;
-    d.xf = h->act, d.x_div = 1;
+    d.xq = h->aq, d.xd = h->ad, d.xbl = h->abl, d.xbh = h->abh, d.x_div = 1;
     d.perm = h->perm, d.offsets = h->offsets, d.active = h->active, d.n_active = h->n_active;
-    d.n_slots = t->n_slots, d.max_active = max_active, d.n_pairs = (int)P;
+    d.n_slots = t->n_slots, d.max_active = max_active, d.n_pairs = (int)P, d.work = h->counters + 1;
     d.out = h->dout, d.err = h->err;
     {
         PhaseMark pm(h, st, TMOE_PHASE_DOWN);
-        e = tmoe::launch_gemv(wt_of(c.down_type), false, d, max_active, h->sm_count, st);
+        e = tmoe::launch_gemv(wd, false, d, max_active, h->sm_count, st);
     }
     if (e != cudaSuccess) return cuda_fail(h, e, "down gemv");
     {
@@ -338,7 +355,7 @@ int tmoe_route(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
         float *dst = logits_out ? logits_out : h->logits;
         {
             PhaseMark pm(h, st, TMOE_PHASE_ROUTER_LOGITS);
-            e = tmoe::launch_router_logits(xs, router_w, T, c.n_embd, c.n_expert, dst, nullptr, nullptr, nullptr, st);
+            e = tmoe::launch_router_logits(xs, router_w, T, c.n_embd, c.n_expert, dst, nullptr, st);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "router logits");
         lg = dst;
@@ -402,10 +419,11 @@ int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
     const float *lg = logits;
     if (router_w) {
         x_quantized = tmoe::router_fuses_q8(c.n_embd);
+        const tmoe::Q8Rows q8{h->xq, h->xd, h->xbl, h->xbh, wt_of(c.gate_type)};
         {
             PhaseMark pm(h, st, TMOE_PHASE_ROUTER_LOGITS);
             e = tmoe::launch_router_logits(xn, router_w, T, c.n_embd, c.n_expert, h->logits,
-                                           x_quantized ? h->xq : nullptr, h->xd, h->xb, st);
+                                           x_quantized ? &q8 : nullptr, st);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "router logits");
         lg = h->logits;
@@ -418,7 +436,7 @@ int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
             PhaseMark pm(h, st, TMOE_PHASE_TOPK);
             e = tmoe::launch_route_dispatch(lg, (int)T, c.n_expert, k, id_map, c.n_expert, ids, w, h->mapped,
                                             wts->n_slots, h->counts, h->offsets, h->perm, h->active, h->n_active,
-                                            h->err, st);
+                                            h->counters, kCounters, h->err, st);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "route/dispatch");
         used = h->mapped;
@@ -479,9 +497,11 @@ int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, s
         need = align_up(need + bytes, 256);
         return o;
     };
-    size_t o_q = lay((size_t)rows * K), o_d = lay((size_t)rows * (K / 256) * 4), o_b = lay((size_t)rows * (K / 16) * 2);
+    const size_t nbw = (size_t)tmoe::q8_nbw(wt);
+    size_t o_q = lay((size_t)rows * K), o_d = lay((size_t)rows * (K / 256) * 4);
+    size_t o_bl = lay((size_t)rows * (K / 256) * nbw * 4), o_bh = lay((size_t)rows * (K / 256) * nbw * 4);
     size_t o_cnt = lay(kMaxSlots * 4), o_off = lay((kMaxSlots + 1) * 4), o_act = lay(kMaxSlots * 4), o_na = lay(4);
-    size_t o_perm = lay((size_t)P * 4);
+    size_t o_perm = lay((size_t)P * 4), o_work = lay(kCounters * 4);
     cudaError_t e;
     if (need > h->op_ws_bytes) {
         if (h->op_ws) {
@@ -497,12 +517,14 @@ int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, s
     char *base = (char *)h->op_ws;
     int8_t *q = (int8_t *)(base + o_q);
     float *d = (float *)(base + o_d);
-    int16_t *bs = (int16_t *)(base + o_b);
+    uint32_t *bl = (uint32_t *)(base + o_bl), *bh = (uint32_t *)(base + o_bh);
     int32_t *cnt = (int32_t *)(base + o_cnt), *offs = (int32_t *)(base + o_off), *act = (int32_t *)(base + o_act),
             *na = (int32_t *)(base + o_na), *perm = (int32_t *)(base + o_perm);
-    if ((e = tmoe::launch_sort_pairs(ids, (int)P, (int)n_w, cnt, offs, perm, act, na, h->err, st)) != cudaSuccess)
+    int *work = (int *)(base + o_work);
+    if ((e = tmoe::launch_sort_pairs(ids, (int)P, (int)n_w, cnt, offs, perm, act, na, work, kCounters, h->err, st)) !=
+        cudaSuccess)
         return cuda_fail(h, e, "sort_pairs");
-    if ((e = tmoe::launch_quantize_q8k(b, rows, (int)K, nullptr, q, d, bs, st)) != cudaSuccess)
+    if ((e = tmoe::launch_quantize_q8k(b, rows, (int)K, nullptr, tmoe::Q8Rows{q, d, bl, bh, wt}, st)) != cudaSuccess)
         return cuda_fail(h, e, "quantize b");
     if ((e = tmoe::launch_zero_invalid_rows(ids, P, (int)n_w, (int)N, out, st)) != cudaSuccess)
         return cuda_fail(h, e, "zero rows");
@@ -510,10 +532,10 @@ int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, s
     g.w0 = (const uint8_t *)W;
     g.nb1_0 = nb1, g.nb2_0 = nb2;
     g.K = (int)K, g.N = (int)N;
-    g.xq = q, g.xd = d, g.xb = bs, g.x_div = b1 == 1 ? (int)n_used : 1;
+    g.xq = q, g.xd = d, g.xbl = bl, g.xbh = bh, g.x_div = b1 == 1 ? (int)n_used : 1;
     const int max_active = (int)(P < n_w ? P : n_w);
     g.perm = perm, g.offsets = offs, g.active = act, g.n_active = na;
-    g.n_slots = (int)n_w, g.max_active = max_active, g.n_pairs = (int)P;
+    g.n_slots = (int)n_w, g.max_active = max_active, g.n_pairs = (int)P, g.work = work;
     g.out = out, g.err = h->err;
     if ((e = tmoe::launch_gemv(wt, false, g, max_active, h->sm_count, st)) != cudaSuccess)
         return cuda_fail(h, e, "mul_mat_id gemv");
@@ -529,7 +551,7 @@ int tmoe_dispatch(tmoe_handle *h, void *stream, const int32_t *ids, int64_t T, i
     if (!ids || !counts || !offsets || !perm) return fail(h, TMOE_E_INVALID, "null tensor");
     DeviceGuard dg(c.device);
     cudaError_t e = tmoe::launch_sort_pairs(ids, (int)(T * c.n_expert_used), n_slots, counts, offsets, perm,
-                                            h->active, h->n_active, h->err, (cudaStream_t)stream);
+                                            h->active, h->n_active, nullptr, 0, h->err, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(h, e, "sort_pairs");
     return TMOE_OK;
 }
