@@ -79,11 +79,12 @@ struct GemvArgs {
     float *out;      // [pairs][N]
     int *err;
     // filled by the launcher
-    int tiles;
-    int n_stages;
-    uint32_t stage_bytes;
-    int row_stride;  // shared-memory row (Q4_K) or 8-row group (Q6_K) stride
-    int mat_stride;  // shared-memory bytes of one matrix of a stage
+    int tiles;         // items per active expert
+    int chunk_blocks;  // super-blocks per fill
+    int n_chunks;      // fills per row span of K
+    int row_stride;    // shared-memory bytes per fill row
+    int slot_bytes;    // shared-memory bytes per slot (16 rows)
+    int d_slots;       // slots per warp
 };
 // Rows per work item of the GEMV for K columns and N rows per expert; 0 if N does not fit.
 int gemv_rows_per_item(int wt, int K, int N);
