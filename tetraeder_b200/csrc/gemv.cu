@@ -183,12 +183,13 @@ __device__ __forceinline__ void q4_block(const uint8_t *ra, const uint8_t *rb, c
         int ml[4], mh[4];
         mma_k16_u8u8(ml, a0, a1, x[G].bl);
         mma_k16_u8s8(mh, a0, a1, x[G].bh);
-        const float dd[4] = {da * x[G].d0, da * x[G].d1, db * x[G].d0, db * x[G].d1};
-        const float dm[4] = {ma * x[G].d0, ma * x[G].d1, mb * x[G].d0, mb * x[G].d1};
+        // fragment i: row a (i < 2) or b, token column i & 1: acc += dx * (d * isum - dmin * msum)
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int isum = il[G][i] + (ih[G][i] >> 4), msum = ml[i] + 64 * mh[i];
-            acc[G][i] += __fmul_rn(dd[i], (float)isum) - __fmul_rn(dm[i], (float)msum);
+            const float dr = i < 2 ? da : db, mr = i < 2 ? ma : mb;
+            const float t = __fmaf_rn(-mr, (float)msum, __fmul_rn(dr, (float)isum));
+            acc[G][i] = __fmaf_rn((i & 1) ? x[G].d1 : x[G].d0, t, acc[G][i]);
         }
     }
 }
