@@ -37,6 +37,15 @@
  * ggml's search).  The kernels and this oracle read the same bytes, so that
  * does not affect parity.
  *
+ * Pinning.  Pinned to the reference or an independent decoder: the Q4_K / Q6_K
+ * block decoders (bit for bit against gguf-py golden vectors), the pair order
+ * and the -1 row semantics (the properties of the reference's own tests,
+ * qwen3moe.rs:2954-3070 and mul_mat_id_skip.rs), and the Q8_K dot against the
+ * reference's f64 error bound (iqk_kernels.rs:128-147).  Parity unpinned: the
+ * expert-product arithmetic against ggml itself -- ggml is not in the tree and
+ * the reference holds no golden MoE outputs, so that restatement follows the
+ * published algorithm only.
+ *
  * Canonical orders.  Selected expert ids must be bit-exact between this oracle
  * and the CUDA path, so every floating-point step that feeds the top-k is done
  * in one fixed order of IEEE operations that both sides follow

@@ -19,11 +19,12 @@ constexpr int SORT_WARPS = 32;
 //   3. each warp walks its segment in order, 32 pairs at a time; __match_any_sync ranks the lanes
 //      of equal expert, so the scatter is stable.
 // ids outside [0, n_slots) are not dispatched; ids >= n_slots also latch TMOE_DEV_ERR_BADID.
-// Also writes the increasing list of experts with pairs (active, n_active[0]).
+// Also writes the increasing list of experts with pairs (n_active[0] of them) with their pair
+// ranges: active[i] = {e, offsets[e], offsets[e + 1], 0}.
 // sh: SORT_WARPS * n_slots + n_slots + 1 ints of shared memory.
 __device__ void sort_pairs_cta(const int32_t *ids, int n_pairs, int n_slots, int32_t *__restrict__ counts,
                                int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
-                               int32_t *__restrict__ active, int32_t *__restrict__ n_active, int *counters,
+                               int4 *__restrict__ active, int32_t *__restrict__ n_active, int *counters,
                                int n_counters, int *err, int32_t *sh) {
     int32_t *hist = sh;                         // [SORT_WARPS][n_slots]
     int32_t *offs = sh + SORT_WARPS * n_slots;  // [n_slots + 1]
@@ -77,7 +78,7 @@ __device__ void sort_pairs_cta(const int32_t *ids, int n_pairs, int n_slots, int
             const int e = base + lane;
             const bool has = e < n_slots && (offs[e + 1] - offs[e]) > 0;
             const unsigned m = __ballot_sync(0xffffffffu, has);
-            if (has) active[na + __popc(m & ((1u << lane) - 1u))] = e;
+            if (has) active[na + __popc(m & ((1u << lane) - 1u))] = make_int4(e, offs[e], offs[e + 1], 0);
             na += __popc(m);
         }
         if (lane == 0) n_active[0] = na;
@@ -100,7 +101,7 @@ __device__ void sort_pairs_cta(const int32_t *ids, int n_pairs, int n_slots, int
 
 __global__ void __launch_bounds__(1024) sort_pairs_kernel(const int32_t *__restrict__ ids, int n_pairs, int n_slots,
                                                           int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
-                                                          int32_t *__restrict__ perm, int32_t *__restrict__ active,
+                                                          int32_t *__restrict__ perm, int4 *__restrict__ active,
                                                           int32_t *__restrict__ n_active, int *counters, int n_counters,
                                                           int *err) {
     extern __shared__ int32_t sh[];
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(1024) route_dispatch_kernel(const float *__res
                                                               int32_t *__restrict__ ids_out, float *__restrict__ w_out,
                                                               int32_t *__restrict__ mapped, int n_slots,
                                                               int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
-                                                              int32_t *__restrict__ perm, int32_t *__restrict__ active,
+                                                              int32_t *__restrict__ perm, int4 *__restrict__ active,
                                                               int32_t *__restrict__ n_active, int *counters,
                                                               int n_counters, int *err) {
     extern __shared__ int32_t sh[];
@@ -214,7 +215,7 @@ static cudaError_t set_smem_once(KernT kern, size_t smem, int *cache) {
 }
 
 cudaError_t launch_sort_pairs(const int32_t *ids, int n_pairs, int n_slots, int32_t *counts, int32_t *offsets,
-                              int32_t *perm, int32_t *active, int32_t *n_active, int *counters, int n_counters,
+                              int32_t *perm, int4 *active, int32_t *n_active, int *counters, int n_counters,
                               int *err, cudaStream_t st) {
     const size_t smem = sort_pairs_smem(n_slots);
     static int cache[64] = {};
@@ -231,7 +232,7 @@ bool route_dispatch_fits(int64_t T, int k, int E, int n_slots) {
 
 cudaError_t launch_route_dispatch(const float *logits, int T, int E, int k, const int32_t *table, int n_table,
                                   int32_t *ids_out, float *w_out, int32_t *mapped, int n_slots, int32_t *counts,
-                                  int32_t *offsets, int32_t *perm, int32_t *active, int32_t *n_active,
+                                  int32_t *offsets, int32_t *perm, int4 *active, int32_t *n_active,
                                   int *counters, int n_counters, int *err, cudaStream_t st) {
     const size_t smem = sizeof(int32_t) * ((size_t)((T * k + 3) & ~3)) + sort_pairs_smem(n_slots);
     static int cache[4][64] = {};

@@ -42,11 +42,14 @@ constexpr int Q4_CHUNK_U32 = TMOE_Q4K_BYTES / 4;  // tensor-map elements per Q4_
 constexpr uint32_t NIB = 0x0f0f0f0fu;
 constexpr unsigned FULL = 0xffffffffu;
 
-// What a fill holds, written by lane 0 before the arrive on the slot's barrier.
+// What a fill holds, written by lane 0 before the arrive on the slot's barrier.  At chunk 0 of a
+// pass the fill also carries the pass's pair indices (perm[beg + 16 * pass ...], a bulk copy
+// rounded out to 16 bytes; poff = where the first one landed, in ints).
 struct SlotRec {
-    int item, pass, chunk, e, beg, end, r0, r1;
+    int item, tile, pass, chunk, beg, end, poff, r0;
 };
-static_assert(GEMV_NW * GEMV_MAXD * (8 + (int)sizeof(SlotRec)) <= GEMV_HDR, "header");
+static_assert(GEMV_NW * GEMV_MAXD * (8 + (int)sizeof(SlotRec)) + 8 * 8 + 4 * GEMV_NW <= GEMV_HDR, "header");
+constexpr int PERM_STAGE = 128;  // bytes after a slot's weights for the pass's pair indices
 
 // Tensor maps of the Q4_K matrices (unused for Q6_K).
 struct GemvMaps {
@@ -84,6 +87,10 @@ __device__ __forceinline__ int sbyte(uint32_t w, int i) {
     asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(s));
     return (int)r;
 }
+
+// n / d for 0 <= n < 2^24 and 1 <= d <= 2^16 with m = ceil(2^40 / d): the error of m / 2^40 is
+// below 2^-40, times n below 2^-16 <= 1/d, which does not carry past the next multiple of d.
+__device__ __forceinline__ int fast_div(int n, uint64_t m) { return (int)(((uint64_t)(uint32_t)n * m) >> 40); }
 
 __device__ __forceinline__ uint2 ldg64(const void *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
 __device__ __forceinline__ uint32_t ldg32(const void *p) { return __ldg(reinterpret_cast<const uint32_t *>(p)); }
@@ -306,42 +313,103 @@ __device__ __forceinline__ void q6_block(const uint8_t *ba, const uint8_t *bb, c
 __device__ __forceinline__ float silu_mul(float g, float u) { return (g / (1.0f + expf(-g))) * u; }
 
 // ------------------------------------------------------------------ the warp's feed (warp-uniform state)
-struct Feed {
-    int r_next, r_lim;  // the item range being handed out
-    int pre;            // lane 0: start of the prefetched next range (read at first use)
-    int item, e, beg, end, pass, npass, chunk;  // the next fill (item < 0: none left)
+// Items are handed out in groups of GEMV_NW consecutive items, one per warp of a CTA: warp w takes
+// item 8 * gid + w of each group gid its CTA draws.  A CTA's warps thus work on neighbouring
+// rows of the same expert at about the same time and share its tokens' activation rows in L1.
+// The CTA's group index i maps to gid = i * gridDim.x + blockIdx.x for i < n_static (about 4/5
+// of the groups, no atomics), and the rest come dynamically from a global counter (items differ
+// in token count): the first warp that needs dynamic index d claims ring entry d (once every
+// warp has read index d - GQ_RING from it), draws the id and publishes it; the others wait
+// (bounded) for it.
+constexpr int GQ_RING = 8;
+constexpr int GQ_CLAIM = -0x7fffffff;
+
+struct GroupQueue {
+    unsigned long long *ring;  // {tag = dynamic index d, gid} per entry, as one 64-bit word
+    int *prog;                 // per warp: the last dynamic index it read (INT_MAX when done)
+    int n_static;              // static group indices per CTA
 };
 
-__device__ __forceinline__ void next_item(const GemvArgs &a, Feed &f, int n_items, int ch, int dyn0) {
+__device__ __forceinline__ int gq_tag(unsigned long long v) { return (int)(uint32_t)(v & 0xffffffffull); }
+__device__ __forceinline__ int gq_gid(unsigned long long v) { return (int)(uint32_t)(v >> 32); }
+
+// The CTA's group id for index i (lane 0 only); -1 on a timeout (latched by the caller).
+__device__ int gq_get(const GemvArgs &a, const GroupQueue &q, int i) {
+    if (i < q.n_static) return i * (int)gridDim.x + (int)blockIdx.x;
+    const int d = i - q.n_static;
+    volatile unsigned long long *e = q.ring + (d % GQ_RING);
+    uint64_t t0 = 0;
+    for (int spin = 0;; ++spin) {
+        const unsigned long long v = *e;
+        if (gq_tag(v) == d) return gq_gid(v);
+        if (gq_tag(v) == d - GQ_RING) {
+            bool free = true;  // every warp has read index d - GQ_RING
+            for (int w = 0; w < GEMV_NW; w++)
+                if (((volatile int *)q.prog)[w] < d - GQ_RING) free = false;
+            if (free && atomicCAS(reinterpret_cast<int *>(const_cast<unsigned long long *>(e)), d - GQ_RING,
+                                  GQ_CLAIM) == d - GQ_RING) {
+                const int gid = q.n_static * (int)gridDim.x + atomicAdd(a.work, 1);
+                *e = ((unsigned long long)(uint32_t)gid << 32) | (uint32_t)d;
+                return gid;
+            }
+        }
+        if (spin == 64) t0 = globaltimer_ns();
+        if (spin > 64 && globaltimer_ns() - t0 > TMOE_WAIT_LIMIT_NS) return -1;
+    }
+}
+
+struct Feed {
+    int gi;             // the CTA group index of the next draw
+    int n_item, n_a;    // the next item and its active index (n_item < 0: none)
+    int4 n_info;        // its record, loading
+    int item, tile, beg, end, e, pass, npass, chunk;  // the next fill (item < 0: none left)
+};
+
+__device__ __forceinline__ int grab_item(const GemvArgs &a, Feed &f, const GroupQueue &q, int n_items) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n_groups = (n_items + GEMV_NW - 1) / GEMV_NW;
+    for (;;) {
+        int gid = 0;
+        if (lane == 0) {
+            gid = gq_get(a, q, f.gi);
+            if (gid < 0) latch_error(a.err, TMOE_DEV_ERR_TIMEOUT);
+            const bool done = gid < 0 || gid >= n_groups;
+            if (done || f.gi >= q.n_static) ((volatile int *)q.prog)[warp] = done ? 0x7fffffff : f.gi - q.n_static;
+        }
+        gid = __shfl_sync(FULL, gid, 0);
+        f.gi++;
+        if (gid < 0 || gid >= n_groups) return -1;
+        const int item = gid * GEMV_NW + warp;
+        if (item < n_items) return item;
+    }
+}
+
+__device__ __forceinline__ void fetch_next(const GemvArgs &a, Feed &f, const GroupQueue &q, int n_items) {
+    f.n_item = f.n_item < 0 && f.gi > 0 ? -1 : grab_item(a, f, q, n_items);
+    if (f.n_item >= 0) {
+        f.n_a = fast_div(f.n_item, a.tiles_m);
+        f.n_info = __ldg(a.active + f.n_a);
+    }
+}
+
+__device__ __forceinline__ void next_item(const GemvArgs &a, Feed &f, const GroupQueue &q, int n_items) {
     const int lane = threadIdx.x & 31;
     for (;;) {
-        if (f.r_next >= f.r_lim) {
-            const int start = dyn0 + __shfl_sync(FULL, f.pre, 0);
-            if (start >= n_items) {
-                f.item = -1;
-                return;
-            }
-            f.r_next = start;
-            f.r_lim = start + ch;
-            if (lane == 0) f.pre = atomicAdd(a.work, ch);
-        }
-        if (f.r_next >= n_items) {
+        const int item = f.n_item, ai = f.n_a;
+        if (item < 0) {
             f.item = -1;
             return;
         }
-        const int item = f.r_next++;
-        const int e = __ldg(a.active + item / a.tiles);
-        if (e < 0 || e >= a.n_slots) {
-            if (lane == 0) latch_error(a.err, TMOE_DEV_ERR_BADID);
-            continue;
-        }
-        const int beg = __ldg(a.offsets + e), end = __ldg(a.offsets + e + 1);
-        if (beg < 0 || end > a.n_pairs || end < beg) {
+        const int4 info = f.n_info;
+        fetch_next(a, f, q, n_items);
+        const int e = info.x, beg = info.y, end = info.z;
+        if (e < 0 || e >= a.n_slots || beg < 0 || end > a.n_pairs || end < beg) {
             if (lane == 0) latch_error(a.err, TMOE_DEV_ERR_BADID);
             continue;
         }
         if (end == beg) continue;
         f.item = item;
+        f.tile = item - ai * a.tiles;
         f.e = e;
         f.beg = beg;
         f.end = end;
@@ -356,45 +424,53 @@ __device__ __forceinline__ void next_item(const GemvArgs &a, Feed &f, int n_item
 // feed.  With no items left the fill is an end marker (no copies).
 template <int WT, bool GATEUP>
 __device__ __forceinline__ void fill(const GemvArgs &a, const GemvMaps &tm, Feed &f, uint64_t *bar, SlotRec *rec,
-                                     uint8_t *slot, int n_items, int ch, int dyn0) {
+                                     uint8_t *slot, const GroupQueue &q, int n_items) {
     const int lane = threadIdx.x & 31;
     if (lane == 0) {
         if (f.item < 0) {
             rec->item = -1;
             mbar_arrive_expect_tx(bar, 0u);
         } else {
-            *reinterpret_cast<int4 *>(rec) = make_int4(f.item, f.pass, f.chunk, f.e);
-            *reinterpret_cast<int2 *>(&rec->beg) = make_int2(f.beg, f.end);
-            const int tile = f.item % a.tiles;
+            uint32_t tx = WT == TMOE_WT_Q4K ? 16u * (uint32_t)a.chunk_blocks * TMOE_Q4K_BYTES : 16u * (uint32_t)a.nb1_0;
+            uintptr_t ps = 0;
+            uint32_t pbytes = 0;
+            int poff = 0;
+            if (f.chunk == 0) {  // the pass's pair indices, rounded out to 16 bytes
+                const int t0 = f.beg + f.pass * 2 * TOKG, nt = min(2 * TOKG, f.end - t0);
+                const uintptr_t src = reinterpret_cast<uintptr_t>(a.perm + t0);
+                ps = src & ~(uintptr_t)15;
+                pbytes = (uint32_t)(((src + 4u * (uint32_t)nt + 15) & ~(uintptr_t)15) - ps);
+                poff = (int)((src - ps) >> 2);
+                tx += pbytes;
+            }
+            *reinterpret_cast<int4 *>(rec) = make_int4(f.item, f.tile, f.pass, f.chunk);
+            *reinterpret_cast<int4 *>(&rec->beg) = make_int4(f.beg, f.end, poff, 0);
+            mbar_arrive_expect_tx(bar, tx);
             if constexpr (WT == TMOE_WT_Q4K) {
                 const int x = f.chunk * a.chunk_blocks * Q4_CHUNK_U32;
-                const uint32_t box = (uint32_t)a.chunk_blocks * TMOE_Q4K_BYTES;
                 if constexpr (GATEUP) {
-                    mbar_arrive_expect_tx(bar, 16u * box);
-                    tma_load_3d(slot, &tm.m[0], x, tile * 8, f.e, bar);
-                    tma_load_3d(slot + 8 * box, &tm.m[1], x, tile * 8, f.e, bar);
+                    tma_load_3d(slot, &tm.m[0], x, f.tile * 8, f.e, bar);
+                    tma_load_3d(slot + 8 * a.chunk_blocks * TMOE_Q4K_BYTES, &tm.m[1], x, f.tile * 8, f.e, bar);
                 } else {
-                    mbar_arrive_expect_tx(bar, 16u * box);
-                    tma_load_3d(slot, &tm.m[0], x, tile * 16, f.e, bar);
+                    tma_load_3d(slot, &tm.m[0], x, f.tile * 16, f.e, bar);
                 }
             } else {
                 const uint32_t rb = (uint32_t)a.nb1_0;
                 if constexpr (GATEUP) {
-                    mbar_arrive_expect_tx(bar, 16u * rb);
-                    bulk_g2s(slot, a.w0 + (size_t)f.e * a.nb2_0 + (size_t)tile * 8 * rb, 8u * rb, bar);
-                    bulk_g2s(slot + 8 * rb, a.w1 + (size_t)f.e * a.nb2_1 + (size_t)tile * 8 * rb, 8u * rb, bar);
+                    bulk_g2s(slot, a.w0 + (size_t)f.e * a.nb2_0 + (size_t)f.tile * 8 * rb, 8u * rb, bar);
+                    bulk_g2s(slot + 8 * rb, a.w1 + (size_t)f.e * a.nb2_1 + (size_t)f.tile * 8 * rb, 8u * rb, bar);
                 } else {
-                    mbar_arrive_expect_tx(bar, 16u * rb);
-                    bulk_g2s(slot, a.w0 + (size_t)f.e * a.nb2_0 + (size_t)tile * 16 * rb, 16u * rb, bar);
+                    bulk_g2s(slot, a.w0 + (size_t)f.e * a.nb2_0 + (size_t)f.tile * 16 * rb, 16u * rb, bar);
                 }
             }
+            if (pbytes) bulk_g2s(slot + a.wbytes, reinterpret_cast<const void *>(ps), pbytes, bar);
         }
     }
     __syncwarp();
     if (f.item < 0) return;
     if (++f.chunk == a.n_chunks) {
         f.chunk = 0;
-        if (++f.pass == f.npass) next_item(a, f, n_items, ch, dyn0);
+        if (++f.pass == f.npass) next_item(a, f, q, n_items);
     }
 }
 
@@ -423,19 +499,20 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
         na = na < 0 ? 0 : a.max_active;
     }
     const int n_items = na * a.tiles;
-    // First ranges are static (warp w: [w*ch, (w+1)*ch)); the counter hands out the rest.
-    const int n_warps = gridDim.x * GEMV_NW;
-    const int ch = n_items >= 4 * n_warps ? 2 : 1;
-    const int dyn0 = n_warps * ch;
+    GroupQueue q;
+    q.ring = reinterpret_cast<unsigned long long *>(smem + GEMV_NW * GEMV_MAXD * (8 + (int)sizeof(SlotRec)));
+    q.prog = reinterpret_cast<int *>(q.ring + GQ_RING);
+    q.n_static = (((n_items + GEMV_NW - 1) / GEMV_NW) * 4 / 5) / (int)gridDim.x;
+    if (threadIdx.x < GQ_RING) q.ring[threadIdx.x] = (uint32_t)((int)threadIdx.x - GQ_RING);  // "index d - ring read"
+    if (threadIdx.x < GEMV_NW) q.prog[threadIdx.x] = -1;
+    __syncthreads();
     Feed f;
-    f.r_next = (blockIdx.x * GEMV_NW + warp) * ch;
-    f.r_lim = f.r_next + ch;
-    f.pre = 0;
-    if (lane == 0) f.pre = atomicAdd(a.work, ch);
-    f.item = -1;
-    next_item(a, f, n_items, ch, dyn0);
+    f.gi = 0;
+    f.n_item = -1;
+    fetch_next(a, f, q, n_items);
+    next_item(a, f, q, n_items);
     for (int s = 0; s < D; s++)
-        fill<WT, GATEUP>(a, tm, f, &bars[s], &recs[s], slots + (size_t)s * a.slot_bytes, n_items, ch, dyn0);
+        fill<WT, GATEUP>(a, tm, f, &bars[s], &recs[s], slots + (size_t)s * a.slot_bytes, q, n_items);
 
     TokCols tc[2];
     int ng = 1;
@@ -458,37 +535,37 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
         const int4 rv = *reinterpret_cast<const int4 *>(&recs[s]);
         const int item = rv.x;
         if (item < 0) return;  // every later fill is an end marker too: nothing in flight
-        const int pass = rv.y, chunk = rv.z;
-        const int tile = item % a.tiles;
+        const int tile = rv.y, pass = rv.z, chunk = rv.w;
         const int b0 = chunk * a.chunk_blocks;
         const int nblk = min(a.chunk_blocks, nb - b0);
+        const uint8_t *sl = slots + (size_t)s * a.slot_bytes;
         if (chunk == 0) {  // a new pass: the token columns of its (up to) two groups
-            const int2 be = *reinterpret_cast<const int2 *>(&recs[s].beg);
-            const int t0 = be.x + pass * 2 * TOKG;
-            const int nt = min(2 * TOKG, be.y - t0);
+            const int4 bv = *reinterpret_cast<const int4 *>(&recs[s].beg);
+            const int t0 = bv.x + pass * 2 * TOKG;
+            const int nt = min(2 * TOKG, bv.y - t0);
+            const int *pp = reinterpret_cast<const int *>(sl + a.wbytes) + bv.z;  // the pass's pairs
             ng = nt > TOKG ? 2 : 1;
 #pragma unroll
             for (int G = 0; G < 2; G++) {
-                const int tg = t0 + G * TOKG, ntok = min(TOKG, nt - G * TOKG);
+                const int ntok = min(TOKG, nt - G * TOKG);
                 // past the group's end the group's first token stands in (never written)
-                int pg = ntok > 0 ? __ldg(a.perm + tg + (g < ntok ? g : 0)) : 0;
-                int p0 = ntok > 0 ? __ldg(a.perm + tg + (2 * t4 < ntok ? 2 * t4 : 0)) : 0;
-                int p1 = ntok > 0 ? __ldg(a.perm + tg + (2 * t4 + 1 < ntok ? 2 * t4 + 1 : 0)) : 0;
+                int pg = ntok > 0 ? pp[G * TOKG + (g < ntok ? g : 0)] : 0;
+                int p0 = ntok > 0 ? pp[G * TOKG + (2 * t4 < ntok ? 2 * t4 : 0)] : 0;
+                int p1 = ntok > 0 ? pp[G * TOKG + (2 * t4 + 1 < ntok ? 2 * t4 + 1 : 0)] : 0;
                 pg = (pg >= 0 && pg < a.n_pairs) ? pg : 0;
                 const bool v0 = 2 * t4 < ntok && p0 >= 0 && p0 < a.n_pairs;
                 const bool v1 = 2 * t4 + 1 < ntok && p1 >= 0 && p1 < a.n_pairs;
                 p0 = (p0 >= 0 && p0 < a.n_pairs) ? p0 : 0;
                 p1 = (p1 >= 0 && p1 < a.n_pairs) ? p1 : 0;
-                tc[G].xg = pg / a.x_div;
-                tc[G].x0 = p0 / a.x_div;
-                tc[G].x1 = p1 / a.x_div;
+                tc[G].xg = fast_div(pg, a.xdiv_m);
+                tc[G].x0 = fast_div(p0, a.xdiv_m);
+                tc[G].x1 = fast_div(p1, a.xdiv_m);
                 tc[G].pp0 = v0 ? p0 : -1;
                 tc[G].pp1 = v1 ? p1 : -1;
             }
 #pragma unroll
             for (int G = 0; G < 2; G++) acc[G][0] = acc[G][1] = acc[G][2] = acc[G][3] = 0.0f;
         }
-        const uint8_t *sl = slots + (size_t)s * a.slot_bytes;
         const int S = a.row_stride;
         if constexpr (WT == TMOE_WT_Q4K) {
             const uint8_t *ra = sl + (size_t)g * S, *rb = sl + (size_t)(g + 8) * S;
@@ -543,7 +620,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
             }
         }
         __syncwarp();  // every lane's reads of the slot are done (their values are consumed)
-        fill<WT, GATEUP>(a, tm, f, &bars[s], &recs[s], slots + (size_t)s * a.slot_bytes, n_items, ch, dyn0);
+        fill<WT, GATEUP>(a, tm, f, &bars[s], &recs[s], slots + (size_t)s * a.slot_bytes, q, n_items);
         if (chunk == a.n_chunks - 1) {  // this pass's sums are complete
             // output rows of MMA rows g and g+8
             int row_a, row_b;
@@ -581,7 +658,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
 
 // ------------------------------------------------------------------ launcher
 constexpr int GEMV_SMEM_1CTA = 226 * 1024;
-constexpr int GEMV_SMEM_2CTA = 112 * 1024;
+constexpr int GEMV_SMEM_2CTA = 113 * 1024;  // two CTAs: 2 x (113 + 1 reserved) KB = 228 KB
 
 struct GemvPlan {
     int cb, ctas_per_sm, d;
@@ -594,7 +671,8 @@ template <int WT>
 static GemvPlan plan_for(int K) {
     const int nb = K / TMOE_QK;
     const int cb = WT == TMOE_WT_Q4K ? (nb >= 2 ? 2 : 1) : nb;
-    const int slot = WT == TMOE_WT_Q4K ? ITEM_ROWS * TMOE_Q4K_BYTES * cb : ITEM_ROWS * TMOE_Q6K_BYTES * nb + 16;
+    const int slot = (WT == TMOE_WT_Q4K ? ITEM_ROWS * TMOE_Q4K_BYTES * cb : ITEM_ROWS * TMOE_Q6K_BYTES * nb + 16) +
+                     PERM_STAGE;
     const int d2 = (GEMV_SMEM_2CTA - GEMV_HDR) / (GEMV_NW * slot);
     if (d2 >= (WT == TMOE_WT_Q4K ? 3 : 1)) return {cb, 2, d2 < GEMV_MAXD ? d2 : GEMV_MAXD};
     const int d1 = (GEMV_SMEM_1CTA - GEMV_HDR) / (GEMV_NW * slot);
@@ -650,9 +728,13 @@ static cudaError_t launch_t(const GemvArgs &args_in, int max_items, int sm_count
     a.chunk_blocks = pl.cb;
     a.n_chunks = (nb + pl.cb - 1) / pl.cb;
     a.row_stride = (WT == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES) * pl.cb;
-    a.slot_bytes = WT == TMOE_WT_Q4K ? ITEM_ROWS * a.row_stride : ITEM_ROWS * a.row_stride + 16;
+    a.wbytes = WT == TMOE_WT_Q4K ? ITEM_ROWS * a.row_stride : ITEM_ROWS * a.row_stride + 16;
+    a.slot_bytes = a.wbytes + PERM_STAGE;
     a.d_slots = pl.d;
     a.tiles = a.N / (GATEUP ? ITEM_ROWS / 2 : ITEM_ROWS);
+    const uint64_t two40 = 1ull << 40;
+    a.tiles_m = (two40 + (uint64_t)a.tiles - 1) / (uint64_t)a.tiles;
+    a.xdiv_m = (two40 + (uint64_t)a.x_div - 1) / (uint64_t)a.x_div;
     GemvMaps tm;
     memset(&tm, 0, sizeof(tm));
     if (WT == TMOE_WT_Q4K) {
@@ -689,6 +771,10 @@ int gemv_rows_per_item(int wt, int K, int N) {
 cudaError_t launch_gemv(int wt, bool gateup, const GemvArgs &a, int max_items, int sm_count, cudaStream_t st) {
     if (a.K % TMOE_QK != 0 || a.K <= 0 || a.K > 65536) return cudaErrorInvalidValue;
     if (gemv_rows_per_item(wt, a.K, a.N) == 0) return cudaErrorInvalidValue;
+    // item and pair indices stay below 2^24 and divisors at most 2^16 (fast_div)
+    if (a.n_pairs < 0 || a.n_pairs >= (1 << 24) || a.x_div < 1 || a.x_div > (1 << 16) ||
+        (int64_t)max_items * (a.N / (ITEM_ROWS / 2)) >= (1 << 24))
+        return cudaErrorInvalidValue;
     // contiguous rows, 16-byte aligned expert strides (the fills' alignment arithmetic rests on it)
     const size_t rb = (size_t)(wt == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES) * (a.K / TMOE_QK);
     if (a.nb1_0 != rb || (a.nb2_0 & 15u) || ((uintptr_t)a.w0 & 15u)) return cudaErrorInvalidValue;

@@ -38,15 +38,16 @@ cudaError_t launch_quantize_q8k(const float *x, int64_t rows, int K, const int32
 // dispatch.cu
 size_t sort_pairs_smem(int n_slots);
 // The dispatch also zeroes `counters` (n_counters ints: the GEMV work counters; may be NULL).
+// active: the experts with pairs, {e, offsets[e], offsets[e + 1], 0} each, n_active[0] of them.
 cudaError_t launch_sort_pairs(const int32_t *ids, int n_pairs, int n_slots, int32_t *counts, int32_t *offsets,
-                              int32_t *perm, int32_t *active, int32_t *n_active, int *counters, int n_counters,
+                              int32_t *perm, int4 *active, int32_t *n_active, int *counters, int n_counters,
                               int *err, cudaStream_t st);
 // Fused softmax/top-k + optional EP map + dispatch for T*k <= ROUTE_FUSED_MAX_PAIRS.
 #define ROUTE_FUSED_MAX_PAIRS 4096
 bool route_dispatch_fits(int64_t T, int k, int E, int n_slots);
 cudaError_t launch_route_dispatch(const float *logits, int T, int E, int k, const int32_t *table, int n_table,
                                   int32_t *ids_out, float *w_out, int32_t *mapped, int n_slots, int32_t *counts,
-                                  int32_t *offsets, int32_t *perm, int32_t *active, int32_t *n_active,
+                                  int32_t *offsets, int32_t *perm, int4 *active, int32_t *n_active,
                                   int *counters, int n_counters, int *err, cudaStream_t st);
 cudaError_t launch_map_ids(const int32_t *ids, int64_t n, const int32_t *table, int64_t n_table, int32_t *out,
                            cudaStream_t st);
@@ -71,7 +72,9 @@ struct GemvArgs {
     const float *xd;
     const uint32_t *xbl, *xbh;
     int x_div;
-    const int32_t *perm, *offsets, *active, *n_active;
+    const int32_t *perm;   // 16 bytes past the last pair are readable (bulk copies round up)
+    const int4 *active;    // {e, first pair, end pair, 0} per active expert (launch_sort_pairs)
+    const int32_t *n_active;
     int n_slots;     // experts in the weight tensors (active ids are checked against it)
     int max_active;  // the grid was sized for at most this many active experts
     int n_pairs;     // pair rows of perm / out
@@ -83,8 +86,10 @@ struct GemvArgs {
     int chunk_blocks;  // super-blocks per fill
     int n_chunks;      // fills per row span of K
     int row_stride;    // shared-memory bytes per fill row
-    int slot_bytes;    // shared-memory bytes per slot (16 rows)
+    int slot_bytes;    // shared-memory bytes per slot (16 rows, then the pass's pair indices)
+    int wbytes;        // weight bytes of a slot
     int d_slots;       // slots per warp
+    uint64_t tiles_m, xdiv_m;  // ceil(2^40 / tiles), ceil(2^40 / x_div): exact division of n < 2^24
 };
 // Rows per work item of the GEMV for K columns and N rows per expert; 0 if N does not fit.
 int gemv_rows_per_item(int wt, int K, int N);

@@ -31,7 +31,8 @@ struct tmoe_handle {
     int32_t *ids = nullptr;
     float *w = nullptr;
     int32_t *mapped = nullptr;
-    int32_t *counts = nullptr, *offsets = nullptr, *perm = nullptr, *active = nullptr, *n_active = nullptr;
+    int32_t *counts = nullptr, *offsets = nullptr, *perm = nullptr, *n_active = nullptr;
+    int4 *active = nullptr;
     // activations: Q8_K of the layer input (read by gate/up) and of the SwiGLU output (read by down)
     float *xn = nullptr;
     int8_t *xq = nullptr;
@@ -134,9 +135,9 @@ size_t carve(tmoe_handle *h, char *base) {
     h->mapped = (int32_t *)take(P * 4);
     h->counts = (int32_t *)take(kMaxSlots * 4);
     h->offsets = (int32_t *)take((kMaxSlots + 1) * 4);
-    h->active = (int32_t *)take(kMaxSlots * 4);
+    h->active = (int4 *)take(kMaxSlots * 16);
     h->n_active = (int32_t *)take(4);
-    h->perm = (int32_t *)take(P * 4);
+    h->perm = (int32_t *)take(P * 4 + 16);  // + the GEMV's bulk-copy round-up
     const size_t nbg = (size_t)tmoe::q8_nbw(wt_of(c.gate_type)), nbd = (size_t)tmoe::q8_nbw(wt_of(c.down_type));
     h->xn = (float *)take(T * H * 4);
     h->xq = (int8_t *)take(T * H);
@@ -205,7 +206,7 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
     g.nb1_0 = t->gate_nb1, g.nb2_0 = t->gate_nb2, g.nb1_1 = t->up_nb1, g.nb2_1 = t->up_nb2;
     g.K = H, g.N = I;
     g.xq = h->xq, g.xd = h->xd, g.xbl = h->xbl, g.xbh = h->xbh, g.x_div = k;
-    g.perm = h->perm, g.offsets = h->offsets, g.active = h->active, g.n_active = h->n_active;
+    g.perm = h->perm, g.active = h->active, g.n_active = h->n_active;
     g.n_slots = t->n_slots, g.max_active = max_active, g.n_pairs = (int)P, g.work = h->counters + 0;
     g.out = h->act, g.err = h->err;
     {
@@ -223,7 +224,7 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
     d.nb1_0 = t->down_nb1, d.nb2_0 = t->down_nb2;
     d.K = I, d.N = H;
     d.xq = h->aq, d.xd = h->ad, d.xbl = h->abl, d.xbh = h->abh, d.x_div = 1;
-    d.perm = h->perm, d.offsets = h->offsets, d.active = h->active, d.n_active = h->n_active;
+    d.perm = h->perm, d.active = h->active, d.n_active = h->n_active;
     d.n_slots = t->n_slots, d.max_active = max_active, d.n_pairs = (int)P, d.work = h->counters + 1;
     d.out = h->dout, d.err = h->err;
     {
@@ -500,8 +501,8 @@ int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, s
     const size_t nbw = (size_t)tmoe::q8_nbw(wt);
     size_t o_q = lay((size_t)rows * K), o_d = lay((size_t)rows * (K / 256) * 4);
     size_t o_bl = lay((size_t)rows * (K / 256) * nbw * 4), o_bh = lay((size_t)rows * (K / 256) * nbw * 4);
-    size_t o_cnt = lay(kMaxSlots * 4), o_off = lay((kMaxSlots + 1) * 4), o_act = lay(kMaxSlots * 4), o_na = lay(4);
-    size_t o_perm = lay((size_t)P * 4), o_work = lay(kCounters * 4);
+    size_t o_cnt = lay(kMaxSlots * 4), o_off = lay((kMaxSlots + 1) * 4), o_act = lay(kMaxSlots * 16), o_na = lay(4);
+    size_t o_perm = lay((size_t)P * 4 + 16), o_work = lay(kCounters * 4);
     cudaError_t e;
     if (need > h->op_ws_bytes) {
         if (h->op_ws) {
@@ -518,8 +519,9 @@ int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, s
     int8_t *q = (int8_t *)(base + o_q);
     float *d = (float *)(base + o_d);
     uint32_t *bl = (uint32_t *)(base + o_bl), *bh = (uint32_t *)(base + o_bh);
-    int32_t *cnt = (int32_t *)(base + o_cnt), *offs = (int32_t *)(base + o_off), *act = (int32_t *)(base + o_act),
-            *na = (int32_t *)(base + o_na), *perm = (int32_t *)(base + o_perm);
+    int32_t *cnt = (int32_t *)(base + o_cnt), *offs = (int32_t *)(base + o_off), *na = (int32_t *)(base + o_na),
+            *perm = (int32_t *)(base + o_perm);
+    int4 *act = (int4 *)(base + o_act);
     int *work = (int *)(base + o_work);
     if ((e = tmoe::launch_sort_pairs(ids, (int)P, (int)n_w, cnt, offs, perm, act, na, work, kCounters, h->err, st)) !=
         cudaSuccess)
@@ -534,7 +536,7 @@ int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, s
     g.K = (int)K, g.N = (int)N;
     g.xq = q, g.xd = d, g.xbl = bl, g.xbh = bh, g.x_div = b1 == 1 ? (int)n_used : 1;
     const int max_active = (int)(P < n_w ? P : n_w);
-    g.perm = perm, g.offsets = offs, g.active = act, g.n_active = na;
+    g.perm = perm, g.active = act, g.n_active = na;
     g.n_slots = (int)n_w, g.max_active = max_active, g.n_pairs = (int)P, g.work = work;
     g.out = out, g.err = h->err;
     if ((e = tmoe::launch_gemv(wt, false, g, max_active, h->sm_count, st)) != cudaSuccess)
