@@ -5,6 +5,7 @@
 // (qwen3moe.rs:2912-2923).
 #include "common.cuh"
 #include "kernels.cuh"
+#include "q8k.cuh"
 #include "route.cuh"
 
 namespace tmoe {
@@ -21,18 +22,19 @@ constexpr int SORT_WARPS = 32;
 // ids outside [0, n_slots) are not dispatched; ids >= n_slots also latch TMOE_DEV_ERR_BADID.
 // Also writes the increasing list of experts with pairs (n_active[0] of them) with their pair
 // ranges: active[i] = {e, offsets[e], offsets[e + 1], 0}.
-// sh: SORT_WARPS * n_slots + n_slots + 1 ints of shared memory.
+// NW: the warps of the CTA.  sh: NW * n_slots + n_slots + 1 ints of shared memory.
+template <int NW>
 __device__ void sort_pairs_cta(const int32_t *ids, int n_pairs, int n_slots, int32_t *__restrict__ counts,
                                int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
                                int4 *__restrict__ active, int32_t *__restrict__ n_active, int *counters,
                                int n_counters, int *err, int32_t *sh) {
-    int32_t *hist = sh;                         // [SORT_WARPS][n_slots]
-    int32_t *offs = sh + SORT_WARPS * n_slots;  // [n_slots + 1]
+    int32_t *hist = sh;                         // [NW][n_slots]
+    int32_t *offs = sh + NW * n_slots;  // [n_slots + 1]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (counters && (int)threadIdx.x < n_counters) counters[threadIdx.x] = 0;  // work counters of the GEMVs
-    for (int i = threadIdx.x; i < SORT_WARPS * n_slots; i += blockDim.x) hist[i] = 0;
+    for (int i = threadIdx.x; i < NW * n_slots; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    int seg = (n_pairs + SORT_WARPS - 1) / SORT_WARPS;
+    int seg = (n_pairs + NW - 1) / NW;
     seg = (seg + 31) & ~31;
     const int p0 = warp * seg, p1 = min(n_pairs, p0 + seg);
     bool bad = false;
@@ -45,7 +47,7 @@ __device__ void sort_pairs_cta(const int32_t *ids, int n_pairs, int n_slots, int
     __syncthreads();
     for (int e = threadIdx.x; e < n_slots; e += blockDim.x) {
         int run = 0;
-        for (int w = 0; w < SORT_WARPS; w++) {
+        for (int w = 0; w < NW; w++) {
             const int c = hist[w * n_slots + e];
             hist[w * n_slots + e] = run;
             run += c;
@@ -84,7 +86,7 @@ __device__ void sort_pairs_cta(const int32_t *ids, int n_pairs, int n_slots, int
         if (lane == 0) n_active[0] = na;
     }
     for (int e = threadIdx.x; e < n_slots; e += blockDim.x)
-        for (int w = 0; w < SORT_WARPS; w++) hist[w * n_slots + e] += offs[e];
+        for (int w = 0; w < NW; w++) hist[w * n_slots + e] += offs[e];
     __syncthreads();
     const unsigned lt = (1u << lane) - 1u;
     for (int base = p0; base < p1; base += 32) {
@@ -105,7 +107,8 @@ __global__ void __launch_bounds__(1024) sort_pairs_kernel(const int32_t *__restr
                                                           int32_t *__restrict__ n_active, int *counters, int n_counters,
                                                           int *err) {
     extern __shared__ int32_t sh[];
-    sort_pairs_cta(ids, n_pairs, n_slots, counts, offsets, perm, active, n_active, counters, n_counters, err, sh);
+    sort_pairs_cta<SORT_WARPS>(ids, n_pairs, n_slots, counts, offsets, perm, active, n_active, counters, n_counters,
+                               err, sh);
 }
 
 // Decode regime (T*k <= ROUTE_FUSED_MAX_PAIRS): softmax/top-k of every token, the optional EP
@@ -137,7 +140,132 @@ __global__ void __launch_bounds__(1024) route_dispatch_kernel(const float *__res
         }
     }
     __syncthreads();
-    sort_pairs_cta(sid, T * k, n_slots, counts, offsets, perm, active, n_active, counters, n_counters, err, sort_sh);
+    sort_pairs_cta<SORT_WARPS>(sid, T * k, n_slots, counts, offsets, perm, active, n_active, counters, n_counters,
+                               err, sort_sh);
+}
+
+// The decode regime's whole routing in one launch: router logits, Q8_K of x, softmax/top-k, the
+// optional EP map and the dispatch.  CTA (i, j) of a (ceil(E/8), ceil(T/TT)) grid:
+//  1. stages TT token rows of x and 8 expert rows of the router matrix into shared memory with
+//     bulk copies, and computes those logits in the canonical dot order (the same arithmetic as
+//     router_logits_kernel: bit-identical logits); CTAs i = 0 also write the Q8_K rows of x;
+//  2. the last CTA of token tile j (a counter per tile, threadfence-ordered; no CTA waits on
+//     another) reads the tile's logits back and runs top-k for its tokens, one warp per token;
+//  3. the last token tile to finish runs the dispatch of all T * k pairs and resets the counters.
+// done: gridDim.y + 1 ints, zero before the first launch (the kernel leaves them zero).
+constexpr int FR_WARPS = 8;  // experts per CTA, one warp each
+
+template <int TT, int MAXPER>
+__global__ void __launch_bounds__(FR_WARPS * 32) route_fused_kernel(
+    const float *__restrict__ x, const float *__restrict__ rw, int T, int H, int E, int k, Q8Rows q8,
+    float *__restrict__ logits, const int32_t *__restrict__ table, int n_table, int32_t *__restrict__ ids_out,
+    float *__restrict__ w_out, int32_t *__restrict__ mapped, int n_slots, int32_t *__restrict__ counts,
+    int32_t *__restrict__ offsets, int32_t *__restrict__ perm, int4 *__restrict__ active,
+    int32_t *__restrict__ n_active, int *counters, int n_counters, int *done, int *err) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    __shared__ uint64_t bar_s;
+    __shared__ int flag_s;
+    uint64_t *bar = &bar_s;
+    int *flag = &flag_s;
+    float *xs = reinterpret_cast<float *>(sm);  // [TT][H]
+    float *ws = xs + TT * H;                    // [FR_WARPS][H]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e0 = blockIdx.x * FR_WARPS, t0 = blockIdx.y * TT;
+    const int nt = min(TT, T - t0), ne = min(FR_WARPS, E - e0);
+    const int H4 = H / 4;
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t row = (uint32_t)H * 4u;
+        mbar_arrive_expect_tx(bar, (uint32_t)(nt + ne) * row);
+        for (int j = 0; j < nt; j++) bulk_g2s(xs + j * H, x + (int64_t)(t0 + j) * H, row, bar);
+        for (int j = 0; j < ne; j++) bulk_g2s(ws + j * H, rw + (int64_t)(e0 + j) * H, row, bar);
+    }
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar, 0))) {
+        // nothing else may run on this tile: the copies may still be in flight
+        if (lane == 0) latch_error(err, TMOE_DEV_ERR_TIMEOUT);
+        if (threadIdx.x == 0) mbar_wait_bounded(bar, 0);
+    }
+    const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
+    if (q8.qs && blockIdx.x == 0) {  // Q8_K of the staged rows: one warp per (token, 256-block)
+        const int nb = H / TMOE_QK;
+        for (int u = warp; u < nt * nb; u += FR_WARPS) {
+            const int j = u / nb, b = u % nb;
+            const float4 a0 = xs4[j * H4 + b * 64 + 2 * lane], a1 = xs4[j * H4 + b * 64 + 2 * lane + 1];
+            const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            uint2 q;
+            float d;
+            int s16;
+            q8k_block_warp(v, q, d, s16);
+            q8k_store_warp(q8, t0 + j, H, b, q, d, s16);
+        }
+    }
+    if (warp < ne) {  // canonical dot: lane l takes elements 128m + 4l .. 4l+3 in m order, then a butterfly
+        const float4 *w4 = reinterpret_cast<const float4 *>(ws + warp * H);
+        float acc[TT];
+#pragma unroll
+        for (int j = 0; j < TT; j++) acc[j] = 0.0f;
+        for (int m = 0; m < H / 128; m++) {
+            const float4 w = w4[32 * m + lane];
+#pragma unroll
+            for (int j = 0; j < TT; j++) {
+                const float4 xv = xs4[j * H4 + 32 * m + lane];
+                acc[j] = __fmaf_rn(w.x, xv.x, acc[j]);
+                acc[j] = __fmaf_rn(w.y, xv.y, acc[j]);
+                acc[j] = __fmaf_rn(w.z, xv.z, acc[j]);
+                acc[j] = __fmaf_rn(w.w, xv.w, acc[j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < TT; j++) {
+            const float sv = butterfly_f32(acc[j]);
+            if (lane == 0 && j < nt) logits[(int64_t)(t0 + j) * E + e0 + warp] = sv;
+        }
+    }
+    // 2. the last CTA of this token tile: top-k of its tokens
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        *flag = atomicAdd(&done[blockIdx.y], 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    float *lgs = xs;  // [TT][E], the staged rows are no longer needed
+    for (int i = threadIdx.x; i < nt * E; i += blockDim.x) lgs[i] = __ldcg(logits + (int64_t)t0 * E + i);
+    __syncthreads();
+    if (warp < nt) {
+        const int t = t0 + warp;
+        int id;
+        float wt;
+        topk_token<MAXPER>(lgs + warp * E, E, k, nullptr, id, wt);
+        if (lane < k) {
+            const int m = table ? ((id >= 0 && id < n_table) ? table[id] : -1) : id;
+            ids_out[t * k + lane] = id;
+            w_out[t * k + lane] = wt;
+            mapped[t * k + lane] = m;
+        }
+    }
+    // 3. the last token tile: the dispatch of all pairs
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        done[blockIdx.y] = 0;  // every CTA of this tile has counted
+        __threadfence();
+        *flag = atomicAdd(&done[gridDim.y], 1) == (int)gridDim.y - 1;
+    }
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    const int n_pairs = T * k;
+    int32_t *sid = reinterpret_cast<int32_t *>(sm);  // [n_pairs], then the sort's scratch
+    for (int i = threadIdx.x; i < n_pairs; i += blockDim.x) sid[i] = __ldcg(mapped + i);
+    __syncthreads();
+    sort_pairs_cta<FR_WARPS>(sid, n_pairs, n_slots, counts, offsets, perm, active, n_active, counters, n_counters,
+                             err, sid + ((n_pairs + 3) & ~3));
+    if (threadIdx.x == 0) done[gridDim.y] = 0;
 }
 
 __global__ void map_ids_kernel(const int32_t *__restrict__ ids, int64_t n, const int32_t *__restrict__ table,
@@ -255,6 +383,63 @@ cudaError_t launch_route_dispatch(const float *logits, int T, int E, int k, cons
     else
         return cudaErrorInvalidValue;
 #undef TMOE_RD
+    return cudaGetLastError();
+}
+
+static size_t route_fused_smem(int tt, int H, int T, int k, int n_slots) {
+    const size_t staged = (size_t)(tt + FR_WARPS) * H * 4;
+    const size_t sorting = 4 * ((size_t)((T * k + 3) & ~3) + (size_t)FR_WARPS * n_slots + n_slots + 1);
+    return staged > sorting ? staged : sorting;
+}
+
+static int route_fused_tt(int H, int T, int k, int n_slots) {
+    for (int tt = 8; tt >= 4; tt >>= 1)
+        if (route_fused_smem(tt, H, T, k, n_slots) <= 200 * 1024) return tt;
+    return 0;
+}
+
+bool route_fused_fits(int64_t T, int k, int E, int H, int n_slots) {
+    return route_dispatch_fits(T, k, E, n_slots) && H % 128 == 0 && route_fused_tt(H, (int)T, k, n_slots) > 0;
+}
+
+int route_fused_tiles(int64_t T, int k, int E, int H, int n_slots) {
+    const int tt = route_fused_tt(H, (int)T, k, n_slots);
+    return tt ? (int)((T + tt - 1) / tt) : 0;
+}
+
+cudaError_t launch_route_fused(const float *x, const float *rw, int T, int H, int E, int k, const Q8Rows *q8,
+                               float *logits, const int32_t *table, int n_table, int32_t *ids_out, float *w_out,
+                               int32_t *mapped, int n_slots, int32_t *counts, int32_t *offsets, int32_t *perm,
+                               int4 *active, int32_t *n_active, int *counters, int n_counters, int *done, int *err,
+                               cudaStream_t st) {
+    const int tt = route_fused_tt(H, T, k, n_slots);
+    if (!tt || !route_dispatch_fits(T, k, E, n_slots)) return cudaErrorInvalidValue;
+    const size_t smem = route_fused_smem(tt, H, T, k, n_slots);
+    const dim3 grid((E + FR_WARPS - 1) / FR_WARPS, (T + tt - 1) / tt);
+    const Q8Rows none{nullptr, nullptr, nullptr, nullptr, 0};
+    const Q8Rows qq = q8 ? *q8 : none;
+    static int cache[8][64] = {};
+#define TMOE_RF(TTV, MP, CI)                                                                                   \
+    do {                                                                                                       \
+        cudaError_t e = set_smem_once(route_fused_kernel<TTV, MP>, smem, cache[CI]);                           \
+        if (e != cudaSuccess) return e;                                                                        \
+        route_fused_kernel<TTV, MP><<<grid, FR_WARPS * 32, smem, st>>>(                                         \
+            x, rw, T, H, E, k, qq, logits, table, n_table, ids_out, w_out, mapped, n_slots, counts, offsets,    \
+            perm, active, n_active, counters, n_counters, done, err);                                           \
+    } while (0)
+    const int mp = E <= 32 ? 1 : E <= 64 ? 2 : E <= 128 ? 4 : 8;
+    if (tt == 8) {
+        if (mp == 1) TMOE_RF(8, 1, 0);
+        else if (mp == 2) TMOE_RF(8, 2, 1);
+        else if (mp == 4) TMOE_RF(8, 4, 2);
+        else TMOE_RF(8, 8, 3);
+    } else {
+        if (mp == 1) TMOE_RF(4, 1, 4);
+        else if (mp == 2) TMOE_RF(4, 2, 5);
+        else if (mp == 4) TMOE_RF(4, 4, 6);
+        else TMOE_RF(4, 8, 7);
+    }
+#undef TMOE_RF
     return cudaGetLastError();
 }
 

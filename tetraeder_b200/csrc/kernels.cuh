@@ -49,6 +49,15 @@ cudaError_t launch_route_dispatch(const float *logits, int T, int E, int k, cons
                                   int32_t *ids_out, float *w_out, int32_t *mapped, int n_slots, int32_t *counts,
                                   int32_t *offsets, int32_t *perm, int4 *active, int32_t *n_active,
                                   int *counters, int n_counters, int *err, cudaStream_t st);
+// The decode regime's routing in one launch (logits + Q8_K of x + top-k + map + dispatch) when
+// route_fused_fits; done: route_fused_tiles(...) + 1 ints, zero before the first launch.
+bool route_fused_fits(int64_t T, int k, int E, int H, int n_slots);
+int route_fused_tiles(int64_t T, int k, int E, int H, int n_slots);
+cudaError_t launch_route_fused(const float *x, const float *rw, int T, int H, int E, int k, const Q8Rows *q8,
+                               float *logits, const int32_t *table, int n_table, int32_t *ids_out, float *w_out,
+                               int32_t *mapped, int n_slots, int32_t *counts, int32_t *offsets, int32_t *perm,
+                               int4 *active, int32_t *n_active, int *counters, int n_counters, int *done, int *err,
+                               cudaStream_t st);
 cudaError_t launch_map_ids(const int32_t *ids, int64_t n, const int32_t *table, int64_t n_table, int32_t *out,
                            cudaStream_t st);
 cudaError_t launch_zero_invalid_rows(const int32_t *ids, int64_t n_pairs, int n_slots, int N, float *out,

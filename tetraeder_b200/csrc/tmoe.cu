@@ -43,7 +43,8 @@ struct tmoe_handle {
     float *ad = nullptr;
     uint32_t *abl = nullptr, *abh = nullptr;
     float *dout = nullptr;
-    int *counters = nullptr;  // GEMV work counters
+    int *counters = nullptr;    // GEMV work counters
+    int *route_done = nullptr;  // the fused routing kernel's tile counters (zero between calls)
     int *err = nullptr;
     // growable scratch of tmoe_mul_mat_id
     void *op_ws = nullptr;
@@ -151,6 +152,7 @@ size_t carve(tmoe_handle *h, char *base) {
     h->abh = (uint32_t *)take(P * (I / 256) * nbd * 4);
     h->dout = (float *)take(P * H * 4);
     h->counters = (int *)take(kCounters * 4);
+    h->route_done = (int *)take((T / 4 + 2) * 4);
     h->err = (int *)take(4);
     return off;
 }
@@ -282,7 +284,8 @@ int tmoe_create(const tmoe_config *cfg, tmoe_handle **out) {
         return fail(nullptr, TMOE_E_NOMEM, "cudaMalloc(%zu) failed: %s", h->ws_bytes, cudaGetErrorString(e));
     }
     carve(h, (char *)h->ws);
-    e = cudaMemset(h->err, 0, sizeof(int));
+    e = cudaMemset(h->ws, 0, h->ws_bytes);  // the error flag and the routing counters start at zero
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaFree(h->ws);
         delete h;
@@ -418,6 +421,19 @@ int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
     // logits (and, fused, the Q8_K rows of xn)
     bool x_quantized = false;
     const float *lg = logits;
+    if (router_w && tmoe::route_fused_fits(T, k, c.n_expert, c.n_embd, wts->n_slots)) {
+        // decode regime: logits + Q8_K of xn + top-k + id map + dispatch in one launch
+        const tmoe::Q8Rows q8{h->xq, h->xd, h->xbl, h->xbh, wt_of(c.gate_type)};
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_ROUTER_LOGITS);
+            e = tmoe::launch_route_fused(xn, router_w, (int)T, c.n_embd, c.n_expert, k, &q8, h->logits, id_map,
+                                         c.n_expert, ids, w, h->mapped, wts->n_slots, h->counts, h->offsets,
+                                         h->perm, h->active, h->n_active, h->counters, kCounters, h->route_done,
+                                         h->err, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "fused routing");
+        return run_experts(h, st, xn, T, h->mapped, w, wts, out, true, true);
+    }
     if (router_w) {
         x_quantized = tmoe::router_fuses_q8(c.n_embd);
         const tmoe::Q8Rows q8{h->xq, h->xd, h->xbl, h->xbh, wt_of(c.gate_type)};
