@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(1024) route_dispatch_kernel(const float *__res
 // optional EP map and the dispatch.  CTA (i, j) of a (ceil(E/8), ceil(T/TT)) grid:
 //  1. stages TT token rows of x and 8 expert rows of the router matrix into shared memory with
 //     bulk copies, and computes those logits in the canonical dot order (the same arithmetic as
-//     router_logits_kernel: bit-identical logits); CTAs i = 0 also write the Q8_K rows of x;
+//     router_logits_kernel: bit-identical logits); the tile's CTAs also write the Q8_K rows of x;
 //  2. the last CTA of token tile j (a counter per tile, threadfence-ordered; no CTA waits on
 //     another) reads the tile's logits back and runs top-k for its tokens, one warp per token;
 //  3. the last token tile to finish runs the dispatch of all T * k pairs and resets the counters.
@@ -190,9 +190,9 @@ __global__ void __launch_bounds__(FR_WARPS * 32) route_fused_kernel(
         if (threadIdx.x == 0) mbar_wait_bounded(bar, 0);
     }
     const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
-    if (q8.qs && blockIdx.x == 0) {  // Q8_K of the staged rows: one warp per (token, 256-block)
+    if (q8.qs) {  // Q8_K of the staged rows: one warp per (token, 256-block), spread over the tile's CTAs
         const int nb = H / TMOE_QK;
-        for (int u = warp; u < nt * nb; u += FR_WARPS) {
+        for (int u = blockIdx.x * FR_WARPS + warp; u < nt * nb; u += gridDim.x * FR_WARPS) {
             const int j = u / nb, b = u % nb;
             const float4 a0 = xs4[j * H4 + b * 64 + 2 * lane], a1 = xs4[j * H4 + b * 64 + 2 * lane + 1];
             const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};

@@ -5,7 +5,8 @@
 //   exp:      Cody-Waite reduction by ln 2 and a degree-7 Taylor polynomial (own code);
 //   softmax:  lane l sums e^(x-max) over experts l, l+32, ... then a butterfly over lane
 //             distances 16, 8, 4, 2, 1; p = e / sum (IEEE division);
-//   top-k:    k rounds of a warp argmax under the total order (p descending, index ascending);
+//   top-k:    k rounds of a warp argmax under the total order (p descending, index ascending)
+//             (warp reductions on the probabilities' bit patterns);
 //   weights:  w_j = sel_j / max(sel_0 + sel_1 + ..., 6.1035156e-5) (qwen3moe.rs:2886-2888).
 #pragma once
 
@@ -80,36 +81,34 @@ __device__ __forceinline__ void topk_token(const float *__restrict__ lg, int E, 
             if (probs) probs[e] = v[i];
         }
     }
+    // k rounds of a warp argmax under (p descending, index ascending): probabilities are in
+    // [0, 1], so their bit patterns order like the values; key = bits + 1 for a candidate, 0 for
+    // a removed (or absent, or NaN) one.  Two warp reductions per round: the largest key, then
+    // the smallest index holding it.
     float sel_mine = 0.0f;
     int id_mine = -1;
     for (int j = 0; j < k; j++) {
-        float bp = -2.0f;
+        uint32_t bk = 0u;
         int bi = 0x7fffffff;
 #pragma unroll
         for (int i = 0; i < MAXPER; i++) {
             const int e = lane + 32 * i;
-            if (e < E && v[i] >= 0.0f && (v[i] > bp || (v[i] == bp && e < bi))) {
-                bp = v[i];
+            const uint32_t key = (e < E && v[i] >= 0.0f) ? __float_as_uint(v[i]) + 1u : 0u;
+            if (key > bk) {  // e increases with i: an equal key keeps the lower index
+                bk = key;
                 bi = e;
             }
         }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-            const float op = __shfl_xor_sync(0xffffffffu, bp, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-            if (op > bp || (op == bp && oi < bi)) {
-                bp = op;
-                bi = oi;
-            }
-        }
-        if ((bi & 31) == lane) {
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+        const int mi = (int)__reduce_min_sync(0xffffffffu, bk == mk ? (uint32_t)bi : 0xffffffffu);
+        if ((mi & 31) == lane) {
 #pragma unroll
             for (int i = 0; i < MAXPER; i++)
-                if (lane + 32 * i == bi) v[i] = -1.0f;
+                if (lane + 32 * i == mi) v[i] = -1.0f;
         }
         if (lane == j) {
-            sel_mine = bp;
-            id_mine = bi;
+            sel_mine = __uint_as_float(mk - 1u);
+            id_mine = mi;
         }
     }
     float s = 0.0f;
