@@ -246,8 +246,11 @@ def run_ours(args, rank, world, local_rank):
     total_phase = sum(v[0] for v in prof.values())
     shares = {k: round(v[0] / total_phase, 4) for k, v in prof.items()}
     d_mean = sum(distinct) / L
-    gate_up_bytes = d_mean * GATE_UP_BYTES + T * (H + H // 256 * 4 + H // 16 * 2) + T * K_USED * I * 4
-    down_bytes = d_mean * DOWN_BYTES + T * K_USED * I * 4 + T * K_USED * H * 4
+    # weights of the distinct experts + the Q8_K activation rows read (qs, d, and the split
+    # sub-block sums: 2 u32 words x 2 planes per super-block for Q4_K, 4 x 2 for Q6_K) + the f32
+    # outputs written
+    gate_up_bytes = d_mean * GATE_UP_BYTES + T * (H + (H // 256) * (4 + 16)) + T * K_USED * I * 4
+    down_bytes = d_mean * DOWN_BYTES + T * K_USED * (I + (I // 256) * (4 + 32)) + T * K_USED * H * 4
     peaks = load_peaks()
     dom = max(("gate_up", "down"), key=lambda k: prof.get(k, (0, 1))[0])
     dom_bytes = gate_up_bytes if dom == "gate_up" else down_bytes
@@ -268,7 +271,7 @@ def run_ours(args, rank, world, local_rank):
         "metric": "moe_layer_tokens_per_s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8 (Q8_K activations x Q4_K/Q6_K weights, dp4a, f32 scales)", "data": "synthetic",
+        "dtype": "int8 x u4/u6 integer MMA (Q8_K activations, Q4_K/Q6_K weights), f32 scales", "data": "synthetic",
         "config": workload(args, world), "roofline": roofline, "layer_roofline": layer_roof,
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
                 "d2h_bytes_per_step": T * H * 4, "ms_per_step": round(e2e_ms / args.steps, 4),
