@@ -109,6 +109,21 @@ TMOE_API int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const v
                     size_t nb2, int64_t K, int64_t N, int64_t n_w, const float *b, int64_t b1,
                     const int32_t *ids, int64_t n_used, int64_t T, float *out);
 
+/* tmoe_mul_mat_id without any device allocation (no counterpart in the reference: an addition
+ * for callers that cannot allocate during the call -- code that runs under a fixed device-memory
+ * budget, or where a cudaMalloc would synchronise the device in the middle of a step).  The same
+ * arguments, arithmetic and results as tmoe_mul_mat_id; its scratch (the Q8_K rows of b, the
+ * dispatch buffers) lives in a 2 MiB module-global device array instead of the handle's growable
+ * buffer.  Limit: about T * b1 * K bytes of Q8_K rows plus T * n_used * 4 bytes of pair indices
+ * must fit in 2 MiB (e.g. T * b1 <= 128 rows at K = 8192 with n_used = 8); larger calls return
+ * TMOE_E_INVALID.  The first call on a device looks the array up (cudaGetSymbolAddress), so make
+ * it before any stream capture.  The array is shared by every handle of the process on that
+ * device: overlapping calls (on different streams, or from different threads) race on it and
+ * must be ordered by the caller. */
+TMOE_API int tmoe_mul_mat_id_noalloc(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1,
+                                     size_t nb2, int64_t K, int64_t N, int64_t n_w, const float *b, int64_t b1,
+                                     const int32_t *ids, int64_t n_used, int64_t T, float *out);
+
 /* router(): optional xn = rms_norm(x, eps) * norm_w (use_norm != 0; norm_w may be NULL),
  * logits = router_w . xn (router_w f32 [E][H], the ggml [H, E] gate_inp) or the given
  * `logits` f32 [T][E] when router_w is NULL; probs = softmax; ids = top-k (descending, ties to

@@ -47,6 +47,8 @@ SIGNATURES = {
     "tmoe_check": ([P, P], C.c_int),
     "tmoe_mul_mat_id": ([P, P, I32, P, C.c_size_t, C.c_size_t, I64, I64, I64, P, I64, P, I64, I64, P],
                         C.c_int),
+    "tmoe_mul_mat_id_noalloc": ([P, P, I32, P, C.c_size_t, C.c_size_t, I64, I64, I64, P, I64, P, I64, I64, P],
+                                C.c_int),
     "tmoe_route": ([P, P, P, I64, I32, P, P, P, P, P, P, P], C.c_int),
     "tmoe_experts": ([P, P, P, I64, P, P, C.POINTER(ExpertTensors), P], C.c_int),
     "tmoe_layer": ([P, P, P, I64, I32, P, P, P, P, C.POINTER(ExpertTensors), P, P, P], C.c_int),

@@ -560,6 +560,104 @@ int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, s
     return TMOE_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Scratch of tmoe_mul_mat_id_noalloc: module-global device memory, so that the call allocates
+// nothing.  One array per device (per CUDA context), shared by every handle of the process.
+constexpr size_t kNoAllocScratchBytes = 2u << 20;  // 2 MiB
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device (cached per device; the first call on
+// a device looks the symbol up, which may load the module there).
+cudaError_t noalloc_scratch(int dev, char **out) {
+    static char *addr[64] = {};
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!addr[dev]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        addr[dev] = (char *)p;
+    }
+    *out = addr[dev];
+    return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tmoe_mul_mat_id_noalloc(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1, size_t nb2,
+                            int64_t K, int64_t N, int64_t n_w, const float *b, int64_t b1, const int32_t *ids,
+                            int64_t n_used, int64_t T, float *out) {
+    if (!h) return TMOE_E_INVALID;
+    if (!is_kquant(type)) return fail(h, TMOE_E_UNSUPPORTED, "mul_mat_id type %d (need Q4_K or Q6_K)", type);
+    if (K <= 0 || K % 256 || N <= 0 || n_w <= 0 || n_w > kMaxSlots || n_used <= 0 || T < 0 ||
+        (b1 != 1 && b1 != n_used))
+        return fail(h, TMOE_E_INVALID, "bad mul_mat_id shape");
+    if (!W || !b || !ids || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    if (!aligned16(b)) return fail(h, TMOE_E_INVALID, "b must be 16-byte aligned");
+    const int wt = wt_of(type);
+    if (nb1 != row_size(type, K)) return fail(h, TMOE_E_UNSUPPORTED, "rows must be contiguous (nb1 == row size)");
+    if (((uintptr_t)W & 15u) || (nb2 & 15u)) return fail(h, TMOE_E_INVALID, "W and nb2 must be 16-byte aligned");
+    if (!tmoe::gemv_rows_per_item(wt, (int)K, (int)N))
+        return fail(h, TMOE_E_UNSUPPORTED, "N=%lld rows per expert fit no GEMV row tile (multiples of 16)",
+                    (long long)N);
+    const int64_t P = T * n_used, rows = T * b1;
+    // the same layout as tmoe_mul_mat_id's scratch, placed in the static array
+    size_t need = 0;
+    auto lay = [&](size_t bytes) {
+        size_t o = need;
+        need = align_up(need + bytes, 256);
+        return o;
+    };
+    const size_t nbw = (size_t)tmoe::q8_nbw(wt);
+    size_t o_q = lay((size_t)rows * K), o_d = lay((size_t)rows * (K / 256) * 4);
+    size_t o_bl = lay((size_t)rows * (K / 256) * nbw * 4), o_bh = lay((size_t)rows * (K / 256) * nbw * 4);
+    size_t o_cnt = lay(kMaxSlots * 4), o_off = lay((kMaxSlots + 1) * 4), o_act = lay(kMaxSlots * 16), o_na = lay(4);
+    size_t o_perm = lay((size_t)P * 4 + 16), o_work = lay(kCounters * 4);
+    if (need > kNoAllocScratchBytes)
+        return fail(h, TMOE_E_INVALID,
+                    "mul_mat_id_noalloc needs %zu bytes of scratch for T=%lld, b1=%lld, K=%lld, n_used=%lld; the static "
+                    "scratch holds %zu (use tmoe_mul_mat_id)",
+                    need, (long long)T, (long long)b1, (long long)K, (long long)n_used, kNoAllocScratchBytes);
+    if (T == 0) return TMOE_OK;
+    DeviceGuard dg(h->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    char *base = nullptr;
+    cudaError_t e = noalloc_scratch(h->cfg.device, &base);
+    if (e != cudaSuccess) return cuda_fail(h, e, "cudaGetSymbolAddress(noalloc scratch)");
+    int8_t *q = (int8_t *)(base + o_q);
+    float *d = (float *)(base + o_d);
+    uint32_t *bl = (uint32_t *)(base + o_bl), *bh = (uint32_t *)(base + o_bh);
+    int32_t *cnt = (int32_t *)(base + o_cnt), *offs = (int32_t *)(base + o_off), *na = (int32_t *)(base + o_na),
+            *perm = (int32_t *)(base + o_perm);
+    int4 *act = (int4 *)(base + o_act);
+    int *work = (int *)(base + o_work);
+    // nothing in the scratch needs to start at zero: the dispatch kernel writes counts, offsets,
+    // the active list and perm, and zeroes the GEMV work counters, before the GEMV reads them
+    if ((e = tmoe::launch_sort_pairs(ids, (int)P, (int)n_w, cnt, offs, perm, act, na, work, kCounters, h->err, st)) !=
+        cudaSuccess)
+        return cuda_fail(h, e, "sort_pairs");
+    if ((e = tmoe::launch_quantize_q8k(b, rows, (int)K, nullptr, tmoe::Q8Rows{q, d, bl, bh, wt}, st)) != cudaSuccess)
+        return cuda_fail(h, e, "quantize b");
+    if ((e = tmoe::launch_zero_invalid_rows(ids, P, (int)n_w, (int)N, out, st)) != cudaSuccess)
+        return cuda_fail(h, e, "zero rows");
+    tmoe::GemvArgs g{};
+    g.w0 = (const uint8_t *)W;
+    g.nb1_0 = nb1, g.nb2_0 = nb2;
+    g.K = (int)K, g.N = (int)N;
+    g.xq = q, g.xd = d, g.xbl = bl, g.xbh = bh, g.x_div = b1 == 1 ? (int)n_used : 1;
+    const int max_active = (int)(P < n_w ? P : n_w);
+    g.perm = perm, g.active = act, g.n_active = na;
+    g.n_slots = (int)n_w, g.max_active = max_active, g.n_pairs = (int)P, g.work = work;
+    g.out = out, g.err = h->err;
+    if ((e = tmoe::launch_gemv(wt, false, g, max_active, h->sm_count, st)) != cudaSuccess)
+        return cuda_fail(h, e, "mul_mat_id gemv");
+    return TMOE_OK;
+}
+
 int tmoe_dispatch(tmoe_handle *h, void *stream, const int32_t *ids, int64_t T, int32_t n_slots,
                   int32_t *counts, int32_t *offsets, int32_t *perm) {
     if (!h) return TMOE_E_INVALID;
