@@ -126,15 +126,20 @@ class Clocks:
 
 
 # ---------------------------------------------------------------------------------------- ours
-def make_layers(torch, moe, n_layers, seed, device):
+def make_layers(torch, moe, n_layers, seed, device, world=1, rank=0):
+    """n_layers C2 layers.  With world > 1 (expert parallelism) every rank draws the same router
+    (the routing is replicated) and holds only its contiguous share of each layer's experts."""
     g = torch.Generator(device=device)
     g.manual_seed(seed)
+    ge = torch.Generator(device=device)
+    ge.manual_seed(seed + 1000003 * (rank + 1))
+    per = E // world
     layers = []
     for _ in range(n_layers):
         rw = torch.randn((E, H), generator=g, device=device) * 0.02
-        gate = moe.quantize(Q4K, torch.randn((E, I, H), generator=g, device=device) * 0.02)
-        up = moe.quantize(Q4K, torch.randn((E, I, H), generator=g, device=device) * 0.02)
-        down = moe.quantize(Q6K, torch.randn((E, H, I), generator=g, device=device) * 0.02)
+        gate = moe.quantize(Q4K, torch.randn((per, I, H), generator=ge, device=device) * 0.02)
+        up = moe.quantize(Q4K, torch.randn((per, I, H), generator=ge, device=device) * 0.02)
+        down = moe.quantize(Q6K, torch.randn((per, H, I), generator=ge, device=device) * 0.02)
         layers.append((rw, moe.ExpertWeights(gate, up, down)))
     torch.cuda.synchronize()
     return layers
@@ -150,10 +155,13 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     T, L = args.tokens, args.layers
-    layers = make_layers(torch, moe, L, args.seed + 7919 * rank, dev)
-    log(f"{L} layers generated")
+    ep = world > 1
+    # N = 1: the layer on one GPU.  N > 1: the reference's EP mode, experts split contiguously over
+    # the ranks, the same tokens on every rank, partial outputs summed with NCCL (strong scaling)
+    layers = make_layers(torch, moe, L, args.seed, dev, world, rank)
+    log(f"{L} layers generated ({E // world} experts each on this rank)")
     gen = torch.Generator(device=dev)
-    gen.manual_seed(args.seed + 1 + rank)
+    gen.manual_seed(args.seed + 1)
     x_dev = torch.randn((T, H), generator=gen, device=dev)
     x_host = x_dev.cpu().pin_memory()
     out_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
@@ -161,10 +169,23 @@ def run_ours(args, rank, world, local_rank):
     outs = [torch.empty((T, H), device=dev) for _ in range(L)]
     ids = [torch.empty((T, K_USED), dtype=torch.int32, device=dev) for _ in range(L)]
     ws = [torch.empty((T, K_USED), dtype=torch.float32, device=dev) for _ in range(L)]
+    comm, table = None, None
+    if ep:
+        uid = [moe.EPComm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = moe.EPComm(uid[0], world, rank, device=local_rank, timeout_s=120.0)
+        table = torch.tensor(moe.ep_id_map(E, world, rank), dtype=torch.int32, device=dev)
+
+    def call(li, x):
+        rw, wts = layers[li]
+        if ep:
+            moe.ep_moe_ffn(layer, comm, x, wts, table, router_w=rw, out=outs[li], ids_out=ids[li], w_out=ws[li])
+        else:
+            layer.moe_ffn(x, wts, router_w=rw, out=outs[li], ids_out=ids[li], w_out=ws[li])
 
     def one_step(x):
-        for li, (rw, wts) in enumerate(layers):
-            layer.moe_ffn(x, wts, router_w=rw, out=outs[li], ids_out=ids[li], w_out=ws[li])
+        for li in range(L):
+            call(li, x)
 
     def barrier():
         if world > 1:
@@ -214,7 +235,7 @@ def run_ours(args, rank, world, local_rank):
     clocks = clk.summary()
     layer.check()
     log(f"graph timed: {ms / args.steps:.3f} ms/step")
-    units = world * args.steps * L * T
+    units = (1 if ep else world) * args.steps * L * T  # EP: the ranks process the same tokens jointly
     value = units / (ms / 1e3)
 
     def e2e_step():
@@ -228,6 +249,11 @@ def run_ours(args, rank, world, local_rank):
 
     # distinct experts per layer (the D of the roofline bytes)
     distinct = [int(torch.unique(ids[li]).numel()) for li in range(L)]
+    if ep:  # this rank's GEMVs read only the experts it holds
+        lo, hi = rank * (E // world), (rank + 1) * (E // world)
+        local = [int(((u >= lo) & (u < hi)).sum()) for u in (torch.unique(ids[li]) for li in range(L))]
+    else:
+        local = distinct
 
     # per-kernel device time of the same workload (events around each kernel)
     # (a 1 ms device sleep first lets the host queue the 4 layer calls, so no event waits on it)
@@ -236,8 +262,7 @@ def run_ours(args, rank, world, local_rank):
         for l0 in range(0, L, 4):
             torch.cuda._sleep(2_000_000)
             for li in range(l0, min(L, l0 + 4)):
-                rw, wts = layers[li]
-                layer.moe_ffn(x_dev, wts, router_w=rw, out=outs[li], ids_out=ids[li], w_out=ws[li])
+                call(li, x_dev)
             prof = layer.profile_collect()
     layer.profile(False)
     log("per-kernel profile done")
@@ -246,11 +271,12 @@ def run_ours(args, rank, world, local_rank):
     total_phase = sum(v[0] for v in prof.values())
     shares = {k: round(v[0] / total_phase, 4) for k, v in prof.items()}
     d_mean = sum(distinct) / L
+    d_local = sum(local) / L
     # weights of the distinct experts + the Q8_K activation rows read (qs, d, and the split
     # sub-block sums: 2 u32 words x 2 planes per super-block for Q4_K, 4 x 2 for Q6_K) + the f32
     # outputs written
-    gate_up_bytes = d_mean * GATE_UP_BYTES + T * (H + (H // 256) * (4 + 16)) + T * K_USED * I * 4
-    down_bytes = d_mean * DOWN_BYTES + T * K_USED * (I + (I // 256) * (4 + 32)) + T * K_USED * H * 4
+    gate_up_bytes = d_local * GATE_UP_BYTES + T * (H + (H // 256) * (4 + 16)) + T * K_USED * I * 4
+    down_bytes = d_local * DOWN_BYTES + T * K_USED * (I + (I // 256) * (4 + 32)) + T * K_USED * H * 4
     peaks = load_peaks()
     dom = max(("gate_up", "down"), key=lambda k: prof.get(k, (0, 1))[0])
     dom_bytes = gate_up_bytes if dom == "gate_up" else down_bytes
@@ -259,7 +285,7 @@ def run_ours(args, rank, world, local_rank):
     layer_ms = ms / (args.steps * L)
     roofline = {"bound": "hbm", "kernel": f"gemv_kernel ({dom})", "achieved": round(achieved, 1),
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                "peak_source": peaks["source"], "traffic": traffic_from_profiles(dom),
+                "peak_source": peaks["source"], "traffic": None if ep else traffic_from_profiles(dom),
                 "algorithmic_bytes_per_launch": int(dom_bytes), "avg_launch_us": round(phase_ms[dom] * 1e3, 2)}
     layer_roof = {"bytes_per_layer_call": int(layer_bytes), "distinct_experts_mean": round(d_mean, 2),
                   "us_per_layer_call": round(layer_ms * 1e3, 2),
@@ -278,9 +304,15 @@ def run_ours(args, rank, world, local_rank):
                 "path": "tmoe_layer C-ABI calls (ctypes) x 48 + pinned H2D/D2H"},
         "gpu_launches": int(launches_per_call * L * args.steps), "clocks": clocks,
     }
-    if args.sweep and rank == 0:
+    if ep:
+        result["config"]["parallelism"] = f"ep{world} (experts split contiguously, tokens replicated, NCCL all-reduce)"
+        result["scaling"] = "strong"
+    if args.sweep and rank == 0 and not ep:
         result["sweep"] = sweep_tokens(torch, tb, layers, dev)
     del graph
+    torch.cuda.synchronize()
+    if comm is not None:
+        comm.close()
     return result
 
 

@@ -145,6 +145,33 @@ TMOE_API int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T,
                const int32_t *id_map, const tmoe_expert_tensors *wts, float *out,
                int32_t *ids_out, float *w_out);
 
+/* --- expert parallelism (qwen3moe_shard.rs:1038-1056) ----------------------------------------
+ * A communicator over the ranks of an expert-parallel group, one rank per GPU (NCCL).  Rank 0
+ * makes an id (tmoe_comm_unique_id), the caller hands its bytes to every rank (e.g. through
+ * torch.distributed or a store), and every rank calls tmoe_comm_init with it.  Host waits on the
+ * communicator give up after timeout_s seconds (TMOE_E_COMM; the communicator is then aborted).
+ * Errors of these calls: tmoe_comm_last_error() of the calling thread. */
+typedef struct tmoe_comm tmoe_comm;
+#define TMOE_COMM_ID_BYTES 128
+TMOE_API int tmoe_comm_unique_id(void *id_out);
+TMOE_API int tmoe_comm_init(const void *id, int32_t nranks, int32_t rank, int32_t device, double timeout_s,
+                            tmoe_comm **out);
+/* Ends the communicator at once (a host watchdog's call when a peer died); it is then unusable. */
+TMOE_API int tmoe_comm_abort(tmoe_comm *c);
+TMOE_API void tmoe_comm_destroy(tmoe_comm *c);
+TMOE_API const char *tmoe_comm_last_error(void);
+
+/* The reference's EP layer: every rank passes the same tokens x, its id_map (global expert id ->
+ * slot of its own `wts`, or -1 for experts held elsewhere) and its expert tensors; each rank
+ * computes tmoe_layer over its experts and the partial outputs are summed across the ranks
+ * (the all-reduce of qwen3moe_shard.rs:1056), so that every rank ends with the full `out`.
+ * Every rank must make the same calls in the same order; a rank whose local layer fails still
+ * takes part in the sum and then returns the error. */
+TMOE_API int tmoe_ep_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float *x, int64_t T,
+                           int32_t use_norm, const float *norm_w, const float *router_w, const float *logits,
+                           const int32_t *id_map, const tmoe_expert_tensors *wts, float *out, int32_t *ids_out,
+                           float *w_out);
+
 /* ids' = table[ids] for ids in [0, n_table), else -1 (the EP expert_map lookup). */
 TMOE_API int tmoe_map_ids(tmoe_handle *h, void *stream, const int32_t *ids, int64_t n,
                  const int32_t *table, int64_t n_table, int32_t *out);

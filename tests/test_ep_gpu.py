@@ -1,0 +1,78 @@
+"""The reference's EP mode on GPUs: two ranks (processes, one GPU each) hold half of the experts
+each, run tmoe_ep_layer (local experts + NCCL all-reduce), and must agree with the one-rank oracle
+layer: ids bit-exact, outputs within the strict bound.  Needs two GPUs (skipped otherwise)."""
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import oracle as O
+from tests.common import maxabs_over_rms, nrms, quantized_experts
+
+pytestmark = pytest.mark.gpu
+
+needs_two = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                               reason="needs two GPUs")
+
+
+def _case(H, I, E, T, seed):
+    rng = np.random.default_rng(seed)
+    gate = quantized_experts(rng, O.TYPE_Q4_K, E, I, H, exact=False)
+    up = quantized_experts(rng, O.TYPE_Q4_K, E, I, H, exact=False)
+    down = quantized_experts(rng, O.TYPE_Q6_K, E, H, I, exact=False)
+    rw = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    return gate, up, down, rw, x
+
+
+def _rank(rank, world, uid, shape, q):
+    import tetraeder_b200 as tb
+    from tetraeder_b200 import moe
+    H, I, E, k, T, seed = shape
+    torch.cuda.set_device(rank)
+    gate, up, down, rw, x = _case(H, I, E, T, seed)
+    per = E // world
+    sl = slice(rank * per, (rank + 1) * per)
+    cu = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    layer = tb.MoeLayer(H, I, E, k, gate_type=O.TYPE_Q4_K, up_type=O.TYPE_Q4_K, down_type=O.TYPE_Q6_K,
+                        max_tokens=T, device=rank)
+    comm = moe.EPComm(uid, world, rank, device=rank, timeout_s=120.0)
+    try:
+        table = torch.tensor(moe.ep_id_map(E, world, rank), dtype=torch.int32, device="cuda")
+        ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+        out = moe.ep_moe_ffn(layer, comm, cu(x), moe.ExpertWeights(cu(gate[sl]), cu(up[sl]), cu(down[sl])), table,
+                             router_w=cu(rw), ids_out=ids)
+        for _ in range(2):  # the same call again: counters and buffers are reused between calls
+            out = moe.ep_moe_ffn(layer, comm, cu(x), moe.ExpertWeights(cu(gate[sl]), cu(up[sl]), cu(down[sl])),
+                                 table, router_w=cu(rw), ids_out=ids, out=out)
+        torch.cuda.synchronize()
+        layer.check()
+        q.put((rank, out.cpu().numpy(), ids.cpu().numpy()))
+    finally:
+        comm.close()
+        layer.close()
+
+
+@needs_two
+@pytest.mark.parametrize("shape", [(512, 256, 16, 4, 32, 5), (2048, 768, 128, 8, 64, 6)])
+def test_ep_layer_two_ranks_equals_one(shape):
+    from tetraeder_b200 import moe
+    H, I, E, k, T, seed = shape
+    world = 2
+    uid = moe.EPComm.unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, shape, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    gate, up, down, rw, x = _case(H, I, E, T, seed)
+    want, want_ids, _ = O.layer(x, k, gate, up, down, H, I, E, router_w=rw, gate_type=O.TYPE_Q4_K,
+                                up_type=O.TYPE_Q4_K, down_type=O.TYPE_Q6_K)
+    for rank, out, ids in res:
+        assert np.array_equal(ids, want_ids), f"rank {rank}: routing differs"
+        n, m = nrms(out, want), maxabs_over_rms(out, want)
+        assert n <= 1e-3 and m <= 1e-2, f"rank {rank}: nrms={n:.2e} maxabs/rms={m:.2e}"

@@ -58,7 +58,14 @@ SIGNATURES = {
     "tmoe_dequantize": ([I32, P, I64, P, P], C.c_int),
     "tmoe_profile_enable": ([P, I32], C.c_int),
     "tmoe_profile_collect": ([P, P, P], C.c_int),
+    "tmoe_comm_unique_id": ([P], C.c_int),
+    "tmoe_comm_init": ([P, I32, I32, I32, C.c_double, C.POINTER(C.c_void_p)], C.c_int),
+    "tmoe_comm_abort": ([P], C.c_int),
+    "tmoe_comm_destroy": ([P], None),
+    "tmoe_comm_last_error": ([], C.c_char_p),
+    "tmoe_ep_layer": ([P, P, P, P, I64, I32, P, P, P, P, C.POINTER(ExpertTensors), P, P, P], C.c_int),
 }
+COMM_ID_BYTES = 128
 PHASES = ["rms_norm", "router_logits", "topk", "map_ids", "dispatch", "quant_x", "gate_up", "quant_act",
           "down", "combine"]
 
@@ -92,4 +99,11 @@ def load():
 def check(rc: int, handle=None):
     if rc != TMOE_OK:
         msg = load().tmoe_last_error(handle)
+        raise TmoeError(rc, msg.decode() if msg else "")
+
+
+def check_comm(rc: int):
+    """For the communicator calls, whose errors are kept per thread."""
+    if rc != TMOE_OK:
+        msg = load().tmoe_comm_last_error()
         raise TmoeError(rc, msg.decode() if msg else "")

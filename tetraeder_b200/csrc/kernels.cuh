@@ -8,7 +8,14 @@
 #define TMOE_WT_Q4K 0
 #define TMOE_WT_Q6K 1
 
+struct tmoe_comm;
+
 namespace tmoe {
+
+// ep.cu: in-place sum of n floats over the communicator's ranks (stream-ordered); TMOE_OK or
+// TMOE_E_COMM with a message.
+int ep_allreduce_sum(tmoe_comm *c, float *buf, size_t n, cudaStream_t st, char *msg, size_t msg_len);
+int ep_comm_device(const tmoe_comm *c);
 
 // Q8_K rows as the expert GEMV reads them: qs int8 [rows][K], d f32 [rows][K/256], and per
 // super-block the activation sums over the weight type's sub-blocks (32 elements for Q4_K, 16 for

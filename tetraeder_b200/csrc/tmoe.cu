@@ -476,6 +476,28 @@ int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
     return run_experts(h, st, xn, T, used, w, wts, out, dispatched, x_quantized);
 }
 
+int tmoe_ep_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float *x, int64_t T, int32_t use_norm,
+                  const float *norm_w, const float *router_w, const float *logits, const int32_t *id_map,
+                  const tmoe_expert_tensors *wts, float *out, int32_t *ids_out, float *w_out) {
+    if (!h) return TMOE_E_INVALID;
+    const tmoe_config &c = h->cfg;
+    if (!comm) return fail(h, TMOE_E_INVALID, "null communicator");
+    if (tmoe::ep_comm_device(comm) != c.device)
+        return fail(h, TMOE_E_INVALID, "communicator device %d != handle device %d", tmoe::ep_comm_device(comm),
+                    c.device);
+    // the arguments the sum needs; anything else that fails below still joins the sum
+    if (T < 0 || T > c.max_tokens) return fail(h, TMOE_E_INVALID, "T=%lld outside [0, max_tokens]", (long long)T);
+    if (!out) return fail(h, TMOE_E_INVALID, "null tensor");
+    if (T == 0) return TMOE_OK;
+    const int rc = tmoe_layer(h, stream, x, T, use_norm, norm_w, router_w, logits, id_map, wts, out, ids_out, w_out);
+    DeviceGuard dg(c.device);
+    char msg[256];
+    const int rc2 = tmoe::ep_allreduce_sum(comm, out, (size_t)T * c.n_embd, (cudaStream_t)stream, msg, sizeof msg);
+    if (rc) return rc;
+    if (rc2) return fail(h, rc2, "%s", msg);
+    return TMOE_OK;
+}
+
 int tmoe_map_ids(tmoe_handle *h, void *stream, const int32_t *ids, int64_t n, const int32_t *table,
                  int64_t n_table, int32_t *out) {
     if (!h) return TMOE_E_INVALID;

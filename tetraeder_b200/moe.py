@@ -195,4 +195,60 @@ class MoeLayer:
         return out
 
 
-__all__ = ["MoeLayer", "ExpertWeights", "TmoeError", "TYPE_Q4_K", "TYPE_Q6_K", "row_size", "quantize", "dequantize"]
+def ep_id_map(n_expert: int, n_ranks: int, rank: int) -> list[int]:
+    """The global -> local slot table of `rank` when the experts are split contiguously by id over
+    `n_ranks` ranks (qwen3moe_shard.rs:11-14, 617-626): rank r holds [r*E/g, (r+1)*E/g) as slots
+    0..E/g-1; the other experts map to -1."""
+    if n_ranks < 1 or not 0 <= rank < n_ranks or n_expert % n_ranks:
+        raise ValueError("n_expert must split evenly over the ranks")
+    per = n_expert // n_ranks
+    return [e - rank * per if rank * per <= e < (rank + 1) * per else -1 for e in range(n_expert)]
+
+
+class EPComm:
+    """A rank's communicator of an expert-parallel group (NCCL, one rank per GPU).  Rank 0 makes
+    the id with unique_id(); every rank passes the same bytes."""
+
+    def __init__(self, uid: bytes, n_ranks: int, rank: int, device: int | None = None, timeout_s: float = 60.0):
+        self.lib = _lib.load()
+        if len(uid) != _lib.COMM_ID_BYTES:
+            raise ValueError("communicator id must be 128 bytes")
+        dev = torch.cuda.current_device() if device is None else device
+        c = C.c_void_p()
+        buf = C.create_string_buffer(uid, _lib.COMM_ID_BYTES)
+        _lib.check_comm(self.lib.tmoe_comm_init(buf, n_ranks, rank, dev, timeout_s, C.byref(c)))
+        self.c, self.n_ranks, self.rank, self.device = c, n_ranks, rank, dev
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = C.create_string_buffer(_lib.COMM_ID_BYTES)
+        _lib.check_comm(_lib.load().tmoe_comm_unique_id(buf))
+        return buf.raw
+
+    def abort(self):
+        if getattr(self, "c", None):
+            self.lib.tmoe_comm_abort(self.c)
+
+    def close(self):
+        if getattr(self, "c", None):
+            self.lib.tmoe_comm_destroy(self.c)
+            self.c = None
+
+
+def ep_moe_ffn(layer: "MoeLayer", comm: EPComm, x: torch.Tensor, experts: ExpertWeights, id_map: torch.Tensor,
+               router_w: torch.Tensor | None = None, logits: torch.Tensor | None = None,
+               ffn_norm: torch.Tensor | None = None, use_norm: bool = False, out: torch.Tensor | None = None,
+               ids_out: torch.Tensor | None = None, w_out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """The reference's EP MoE layer on this rank: moe_ffn over this rank's experts (id_map: the
+    device int32 [E] table of ep_id_map) summed over the ranks of `comm`; every rank gets `out`."""
+    T = x.shape[0]
+    out = torch.empty((T, layer.cfg.n_embd), dtype=torch.float32, device=layer.device) if out is None else out
+    st = experts.c_struct()
+    _lib.check(layer.lib.tmoe_ep_layer(layer.h, _stream(stream), comm.c, _ptr(x), T, int(use_norm), _ptr(ffn_norm),
+                                       _ptr(router_w), _ptr(logits), _ptr(id_map), C.byref(st), _ptr(out),
+                                       _ptr(ids_out), _ptr(w_out)), layer.h)
+    return out
+
+
+__all__ = ["MoeLayer", "ExpertWeights", "TmoeError", "TYPE_Q4_K", "TYPE_Q6_K", "row_size", "quantize", "dequantize",
+           "EPComm", "ep_moe_ffn", "ep_id_map"]
