@@ -1,6 +1,7 @@
 // Launchers of the MoE layer kernels (host side of each .cu file).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -107,6 +108,17 @@ struct GemvArgs {
     int d_slots;       // slots per warp
     uint64_t tiles_m, xdiv_m;  // ceil(2^40 / tiles), ceil(2^40 / x_div): exact division of n < 2^24
 };
+// prefill.cu: the grouped tcgen05 GEMMs of the large-batch regime (see prefill.cu)
+bool prefill_fits(int H, int I);
+cudaError_t launch_prep_rows(const float *src, const int32_t *perm, int n_rows, int x_div, int K, __half *dst,
+                             cudaStream_t st);
+cudaError_t launch_dequant_f16(int wt, const uint8_t *w, size_t nb2, int N, int K, const int4 *active,
+                               const int32_t *n_active, int max_active, __half *dst, cudaStream_t st);
+cudaError_t launch_prefill_gemm(bool swiglu, const __half *A, int n_rows, int K, const __half *b0, const __half *b1,
+                                int n_slots, int N, const int4 *active, const int32_t *n_active, int max_active,
+                                int *tile_start, const int32_t *perm, float *out, int *err, int sm_count,
+                                cudaStream_t st);
+
 // Rows per work item of the GEMV for K columns and N rows per expert; 0 if N does not fit.
 int gemv_rows_per_item(int wt, int K, int N);
 cudaError_t launch_gemv(int wt, bool gateup, const GemvArgs &a, int max_items, int sm_count, cudaStream_t st);

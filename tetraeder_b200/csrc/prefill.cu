@@ -1,0 +1,502 @@
+// Expert products for the prefill / large-batch regime (many tokens per expert): grouped GEMMs on
+// the 5th-generation tensor cores.  tcgen05.mma (kind::f16, fp16 operands, f32 accumulators in
+// TMEM) issued by one thread, operands staged in shared memory by TMA with 128-byte swizzle, a
+// persistent CTA per SM walking the tiles of all active experts.
+//
+// Numerics.  The reference CPU path quantises the activations to Q8_K before the expert dots
+// (ggml's vec_dot_type for the K-quants); here the activations go through the same Q8_K round
+// trip and are then held exactly enough in fp16 (d * q, q an int8), the weights are dequantised
+// to fp16 (d * scale * q - dmin * min), and the products are summed in f32.  The result differs
+// from the reference's integer block sums by fp16 rounding of the dequantised values only.
+//
+// Dataflow of a layer (rows in the dispatch's expert-sorted pair order r, perm[r] = pair):
+//   prep_rows_kernel   x rows -> Q8_K round trip -> fp16 A1[r][H]
+//   dequant_f16_kernel expert weights of the active experts -> fp16 [expert][row][K]
+//   gemm (SWIGLU)      act[r][I] = silu(A1 . gate^T) * (A1 . up^T)
+//   prep_rows_kernel   act rows -> Q8_K round trip -> fp16 A2[r][I]
+//   gemm (SCATTER)     dout[perm[r]][H] = A2 . down^T
+// GEMM tile: 128 rows of one expert x 256 output columns (SWIGLU: 128 gate + the same 128 up
+// features), K in steps of 64 (one 128-byte swizzle atom), 4 MMAs of K = 16 per step.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "q8k.cuh"
+
+namespace tmoe {
+
+constexpr int PF_BM = 128;
+constexpr int PF_BN = 256;
+constexpr int PF_BK = 64;
+constexpr int PF_STAGES = 4;
+constexpr int PF_THREADS = 192;  // warp 0: TMA, warp 1: MMA, warps 2-5: epilogue
+constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;
+constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;
+constexpr int PF_STAGE_BYTES = PF_A_BYTES + PF_B_BYTES;
+constexpr int PF_SMEM = PF_STAGES * PF_STAGE_BYTES + 1024 /* barriers */ + 1024 /* alignment */;
+constexpr uint32_t PF_TMEM_COLS = 512;  // two accumulators of 256 f32 columns
+
+// ------------------------------------------------------------------ tcgen05 / TMA helpers
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrives on `bar` once every MMA this thread issued before has completed.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *m, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile in the 128-byte swizzle layout that
+// TMA writes for a box of 64 fp16 columns: rows of 128 bytes, 8-row groups 1024 bytes apart
+// (stride byte offset), start address advanced by 32 bytes per K = 16 step inside the atom.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = (uint64_t)((saddr & 0x3ffffu) >> 4);  // start address >> 4, bits [0, 14)
+    d |= (uint64_t)1 << 16;                             // leading byte offset (unused for this layout)
+    d |= (uint64_t)(1024 >> 4) << 32;                   // stride byte offset >> 4, bits [32, 46)
+    d |= (uint64_t)1 << 46;                             // descriptor version of sm_100
+    d |= (uint64_t)2 << 61;                             // layout: 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor of kind::f16: fp16 A and B (K-major), f32 D, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ float silu_mul_pf(float g, float u) { return (g / (1.0f + expf(-g))) * u; }
+
+// ------------------------------------------------------------------ preparation kernels
+// A rows of the GEMM: row r of `rows` (expert-sorted pairs; src row = perm[r] / x_div) through the
+// Q8_K round trip, as fp16.  One warp per (row, 256-block).
+__global__ void prep_rows_kernel(const float *__restrict__ src, const int32_t *__restrict__ perm, int n_rows,
+                                 int x_div, int K, __half *__restrict__ dst) {
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nb = K / TMOE_QK;
+    const int64_t r = gw / nb;
+    const int b = (int)(gw % nb);
+    if (r >= n_rows) return;
+    int p = perm ? perm[r] : (int)r;
+    if (p < 0) p = 0;
+    const float *xr = src + (int64_t)(p / x_div) * K + b * TMOE_QK + 8 * lane;
+    const float4 a0 = *reinterpret_cast<const float4 *>(xr), a1 = *reinterpret_cast<const float4 *>(xr + 4);
+    const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    uint2 q;
+    float d;
+    int s16;
+    q8k_block_warp(v, q, d, s16);
+    __align__(16) __half h[8];
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+        const int qi = (int)(int8_t)(((c < 4 ? q.x : q.y) >> (8 * (c & 3))) & 0xff);
+        h[c] = __float2half_rn(__fmul_rn(d, (float)qi));
+    }
+    *reinterpret_cast<uint4 *>(dst + r * K + b * TMOE_QK + 8 * lane) = *reinterpret_cast<const uint4 *>(h);
+}
+
+// fp16 copies of the active experts' rows: dst[e][row][K] for the experts of `active` (others are
+// left alone).  One thread per 32-element chunk.
+__global__ void dequant_f16_kernel(int wt, const uint8_t *__restrict__ w, size_t nb2, int N, int K,
+                                   const int4 *__restrict__ active, const int32_t *__restrict__ n_active,
+                                   int max_active, __half *__restrict__ dst) {
+    const int na = min(n_active[0], max_active);
+    const int nb = K / TMOE_QK;
+    const int64_t per_expert = (int64_t)N * nb * 8;
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= per_expert * na) return;
+    const int ai = (int)(g / per_expert);
+    const int64_t l = g % per_expert;
+    const int e = active[ai].x;
+    const int row = (int)(l / (nb * 8));
+    const int b = (int)(l / 8 % nb), c = (int)(l % 8);
+    __half *o = dst + ((int64_t)e * N + row) * K + b * TMOE_QK + 32 * c;
+    const size_t row_bytes = (size_t)nb * (wt == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES);
+    const uint8_t *rw = w + (size_t)e * nb2 + (size_t)row * row_bytes;
+    __align__(16) __half h[32];
+    if (wt == TMOE_WT_Q4K) {
+        const uint8_t *blk = rw + (size_t)b * TMOE_Q4K_BYTES;
+        const float d = h2f((uint16_t)(blk[0] | (blk[1] << 8))), dmin = h2f((uint16_t)(blk[2] | (blk[3] << 8)));
+        const uint8_t *sc = blk + 4;
+        int scale, mn;
+        if (c < 4) {
+            scale = sc[c] & 63;
+            mn = sc[c + 4] & 63;
+        } else {
+            scale = (sc[c + 4] & 0x0f) | ((sc[c - 4] >> 6) << 4);
+            mn = (sc[c + 4] >> 4) | ((sc[c] >> 6) << 4);
+        }
+        const float d1 = __fmul_rn(d, (float)scale), m1 = __fmul_rn(dmin, (float)mn);
+        const uint8_t *qs = blk + 16 + 32 * (c / 2);
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const int q = (c & 1) ? (qs[i] >> 4) : (qs[i] & 0x0f);
+            h[i] = __float2half_rn(__fsub_rn(__fmul_rn(d1, (float)q), m1));
+        }
+    } else {
+        const uint8_t *blk = rw + (size_t)b * TMOE_Q6K_BYTES;
+        const uint8_t *ql = blk, *qh = blk + 128;
+        const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192);
+        const float d = h2f((uint16_t)(blk[208] | (blk[209] << 8)));
+#pragma unroll 4
+        for (int i = 0; i < 32; i++) {
+            const int k = 32 * c + i, hh = k / 128, rr = k % 128;
+            const int lo = rr < 64 ? (ql[64 * hh + rr] & 0x0f) : (ql[64 * hh + rr - 64] >> 4);
+            const int hi = (qh[32 * hh + (rr % 32)] >> (2 * (rr / 32))) & 3;
+            h[i] = __float2half_rn(__fmul_rn(__fmul_rn(d, (float)sc[k / 16]), (float)((lo | (hi << 4)) - 32)));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) reinterpret_cast<uint4 *>(o)[i] = reinterpret_cast<const uint4 *>(h)[i];
+}
+
+// tile_start[a] = sum over the active experts before a of ceil(rows / 128) * n_tiles_n;
+// tile_start[n_active] = all tiles.  One CTA.
+__global__ void tiles_kernel(const int4 *__restrict__ active, const int32_t *__restrict__ n_active, int max_active,
+                             int n_tiles_n, int *__restrict__ tile_start) {
+    __shared__ int sums[1024];
+    const int na = min(n_active[0], max_active);
+    int run = 0;
+    for (int base = 0; base < na; base += blockDim.x) {
+        const int a = base + threadIdx.x;
+        const int m = a < na ? ((active[a].z - active[a].y + PF_BM - 1) / PF_BM) * n_tiles_n : 0;
+        sums[threadIdx.x] = m;
+        __syncthreads();
+        for (int off = 1; off < (int)blockDim.x; off <<= 1) {  // inclusive scan (Hillis-Steele)
+            const int v = threadIdx.x >= (unsigned)off ? sums[threadIdx.x - off] : 0;
+            __syncthreads();
+            sums[threadIdx.x] += v;
+            __syncthreads();
+        }
+        if (a < na) tile_start[a] = run + sums[threadIdx.x] - m;
+        run += sums[blockDim.x - 1];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) tile_start[na] = run;
+}
+
+// ------------------------------------------------------------------ the grouped GEMM
+struct PfMaps {
+    CUtensorMap a;   // A rows: fp16 [rows][K], box 64 x 128
+    CUtensorMap b0;  // gate (SWIGLU, box 64 x 128) or down (SCATTER, box 64 x 256): fp16 [E * N][K]
+    CUtensorMap b1;  // up (SWIGLU)
+};
+
+struct PfArgs {
+    int K;          // reduction length (multiple of 64)
+    int N;          // rows of one expert's matrix (I for gate/up, H for down)
+    int n_tiles_n;  // output column tiles per expert
+    const int4 *active;
+    const int32_t *n_active;
+    int max_active;
+    const int *tile_start;
+    const int32_t *perm;
+    int n_rows;     // rows of A (pairs)
+    float *out;     // SWIGLU: act [rows][N]; SCATTER: dout [pairs][N]
+    int *err;
+};
+
+enum { PF_SWIGLU = 0, PF_SCATTER = 1 };
+
+// Which expert (active index), row tile and column tile a tile is.
+__device__ __forceinline__ void pf_decode(const PfArgs &a, int na, int tile, int &ai, int &m, int &n) {
+    int lo = 0, hi = na - 1;  // the last active index with tile_start <= tile
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (__ldg(a.tile_start + mid) <= tile) lo = mid;
+        else hi = mid - 1;
+    }
+    ai = lo;
+    const int4 info = __ldg(a.active + ai);
+    const int m_tiles = (info.z - info.y + PF_BM - 1) / PF_BM;
+    const int local = tile - __ldg(a.tile_start + ai);
+    n = local / m_tiles;  // consecutive tiles share a weight tile
+    m = local % m_tiles;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(const __grid_constant__ PfMaps maps, const PfArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *stages = smem;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + PF_STAGES * PF_STAGE_BYTES);
+    uint64_t *empty = full + PF_STAGES;
+    uint64_t *tfull = empty + PF_STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PF_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, PF_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    int na = a.n_active[0];
+    if (na > a.max_active || na < 0) na = na < 0 ? 0 : a.max_active;
+    const int n_tiles = na > 0 ? __ldg(a.tile_start + na) : 0;
+    const int kb_n = a.K / PF_BK;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            int it = 0;
+            for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x) {
+                int ai, m, n;
+                pf_decode(a, na, tile, ai, m, n);
+                const int4 info = __ldg(a.active + ai);
+                const int row0 = info.y + m * PF_BM;
+                for (int kb = 0; kb < kb_n; kb++, it++) {
+                    const int s = it % PF_STAGES;
+                    if (it >= PF_STAGES && !mbar_wait_bounded(&empty[s], ((it / PF_STAGES) - 1) & 1)) {
+                        latch_error(a.err, TMOE_DEV_ERR_TIMEOUT);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    uint8_t *sa = stages + (size_t)s * PF_STAGE_BYTES, *sb = sa + PF_A_BYTES;
+                    mbar_arrive_expect_tx(&full[s], (uint32_t)PF_STAGE_BYTES);
+                    tma_load_2d(sa, &maps.a, kb * PF_BK, row0, &full[s]);
+                    if (EPI == PF_SWIGLU) {
+                        const int brow = info.x * a.N + n * (PF_BN / 2);
+                        tma_load_2d(sb, &maps.b0, kb * PF_BK, brow, &full[s]);
+                        tma_load_2d(sb + PF_B_BYTES / 2, &maps.b1, kb * PF_BK, brow, &full[s]);
+                    } else {
+                        tma_load_2d(sb, &maps.b0, kb * PF_BK, info.x * a.N + n * PF_BN, &full[s]);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = idesc_f16(PF_BM, PF_BN);
+            int it = 0, tcount = 0;
+            for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x, tcount++) {
+                const int buf = tcount & 1;
+                if (tcount >= 2 && !mbar_wait_bounded(&tempty[buf], ((tcount >> 1) - 1) & 1)) {
+                    latch_error(a.err, TMOE_DEV_ERR_TIMEOUT);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * PF_BN);
+                bool ok = true;
+                for (int kb = 0; kb < kb_n; kb++, it++) {
+                    const int s = it % PF_STAGES;
+                    if (!mbar_wait_bounded(&full[s], (it / PF_STAGES) & 1)) {
+                        latch_error(a.err, TMOE_DEV_ERR_TIMEOUT);
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(stages + (size_t)s * PF_STAGE_BYTES), sb = sa + PF_A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < PF_BK / 16; k++)
+                        umma_f16(d, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), idesc, (kb | k) != 0);
+                    umma_commit(&empty[s]);  // the stage is free once these MMAs are done
+                }
+                if (!ok) break;
+                umma_commit(&tfull[buf]);  // the accumulator is complete
+            }
+        }
+    } else {  // epilogue: warps 2-5, TMEM lane quarter warp % 4
+        const int q = warp & 3;
+        int tcount = 0;
+        for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x, tcount++) {
+            const int buf = tcount & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(&tfull[buf], (tcount >> 1) & 1))) {
+                if (lane == 0) latch_error(a.err, TMOE_DEV_ERR_TIMEOUT);
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            int ai, m, n;
+            pf_decode(a, na, tile, ai, m, n);
+            const int4 info = __ldg(a.active + ai);
+            const int r = info.y + m * PF_BM + q * 32 + lane;
+            const bool valid = r < info.z && r < a.n_rows;
+            const uint32_t taddr = tmem_base + (uint32_t)(buf * PF_BN) + ((uint32_t)(q * 32) << 16);
+            if (EPI == PF_SWIGLU) {
+                float *orow = a.out + (int64_t)r * a.N + n * (PF_BN / 2);
+#pragma unroll 1
+                for (int c0 = 0; c0 < PF_BN / 2; c0 += 32) {
+                    float g[32], u[32];
+                    tmem_ld32(taddr + c0, g);
+                    tmem_ld32(taddr + PF_BN / 2 + c0, u);
+                    tmem_wait_ld();
+                    if (valid) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4)
+                            *reinterpret_cast<float4 *>(orow + c0 + i) =
+                                make_float4(silu_mul_pf(g[i], u[i]), silu_mul_pf(g[i + 1], u[i + 1]),
+                                            silu_mul_pf(g[i + 2], u[i + 2]), silu_mul_pf(g[i + 3], u[i + 3]));
+                    }
+                }
+            } else {
+                const int p = valid ? __ldg(a.perm + r) : 0;
+                float *orow = a.out + (int64_t)p * a.N + n * PF_BN;
+#pragma unroll 1
+                for (int c0 = 0; c0 < PF_BN; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(taddr + c0, v);
+                    tmem_wait_ld();
+                    if (valid) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4)
+                            *reinterpret_cast<float4 *>(orow + c0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, PF_TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 pf_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// fp16 [rows][K] with a box of 64 columns x box_rows rows, 128-byte swizzle.
+static bool encode_f16_rows(CUtensorMap *m, const void *base, int64_t rows, int K, int box_rows) {
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = pf_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)PF_BK, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1u, 1u};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t launch_prep_rows(const float *src, const int32_t *perm, int n_rows, int x_div, int K, __half *dst,
+                             cudaStream_t st) {
+    if (n_rows <= 0) return cudaSuccess;
+    const int64_t warps = (int64_t)n_rows * (K / TMOE_QK);
+    prep_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(src, perm, n_rows, x_div, K, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_f16(int wt, const uint8_t *w, size_t nb2, int N, int K, const int4 *active,
+                               const int32_t *n_active, int max_active, __half *dst, cudaStream_t st) {
+    const int64_t threads = (int64_t)max_active * N * (K / TMOE_QK) * 8;
+    if (threads <= 0) return cudaSuccess;
+    dequant_f16_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(wt, w, nb2, N, K, active, n_active,
+                                                                          max_active, dst);
+    return cudaGetLastError();
+}
+
+bool prefill_fits(int H, int I) { return H % PF_BN == 0 && I % (PF_BN / 2) == 0 && H % PF_BK == 0 && I % PF_BK == 0; }
+
+// gate/up (swiglu = true: act[r][I] from A1 [rows][H]) or down (dout[perm[r]][H] from A2 [rows][I]).
+cudaError_t launch_prefill_gemm(bool swiglu, const __half *A, int n_rows, int K, const __half *b0, const __half *b1,
+                                int n_slots, int N, const int4 *active, const int32_t *n_active, int max_active,
+                                int *tile_start, const int32_t *perm, float *out, int *err, int sm_count,
+                                cudaStream_t st) {
+    if (n_rows <= 0) return cudaSuccess;
+    const int n_tiles_n = swiglu ? N / (PF_BN / 2) : N / PF_BN;
+    tiles_kernel<<<1, 1024, 0, st>>>(active, n_active, max_active, n_tiles_n, tile_start);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    PfMaps maps;
+    memset(&maps, 0, sizeof maps);
+    if (!encode_f16_rows(&maps.a, A, n_rows, K, PF_BM)) return cudaErrorInvalidValue;
+    if (!encode_f16_rows(&maps.b0, b0, (int64_t)n_slots * N, K, swiglu ? PF_BN / 2 : PF_BN))
+        return cudaErrorInvalidValue;
+    if (swiglu && !encode_f16_rows(&maps.b1, b1, (int64_t)n_slots * N, K, PF_BN / 2)) return cudaErrorInvalidValue;
+    PfArgs a{K, N, n_tiles_n, active, n_active, max_active, tile_start, perm, n_rows, out, err};
+    static int set1[64] = {}, set2[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    int *set = swiglu ? set1 : set2;
+    if (!set[dev]) {
+        e = swiglu ? cudaFuncSetAttribute(prefill_gemm_kernel<PF_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          PF_SMEM)
+                   : cudaFuncSetAttribute(prefill_gemm_kernel<PF_SCATTER>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
+        if (e != cudaSuccess) return e;
+        set[dev] = 1;
+    }
+    if (swiglu)
+        prefill_gemm_kernel<PF_SWIGLU><<<sm_count, PF_THREADS, PF_SMEM, st>>>(maps, a);
+    else
+        prefill_gemm_kernel<PF_SCATTER><<<sm_count, PF_THREADS, PF_SMEM, st>>>(maps, a);
+    return cudaGetLastError();
+}
+
+}  // namespace tmoe

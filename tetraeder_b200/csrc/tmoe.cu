@@ -1,5 +1,6 @@
 // C ABI of the MoE layer hot path (include/tmoe.h): handle, workspace and the launch sequences
 // route -> dispatch -> gate/up (+SwiGLU) -> Q8_K of the activation -> down -> combine.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -15,6 +16,9 @@ namespace {
 
 constexpr int kMaxSlots = 1024;
 constexpr int kCounters = 4;
+// Pairs (T * k) from which the expert products run as grouped tcgen05 GEMMs instead of the
+// decode GEMV; handles sized for fewer pairs carry no prefill buffers.
+constexpr int64_t kPrefillMinPairs = 4096;
 thread_local std::string g_create_error;
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -43,6 +47,9 @@ struct tmoe_handle {
     float *ad = nullptr;
     uint32_t *abl = nullptr, *abh = nullptr;
     float *dout = nullptr;
+    // prefill (grouped GEMM) buffers: fp16 A rows of the two GEMMs, fp16 weights, tile tables
+    __half *a2 = nullptr, *w16_down = nullptr;
+    int *tile_start = nullptr;
     int *counters = nullptr;    // GEMV work counters
     int *route_done = nullptr;  // the fused routing kernel's tile counters (zero between calls)
     int *err = nullptr;
@@ -151,6 +158,11 @@ size_t carve(tmoe_handle *h, char *base) {
     h->abl = (uint32_t *)take(P * (I / 256) * nbd * 4);
     h->abh = (uint32_t *)take(P * (I / 256) * nbd * 4);
     h->dout = (float *)take(P * H * 4);
+    if ((int64_t)P >= kPrefillMinPairs && tmoe::prefill_fits((int)H, (int)I)) {
+        h->a2 = (__half *)take(P * I * 2);
+        h->w16_down = (__half *)take(E * H * I * 2);
+        h->tile_start = (int *)take((kMaxSlots + 1) * 4);
+    }
     h->counters = (int *)take(kCounters * 4);
     h->route_done = (int *)take((T / 4 + 2) * 4);
     h->err = (int *)take(4);
@@ -179,6 +191,25 @@ int check_tensors(tmoe_handle *h, const tmoe_expert_tensors *t) {
 // a4-a8 on `ids` (already slot ids) and `w`.  dispatched: the dispatch buffers (counts, offsets,
 // perm, active, zeroed work counters) already hold this call's dispatch; x_quantized: the Q8_K
 // rows of xn are already in h->xq/xd/xbl/xbh.
+// The down product of the large-batch regime as a grouped tcgen05 GEMM: A2 = Q8_K round trip of
+// the SwiGLU activations in expert-sorted order, as fp16; fp16 copies of the active experts'
+// down rows; dout[pair] = A2 . down^T.  (gate/up stay on the integer MMA path: their outputs feed
+// the Q8_K quantisation of the activations, and fp16 operands there move enough values across a
+// Q8_K rounding boundary to leave the north-star max-abs bound.)
+cudaError_t prefill_down(tmoe_handle *h, cudaStream_t st, int64_t P, const tmoe_expert_tensors *t, int max_active) {
+    const tmoe_config &c = h->cfg;
+    const int H = c.n_embd, I = c.n_ff;
+    cudaError_t e = tmoe::launch_prep_rows(h->act, h->perm, (int)P, 1, I, h->a2, st);
+    if (e == cudaSuccess)
+        e = tmoe::launch_dequant_f16(wt_of(c.down_type), (const uint8_t *)t->down, t->down_nb2, H, I, h->active,
+                                     h->n_active, max_active, h->w16_down, st);
+    if (e == cudaSuccess)
+        e = tmoe::launch_prefill_gemm(false, h->a2, (int)P, I, h->w16_down, nullptr, c.n_expert, H, h->active,
+                                      h->n_active, max_active, h->tile_start, h->perm, h->dout, h->err, h->sm_count,
+                                      st);
+    return e;
+}
+
 int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, const int32_t *ids, const float *w,
                 const tmoe_expert_tensors *t, float *out, bool dispatched, bool x_quantized) {
     const tmoe_config &c = h->cfg;
@@ -194,6 +225,8 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "sort_pairs");
     }
+    const int max_active = (int)(P < t->n_slots ? P : t->n_slots);
+    const bool prefill = P >= kPrefillMinPairs && h->a2 && t->n_slots <= c.n_expert;
     if (!x_quantized) {
         {
             PhaseMark pm(h, st, TMOE_PHASE_QUANT_X);
@@ -201,7 +234,6 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "quantize x");
     }
-    const int max_active = (int)(P < t->n_slots ? P : t->n_slots);
     tmoe::GemvArgs g{};
     g.w0 = (const uint8_t *)t->gate;
     g.w1 = (const uint8_t *)t->up;
@@ -216,6 +248,19 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
         e = tmoe::launch_gemv(wg, true, g, max_active, h->sm_count, st);
     }
     if (e != cudaSuccess) return cuda_fail(h, e, "gate/up gemv");
+    if (prefill) {
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_DOWN);
+            e = prefill_down(h, st, P, t, max_active);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "prefill down");
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_COMBINE);
+            e = tmoe::launch_combine(h->dout, ids, w, T, k, H, t->n_slots, out, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "combine");
+        return TMOE_OK;
+    }
     {
         PhaseMark pm(h, st, TMOE_PHASE_QUANT_ACT);
         e = tmoe::launch_quantize_q8k(h->act, P, I, ids, tmoe::Q8Rows{h->aq, h->ad, h->abl, h->abh, wd}, st);
