@@ -119,6 +119,14 @@ cudaError_t launch_prefill_gemm(bool swiglu, const __half *A, int n_rows, int K,
                                 int *tile_start, const int32_t *perm, float *out, int *err, int sm_count,
                                 cudaStream_t st);
 
+cudaError_t launch_prep_gateup_a(const float *x, int T, const int32_t *perm, int n_rows, int x_div, int K,
+                                 __half *aq_t, float *ad_t, __half *ab_t, __half *aq, float *ad, __half *ab,
+                                 cudaStream_t st);
+cudaError_t launch_prefill_gateup(const __half *aq, const float *ad, const __half *ab, int n_rows, int K, int I,
+                                  const uint8_t *gate, const uint8_t *up, size_t nb1, size_t nb2_gate,
+                                  size_t nb2_up, const int4 *active, const int32_t *n_active, int max_active,
+                                  int *tile_start, float *act, int *err, int sm_count, cudaStream_t st);
+
 // Rows per work item of the GEMV for K columns and N rows per expert; 0 if N does not fit.
 int gemv_rows_per_item(int wt, int K, int N);
 cudaError_t launch_gemv(int wt, bool gateup, const GemvArgs &a, int max_items, int sm_count, cudaStream_t st);

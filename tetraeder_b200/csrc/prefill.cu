@@ -417,6 +417,478 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(const __gri
     }
 }
 
+// ------------------------------------------------------------------ exact gate/up (Q4_K)
+// The gate/up products of the large-batch regime, exact like the reference's integer block sums
+// and still on tcgen05: both operands are integers that fp16 holds exactly, and f32 sums them
+// exactly (below 2^24), so each super-block b of K gives exact integer dots.
+//   main_b[t][n] = sum_{k in b} q_x[t][k] * (sc[n][s(k)] * q[n][k])   (q_x int8, sc*q <= 945)
+//   min_b[t][n]  = sum_s  B[t][b][s] * m[n][b][s]                       (B = 64 * hi + lo: K = 16)
+//   out[t][n]   += d_x[t][b] * (d[n][b] * main_b - dmin[n][b] * min_b)   (the ggml Q4_K x Q8_K dot)
+// The per-block accumulators live in TMEM (main and min, double-buffered: 4 x 128 columns) and
+// the epilogue warps fold them into per-thread running sums while the next block's MMAs run.  A
+// tile is 128 token rows x 64 features of gate and the same 64 of up (128 MMA columns); the
+// SwiGLU happens once per tile.  Warps: 0 TMA (q_x rows, block sums), 1 MMA, 2-5 dequantise the
+// weights into the swizzled fp16 layout (sc * q, the mins, d/dmin), 6-13 epilogue (lane quarter
+// warp % 4; features 32h .. 32h+31 of gate and of up, h = (warp - 6) / 4).
+constexpr int GU_S = 4;            // A / B stage ring
+constexpr int GU_THREADS = 448;  // 14 warps
+constexpr int GU_AP_BYTES = 128 * 16 * 2;  // min operand of one block: 128 rows x K 16 fp16
+constexpr int GU_RAW_BYTES = 128 * TMOE_Q4K_BYTES;  // one super-block of the tile's 128 weight rows
+constexpr int GU_RAWN = 3;  // raw prefetch buffers: two blocks ahead
+// shared memory: the rings, the scales, 512 bytes of barriers, then the tile tables; plus 1024 bytes
+// of alignment slack
+constexpr int GU_FIXED = GU_S * (2 * PF_A_BYTES) + 2 * 2 * GU_AP_BYTES + GU_RAWN * GU_RAW_BYTES + 2 * 128 * 8 + 512;
+static_assert((GU_S * 4 + 12) * 8 + 16 <= 512, "barrier room");
+
+// K-major, no swizzle: 8-row x 16-byte core matrices, rows 16 bytes apart, 8-row groups 128 bytes
+// apart (stride byte offset), the two K halves of a K = 16 tile 2048 bytes apart (leading byte
+// offset).
+__device__ __forceinline__ uint64_t kmajor_plain_desc(uint32_t saddr) {
+    uint64_t d = (uint64_t)((saddr & 0x3ffffu) >> 4);
+    d |= (uint64_t)(2048 >> 4) << 16;
+    d |= (uint64_t)(128 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    return d;  // layout type 0: no swizzle
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) {
+    uint32_t u;
+    memcpy(&u, &h, 4);
+    return u;
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait2() { asm volatile("cp.async.wait_group 2;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// A rows of the exact gate/up GEMM from the tokens' Q8_K: q_x as fp16 [rows][K], d [rows][K/256],
+// and per super-block the 8 sub-block sums of 32 split as {hi, lo} with B = 64 * hi + lo, as fp16
+// [rows][K/256][16].  One warp per (row, 256-block).
+__global__ void prep_gateup_a_kernel(const float *__restrict__ x, const int32_t *__restrict__ perm, int n_rows,
+                                     int x_div, int K, __half *__restrict__ aq, float *__restrict__ ad,
+                                     __half *__restrict__ ab) {
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nb = K / TMOE_QK;
+    const int64_t r = gw / nb;
+    const int b = (int)(gw % nb);
+    if (r >= n_rows) return;
+    int p = perm ? perm[r] : (int)r;
+    if (p < 0) p = 0;
+    const float *xr = x + (int64_t)(p / x_div) * K + b * TMOE_QK + 8 * lane;
+    const float4 a0 = *reinterpret_cast<const float4 *>(xr), a1 = *reinterpret_cast<const float4 *>(xr + 4);
+    const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    uint2 q;
+    float d;
+    int s16;
+    q8k_block_warp(v, q, d, s16);
+    __align__(16) __half h[8];
+#pragma unroll
+    for (int c = 0; c < 8; c++)
+        h[c] = __int2half_rn((int)(int8_t)(((c < 4 ? q.x : q.y) >> (8 * (c & 3))) & 0xff));
+    *reinterpret_cast<uint4 *>(aq + r * K + b * TMOE_QK + 8 * lane) = *reinterpret_cast<const uint4 *>(h);
+    const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);  // lanes 4s hold sub-block s's sum
+    if ((lane & 3) == 0) {
+        const int sb = lane >> 2, hi = s32 >> 6, lo = s32 - 64 * hi;
+        __half2 pr = __halves2half2(__int2half_rn(hi), __int2half_rn(lo));
+        *reinterpret_cast<__half2 *>(ab + (r * nb + b) * 16 + 2 * sb) = pr;
+    }
+    if (lane == 0) ad[r * nb + b] = d;
+}
+
+// Row r of the expert-sorted A operands = row perm[r] / x_div of the per-token ones: fp16 q_x
+// [K], d [K/256], block sums [K/256][16].  One warp per row, 16-byte copies.
+__global__ void gather_gateup_a_kernel(const __half *__restrict__ aq_t, const float *__restrict__ ad_t,
+                                       const __half *__restrict__ ab_t, const int32_t *__restrict__ perm,
+                                       int n_rows, int x_div, int K, __half *__restrict__ aq, float *__restrict__ ad,
+                                       __half *__restrict__ ab) {
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= n_rows) return;
+    int p = perm[r];
+    if (p < 0) p = 0;
+    const int64_t t = p / x_div;
+    const int nb = K / TMOE_QK;
+    const uint4 *sq = reinterpret_cast<const uint4 *>(aq_t + t * K);
+    uint4 *dq = reinterpret_cast<uint4 *>(aq + r * K);
+    for (int i = lane; i < K / 8; i += 32) dq[i] = __ldg(sq + i);
+    const uint4 *sb = reinterpret_cast<const uint4 *>(ab_t + t * nb * 16);
+    uint4 *db = reinterpret_cast<uint4 *>(ab + r * nb * 16);
+    for (int i = lane; i < nb * 2; i += 32) db[i] = __ldg(sb + i);
+    for (int i = lane; i < nb; i += 32) ad[r * nb + i] = __ldg(ad_t + t * nb + i);
+}
+
+// pf_decode over tables staged in shared memory (tile_start [na + 1], active [na]).
+__device__ __forceinline__ void gu_decode(const int *ts, const int4 *act, int na, int tile, int &ai, int &m, int &n) {
+    int lo = 0, hi = na - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (ts[mid] <= tile) lo = mid;
+        else hi = mid - 1;
+    }
+    ai = lo;
+    const int4 info = act[ai];
+    const int m_tiles = (info.z - info.y + PF_BM - 1) / PF_BM;
+    const int local = tile - ts[ai];
+    n = local / m_tiles;
+    m = local % m_tiles;
+}
+
+struct GuArgs {
+    const uint8_t *gate, *up;
+    size_t nb1, nb2_gate, nb2_up;
+    int K, I;  // H, n_ff
+    const int4 *active;
+    const int32_t *n_active;
+    int max_active;
+    const int *tile_start;
+    const float *ad;  // d of the rows' Q8_K blocks
+    int n_rows;
+    float *act;       // [rows][I], expert-sorted rows
+    int *err;
+};
+struct GuMaps {
+    CUtensorMap aq;  // fp16 [rows][K], box 64 x 128, 128-byte swizzle
+    CUtensorMap ab;  // fp16 [rows][K/256 * 16], box 8 x 128, no swizzle
+};
+
+// Bounded waits of the roles; a timeout latches the error and stops the role (and the CTA).
+#define GU_WAIT(bar, ph)                                                                                   \
+    if (!mbar_wait_bounded(bar, ph)) {                                                                     \
+        latch_error(a.err, TMOE_DEV_ERR_TIMEOUT);                                                          \
+        *abort_flag = 1;                                                                                   \
+        goto done;                                                                                         \
+    }
+#define GU_WAIT_WARP(bar, ph)                                                                              \
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar, ph))) {                                            \
+        if (lane == 0) latch_error(a.err, TMOE_DEV_ERR_TIMEOUT);                                           \
+        *abort_flag = 1;                                                                                   \
+        goto done;                                                                                         \
+    }
+
+__global__ void __launch_bounds__(GU_THREADS, 1) prefill_gateup_kernel(const __grid_constant__ GuMaps maps,
+                                                                        const GuArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = smem;                                  // [GU_S][128 x 64 fp16, sw128]
+    uint8_t *sB = sA + GU_S * PF_A_BYTES;                // [GU_S][128 x 64 fp16, sw128]
+    uint8_t *sAp = sB + GU_S * PF_A_BYTES;               // [2][min operand A]
+    uint8_t *sBp = sAp + 2 * GU_AP_BYTES;                // [2][min operand B]
+    uint8_t *sRaw = sBp + 2 * GU_AP_BYTES;               // [GU_RAWN][128 rows x 144 B], the dequant prefetch
+    float2 *scl = reinterpret_cast<float2 *>(sRaw + GU_RAWN * GU_RAW_BYTES);  // [2][128] {d, dmin}
+    uint64_t *bars = reinterpret_cast<uint64_t *>(scl + 2 * 128);
+    uint64_t *fa = bars, *ea = fa + GU_S, *fb = ea + GU_S, *eb = fb + GU_S;
+    uint64_t *fap = eb + GU_S, *eap = fap + 2, *fbp = eap + 2, *ebp = fbp + 2, *fsc = ebp + 2, *esc = fsc + 2;
+    uint64_t *tf = esc + 2, *te = tf + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(te + 2);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    int *s_ts = reinterpret_cast<int *>(smem + GU_FIXED);  // tile tables: tile_start [na + 1], active [na]
+    int4 *s_act = reinterpret_cast<int4 *>(s_ts + ((a.max_active + 4) & ~3));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int na = a.n_active[0];
+    if (na > a.max_active || na < 0) na = na < 0 ? 0 : a.max_active;
+    for (int i = threadIdx.x; i <= na; i += blockDim.x) s_ts[i] = na > 0 ? __ldg(a.tile_start + i) : 0;
+    for (int i = threadIdx.x; i < na; i += blockDim.x) s_act[i] = __ldg(a.active + i);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < GU_S; s++) {
+            mbar_init(&fa[s], 1);
+            mbar_init(&ea[s], 1);
+            mbar_init(&fb[s], 4);
+            mbar_init(&eb[s], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&fap[i], 1);
+            mbar_init(&eap[i], 1);
+            mbar_init(&fbp[i], 4);
+            mbar_init(&ebp[i], 1);
+            mbar_init(&fsc[i], 4);
+            mbar_init(&esc[i], 8);
+            mbar_init(&tf[i], 1);
+            mbar_init(&te[i], 8);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, PF_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int n_tiles = na > 0 ? s_ts[na] : 0;
+    const int nb = a.K / TMOE_QK;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA: q_x stages and the blocks' sums
+            int it_s = 0, it_b = 0;
+            for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x) {
+                int ai, m, n;
+                gu_decode(s_ts, s_act, na, tile, ai, m, n);
+                const int row0 = s_act[ai].y + m * PF_BM;
+                for (int b = 0; b < nb; b++, it_b++) {
+                    const int i = it_b & 1;
+                    if (it_b >= 2) GU_WAIT(&eap[i], ((it_b >> 1) - 1) & 1);
+                    mbar_arrive_expect_tx(&fap[i], (uint32_t)GU_AP_BYTES);
+                    tma_load_2d(sAp + i * GU_AP_BYTES, &maps.ab, 16 * b, row0, &fap[i]);
+                    tma_load_2d(sAp + i * GU_AP_BYTES + GU_AP_BYTES / 2, &maps.ab, 16 * b + 8, row0, &fap[i]);
+                    for (int st = 0; st < 4; st++, it_s++) {
+                        const int s = it_s % GU_S;
+                        if (it_s >= GU_S) GU_WAIT(&ea[s], ((it_s / GU_S) - 1) & 1);
+                        mbar_arrive_expect_tx(&fa[s], (uint32_t)PF_A_BYTES);
+                        tma_load_2d(sA + s * PF_A_BYTES, &maps.aq, TMOE_QK * b + 64 * st, row0, &fa[s]);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA
+            constexpr uint32_t idesc = idesc_f16(PF_BM, 128);
+            int it_s = 0, it_b = 0;
+            for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x) {
+                for (int b = 0; b < nb; b++, it_b++) {
+                    const int buf = it_b & 1;
+                    if (it_b >= 2) GU_WAIT(&te[buf], ((it_b >> 1) - 1) & 1);
+                    tc_fence_after();
+                    const uint32_t dmain = tmem_base + (uint32_t)(buf * 256), dmin = dmain + 128;
+                    for (int st = 0; st < 4; st++, it_s++) {
+                        const int s = it_s % GU_S;
+                        GU_WAIT(&fa[s], (it_s / GU_S) & 1);
+                        GU_WAIT(&fb[s], (it_s / GU_S) & 1);
+                        tc_fence_after();
+                        const uint32_t sa = smem_u32(sA + s * PF_A_BYTES), sb = smem_u32(sB + s * PF_A_BYTES);
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+                            umma_f16(dmain, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), idesc, (st | k) != 0);
+                        umma_commit(&ea[s]);
+                        umma_commit(&eb[s]);
+                    }
+                    GU_WAIT(&fap[buf], (it_b >> 1) & 1);
+                    GU_WAIT(&fbp[buf], (it_b >> 1) & 1);
+                    tc_fence_after();
+                    umma_f16(dmin, kmajor_plain_desc(smem_u32(sAp + buf * GU_AP_BYTES)),
+                             kmajor_plain_desc(smem_u32(sBp + buf * GU_AP_BYTES)), idesc, 0u);
+                    umma_commit(&eap[buf]);
+                    umma_commit(&ebp[buf]);
+                    umma_commit(&tf[buf]);
+                }
+            }
+        }
+    } else if (warp < 6) {  // dequantise: thread n = weight row n of the tile (0-63 gate, 64-127 up)
+        const int n = threadIdx.x - 64;
+        int it_s = 0, it_b = 0;
+        // the CTA's (tile, block) sequence; each block's 144 raw bytes are copied (cp.async) into one
+        // of GU_RAWN buffers two steps before the block is dequantised
+        auto row_of = [&](int t) {
+            int ai, m, nt;
+            gu_decode(s_ts, s_act, na, t, ai, m, nt);
+            const int e = s_act[ai].x;
+            const int f = nt * 64 + (n & 63);
+            return n < 64 ? a.gate + (size_t)e * a.nb2_gate + (size_t)f * a.nb1
+                          : a.up + (size_t)e * a.nb2_up + (size_t)f * a.nb1;
+        };
+        uint8_t *my_raw = sRaw + n * TMOE_Q4K_BYTES;  // + buffer * GU_RAW_BYTES
+        int tile = blockIdx.x, b = 0;                   // the block being dequantised
+        int pt = blockIdx.x, pb = 0;                    // the next block to prefetch
+        const uint8_t *prow = pt < n_tiles ? row_of(pt) : nullptr;
+        int rb = 0, pbuf = 0;
+        auto prefetch = [&]() {
+            if (pt < n_tiles) {
+                uint8_t *dst = my_raw + pbuf * GU_RAW_BYTES;
+                const uint8_t *src = prow + (size_t)pb * TMOE_Q4K_BYTES;
+#pragma unroll
+                for (int i = 0; i < 9; i++) cp_async16(dst + 16 * i, src + 16 * i);
+                if (++pb == nb) {
+                    pb = 0;
+                    pt += gridDim.x;
+                    if (pt < n_tiles) prow = row_of(pt);
+                }
+            }
+            cp_async_commit();
+            pbuf = pbuf + 1 == GU_RAWN ? 0 : pbuf + 1;
+        };
+        prefetch();
+        prefetch();
+        const uint32_t EXP2 = 0x64006400u;  // fp16 1024 in both halves
+        while (tile < n_tiles && !*abort_flag) {
+            const uint8_t *cur = my_raw + rb * GU_RAW_BYTES;
+            prefetch();        // two blocks ahead
+            cp_async_wait2();  // this block's copies are done
+            uint4 raw[9];
+#pragma unroll
+            for (int i = 0; i < 9; i++) raw[i] = reinterpret_cast<const uint4 *>(cur)[i];
+            rb = rb + 1 == GU_RAWN ? 0 : rb + 1;
+            if (++b == nb) {
+                b = 0;
+                tile += gridDim.x;
+            }
+            const uint32_t w0 = raw[0].x, sc0 = raw[0].y, sc1 = raw[0].z, sc2 = raw[0].w;
+            const float d = h2f((uint16_t)(w0 & 0xffffu)), dmin = h2f((uint16_t)(w0 >> 16));
+            // 6-bit scales / mins of the 8 sub-blocks, byte-packed
+            const uint32_t s_lo = sc0 & 0x3f3f3f3fu, s_hi = (sc2 & 0x0f0f0f0fu) | ((sc0 >> 2) & 0x30303030u);
+            const uint32_t m_lo = sc1 & 0x3f3f3f3fu, m_hi = ((sc2 >> 4) & 0x0f0f0f0fu) | ((sc1 >> 2) & 0x30303030u);
+            const int i2 = it_b & 1;
+            if (it_b >= 2) {
+                GU_WAIT_WARP(&esc[i2], ((it_b >> 1) - 1) & 1);
+                GU_WAIT_WARP(&ebp[i2], ((it_b >> 1) - 1) & 1);
+            }
+            scl[i2 * 128 + n] = make_float2(d, dmin);
+            {  // min operand row n: {64 m_s, m_s} for s = 0..7 at K 2s, 2s+1
+                uint32_t mw[8];
+#pragma unroll
+                for (int sb = 0; sb < 8; sb++) {
+                    const int mv = (int)((sb < 4 ? m_lo : m_hi) >> (8 * (sb & 3))) & 0xff;
+                    mw[sb] = h2_bits(__halves2half2(__int2half_rn(64 * mv), __int2half_rn(mv)));
+                }
+                uint8_t *bp = sBp + i2 * GU_AP_BYTES + n * 16;
+                *reinterpret_cast<uint4 *>(bp) = make_uint4(mw[0], mw[1], mw[2], mw[3]);
+                *reinterpret_cast<uint4 *>(bp + 2048) = make_uint4(mw[4], mw[5], mw[6], mw[7]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&fsc[i2]);
+                mbar_arrive(&fbp[i2]);
+            }
+#pragma unroll
+            for (int st = 0; st < 4; st++) {
+                const int s = (it_s + st) % GU_S;
+                if (it_s + st >= GU_S) GU_WAIT_WARP(&eb[s], (((it_s + st) / GU_S) - 1) & 1);
+                // K [64 st, 64 st + 64): low nibbles of qs[32 st ..] (sub-block 2 st), then high nibbles
+                // (sub-block 2 st + 1).  fp16 of a nibble pair by exponent magic: (1024 + q) * sc -
+                // 1024 * sc = q * sc; for the high nibble in place (1024 + 16 q) * sc/16 - 64 sc.  All
+                // values and products stay integers below 2^11 x 2^5: exact.
+                const uint4 qa = raw[1 + 2 * st], qb = raw[2 + 2 * st];
+                const int scl_l = (int)((st < 2 ? s_lo : s_hi) >> (16 * (st & 1))) & 0xff;
+                const int scl_h = (int)((st < 2 ? s_lo : s_hi) >> (16 * (st & 1) + 8)) & 0xff;
+                const __half2 ml = __half2half2(__int2half_rn(scl_l));
+                const __half2 al = __half2half2(__int2half_rn(-1024 * scl_l));
+                const __half2 mh = __half2half2(__hmul(__int2half_rn(scl_h), __float2half_rn(0.0625f)));
+                const __half2 ah = __half2half2(__int2half_rn(-64 * scl_h));
+                const uint32_t wq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                uint8_t *brow = sB + s * PF_A_BYTES + n * 128;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {  // 16-byte chunk c: elements 8c .. 8c+7
+                    uint32_t hv[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int el = 8 * c + 2 * u;  // element pair el, el + 1 (same sub-block)
+                        const int src = el & 31;       // byte of the 32 qs bytes
+                        const uint32_t t = __byte_perm(wq[src >> 2], 0u, (src & 2) ? 0x4342u : 0x4140u);
+                        __half2 v;
+                        if (el < 32) {
+                            const uint32_t bits = (t & 0x000f000fu) | EXP2;
+                            memcpy(&v, &bits, 4);
+                            v = __hfma2(v, ml, al);
+                        } else {
+                            const uint32_t bits = (t & 0x00f000f0u) | EXP2;
+                            memcpy(&v, &bits, 4);
+                            v = __hfma2(v, mh, ah);
+                        }
+                        hv[u] = h2_bits(v);
+                    }
+                    *reinterpret_cast<uint4 *>(brow + 16 * (c ^ (n & 7))) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&fb[s]);
+            }
+            it_s += 4;
+            it_b++;
+        }
+    } else {  // epilogue: warps 6-13
+        const int q = warp & 3, h = (warp - 6) >> 2;
+        int it_b = 0;
+        for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x) {
+            int ai, m, nt;
+            gu_decode(s_ts, s_act, na, tile, ai, m, nt);
+            const int4 info = s_act[ai];
+            const int r = info.y + m * PF_BM + q * 32 + lane;
+            const bool valid = r < info.z && r < a.n_rows;
+            float tg[32], tu[32];
+#pragma unroll
+            for (int c = 0; c < 32; c++) tg[c] = tu[c] = 0.0f;
+            float dx_next = valid ? __ldg(a.ad + (int64_t)r * nb) : 0.0f;
+            for (int b = 0; b < nb; b++, it_b++) {
+                const float dx = dx_next;  // loaded one block ahead
+                if (b + 1 < nb) dx_next = valid ? __ldg(a.ad + (int64_t)r * nb + b + 1) : 0.0f;
+                const int buf = it_b & 1;
+                GU_WAIT_WARP(&tf[buf], (it_b >> 1) & 1);
+                GU_WAIT_WARP(&fsc[buf], (it_b >> 1) & 1);
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + (uint32_t)(buf * 256) + ((uint32_t)(q * 32) << 16);
+                const float4 *sg = reinterpret_cast<const float4 *>(scl + buf * 128 + 32 * h);  // {d, dmin} x 2
+                const float4 *su = sg + 32;
+                float v[32];
+                tmem_ld32(taddr + 32 * h, v);  // main, gate features
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float4 s4 = sg[i >> 1];
+                    tg[i] = __fmaf_rn(dx * s4.x, v[i], tg[i]);
+                    tg[i + 1] = __fmaf_rn(dx * s4.z, v[i + 1], tg[i + 1]);
+                }
+                tmem_ld32(taddr + 128 + 32 * h, v);  // min, gate
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float4 s4 = sg[i >> 1];
+                    tg[i] = __fmaf_rn(-dx * s4.y, v[i], tg[i]);
+                    tg[i + 1] = __fmaf_rn(-dx * s4.w, v[i + 1], tg[i + 1]);
+                }
+                tmem_ld32(taddr + 64 + 32 * h, v);  // main, up
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float4 s4 = su[i >> 1];
+                    tu[i] = __fmaf_rn(dx * s4.x, v[i], tu[i]);
+                    tu[i + 1] = __fmaf_rn(dx * s4.z, v[i + 1], tu[i + 1]);
+                }
+                tmem_ld32(taddr + 192 + 32 * h, v);  // min, up
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float4 s4 = su[i >> 1];
+                    tu[i] = __fmaf_rn(-dx * s4.y, v[i], tu[i]);
+                    tu[i + 1] = __fmaf_rn(-dx * s4.w, v[i + 1], tu[i + 1]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&te[buf]);
+                    mbar_arrive(&esc[buf]);
+                }
+            }
+            if (valid) {
+                float *orow = a.act + (int64_t)r * a.I + nt * 64 + 32 * h;
+#pragma unroll
+                for (int c = 0; c < 32; c += 4)
+                    *reinterpret_cast<float4 *>(orow + c) =
+                        make_float4(silu_mul_pf(tg[c], tu[c]), silu_mul_pf(tg[c + 1], tu[c + 1]),
+                                    silu_mul_pf(tg[c + 2], tu[c + 2]), silu_mul_pf(tg[c + 3], tu[c + 3]));
+            }
+        }
+    }
+done:
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, PF_TMEM_COLS);
+    }
+}
+#undef GU_WAIT
+#undef GU_WAIT_WARP
+
 // ------------------------------------------------------------------ host side
 static PFN_cuTensorMapEncodeTiled_v12000 pf_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
@@ -457,6 +929,63 @@ cudaError_t launch_dequant_f16(int wt, const uint8_t *w, size_t nb2, int N, int 
     if (threads <= 0) return cudaSuccess;
     dequant_f16_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(wt, w, nb2, N, K, active, n_active,
                                                                           max_active, dst);
+    return cudaGetLastError();
+}
+
+// The Q8_K of the T token rows (token order), then their copies in expert-sorted pair order.
+cudaError_t launch_prep_gateup_a(const float *x, int T, const int32_t *perm, int n_rows, int x_div, int K,
+                                 __half *aq_t, float *ad_t, __half *ab_t, __half *aq, float *ad, __half *ab,
+                                 cudaStream_t st) {
+    if (n_rows <= 0 || T <= 0) return cudaSuccess;
+    const int64_t warps = (int64_t)T * (K / TMOE_QK);
+    prep_gateup_a_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(x, nullptr, T, 1, K, aq_t, ad_t, ab_t);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    gather_gateup_a_kernel<<<(unsigned)((n_rows + 7) / 8), 256, 0, st>>>(aq_t, ad_t, ab_t, perm, n_rows, x_div, K, aq,
+                                                                         ad, ab);
+    return cudaGetLastError();
+}
+
+static bool encode_f16_plain(CUtensorMap *m, const void *base, int64_t rows, int cols, int box_cols, int box_rows) {
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = pf_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1u, 1u};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// act[r][I] (expert-sorted rows) = silu(x . gate^T) * (x . up^T) for Q4_K gate/up, exact block sums.
+cudaError_t launch_prefill_gateup(const __half *aq, const float *ad, const __half *ab, int n_rows, int K, int I,
+                                  const uint8_t *gate, const uint8_t *up, size_t nb1, size_t nb2_gate,
+                                  size_t nb2_up, const int4 *active, const int32_t *n_active, int max_active,
+                                  int *tile_start, float *act, int *err, int sm_count, cudaStream_t st) {
+    if (n_rows <= 0) return cudaSuccess;
+    if (I % 64 || K % TMOE_QK) return cudaErrorInvalidValue;
+    tiles_kernel<<<1, 1024, 0, st>>>(active, n_active, max_active, I / 64, tile_start);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    GuMaps maps;
+    memset(&maps, 0, sizeof maps);
+    if (!encode_f16_rows(&maps.aq, aq, n_rows, K, PF_BM)) return cudaErrorInvalidValue;
+    if (!encode_f16_plain(&maps.ab, ab, n_rows, (K / TMOE_QK) * 16, 8, PF_BM)) return cudaErrorInvalidValue;
+    GuArgs a{gate, up, nb1, nb2_gate, nb2_up, K, I, active, n_active, max_active, tile_start, ad, n_rows, act, err};
+    static int set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    const size_t tables = (size_t)((max_active + 4) & ~3) * 4 + (size_t)max_active * 16;
+    const size_t smem = GU_FIXED + tables + 1024;
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    if ((int)smem > set[dev]) {
+        e = cudaFuncSetAttribute(prefill_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        set[dev] = (int)smem;
+    }
+    prefill_gateup_kernel<<<sm_count, GU_THREADS, smem, st>>>(maps, a);
     return cudaGetLastError();
 }
 

@@ -48,8 +48,9 @@ struct tmoe_handle {
     uint32_t *abl = nullptr, *abh = nullptr;
     float *dout = nullptr;
     // prefill (grouped GEMM) buffers: fp16 A rows of the two GEMMs, fp16 weights, tile tables
-    __half *a2 = nullptr, *w16_down = nullptr;
-    int *tile_start = nullptr;
+    __half *a2 = nullptr, *w16_down = nullptr, *aq16 = nullptr, *ab16 = nullptr, *aq16_t = nullptr, *ab16_t = nullptr;
+    float *ad16 = nullptr, *ad16_t = nullptr;  // d of the A rows' Q8_K blocks (sorted rows, token rows)
+    int *tile_start = nullptr, *tile_start2 = nullptr;
     int *counters = nullptr;    // GEMV work counters
     int *route_done = nullptr;  // the fused routing kernel's tile counters (zero between calls)
     int *err = nullptr;
@@ -162,6 +163,13 @@ size_t carve(tmoe_handle *h, char *base) {
         h->a2 = (__half *)take(P * I * 2);
         h->w16_down = (__half *)take(E * H * I * 2);
         h->tile_start = (int *)take((kMaxSlots + 1) * 4);
+        h->tile_start2 = (int *)take((kMaxSlots + 1) * 4);
+        h->aq16 = (__half *)take(P * H * 2);
+        h->ad16 = (float *)take(P * (H / 256) * 4);
+        h->ab16 = (__half *)take(P * (H / 256) * 16 * 2);
+        h->aq16_t = (__half *)take(T * H * 2);
+        h->ad16_t = (float *)take(T * (H / 256) * 4);
+        h->ab16_t = (__half *)take(T * (H / 256) * 16 * 2);
     }
     h->counters = (int *)take(kCounters * 4);
     h->route_done = (int *)take((T / 4 + 2) * 4);
@@ -196,10 +204,11 @@ int check_tensors(tmoe_handle *h, const tmoe_expert_tensors *t) {
 // down rows; dout[pair] = A2 . down^T.  (gate/up stay on the integer MMA path: their outputs feed
 // the Q8_K quantisation of the activations, and fp16 operands there move enough values across a
 // Q8_K rounding boundary to leave the north-star max-abs bound.)
-cudaError_t prefill_down(tmoe_handle *h, cudaStream_t st, int64_t P, const tmoe_expert_tensors *t, int max_active) {
+cudaError_t prefill_down(tmoe_handle *h, cudaStream_t st, int64_t P, const tmoe_expert_tensors *t, int max_active,
+                         bool act_sorted) {
     const tmoe_config &c = h->cfg;
     const int H = c.n_embd, I = c.n_ff;
-    cudaError_t e = tmoe::launch_prep_rows(h->act, h->perm, (int)P, 1, I, h->a2, st);
+    cudaError_t e = tmoe::launch_prep_rows(h->act, act_sorted ? nullptr : h->perm, (int)P, 1, I, h->a2, st);
     if (e == cudaSuccess)
         e = tmoe::launch_dequant_f16(wt_of(c.down_type), (const uint8_t *)t->down, t->down_nb2, H, I, h->active,
                                      h->n_active, max_active, h->w16_down, st);
@@ -227,6 +236,33 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
     }
     const int max_active = (int)(P < t->n_slots ? P : t->n_slots);
     const bool prefill = P >= kPrefillMinPairs && h->a2 && t->n_slots <= c.n_expert;
+    if (prefill && wg == TMOE_WT_Q4K) {
+        // gate/up as exact grouped tcgen05 GEMMs (rows in expert-sorted order), then the down GEMM
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_QUANT_X);
+            e = tmoe::launch_prep_gateup_a(xn, (int)T, h->perm, (int)P, k, H, h->aq16_t, h->ad16_t, h->ab16_t, h->aq16,
+                                           h->ad16, h->ab16, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "prefill gate/up rows");
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_GATE_UP);
+            e = tmoe::launch_prefill_gateup(h->aq16, h->ad16, h->ab16, (int)P, H, I, (const uint8_t *)t->gate,
+                                            (const uint8_t *)t->up, t->gate_nb1, t->gate_nb2, t->up_nb2, h->active,
+                                            h->n_active, max_active, h->tile_start2, h->act, h->err, h->sm_count, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "prefill gate/up");
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_DOWN);
+            e = prefill_down(h, st, P, t, max_active, true);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "prefill down");
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_COMBINE);
+            e = tmoe::launch_combine(h->dout, ids, w, T, k, H, t->n_slots, out, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "combine");
+        return TMOE_OK;
+    }
     if (!x_quantized) {
         {
             PhaseMark pm(h, st, TMOE_PHASE_QUANT_X);
@@ -251,7 +287,7 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
     if (prefill) {
         {
             PhaseMark pm(h, st, TMOE_PHASE_DOWN);
-            e = prefill_down(h, st, P, t, max_active);
+            e = prefill_down(h, st, P, t, max_active, false);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "prefill down");
         {
