@@ -62,14 +62,26 @@ def parse():
     p.add_argument("--cpu-sample-s", type=float, default=15.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--sweep", action="store_true", help="also time T in {1,4,16,64}")
-    return p.parse_args()
+    p.add_argument("--mode", choices=["decode", "prefill", "streamed"], default="decode",
+                   help="decode: C2 at T tokens (the metric's config); prefill: C2-shaped layer at T=8192 "
+                        "(tensor roofline); streamed: config 5, skewed routing over 64 device slots of 128 experts")
+    p.add_argument("--slots", type=int, default=64)
+    a = p.parse_args()
+    if a.mode != "decode" and a.tokens == 64:
+        a.tokens = 8192
+    if a.mode == "prefill" and a.layers == 48:
+        a.layers = 4
+    return a
 
 
 def workload(args, n_gpus):
-    return {"workload": "C2 Qwen3-30B-A3B MoE layer, decode", "tokens_per_layer_call": args.tokens,
+    name = {"decode": "C2 Qwen3-30B-A3B MoE layer, decode",
+            "prefill": "C2-shaped Qwen3-30B-A3B MoE layer, prefill (north-star tensor target)",
+            "streamed": "C5 skewed large-batch stress, 64 of 128 experts in device slots"}[args.mode]
+    return {"workload": name, "tokens_per_layer_call": args.tokens,
             "n_embd": H, "n_ff": I, "n_expert": E, "n_expert_used": K_USED,
             "types": "gate/up Q4_K, down Q6_K (this repo's quantiser)", "layers_per_step": args.layers,
-            "l2": "inputs larger than L2: 48 distinct resident layers rotated each step",
+            "l2": f"inputs larger than L2: {args.layers} distinct resident layers rotated each step",
             "parallelism": f"replicas x{n_gpus}" if n_gpus > 1 else "single GPU", "seed": args.seed}
 
 
@@ -292,12 +304,30 @@ def run_ours(args, rank, world, local_rank):
                   "achieved_gbs": round(layer_bytes / (layer_ms / 1e3) / 1e9, 1),
                   "frac": round(layer_bytes / (layer_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
                   "kernel_us": {k: round(v * 1e3, 2) for k, v in phase_ms.items()}, "kernel_share": shares}
+    dtype = "int8 x u4/u6 integer MMA (Q8_K activations, Q4_K/Q6_K weights), f32 scales"
+    if args.mode == "prefill":
+        # tensor bound: the routed GEMM flops (no dequant, no padding); gate/up is the dominant kernel
+        gu_flops = 2 * T * K_USED * 2 * H * I
+        layer_flops = 2 * T * K_USED * 3 * H * I
+        ach = gu_flops / (phase_ms["gate_up"] / 1e3) / 1e12
+        roofline = {"bound": "tensor", "kernel": "prefill_gateup_kernel (tcgen05, exact Q8_K x Q4_K in fp16)",
+                    "achieved": round(ach, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                    "frac": round(ach / peaks["bf16_tflops"], 4), "peak_source": peaks["source"] + ", burst bf16",
+                    "traffic": None, "algorithmic_flops_per_launch": int(gu_flops),
+                    "avg_launch_us": round(phase_ms["gate_up"] * 1e3, 2)}
+        lt = layer_flops / (layer_ms / 1e3) / 1e12
+        layer_roof = {"flops_per_layer_call": int(layer_flops), "us_per_layer_call": round(layer_ms * 1e3, 2),
+                      "achieved_tflops": round(lt, 1), "frac": round(lt / peaks["bf16_tflops"], 4),
+                      "distinct_experts_mean": round(d_mean, 2),
+                      "kernel_us": {k: round(v * 1e3, 2) for k, v in phase_ms.items()}, "kernel_share": shares}
+        dtype = ("gate/up: Q8_K int8 x Q4_K integer values carried exactly in fp16 on tcgen05 (f32 TMEM "
+                 "accumulators per super-block); down: fp16 x fp16 tcgen05")
     launches_per_call = sum(v[1] for v in prof.values()) / n_calls
     result = {
         "metric": "moe_layer_tokens_per_s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8 x u4/u6 integer MMA (Q8_K activations, Q4_K/Q6_K weights), f32 scales", "data": "synthetic",
+        "dtype": dtype, "data": "synthetic",
         "config": workload(args, world), "roofline": roofline, "layer_roofline": layer_roof,
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
                 "d2h_bytes_per_step": T * H * 4, "ms_per_step": round(e2e_ms / args.steps, 4),
@@ -314,6 +344,119 @@ def run_ours(args, rank, world, local_rank):
     if comm is not None:
         comm.close()
     return result
+
+
+def zipf_bias(torch, E_, seed, s_=1.2):
+    """A Zipf(s) bias over a seeded expert permutation: expert perm[r] gets -s * ln(r + 1)."""
+    g = np.random.default_rng(seed)
+    perm = g.permutation(E_)
+    bias = np.empty(E_, np.float32)
+    bias[perm] = -s_ * np.log(np.arange(1, E_ + 1, dtype=np.float64))
+    return torch.from_numpy(bias), perm
+
+
+def run_streamed(args, local_rank):
+    """Config 5: T tokens with router logits ~N(0,1) plus a Zipf(1.2) bias over a seeded expert
+    permutation, `--slots` of the 128 experts in device slots and all 128 in a pinned host store;
+    every step is one streamed layer step (device plan, paging of the misses over the host link,
+    chunked grouped expert products, combine).  The slot table carries over between steps, as in a
+    running model; it starts with the `--slots` most-routed experts of the bias resident."""
+    import torch
+
+    import tetraeder_b200 as tb
+    from tetraeder_b200 import moe
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    T, NS = args.tokens, args.slots
+    (rw, wts), = make_layers(torch, moe, 1, args.seed, dev)
+    store = moe.ExpertWeights(*(t.cpu().pin_memory() for t in (wts.gate, wts.up, wts.down)))
+    slots = moe.ExpertWeights(*(torch.zeros((NS,) + tuple(t.shape[1:]), dtype=torch.uint8, device=dev)
+                                for t in (wts.gate, wts.up, wts.down)))
+    del wts, rw
+    torch.cuda.synchronize()
+    bias, perm = zipf_bias(torch, E, args.seed + 5)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed + 1)
+    x = torch.randn((T, H), generator=gen, device=dev)
+    lg = torch.randn((T, E), generator=gen, device=dev) + bias.to(dev)
+    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=Q6K, max_tokens=T, device=local_rank)
+    cache = tb.SlotCache(layer, slots, store)
+    cache.make_resident([int(e) for e in perm[:NS]])
+    out = torch.empty((T, H), device=dev)
+    x_host, out_host = x.cpu().pin_memory(), torch.empty((T, H)).pin_memory()
+
+    def step():
+        layer.moe_ffn_streamed(x, cache, logits=lg, out=out)
+
+    step()
+    layer.check()
+    _, st0, _ = cache.state()
+    W = max(args.warmup, 3)
+
+    def timed(fn):
+        for _ in range(W):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    _, sa, _ = cache.state()
+    with Clocks(local_rank) as clk:
+        ms = timed(step)
+    clocks = clk.summary()
+    _, sb, _ = cache.state()
+    layer.check()
+    misses_per_step = (sb[1] - sa[1]) / (W + args.steps)
+    hits_per_step = (sb[0] - sa[0]) / (W + args.steps)
+
+    def e2e():
+        x.copy_(x_host, non_blocking=True)
+        step()
+        out_host.copy_(out, non_blocking=True)
+
+    e2e_ms = timed(e2e)
+    layer.profile(True)
+    step()
+    prof = layer.profile_collect()
+    layer.profile(False)
+    n_chunks, _, loads = cache.last_plan()
+    phase_ms = {k: v[0] for k, v in prof.items()}
+    peaks = load_peaks()
+    gu_flops = 2 * T * K_USED * 2 * H * I
+    ach = gu_flops / (phase_ms["gate_up"] / 1e3) / 1e12
+    page_bytes = sum(len(c) for c in loads) * EXPERT_BYTES
+    page_gbs = page_bytes / (phase_ms["slot_page"] / 1e3) / 1e9 if phase_ms.get("slot_page") else None
+    value = args.steps * T / (ms / 1e3)
+    res = {
+        "metric": "moe_layer_tokens_per_s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": W, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "gate/up exact Q8_K x Q4_K on tcgen05 (fp16-carried integers), down fp16 tcgen05", "data": "synthetic",
+        "config": dict(workload(args, 1), slots=NS, routing="logits ~N(0,1) + Zipf(1.2) bias over a seeded "
+                       "permutation", store="all 128 experts in pinned host memory, paged in by a copy kernel"),
+        "roofline": {"bound": "tensor", "kernel": "prefill_gateup_kernel (all chunks)", "achieved": round(ach, 1),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4),
+                     "peak_source": peaks["source"] + ", burst bf16", "traffic": None,
+                     "algorithmic_flops_per_launch": int(gu_flops), "avg_launch_us": round(phase_ms["gate_up"] * 1e3, 2)},
+        "slots": {"hits_per_step": hits_per_step, "misses_per_step": misses_per_step,
+                  "miss_bytes_per_step": int(misses_per_step * EXPERT_BYTES), "chunks_last_step": n_chunks,
+                  "page_us_last_step": round(phase_ms.get("slot_page", 0) * 1e3, 1),
+                  "host_link_gbs": round(page_gbs, 1) if page_gbs else None},
+        "kernel_us": {k: round(v * 1e3, 2) for k, v in phase_ms.items()},
+        "e2e": {"value": round(args.steps * T / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
+                "ms_per_step": round(e2e_ms / args.steps, 4), "path": "tmoe_streamed_layer C-ABI call + pinned H2D/D2H"},
+        "gpu_launches": int(sum(v[1] for v in prof.values()) * args.steps), "clocks": clocks,
+    }
+    cache.close()
+    layer.close()
+    return res
 
 
 def sweep_tokens(torch, tb, layers, dev):
@@ -466,7 +609,7 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
-    res = run_ours(args, rank, world, local_rank)
+    res = run_streamed(args, local_rank) if args.mode == "streamed" else run_ours(args, rank, world, local_rank)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(args)

@@ -19,6 +19,11 @@
  *   tmoe_ep_*         <- the EP combine b.reduce -> Executor::all_reduce -> Comm::all_reduce
  *                        crates/model/src/qwen3moe_shard.rs:1051-1056,
  *                        crates/executor/src/exec.rs:326-351, crates/ggml-sys/src/comm.rs:69-87
+ *                        (tmoe_ep_a2a_layer: the same partial sums, tokens dispatched all-to-all)
+ *   tmoe_slots_*      <- LayerSlots                     crates/memory/src/slots.rs:67-262
+ *                        and Streamer::make_resident    crates/model/src/experts.rs:1492-1543
+ *   tmoe_streamed_layer <- the streamed step's readback, plan, uploads and chunk groups
+ *                        crates/model/src/qwen3moe.rs:1829,2021-2050; experts.rs:644-662
  *
  * Conventions (the same as ggml's, so a binding passes ggml tensor data pointers through):
  *   - tensors are row-major with ne[0] fastest; an expert weight tensor is
@@ -172,6 +177,59 @@ TMOE_API int tmoe_ep_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const 
                            const int32_t *id_map, const tmoe_expert_tensors *wts, float *out, int32_t *ids_out,
                            float *w_out);
 
+/* --- expert slots and the streamed layer step --------------------------------------------------
+ * The expert-slot cache of one MoE layer (LayerSlots, crates/memory/src/slots.rs:67-262) with its
+ * table on the device, and the streamed step of `--expert-slots N < E` (qwen3moe.rs:2021-2050,
+ * Streamer::plan experts.rs:644-662, make_resident experts.rs:1507-1543).  The reference reads the
+ * ids back to the host every layer (qwen3moe.rs:1829) and plans there; here the plan (distinct
+ * experts in order of first appearance, residents first, chunks of the slot count, one LRU lookup
+ * per expert) runs in one CTA on the device, and a copy kernel pages each miss in from the host
+ * store, so the step is stream-ordered with no host round trip.
+ * `slots`: device slot tensors (n_slots = the slot count); `store`: the layer's E experts in pinned
+ * host memory (cudaHostAlloc / cudaHostRegister, i.e. device-mapped), the same row layout
+ * (nb1) as the slots.  The cache keeps both pointers; neither is copied.  One cache per layer;
+ * calls on a cache are stream-ordered like the handle's. */
+typedef struct tmoe_slots tmoe_slots;
+TMOE_API int tmoe_slots_create(tmoe_handle *h, const tmoe_expert_tensors *slots, const tmoe_expert_tensors *store,
+                               tmoe_slots **out);
+TMOE_API void tmoe_slots_destroy(tmoe_slots *s);
+/* Chunk passes of a streamed step: ceil(E / slot count). */
+TMOE_API int tmoe_slots_max_chunks(const tmoe_slots *s);
+/* make_resident (experts.rs:1492): looks up the n (<= slot count) listed experts (host array) in
+ * order and pages their misses in.  A lookup that finds every slot pinned sets the device error
+ * (tmoe_check: TMOE_E_INVALID, "no free expert slot (all pinned)"). */
+TMOE_API int tmoe_slots_make_resident(tmoe_slots *s, void *stream, const int32_t *experts, int32_t n);
+/* set_hot_set (slots.rs:189-207) then make_resident of the pinned experts that are not resident,
+ * in increasing id (refresh_hot_set, experts.rs:1549-1566).  Synchronises `stream`. */
+TMOE_API int tmoe_slots_set_hot_set(tmoe_slots *s, void *stream, const int32_t *hot, int32_t n);
+/* Synchronising reads: owner[slot count] (expert per slot, -1 free), stats[3] = hits, misses,
+ * bypasses, counts[E] = routed pairs per expert since creation; any may be NULL. */
+TMOE_API int tmoe_slots_state(tmoe_slots *s, void *stream, int32_t *owner, int64_t *stats, int64_t *counts);
+/* Synchronising read of the last step's plan: n_chunks; map int32 [max_chunks][E] (slot of each
+ * expert of the chunk, -1 others); loads int32 [max_chunks][slot count][2] (expert, slot) of each
+ * chunk's misses; n_loads [max_chunks]; any may be NULL. */
+TMOE_API int tmoe_slots_last_plan(tmoe_slots *s, void *stream, int32_t *n_chunks, int32_t *map, int32_t *loads,
+                                  int32_t *n_loads);
+/* The streamed layer step: tmoe_route, the device plan, then per chunk: page its misses in, compute
+ * its pairs from the slot tensors (dout rows of the chunk's pairs), and finally one combine of all
+ * pairs in choice order -- the same per-pair arithmetic as tmoe_layer on resident experts. */
+TMOE_API int tmoe_streamed_layer(tmoe_handle *h, void *stream, tmoe_slots *s, const float *x, int64_t T,
+                                 int32_t use_norm, const float *norm_w, const float *router_w, const float *logits,
+                                 float *out, int32_t *ids_out, float *w_out);
+
+/* Expert parallelism with token dispatch/combine over an all-to-all (the survey's mode B), for
+ * ranks that hold different tokens: rank r holds experts [r*E/g, (r+1)*E/g) in `wts` (n_slots =
+ * E/g) and its own T tokens (T <= max_tokens / g; create the handle with max_tokens = g x the
+ * tokens per rank, since it computes the rows the other ranks send).  Each token is sent once to
+ * every rank that holds one of its choices; that rank computes its experts' pairs and combines
+ * them in choice order (the reference's per-rank partial, qwen3moe_shard.rs:1043-1056), sends the
+ * partial row back, and the token's rank adds the partials in rank order.  Messages have a fixed
+ * capacity of max_tokens / g rows per peer (no host readback).  Every rank must make the same
+ * calls in the same order; a rank whose routing fails still takes both exchange steps. */
+TMOE_API int tmoe_ep_a2a_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float *x, int64_t T,
+                               int32_t use_norm, const float *norm_w, const float *router_w, const float *logits,
+                               const tmoe_expert_tensors *wts, float *out, int32_t *ids_out, float *w_out);
+
 /* ids' = table[ids] for ids in [0, n_table), else -1 (the EP expert_map lookup). */
 TMOE_API int tmoe_map_ids(tmoe_handle *h, void *stream, const int32_t *ids, int64_t n,
                  const int32_t *table, int64_t n_table, int32_t *out);
@@ -208,7 +266,9 @@ TMOE_API int tmoe_dequantize(int32_t type, const void *in, int64_t n, float *out
 #define TMOE_PHASE_QUANT_ACT 7
 #define TMOE_PHASE_DOWN 8
 #define TMOE_PHASE_COMBINE 9
-#define TMOE_N_PHASES 10
+#define TMOE_PHASE_SLOT_PLAN 10 /* the device slot planner of tmoe_streamed_layer */
+#define TMOE_PHASE_SLOT_PAGE 11 /* paging misses in from the host store */
+#define TMOE_N_PHASES 12
 TMOE_API int tmoe_profile_enable(tmoe_handle *h, int32_t enable);
 TMOE_API int tmoe_profile_collect(tmoe_handle *h, double *ms_out, int64_t *count_out);
 

@@ -76,3 +76,60 @@ def test_ep_layer_two_ranks_equals_one(shape):
         assert np.array_equal(ids, want_ids), f"rank {rank}: routing differs"
         n, m = nrms(out, want), maxabs_over_rms(out, want)
         assert n <= 1e-3 and m <= 1e-2, f"rank {rank}: nrms={n:.2e} maxabs/rms={m:.2e}"
+
+
+def _rank_a2a(rank, world, uid, shape, q):
+    import tetraeder_b200 as tb
+    from tetraeder_b200 import moe
+    H, I, E, k, T, seed = shape  # T: tokens per rank
+    torch.cuda.set_device(rank)
+    gate, up, down, rw, x = _case(H, I, E, world * T, seed)
+    per = E // world
+    sl = slice(rank * per, (rank + 1) * per)
+    cu = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    layer = tb.MoeLayer(H, I, E, k, gate_type=O.TYPE_Q4_K, up_type=O.TYPE_Q4_K, down_type=O.TYPE_Q6_K,
+                        max_tokens=world * T, device=rank)
+    comm = moe.EPComm(uid, world, rank, device=rank, timeout_s=120.0)
+    try:
+        wts = moe.ExpertWeights(cu(gate[sl]), cu(up[sl]), cu(down[sl]))
+        xs = cu(x[rank * T:(rank + 1) * T])
+        ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+        out = moe.ep_a2a_moe_ffn(layer, comm, xs, wts, router_w=cu(rw), ids_out=ids)
+        for _ in range(2):  # again: the exchange buffers are reused between calls
+            out = moe.ep_a2a_moe_ffn(layer, comm, xs, wts, router_w=cu(rw), ids_out=ids, out=out)
+        torch.cuda.synchronize()
+        layer.check()
+        q.put((rank, out.cpu().numpy(), ids.cpu().numpy()))
+    finally:
+        comm.close()
+        layer.close()
+
+
+@needs_two
+@pytest.mark.parametrize("shape", [(512, 256, 16, 4, 32, 7), (2048, 768, 128, 8, 64, 8), (512, 256, 16, 4, 512, 9)],
+                         ids=["tiny", "30B decode", "tiny large-batch"])
+def test_ep_a2a_two_ranks_equal_the_one_rank_layer(shape):
+    """Mode B: each rank holds half of the tokens of a global batch and half of the experts; the
+    tokens of each rank must come out as the one-rank oracle layer computes them."""
+    from tetraeder_b200 import moe
+    H, I, E, k, T, seed = shape
+    world = 2
+    uid = moe.EPComm.unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_a2a, args=(r, world, uid, shape, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    gate, up, down, rw, x = _case(H, I, E, world * T, seed)
+    want, want_ids, _ = O.layer(x, k, gate, up, down, H, I, E, router_w=rw, gate_type=O.TYPE_Q4_K,
+                                up_type=O.TYPE_Q4_K, down_type=O.TYPE_Q6_K)
+    for rank, out, ids in res:
+        rows = slice(rank * T, (rank + 1) * T)
+        assert np.array_equal(ids, want_ids[rows]), f"rank {rank}: routing differs"
+        n, m = nrms(out, want[rows]), maxabs_over_rms(out, want[rows])
+        bound = (1e-3, 2.5e-2) if T * world * k >= 4096 else (1e-3, 1e-2)
+        assert n <= bound[0] and m <= bound[1], f"rank {rank}: nrms={n:.2e} maxabs/rms={m:.2e}"

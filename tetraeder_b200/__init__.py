@@ -3,11 +3,12 @@ router -> token-to-expert dispatch -> Q4_K/Q6_K SwiGLU expert products -> weight
 behind the C ABI of include/tmoe.h (libtmoe.so, built from csrc/ by build.py)."""
 from ._lib import TYPE_Q4_K, TYPE_Q6_K, TmoeError, header_symbols, load  # noqa: F401
 
-__all__ = ["TYPE_Q4_K", "TYPE_Q6_K", "TmoeError", "header_symbols", "load", "MoeLayer", "ExpertWeights"]
+__all__ = ["TYPE_Q4_K", "TYPE_Q6_K", "TmoeError", "header_symbols", "load", "MoeLayer", "ExpertWeights",
+           "SlotCache"]
 
 
 def __getattr__(name):
-    if name in ("MoeLayer", "ExpertWeights", "row_size"):
+    if name in ("MoeLayer", "ExpertWeights", "SlotCache", "row_size"):
         from . import moe
         return getattr(moe, name)
     raise AttributeError(name)

@@ -64,10 +64,19 @@ SIGNATURES = {
     "tmoe_comm_destroy": ([P], None),
     "tmoe_comm_last_error": ([], C.c_char_p),
     "tmoe_ep_layer": ([P, P, P, P, I64, I32, P, P, P, P, C.POINTER(ExpertTensors), P, P, P], C.c_int),
+    "tmoe_ep_a2a_layer": ([P, P, P, P, I64, I32, P, P, P, C.POINTER(ExpertTensors), P, P, P], C.c_int),
+    "tmoe_slots_create": ([P, C.POINTER(ExpertTensors), C.POINTER(ExpertTensors), C.POINTER(C.c_void_p)], C.c_int),
+    "tmoe_slots_destroy": ([P], None),
+    "tmoe_slots_max_chunks": ([P], C.c_int),
+    "tmoe_slots_make_resident": ([P, P, P, I32], C.c_int),
+    "tmoe_slots_set_hot_set": ([P, P, P, I32], C.c_int),
+    "tmoe_slots_state": ([P, P, P, P, P], C.c_int),
+    "tmoe_slots_last_plan": ([P, P, P, P, P, P], C.c_int),
+    "tmoe_streamed_layer": ([P, P, P, P, I64, I32, P, P, P, P, P, P], C.c_int),
 }
 COMM_ID_BYTES = 128
 PHASES = ["rms_norm", "router_logits", "topk", "map_ids", "dispatch", "quant_x", "gate_up", "quant_act",
-          "down", "combine"]
+          "down", "combine", "slot_plan", "slot_page"]
 
 _lib = None
 

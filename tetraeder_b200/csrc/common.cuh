@@ -11,6 +11,7 @@
 // Device error codes latched in tmoe_handle's flag word (first error wins).
 #define TMOE_DEV_ERR_TIMEOUT 1
 #define TMOE_DEV_ERR_BADID 2
+#define TMOE_DEV_ERR_NOSLOT 3  // every expert slot is pinned: a miss has nowhere to go
 
 // A bounded wait gives up after this many nanoseconds of %globaltimer.
 #define TMOE_WAIT_LIMIT_NS 1000000000ull

@@ -60,6 +60,50 @@ int ep_allreduce_sum(tmoe_comm *c, float *buf, size_t n, cudaStream_t st, char *
     return TMOE_OK;
 }
 
+int ep_comm_ranks(const tmoe_comm *c, int *rank) {
+    if (rank) *rank = c->rank;
+    return c->nranks;
+}
+
+// All-to-all of fixed-size blocks: block p of every buffer's `send` goes to rank p, whose block
+// `rank` of `recv` receives it.  The local block is a device copy; the others are one NCCL group
+// of sends and receives, so the exchange is one collective step for the ranks.
+int ep_alltoall(tmoe_comm *c, const EpBuf *bufs, int nbufs, cudaStream_t st, char *msg, size_t msg_len) {
+    if (!c->comm) {
+        snprintf(msg, msg_len, "the communicator was aborted");
+        return TMOE_E_COMM;
+    }
+    for (int b = 0; b < nbufs; b++) {
+        const size_t n = bufs[b].bytes_per_peer;
+        const cudaError_t e = cudaMemcpyAsync((char *)bufs[b].recv + (size_t)c->rank * n,
+                                              (const char *)bufs[b].send + (size_t)c->rank * n, n,
+                                              cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) {
+            snprintf(msg, msg_len, "local block copy: %s", cudaGetErrorString(e));
+            return TMOE_E_CUDA;
+        }
+    }
+    ncclResult_t r = ncclGroupStart();
+    for (int b = 0; b < nbufs && (r == ncclSuccess || r == ncclInProgress); b++) {
+        const size_t n = bufs[b].bytes_per_peer;
+        for (int p = 0; p < c->nranks; p++) {
+            if (p == c->rank) continue;
+            r = ncclSend((const char *)bufs[b].send + (size_t)p * n, n, ncclUint8, p, c->comm, st);
+            if (r != ncclSuccess && r != ncclInProgress) break;
+            r = ncclRecv((char *)bufs[b].recv + (size_t)p * n, n, ncclUint8, p, c->comm, st);
+            if (r != ncclSuccess && r != ncclInProgress) break;
+        }
+    }
+    const ncclResult_t re = ncclGroupEnd();
+    if (r == ncclSuccess || r == ncclInProgress) r = re;
+    if (r == ncclInProgress) r = nccl_wait(c);
+    if (r != ncclSuccess) {
+        snprintf(msg, msg_len, "all-to-all: %s", ncclGetErrorString(r));
+        return TMOE_E_COMM;
+    }
+    return TMOE_OK;
+}
+
 }  // namespace tmoe
 
 namespace {

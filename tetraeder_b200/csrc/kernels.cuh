@@ -17,6 +17,19 @@ namespace tmoe {
 // TMOE_E_COMM with a message.
 int ep_allreduce_sum(tmoe_comm *c, float *buf, size_t n, cudaStream_t st, char *msg, size_t msg_len);
 int ep_comm_device(const tmoe_comm *c);
+int ep_comm_ranks(const tmoe_comm *c, int *rank);
+struct EpBuf {
+    const void *send;  // [nranks][bytes_per_peer]
+    void *recv;        // [nranks][bytes_per_peer]
+    size_t bytes_per_peer;
+};
+int ep_alltoall(tmoe_comm *c, const EpBuf *bufs, int nbufs, cudaStream_t st, char *msg, size_t msg_len);
+// ep_a2a.cu: the token dispatch and combine of the all-to-all mode (see ep_a2a.cu)
+cudaError_t launch_ep_pack(const int32_t *ids, const float *w, const float *x, int T, int k, int H, int per, int g,
+                           int cap, int32_t *row_of, int32_t *s_ids, float *s_w, int32_t *s_tok, int32_t *counts,
+                           float *s_x, cudaStream_t st);
+cudaError_t launch_ep_combine(const float *ret, const int32_t *row_of, int T, int H, int g, int cap, float *out,
+                              cudaStream_t st);
 
 // Q8_K rows as the expert GEMV reads them: qs int8 [rows][K], d f32 [rows][K/256], and per
 // super-block the activation sums over the weight type's sub-blocks (32 elements for Q4_K, 16 for
@@ -33,10 +46,10 @@ inline int q8_nbw(int wt) { return wt == TMOE_WT_Q4K ? 2 : 4; }
 // route.cu
 cudaError_t launch_rms_norm(const float *x, const float *norm_w, float eps, int64_t T, int H, float *out,
                             cudaStream_t st);
-// The router logits; with q8 (non-NULL, router_fuses_q8(H)) also the Q8_K rows of xn.
+// The router logits; with q8 (non-NULL, router_fuses_q8(H, T)) also the Q8_K rows of xn.
 cudaError_t launch_router_logits(const float *xn, const float *rw, int64_t T, int H, int E, float *logits,
-                                 const Q8Rows *q8, cudaStream_t st);
-bool router_fuses_q8(int H);
+                                 const Q8Rows *q8, int *err, cudaStream_t st);
+bool router_fuses_q8(int H, int64_t T);
 cudaError_t launch_softmax_topk(const float *logits, int64_t T, int E, int k, int32_t *ids, float *w, float *probs,
                                 cudaStream_t st);
 // Q8_K of rows of K f32; rows whose valid entry is negative are skipped (valid may be NULL).
@@ -126,6 +139,33 @@ cudaError_t launch_prefill_gateup(const __half *aq, const float *ad, const __hal
                                   const uint8_t *gate, const uint8_t *up, size_t nb1, size_t nb2_gate,
                                   size_t nb2_up, const int4 *active, const int32_t *n_active, int max_active,
                                   int *tile_start, float *act, int *err, int sm_count, cudaStream_t st);
+
+// slots.cu: the expert-slot cache of one layer on the device (see slots.cu)
+struct SlotsDev {
+    int n_expert, max_slots, max_chunks;
+    int32_t *owner;               // [max_slots] expert in the slot, -1 free
+    unsigned long long *stamp;    // [max_slots] LRU stamps
+    int32_t *slot_of;             // [n_expert] slot of a resident expert, -1 otherwise
+    uint8_t *pinned;              // [n_expert]
+    int32_t *active;              // [1] slots in use
+    unsigned long long *meta;     // [4] clock, hits, misses, bypasses
+    unsigned long long *counts;   // [n_expert] routed pairs since creation
+    int32_t *n_chunks;            // [1] chunks of the last step
+    int32_t *map;                 // [max_chunks][n_expert] slot of the chunk's experts, -1 others
+    int2 *loads;                  // [max_chunks][max_slots] (expert, slot) of the chunk's misses
+    int32_t *n_loads;             // [max_chunks]
+};
+struct SlotCopy {  // gate, up, down: the host store (mapped device addresses) and the slot tensors
+    const uint8_t *src[3];
+    size_t src_nb2[3];
+    uint8_t *dst[3];
+    size_t dst_nb2[3];
+    size_t bytes[3];  // bytes of one expert's matrix, a multiple of 16
+};
+bool slots_fit(int n_expert, int max_slots);
+cudaError_t launch_slot_plan(const int32_t *ids, int n_pairs, const SlotsDev &s, int *err, cudaStream_t st);
+cudaError_t launch_slot_lookup_list(const int32_t *list, int n, const SlotsDev &s, int *err, cudaStream_t st);
+cudaError_t launch_slot_page(const SlotsDev &s, int chunk, const SlotCopy &cp, int sm_count, cudaStream_t st);
 
 // Rows per work item of the GEMV for K columns and N rows per expert; 0 if N does not fit.
 int gemv_rows_per_item(int wt, int K, int N);

@@ -138,58 +138,78 @@ __global__ void prep_rows_kernel(const float *__restrict__ src, const int32_t *_
 }
 
 // fp16 copies of the active experts' rows: dst[e][row][K] for the experts of `active` (others are
-// left alone).  One thread per 32-element chunk.
-__global__ void dequant_f16_kernel(int wt, const uint8_t *__restrict__ w, size_t nb2, int N, int K,
-                                   const int4 *__restrict__ active, const int32_t *__restrict__ n_active,
-                                   int max_active, __half *__restrict__ dst) {
-    const int na = min(n_active[0], max_active);
+// left alone).  A CTA takes DQ_ROWS consecutive rows of one active expert: the rows' bytes (contiguous
+// in the ggml layout) are staged in shared memory with 16-byte loads, then each warp dequantises one
+// super-block at a time, lane t the 8 consecutive elements 8t..8t+7 (one 16-byte store), whose Q4_K
+// quants are 8 consecutive bytes of one 32-byte run and whose Q6_K low/high quants are 8 consecutive
+// bytes of ql and of qh.  Values: Q4_K fp16((d*sc)*q - dmin*m), Q6_K fp16((d*sc)*(q - 32)).
+constexpr int DQ_ROWS = 16;
+
+__device__ __forceinline__ uint2 lds_u64_a2(const uint8_t *p) {
+    return make_uint2(lds_u32_a2(p), lds_u32_a2(p + 4));
+}
+
+template <int WT>
+__global__ void __launch_bounds__(256) dequant_f16_kernel(const uint8_t *__restrict__ w, size_t nb2, int N, int K,
+                                                          const int4 *__restrict__ active,
+                                                          const int32_t *__restrict__ n_active, int max_active,
+                                                          __half *__restrict__ dst) {
+    extern __shared__ __align__(16) uint8_t dq_rows[];
+    const int ai = blockIdx.y;
+    if (ai >= min(n_active[0], max_active)) return;
+    constexpr int BB = WT == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES;
     const int nb = K / TMOE_QK;
-    const int64_t per_expert = (int64_t)N * nb * 8;
-    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= per_expert * na) return;
-    const int ai = (int)(g / per_expert);
-    const int64_t l = g % per_expert;
+    const int row_bytes = nb * BB;
     const int e = active[ai].x;
-    const int row = (int)(l / (nb * 8));
-    const int b = (int)(l / 8 % nb), c = (int)(l % 8);
-    __half *o = dst + ((int64_t)e * N + row) * K + b * TMOE_QK + 32 * c;
-    const size_t row_bytes = (size_t)nb * (wt == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES);
-    const uint8_t *rw = w + (size_t)e * nb2 + (size_t)row * row_bytes;
-    __align__(16) __half h[32];
-    if (wt == TMOE_WT_Q4K) {
-        const uint8_t *blk = rw + (size_t)b * TMOE_Q4K_BYTES;
-        const float d = h2f((uint16_t)(blk[0] | (blk[1] << 8))), dmin = h2f((uint16_t)(blk[2] | (blk[3] << 8)));
-        const uint8_t *sc = blk + 4;
-        int scale, mn;
-        if (c < 4) {
-            scale = sc[c] & 63;
-            mn = sc[c + 4] & 63;
+    const int row0 = blockIdx.x * DQ_ROWS, nr = min(DQ_ROWS, N - row0);
+    const uint4 *src = reinterpret_cast<const uint4 *>(w + (size_t)e * nb2 + (size_t)row0 * row_bytes);
+    const int n16 = (nr * row_bytes) >> 4;  // nr * row_bytes % 16 == 0 (checked by the launcher)
+    for (int i = threadIdx.x; i < n16; i += blockDim.x)
+        reinterpret_cast<uint4 *>(dq_rows)[i] = __ldg(src + i);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int u = warp; u < nr * nb; u += blockDim.x >> 5) {
+        const int r = u / nb, b = u - r * nb;
+        const uint8_t *blk = dq_rows + r * row_bytes + b * BB;
+        __align__(16) __half h[8];
+        if constexpr (WT == TMOE_WT_Q4K) {
+            const int c = lane >> 2;  // sub-block of 32
+            const float d = h2f(*reinterpret_cast<const uint16_t *>(blk)),
+                        dmin = h2f(*reinterpret_cast<const uint16_t *>(blk + 2));
+            const uint8_t *sc = blk + 4;
+            int scale, mn;
+            if (c < 4) {
+                scale = sc[c] & 63;
+                mn = sc[c + 4] & 63;
+            } else {
+                scale = (sc[c + 4] & 0x0f) | ((sc[c - 4] >> 6) << 4);
+                mn = (sc[c + 4] >> 4) | ((sc[c] >> 6) << 4);
+            }
+            const float d1 = __fmul_rn(d, (float)scale), m1 = __fmul_rn(dmin, (float)mn);
+            const uint2 q = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * (c >> 1) + 8 * (lane & 3));
+            const int sh = (c & 1) * 4;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int v = (((i < 4 ? q.x : q.y) >> (8 * (i & 3) + sh)) & 0x0f);
+                h[i] = __float2half_rn(__fsub_rn(__fmul_rn(d1, (float)v), m1));
+            }
         } else {
-            scale = (sc[c + 4] & 0x0f) | ((sc[c - 4] >> 6) << 4);
-            mn = (sc[c + 4] >> 4) | ((sc[c] >> 6) << 4);
-        }
-        const float d1 = __fmul_rn(d, (float)scale), m1 = __fmul_rn(dmin, (float)mn);
-        const uint8_t *qs = blk + 16 + 32 * (c / 2);
+            const int hh = lane >> 4, rr = 8 * (lane & 15);  // element k = 128 hh + rr + i
+            const uint2 lo = lds_u64_a2(blk + 64 * hh + (rr & 63));
+            const uint2 hi = lds_u64_a2(blk + 128 + 32 * hh + (rr & 31));
+            const int lsh = rr < 64 ? 0 : 4, hsh = 2 * (rr >> 5);
+            const float d = h2f((uint16_t)(blk[208] | (blk[209] << 8)));
+            const float ds = __fmul_rn(d, (float)reinterpret_cast<const int8_t *>(blk + 192)[(128 * hh + rr) >> 4]);
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-            const int q = (c & 1) ? (qs[i] >> 4) : (qs[i] & 0x0f);
-            h[i] = __float2half_rn(__fsub_rn(__fmul_rn(d1, (float)q), m1));
+            for (int i = 0; i < 8; i++) {
+                const uint32_t lw = i < 4 ? lo.x : lo.y, hw = i < 4 ? hi.x : hi.y;
+                const int q = (int)((lw >> (8 * (i & 3) + lsh)) & 0x0f) | (int)(((hw >> (8 * (i & 3) + hsh)) & 3) << 4);
+                h[i] = __float2half_rn(__fmul_rn(ds, (float)(q - 32)));
+            }
         }
-    } else {
-        const uint8_t *blk = rw + (size_t)b * TMOE_Q6K_BYTES;
-        const uint8_t *ql = blk, *qh = blk + 128;
-        const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192);
-        const float d = h2f((uint16_t)(blk[208] | (blk[209] << 8)));
-#pragma unroll 4
-        for (int i = 0; i < 32; i++) {
-            const int k = 32 * c + i, hh = k / 128, rr = k % 128;
-            const int lo = rr < 64 ? (ql[64 * hh + rr] & 0x0f) : (ql[64 * hh + rr - 64] >> 4);
-            const int hi = (qh[32 * hh + (rr % 32)] >> (2 * (rr / 32))) & 3;
-            h[i] = __float2half_rn(__fmul_rn(__fmul_rn(d, (float)sc[k / 16]), (float)((lo | (hi << 4)) - 32)));
-        }
+        *reinterpret_cast<uint4 *>(dst + ((int64_t)e * N + row0 + r) * K + b * TMOE_QK + 8 * lane) =
+            *reinterpret_cast<const uint4 *>(h);
     }
-#pragma unroll
-    for (int i = 0; i < 4; i++) reinterpret_cast<uint4 *>(o)[i] = reinterpret_cast<const uint4 *>(h)[i];
 }
 
 // tile_start[a] = sum over the active experts before a of ceil(rows / 128) * n_tiles_n;
@@ -925,10 +945,20 @@ cudaError_t launch_prep_rows(const float *src, const int32_t *perm, int n_rows, 
 
 cudaError_t launch_dequant_f16(int wt, const uint8_t *w, size_t nb2, int N, int K, const int4 *active,
                                const int32_t *n_active, int max_active, __half *dst, cudaStream_t st) {
-    const int64_t threads = (int64_t)max_active * N * (K / TMOE_QK) * 8;
-    if (threads <= 0) return cudaSuccess;
-    dequant_f16_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(wt, w, nb2, N, K, active, n_active,
-                                                                          max_active, dst);
+    if (max_active <= 0 || N <= 0) return cudaSuccess;
+    const size_t row_bytes = (size_t)(K / TMOE_QK) * (wt == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES);
+    const size_t smem = DQ_ROWS * row_bytes;
+    // 16-byte staging: the expert slabs and every DQ_ROWS-row run start on a 16-byte boundary
+    if ((reinterpret_cast<uintptr_t>(w) & 15) || (nb2 & 15) || (smem & 15) || (N % DQ_ROWS && (row_bytes & 15)) ||
+        smem > 200 * 1024 || max_active > 65535)
+        return cudaErrorInvalidValue;
+    const dim3 grid((unsigned)((N + DQ_ROWS - 1) / DQ_ROWS), (unsigned)max_active);
+    auto kern = wt == TMOE_WT_Q4K ? dequant_f16_kernel<TMOE_WT_Q4K> : dequant_f16_kernel<TMOE_WT_Q6K>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    kern<<<grid, 256, smem, st>>>(w, nb2, N, K, active, n_active, max_active, dst);
     return cudaGetLastError();
 }
 

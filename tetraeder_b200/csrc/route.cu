@@ -99,6 +99,113 @@ __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_kernel(const floa
     }
 }
 
+// Router logits for many tokens (H % 256 == 0): a CTA of 8 warps owns 32 tokens x 16 experts and
+// streams K in chunks of 256 columns through a ring of RT_STAGES shared-memory stages (one bulk copy
+// per 1 KB row chunk).  A warp holds 8 tokens x 8 experts; lane l keeps the canonical partial sums
+// of slice l for all 64 logits in registers (the same fma chain as router_logits_kernel), so every
+// shared-memory load feeds 32 FMAs.  The 32 partials of a logit are then summed over the lanes in
+// the butterfly's tree (pairs at lane distance 16, 8, 4, 2, 1), transposed so that 32 logits take
+// 31 shuffles instead of 160: bit-identical to butterfly_f32 since each add has the same operands.
+constexpr int RT_TOK = 32, RT_EXP = 16, RT_KC = 256, RT_STAGES = 4;
+constexpr int RT_STAGE_FLOATS = (RT_TOK + RT_EXP) * RT_KC;
+constexpr size_t RT_SMEM = (size_t)RT_STAGES * RT_STAGE_FLOATS * 4;
+
+__device__ __forceinline__ float transposed_butterfly(float (&v)[32], int lane) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const bool up = (lane & off) != 0;
+#pragma unroll
+        for (int j = 0; j < off; j++) {
+            const float send = up ? v[j] : v[j + off];
+            const float keep = up ? v[j + off] : v[j];
+            v[j] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, off));
+        }
+    }
+    return v[0];  // the logit of index `lane`
+}
+
+__global__ void __launch_bounds__(256, 1) router_logits_tiled_kernel(const float *__restrict__ xn,
+                                                                     const float *__restrict__ rw, int64_t T, int H,
+                                                                     int E, float *__restrict__ logits, int *err) {
+    extern __shared__ __align__(128) float rt_smem[];  // [RT_STAGES][32 token rows + 16 expert rows][RT_KC]
+    __shared__ __align__(8) uint64_t full[RT_STAGES];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t t0 = (int64_t)blockIdx.y * RT_TOK;  // the expert tiles of a token tile run together:
+    const int e0 = blockIdx.x * RT_EXP;                // the tile's rows of xn are read from HBM once
+    const int nt = (int)min((int64_t)RT_TOK, T - t0), ne = min(RT_EXP, E - e0);
+    const int n_ch = H / RT_KC;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < RT_STAGES; s++) mbar_init(&full[s], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    auto issue = [&](int c) {  // warp 0: chunk c into stage c % RT_STAGES
+        float *st = rt_smem + (c % RT_STAGES) * RT_STAGE_FLOATS;
+        if (lane == 0) mbar_arrive_expect_tx(&full[c % RT_STAGES], (uint32_t)(nt + ne) * RT_KC * 4);
+        __syncwarp();
+        const int64_t col = (int64_t)c * RT_KC;
+        if (lane < nt) bulk_g2s(st + lane * RT_KC, xn + (t0 + lane) * H + col, RT_KC * 4, &full[c % RT_STAGES]);
+        if (lane < ne)
+            bulk_g2s(st + (RT_TOK + lane) * RT_KC, rw + (int64_t)(e0 + lane) * H + col, RT_KC * 4,
+                     &full[c % RT_STAGES]);
+    };
+    if (warp == 0)
+        for (int c = 0; c < RT_STAGES && c < n_ch; c++) issue(c);
+    const int wt = warp & 3, we = warp >> 2;
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+    for (int c = 0; c < n_ch; c++) {
+        const int s = c % RT_STAGES;
+        const bool ok = mbar_wait_bounded(&full[s], (uint32_t)(c / RT_STAGES) & 1u);
+        if (__syncthreads_or(!ok)) {  // every thread leaves together
+            if (threadIdx.x == 0) latch_error(err, TMOE_DEV_ERR_TIMEOUT);
+            return;
+        }
+        const float4 *xs = reinterpret_cast<const float4 *>(rt_smem + s * RT_STAGE_FLOATS) + wt * 8 * (RT_KC / 4);
+        const float4 *ws =
+            reinterpret_cast<const float4 *>(rt_smem + s * RT_STAGE_FLOATS + RT_TOK * RT_KC) + we * 8 * (RT_KC / 4);
+#pragma unroll
+        for (int ms = 0; ms < RT_KC / 128; ms++) {
+            float4 wv[8], xv[8];
+#pragma unroll
+            for (int ee = 0; ee < 8; ee++) wv[ee] = ws[ee * (RT_KC / 4) + ms * 32 + lane];
+#pragma unroll
+            for (int tt = 0; tt < 8; tt++) xv[tt] = xs[tt * (RT_KC / 4) + ms * 32 + lane];
+            // element order per accumulator: .x, .y, .z, .w; consecutive FMAs are independent
+#pragma unroll
+            for (int tt = 0; tt < 8; tt++)
+#pragma unroll
+                for (int ee = 0; ee < 8; ee++) acc[tt][ee] = __fmaf_rn(wv[ee].x, xv[tt].x, acc[tt][ee]);
+#pragma unroll
+            for (int tt = 0; tt < 8; tt++)
+#pragma unroll
+                for (int ee = 0; ee < 8; ee++) acc[tt][ee] = __fmaf_rn(wv[ee].y, xv[tt].y, acc[tt][ee]);
+#pragma unroll
+            for (int tt = 0; tt < 8; tt++)
+#pragma unroll
+                for (int ee = 0; ee < 8; ee++) acc[tt][ee] = __fmaf_rn(wv[ee].z, xv[tt].z, acc[tt][ee]);
+#pragma unroll
+            for (int tt = 0; tt < 8; tt++)
+#pragma unroll
+                for (int ee = 0; ee < 8; ee++) acc[tt][ee] = __fmaf_rn(wv[ee].w, xv[tt].w, acc[tt][ee]);
+        }
+        __syncthreads();  // stage s is free again
+        if (warp == 0 && c + RT_STAGES < n_ch) issue(c + RT_STAGES);
+    }
+#pragma unroll
+    for (int g = 0; g < 2; g++) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = acc[4 * g + j / 8][j % 8];
+        const float s = transposed_butterfly(v, lane);
+        const int tt = wt * 8 + 4 * g + lane / 8, ee = we * 8 + lane % 8;
+        if (tt < nt && ee < ne) logits[(t0 + tt) * E + e0 + ee] = s;
+    }
+}
+
 // Router logits for any H: one warp per (expert, token), scalar loads in the canonical order.
 __global__ void router_logits_generic_kernel(const float *__restrict__ xn, const float *__restrict__ rw, int64_t T,
                                              int H, int E, float *__restrict__ logits) {
@@ -164,9 +271,27 @@ cudaError_t launch_rms_norm(const float *x, const float *norm_w, float eps, int6
     return cudaGetLastError();
 }
 
+static bool router_tiled(int64_t T, int H) { return T >= 1024 && H % RT_KC == 0; }
+
 cudaError_t launch_router_logits(const float *xn, const float *rw, int64_t T, int H, int E, float *logits,
-                                 const Q8Rows *q8, cudaStream_t st) {
+                                 const Q8Rows *q8, int *err, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
+    if (!q8 && router_tiled(T, H) && ((uintptr_t)xn & 15) == 0 && ((uintptr_t)rw & 15) == 0) {
+        static int set_tiled[64] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+        if (!set_tiled[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(router_logits_tiled_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RT_SMEM);
+            if (e != cudaSuccess) return e;
+            set_tiled[dev] = 1;
+        }
+        dim3 grid((unsigned)((E + RT_EXP - 1) / RT_EXP), (unsigned)((T + RT_TOK - 1) / RT_TOK));
+        if (grid.y > 65535) return cudaErrorInvalidValue;
+        router_logits_tiled_kernel<<<grid, 256, RT_SMEM, st>>>(xn, rw, T, H, E, logits, err);
+        return cudaGetLastError();
+    }
     constexpr int TT = 8;
     const size_t smem = (size_t)TT * H * 4;
     if (H % 512 == 0 && smem <= 200 * 1024) {
@@ -191,7 +316,9 @@ cudaError_t launch_router_logits(const float *xn, const float *rw, int64_t T, in
     return cudaGetLastError();
 }
 
-bool router_fuses_q8(int H) { return H % 512 == 0 && (size_t)8 * H * 4 <= 200 * 1024; }
+bool router_fuses_q8(int H, int64_t T) {
+    return !router_tiled(T, H) && H % 512 == 0 && (size_t)8 * H * 4 <= 200 * 1024;
+}
 
 cudaError_t launch_softmax_topk(const float *logits, int64_t T, int E, int k, int32_t *ids, float *w, float *probs,
                                 cudaStream_t st) {

@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "../../include/tmoe.h"
 #include "common.cuh"
@@ -54,6 +55,13 @@ struct tmoe_handle {
     int *counters = nullptr;    // GEMV work counters
     int *route_done = nullptr;  // the fused routing kernel's tile counters (zero between calls)
     int *err = nullptr;
+    // exchange buffers of the all-to-all EP mode (allocated on its first call; see tmoe_ep_a2a_layer)
+    struct A2A {
+        void *mem = nullptr;
+        int g = 0, cap = 0;
+        int32_t *row_of = nullptr, *s_ids = nullptr, *r_ids = nullptr, *s_tok = nullptr, *counts = nullptr;
+        float *s_w = nullptr, *r_w = nullptr, *s_x = nullptr, *r_x = nullptr, *part = nullptr, *ret = nullptr;
+    } a2a;
     // growable scratch of tmoe_mul_mat_id
     void *op_ws = nullptr;
     size_t op_ws_bytes = 0;
@@ -68,6 +76,16 @@ struct tmoe_handle {
         double ms[TMOE_N_PHASES] = {};
         int64_t count[TMOE_N_PHASES] = {};
     } prof;
+};
+
+struct tmoe_slots {
+    tmoe_handle *h = nullptr;
+    tmoe::SlotsDev dev{};
+    tmoe::SlotCopy copy{};
+    tmoe_expert_tensors slot_wts{};
+    void *mem = nullptr;
+    int32_t *list = nullptr;  // device copy of a make_resident list
+    int active = 0;           // host mirror of the slots in use (LayerSlots::active)
 };
 
 namespace {
@@ -220,7 +238,7 @@ cudaError_t prefill_down(tmoe_handle *h, cudaStream_t st, int64_t P, const tmoe_
 }
 
 int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, const int32_t *ids, const float *w,
-                const tmoe_expert_tensors *t, float *out, bool dispatched, bool x_quantized) {
+                const tmoe_expert_tensors *t, float *out, bool dispatched, bool x_quantized, bool combine = true) {
     const tmoe_config &c = h->cfg;
     const int k = c.n_expert_used, H = c.n_embd, I = c.n_ff;
     const int64_t P = T * k;
@@ -256,6 +274,7 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
             e = prefill_down(h, st, P, t, max_active, true);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "prefill down");
+        if (!combine) return TMOE_OK;
         {
             PhaseMark pm(h, st, TMOE_PHASE_COMBINE);
             e = tmoe::launch_combine(h->dout, ids, w, T, k, H, t->n_slots, out, st);
@@ -290,6 +309,7 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
             e = prefill_down(h, st, P, t, max_active, false);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "prefill down");
+        if (!combine) return TMOE_OK;
         {
             PhaseMark pm(h, st, TMOE_PHASE_COMBINE);
             e = tmoe::launch_combine(h->dout, ids, w, T, k, H, t->n_slots, out, st);
@@ -315,6 +335,7 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
         e = tmoe::launch_gemv(wd, false, d, max_active, h->sm_count, st);
     }
     if (e != cudaSuccess) return cuda_fail(h, e, "down gemv");
+    if (!combine) return TMOE_OK;
     {
         PhaseMark pm(h, st, TMOE_PHASE_COMBINE);
         e = tmoe::launch_combine(h->dout, ids, w, T, k, H, t->n_slots, out, st);
@@ -381,6 +402,7 @@ void tmoe_destroy(tmoe_handle *h) {
     DeviceGuard dg(h->cfg.device);
     if (h->ws) cudaFree(h->ws);
     if (h->op_ws) cudaFree(h->op_ws);
+    if (h->a2a.mem) cudaFree(h->a2a.mem);
     for (auto &ev : h->prof.ev)
         if (ev) cudaEventDestroy(ev);
     delete h;
@@ -401,6 +423,7 @@ int tmoe_check(tmoe_handle *h, void *stream) {
     if (flag) {
         cudaMemset(h->err, 0, sizeof(int));
         if (flag == TMOE_DEV_ERR_BADID) return fail(h, TMOE_E_INVALID, "an expert id was >= n_slots");
+        if (flag == TMOE_DEV_ERR_NOSLOT) return fail(h, TMOE_E_INVALID, "no free expert slot (all pinned)");
         return fail(h, TMOE_E_DEVICE, "a kernel gave up on a bounded wait (code %d)", flag);
     }
     return TMOE_OK;
@@ -440,7 +463,7 @@ int tmoe_route(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
         float *dst = logits_out ? logits_out : h->logits;
         {
             PhaseMark pm(h, st, TMOE_PHASE_ROUTER_LOGITS);
-            e = tmoe::launch_router_logits(xs, router_w, T, c.n_embd, c.n_expert, dst, nullptr, st);
+            e = tmoe::launch_router_logits(xs, router_w, T, c.n_embd, c.n_expert, dst, nullptr, h->err, st);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "router logits");
         lg = dst;
@@ -516,12 +539,12 @@ int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
         return run_experts(h, st, xn, T, h->mapped, w, wts, out, true, true);
     }
     if (router_w) {
-        x_quantized = tmoe::router_fuses_q8(c.n_embd);
+        x_quantized = tmoe::router_fuses_q8(c.n_embd, T);
         const tmoe::Q8Rows q8{h->xq, h->xd, h->xbl, h->xbh, wt_of(c.gate_type)};
         {
             PhaseMark pm(h, st, TMOE_PHASE_ROUTER_LOGITS);
             e = tmoe::launch_router_logits(xn, router_w, T, c.n_embd, c.n_expert, h->logits,
-                                           x_quantized ? &q8 : nullptr, st);
+                                           x_quantized ? &q8 : nullptr, h->err, st);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "router logits");
         lg = h->logits;
@@ -577,6 +600,90 @@ int tmoe_ep_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float *x,
     if (rc) return rc;
     if (rc2) return fail(h, rc2, "%s", msg);
     return TMOE_OK;
+}
+
+int tmoe_ep_a2a_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float *x, int64_t T, int32_t use_norm,
+                      const float *norm_w, const float *router_w, const float *logits, const tmoe_expert_tensors *wts,
+                      float *out, int32_t *ids_out, float *w_out) {
+    if (!h) return TMOE_E_INVALID;
+    const tmoe_config &c = h->cfg;
+    if (!comm) return fail(h, TMOE_E_INVALID, "null communicator");
+    if (tmoe::ep_comm_device(comm) != c.device)
+        return fail(h, TMOE_E_INVALID, "communicator device %d != handle device %d", tmoe::ep_comm_device(comm),
+                    c.device);
+    int rank = 0;
+    const int g = tmoe::ep_comm_ranks(comm, &rank);
+    const int cap = c.max_tokens / g, k = c.n_expert_used, H = c.n_embd, E = c.n_expert;
+    if (E % g) return fail(h, TMOE_E_INVALID, "%d experts do not split over %d ranks", E, g);
+    if (cap < 1) return fail(h, TMOE_E_INVALID, "max_tokens %d < %d ranks", c.max_tokens, g);
+    if (T < 0 || T > cap) return fail(h, TMOE_E_INVALID, "T=%lld outside [0, max_tokens / ranks = %d]", (long long)T, cap);
+    if (!out || !x) return fail(h, TMOE_E_INVALID, "null tensor");
+    if (!aligned16(x) || !aligned16(out)) return fail(h, TMOE_E_INVALID, "x and out must be 16-byte aligned");
+    int rc = check_tensors(h, wts);
+    if (rc) return rc;
+    if (wts->n_slots != E / g) return fail(h, TMOE_E_INVALID, "wts hold %d experts, the rank's share is %d",
+                                          wts->n_slots, E / g);
+    DeviceGuard dg(c.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    auto &A = h->a2a;
+    if (A.g != g || A.cap != cap) {  // the exchange buffers of this rank count
+        if (A.mem) cudaFree(A.mem), A.mem = nullptr;
+        const size_t ni = (size_t)g * cap, rows_x = ni * H * 4;
+        const size_t bytes = align_up(ni * 4, 256) * 2 /* row_of, s_tok */ + align_up((size_t)g * 4, 256) +
+                             align_up(ni * k * 4, 256) * 4 /* ids, w both ways */ + align_up(rows_x, 256) * 4;
+        if (cudaMalloc(&A.mem, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            A.g = A.cap = 0;
+            return fail(h, TMOE_E_NOMEM, "all-to-all buffers (%zu bytes)", bytes);
+        }
+        uint8_t *p = (uint8_t *)A.mem;
+        auto take = [&](size_t n) {
+            void *r = p;
+            p += align_up(n, 256);
+            return r;
+        };
+        A.row_of = (int32_t *)take(ni * 4), A.s_tok = (int32_t *)take(ni * 4), A.counts = (int32_t *)take(g * 4);
+        A.s_ids = (int32_t *)take(ni * k * 4), A.r_ids = (int32_t *)take(ni * k * 4);
+        A.s_w = (float *)take(ni * k * 4), A.r_w = (float *)take(ni * k * 4);
+        A.s_x = (float *)take(rows_x), A.r_x = (float *)take(rows_x);
+        A.part = (float *)take(rows_x), A.ret = (float *)take(rows_x);
+        A.g = g, A.cap = cap;
+    }
+    int32_t *ids = ids_out ? ids_out : h->ids;
+    float *w = w_out ? w_out : h->w;
+    // route this rank's tokens and pack the messages; on a failure the rank still takes both
+    // exchange steps, with messages that carry no rows
+    cudaError_t e = cudaSuccess;
+    rc = T ? tmoe_route(h, stream, x, T, use_norm, norm_w, router_w, logits, ids, w, use_norm ? h->xn : nullptr,
+                        nullptr)
+           : TMOE_OK;
+    const float *xn = use_norm ? h->xn : x;
+    if (rc == TMOE_OK && T) {
+        PhaseMark pm(h, st, TMOE_PHASE_MAP_IDS);
+        e = tmoe::launch_ep_pack(ids, w, xn, (int)T, k, H, E / g, g, cap, A.row_of, A.s_ids, A.s_w, A.s_tok, A.counts,
+                                 A.s_x, st);
+        if (e != cudaSuccess) rc = cuda_fail(h, e, "all-to-all pack");
+    }
+    if (rc != TMOE_OK || T == 0) cudaMemsetAsync(A.s_ids, 0xff, (size_t)g * cap * k * 4, st);
+    char msg[256];
+    const size_t nk = (size_t)cap * k * 4;
+    const tmoe::EpBuf out_bufs[3] = {{A.s_ids, A.r_ids, nk}, {A.s_w, A.r_w, nk}, {A.s_x, A.r_x, (size_t)cap * H * 4}};
+    int rc2 = tmoe::ep_alltoall(comm, out_bufs, 3, st, msg, sizeof msg);
+    if (rc2) return fail(h, rc2, "%s", msg);
+    // this rank's experts over every received row (rows of other ranks' tokens), combined per row
+    // in choice order: the partial sums of the reference's EP mode
+    const int rc3 = run_experts(h, st, A.r_x, (int64_t)g * cap, A.r_ids, A.r_w, wts, A.part, false, false);
+    if (rc3 != TMOE_OK) cudaMemsetAsync(A.part, 0, (size_t)g * cap * H * 4, st);
+    const tmoe::EpBuf back = {A.part, A.ret, (size_t)cap * H * 4};
+    rc2 = tmoe::ep_alltoall(comm, &back, 1, st, msg, sizeof msg);
+    if (rc2) return fail(h, rc2, "%s", msg);
+    if (rc) return rc;
+    if (rc3) return rc3;
+    if (T) {
+        PhaseMark pm(h, st, TMOE_PHASE_COMBINE);
+        e = tmoe::launch_ep_combine(A.ret, A.row_of, (int)T, H, g, cap, out, st);
+    }
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "all-to-all combine");
 }
 
 int tmoe_map_ids(tmoe_handle *h, void *stream, const int32_t *ids, int64_t n, const int32_t *table,
@@ -830,6 +937,213 @@ int tmoe_profile_collect(tmoe_handle *h, double *ms_out, int64_t *count_out) {
         if (count_out) count_out[i] = p.count[i];
     }
     return TMOE_OK;
+}
+
+// ------------------------------------------------------------------ expert slots (a10)
+int tmoe_slots_create(tmoe_handle *h, const tmoe_expert_tensors *slots, const tmoe_expert_tensors *store,
+                      tmoe_slots **out) {
+    if (!h || !out || !store) return h ? fail(h, TMOE_E_INVALID, "null argument") : TMOE_E_INVALID;
+    *out = nullptr;
+    const tmoe_config &c = h->cfg;
+    int rc = check_tensors(h, slots);
+    if (rc) return rc;
+    const int E = c.n_expert, S = slots->n_slots;
+    if (store->n_slots != E) return fail(h, TMOE_E_INVALID, "the store must hold all %d experts", E);
+    if (!tmoe::slots_fit(E, S)) return fail(h, TMOE_E_UNSUPPORTED, "E=%d / %d slots not supported", E, S);
+    if (store->gate_nb1 != slots->gate_nb1 || store->up_nb1 != slots->up_nb1 || store->down_nb1 != slots->down_nb1)
+        return fail(h, TMOE_E_INVALID, "store and slot rows differ (nb1)");
+    const size_t bytes[3] = {slots->gate_nb1 * (size_t)c.n_ff, slots->up_nb1 * (size_t)c.n_ff,
+                             slots->down_nb1 * (size_t)c.n_embd};
+    const void *src[3] = {store->gate, store->up, store->down};
+    const size_t src_nb2[3] = {store->gate_nb2, store->up_nb2, store->down_nb2};
+    const size_t dst_nb2[3] = {slots->gate_nb2, slots->up_nb2, slots->down_nb2};
+    uint8_t *dst[3] = {(uint8_t *)slots->gate, (uint8_t *)slots->up, (uint8_t *)slots->down};
+    DeviceGuard dg(c.device);
+    tmoe_slots *sl = new tmoe_slots;
+    sl->h = h;
+    sl->slot_wts = *slots;
+    for (int m = 0; m < 3; m++) {
+        if ((bytes[m] & 15) || (src_nb2[m] & 15) || src_nb2[m] < bytes[m] || ((uintptr_t)src[m] & 15)) {
+            delete sl;
+            return fail(h, TMOE_E_INVALID, "store matrices must be 16-byte aligned multiples of 16 bytes");
+        }
+        void *dp = nullptr;  // the mapped device address of the pinned store
+        if (cudaHostGetDevicePointer(&dp, const_cast<void *>(src[m]), 0) != cudaSuccess || !dp) {
+            cudaGetLastError();
+            delete sl;
+            return fail(h, TMOE_E_INVALID, "the expert store must be pinned (device-mapped) host memory");
+        }
+        sl->copy.src[m] = (const uint8_t *)dp;
+        sl->copy.src_nb2[m] = src_nb2[m];
+        sl->copy.dst[m] = dst[m];
+        sl->copy.dst_nb2[m] = dst_nb2[m];
+        sl->copy.bytes[m] = bytes[m];
+    }
+    const int MC = (E + S - 1) / S;
+    // one allocation: stamps and meta/counts first (8-byte), then the int arrays
+    const size_t n8 = (size_t)S + 4 + E, n4 = (size_t)S + E + 1 + 1 + (size_t)MC * E + (size_t)MC * S * 2 + MC + E,
+                 nbytes = n8 * 8 + n4 * 4 + E + 64;
+    if (cudaMalloc(&sl->mem, nbytes) != cudaSuccess) {
+        cudaGetLastError();
+        delete sl;
+        return fail(h, TMOE_E_NOMEM, "slot tables (%zu bytes)", nbytes);
+    }
+    uint8_t *p = (uint8_t *)sl->mem;
+    tmoe::SlotsDev &d = sl->dev;
+    d.n_expert = E, d.max_slots = S, d.max_chunks = MC;
+    d.stamp = (unsigned long long *)p, p += (size_t)S * 8;
+    d.meta = (unsigned long long *)p, p += 4 * 8;
+    d.counts = (unsigned long long *)p, p += (size_t)E * 8;
+    d.loads = (int2 *)p, p += (size_t)MC * S * 8;
+    d.owner = (int32_t *)p, p += (size_t)S * 4;
+    d.slot_of = (int32_t *)p, p += (size_t)E * 4;
+    d.active = (int32_t *)p, p += 4;
+    d.n_chunks = (int32_t *)p, p += 4;
+    d.map = (int32_t *)p, p += (size_t)MC * E * 4;
+    d.n_loads = (int32_t *)p, p += (size_t)MC * 4;
+    sl->list = (int32_t *)p, p += (size_t)E * 4;
+    d.pinned = p;
+    // initial state: nothing resident, no pins, every slot active
+    cudaError_t e = cudaMemset(sl->mem, 0, nbytes);
+    if (e == cudaSuccess) e = cudaMemset(d.owner, 0xff, (size_t)S * 4);
+    if (e == cudaSuccess) e = cudaMemset(d.slot_of, 0xff, (size_t)E * 4);
+    if (e == cudaSuccess) e = cudaMemset(d.map, 0xff, (size_t)MC * E * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(d.active, &S, 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(sl->mem);
+        delete sl;
+        return cuda_fail(h, e, "slot tables init");
+    }
+    sl->active = S;
+    *out = sl;
+    return TMOE_OK;
+}
+
+void tmoe_slots_destroy(tmoe_slots *s) {
+    if (!s) return;
+    DeviceGuard dg(s->h->cfg.device);
+    cudaFree(s->mem);
+    delete s;
+}
+
+int tmoe_slots_max_chunks(const tmoe_slots *s) { return s ? s->dev.max_chunks : TMOE_E_INVALID; }
+
+int tmoe_slots_make_resident(tmoe_slots *s, void *stream, const int32_t *experts, int32_t n) {
+    if (!s) return TMOE_E_INVALID;
+    tmoe_handle *h = s->h;
+    if (n < 0 || n > s->dev.max_slots || (n && !experts))
+        return fail(h, TMOE_E_INVALID, "make_resident of %d experts (at most the %d slots)", n, s->dev.max_slots);
+    if (n == 0) return TMOE_OK;
+    DeviceGuard dg(h->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e = cudaMemcpyAsync(s->list, experts, (size_t)n * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = tmoe::launch_slot_lookup_list(s->list, n, s->dev, h->err, st);
+    if (e == cudaSuccess) e = tmoe::launch_slot_page(s->dev, 0, s->copy, h->sm_count, st);
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "make_resident");
+}
+
+int tmoe_slots_set_hot_set(tmoe_slots *s, void *stream, const int32_t *hot, int32_t n) {
+    if (!s) return TMOE_E_INVALID;
+    tmoe_handle *h = s->h;
+    const int E = s->dev.n_expert;
+    if (n < 0 || (n && !hot)) return fail(h, TMOE_E_INVALID, "bad hot set");
+    std::vector<uint8_t> pinned(E, 0);
+    int count = 0;
+    for (int i = 0; i < n; i++) {
+        const int e = hot[i];
+        if (count < s->active && e >= 0 && e < E && !pinned[e]) pinned[e] = 1, count++;
+    }
+    DeviceGuard dg(h->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    std::vector<int32_t> slot_of(E);
+    cudaError_t e = cudaMemcpyAsync(s->dev.pinned, pinned.data(), E, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(slot_of.data(), s->dev.slot_of, (size_t)E * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "set_hot_set");
+    std::vector<int32_t> missing;
+    for (int x = 0; x < E; x++)
+        if (pinned[x] && slot_of[x] < 0) missing.push_back(x);
+    const int rc = tmoe_slots_make_resident(s, stream, missing.data(), (int32_t)missing.size());
+    if (rc) return rc;
+    return cudaStreamSynchronize(st) == cudaSuccess ? TMOE_OK : cuda_fail(h, cudaGetLastError(), "set_hot_set");
+}
+
+int tmoe_slots_state(tmoe_slots *s, void *stream, int32_t *owner, int64_t *stats, int64_t *counts) {
+    if (!s) return TMOE_E_INVALID;
+    tmoe_handle *h = s->h;
+    DeviceGuard dg(h->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e = cudaStreamSynchronize(st);
+    unsigned long long meta[4];
+    if (e == cudaSuccess && owner)
+        e = cudaMemcpy(owner, s->dev.owner, (size_t)s->dev.max_slots * 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(meta, s->dev.meta, sizeof meta, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && counts)
+        e = cudaMemcpy(counts, s->dev.counts, (size_t)s->dev.n_expert * 8, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(h, e, "slot state");
+    if (stats)
+        for (int i = 0; i < 3; i++) stats[i] = (int64_t)meta[i + 1];
+    return TMOE_OK;
+}
+
+int tmoe_slots_last_plan(tmoe_slots *s, void *stream, int32_t *n_chunks, int32_t *map, int32_t *loads,
+                         int32_t *n_loads) {
+    if (!s) return TMOE_E_INVALID;
+    tmoe_handle *h = s->h;
+    const tmoe::SlotsDev &d = s->dev;
+    DeviceGuard dg(h->cfg.device);
+    cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e == cudaSuccess && n_chunks) e = cudaMemcpy(n_chunks, d.n_chunks, 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && map)
+        e = cudaMemcpy(map, d.map, (size_t)d.max_chunks * d.n_expert * 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && loads)
+        e = cudaMemcpy(loads, d.loads, (size_t)d.max_chunks * d.max_slots * 8, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && n_loads) e = cudaMemcpy(n_loads, d.n_loads, (size_t)d.max_chunks * 4, cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "last plan");
+}
+
+int tmoe_streamed_layer(tmoe_handle *h, void *stream, tmoe_slots *s, const float *x, int64_t T, int32_t use_norm,
+                        const float *norm_w, const float *router_w, const float *logits, float *out,
+                        int32_t *ids_out, float *w_out) {
+    if (!h || !s || s->h != h) return h ? fail(h, TMOE_E_INVALID, "slot cache of another handle") : TMOE_E_INVALID;
+    const tmoe_config &c = h->cfg;
+    if (!x || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    if (!aligned16(out)) return fail(h, TMOE_E_INVALID, "out must be 16-byte aligned");
+    int32_t *ids = ids_out ? ids_out : h->ids;
+    float *w = w_out ? w_out : h->w;
+    int rc = tmoe_route(h, stream, x, T, use_norm, norm_w, router_w, logits, ids, w, use_norm ? h->xn : nullptr,
+                        nullptr);
+    if (rc || T == 0) return rc;
+    DeviceGuard dg(c.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    const float *xn = use_norm ? h->xn : x;
+    const int k = c.n_expert_used, E = c.n_expert;
+    const int64_t P = T * k;
+    cudaError_t e;
+    {
+        PhaseMark pm(h, st, TMOE_PHASE_SLOT_PLAN);
+        e = tmoe::launch_slot_plan(ids, (int)P, s->dev, h->err, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "slot plan");
+    for (int ch = 0; ch < s->dev.max_chunks; ch++) {
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_SLOT_PAGE);
+            e = tmoe::launch_slot_page(s->dev, ch, s->copy, h->sm_count, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "slot paging");
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_MAP_IDS);
+            e = tmoe::launch_map_ids(ids, P, s->dev.map + (size_t)ch * E, E, h->mapped, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "chunk map");
+        rc = run_experts(h, st, xn, T, h->mapped, w, &s->slot_wts, out, false, ch > 0, false);
+        if (rc) return rc;
+    }
+    {
+        PhaseMark pm(h, st, TMOE_PHASE_COMBINE);
+        e = tmoe::launch_combine(h->dout, ids, w, T, k, c.n_embd, E, out, st);
+    }
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "combine");
 }
 
 }  // extern "C"

@@ -49,10 +49,13 @@ class ExpertWeights:
     up: torch.Tensor
     down: torch.Tensor
 
-    def c_struct(self) -> _lib.ExpertTensors:
+    def c_struct(self, host: bool = False) -> _lib.ExpertTensors:
         for t in (self.gate, self.up, self.down):
-            if t.dtype != torch.uint8 or t.dim() != 3 or not t.is_cuda or not t.is_contiguous():
-                raise ValueError("expert tensors must be contiguous uint8 CUDA tensors [slots, rows, bytes]")
+            if t.dtype != torch.uint8 or t.dim() != 3 or not t.is_contiguous():
+                raise ValueError("expert tensors must be contiguous uint8 tensors [slots, rows, bytes]")
+            if (not host and not t.is_cuda) or (host and (t.is_cuda or not t.is_pinned())):
+                raise ValueError("expert tensors must be CUDA tensors" if not host else
+                                 "a host expert store must be pinned CPU tensors")
         g, u, d = self.gate, self.up, self.down
         return _lib.ExpertTensors(g.data_ptr(), u.data_ptr(), d.data_ptr(),
                                   g.shape[2], g.shape[1] * g.shape[2],
@@ -163,6 +166,18 @@ class MoeLayer:
                                        _ptr(ids_out), _ptr(w_out)), self.h)
         return out
 
+    def moe_ffn_streamed(self, x: torch.Tensor, cache: "SlotCache", router_w: torch.Tensor | None = None,
+                         logits: torch.Tensor | None = None, ffn_norm: torch.Tensor | None = None,
+                         use_norm: bool = False, out=None, ids_out=None, w_out=None, stream=None):
+        """The streamed step of `--expert-slots N < E` (qwen3moe.rs:2021-2050): route, plan the
+        chunks on the device, page misses in from the cache's host store, compute from the slots."""
+        T = x.shape[0]
+        out = torch.empty((T, self.cfg.n_embd), dtype=torch.float32, device=self.device) if out is None else out
+        _lib.check(self.lib.tmoe_streamed_layer(self.h, _stream(stream), cache.s, _ptr(x), T, int(use_norm),
+                                                _ptr(ffn_norm), _ptr(router_w), _ptr(logits), _ptr(out),
+                                                _ptr(ids_out), _ptr(w_out)), self.h)
+        return out
+
     def mul_mat_id(self, qtype: int, W: torch.Tensor, b: torch.Tensor, ids: torch.Tensor,
                    out: torch.Tensor | None = None, stream=None):
         """ggml mul_mat_id: W uint8 [n_w, N, row_size(K)], b f32 [T, b1, K], ids [T, n_used]
@@ -193,6 +208,65 @@ class MoeLayer:
         _lib.check(self.lib.tmoe_map_ids(self.h, _stream(stream), _ptr(ids), ids.numel(), _ptr(table),
                                          table.numel(), _ptr(out)), self.h)
         return out
+
+
+class SlotCache:
+    """The expert-slot cache of one MoE layer (LayerSlots, crates/memory/src/slots.rs) with its
+    table on the device: `slots` are the device slot tensors, `store` the layer's experts in
+    pinned host memory."""
+
+    def __init__(self, layer: "MoeLayer", slots: ExpertWeights, store: ExpertWeights):
+        self.layer, self.slots, self.store = layer, slots, store  # the cache keeps their pointers
+        self._st = slots.c_struct()
+        self._store = store.c_struct(host=True)
+        h = C.c_void_p()
+        _lib.check(layer.lib.tmoe_slots_create(layer.h, C.byref(self._st), C.byref(self._store), C.byref(h)),
+                   layer.h)
+        self.s = h
+        self.n_slots = slots.gate.shape[0]
+        self.n_expert = layer.cfg.n_expert
+        self.max_chunks = layer.lib.tmoe_slots_max_chunks(self.s)
+
+    def close(self):
+        if self.s:
+            self.layer.lib.tmoe_slots_destroy(self.s)
+            self.s = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def make_resident(self, experts, stream=None):
+        arr = (C.c_int32 * max(len(experts), 1))(*experts)
+        _lib.check(self.layer.lib.tmoe_slots_make_resident(self.s, _stream(stream), arr, len(experts)),
+                   self.layer.h)
+
+    def set_hot_set(self, hot, stream=None):
+        arr = (C.c_int32 * max(len(hot), 1))(*hot)
+        _lib.check(self.layer.lib.tmoe_slots_set_hot_set(self.s, _stream(stream), arr, len(hot)), self.layer.h)
+
+    def state(self, stream=None):
+        """(owner per slot, (hits, misses, bypasses), routed pairs per expert)."""
+        owner = (C.c_int32 * self.n_slots)()
+        stats = (C.c_int64 * 3)()
+        counts = (C.c_int64 * self.n_expert)()
+        _lib.check(self.layer.lib.tmoe_slots_state(self.s, _stream(stream), owner, stats, counts), self.layer.h)
+        return list(owner), tuple(stats), list(counts)
+
+    def last_plan(self, stream=None):
+        """(n_chunks, map [max_chunks][E], loads per chunk as (expert, slot) lists)."""
+        mc, E, S = self.max_chunks, self.n_expert, self.n_slots
+        n = C.c_int32()
+        m = (C.c_int32 * (mc * E))()
+        ld = (C.c_int32 * (mc * S * 2))()
+        nl = (C.c_int32 * mc)()
+        _lib.check(self.layer.lib.tmoe_slots_last_plan(self.s, _stream(stream), C.byref(n), m, ld, nl),
+                   self.layer.h)
+        maps = [list(m[c * E:(c + 1) * E]) for c in range(mc)]
+        loads = [[(ld[(c * S + i) * 2], ld[(c * S + i) * 2 + 1]) for i in range(nl[c])] for c in range(mc)]
+        return n.value, maps, loads
 
 
 def ep_id_map(n_expert: int, n_ranks: int, rank: int) -> list[int]:
@@ -250,5 +324,22 @@ def ep_moe_ffn(layer: "MoeLayer", comm: EPComm, x: torch.Tensor, experts: Expert
     return out
 
 
+def ep_a2a_moe_ffn(layer: "MoeLayer", comm: EPComm, x: torch.Tensor, experts: ExpertWeights,
+                   router_w: torch.Tensor | None = None, logits: torch.Tensor | None = None,
+                   ffn_norm: torch.Tensor | None = None, use_norm: bool = False, out: torch.Tensor | None = None,
+                   ids_out: torch.Tensor | None = None, w_out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Expert parallelism with token dispatch/combine over an all-to-all: `x` are this rank's own
+    tokens, `experts` its contiguous share (E / ranks experts); `out` gets this rank's tokens.
+    The layer's max_tokens must be ranks x the tokens per rank (it computes the rows the other
+    ranks send)."""
+    T = x.shape[0]
+    out = torch.empty((T, layer.cfg.n_embd), dtype=torch.float32, device=layer.device) if out is None else out
+    st = experts.c_struct()
+    _lib.check(layer.lib.tmoe_ep_a2a_layer(layer.h, _stream(stream), comm.c, _ptr(x), T, int(use_norm),
+                                           _ptr(ffn_norm), _ptr(router_w), _ptr(logits), C.byref(st), _ptr(out),
+                                           _ptr(ids_out), _ptr(w_out)), layer.h)
+    return out
+
+
 __all__ = ["MoeLayer", "ExpertWeights", "TmoeError", "TYPE_Q4_K", "TYPE_Q6_K", "row_size", "quantize", "dequantize",
-           "EPComm", "ep_moe_ffn", "ep_id_map"]
+           "EPComm", "ep_moe_ffn", "ep_a2a_moe_ffn", "ep_id_map", "SlotCache"]
