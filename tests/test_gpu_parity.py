@@ -39,7 +39,7 @@ def assert_close(got, want, strict=True, what=""):
 
 # ------------------------------------------------------------------------------------ routing
 @pytest.mark.parametrize("T,H,E,k", [(32, 512, 16, 4), (1, 2048, 128, 8), (64, 2048, 128, 8),
-                                     (8192, 2048, 128, 8), (64, 4096, 128, 8), (1100, 768, 40, 6),
+                                     (8192, 2048, 128, 8), (64, 4096, 128, 8), (1100, 768, 40, 6), (1100, 768, 128, 8),
                                      (1024, 4096, 128, 8)])
 def test_route_bit_exact(T, H, E, k):
     rng = np.random.default_rng(T * 7 + H)

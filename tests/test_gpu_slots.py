@@ -161,3 +161,47 @@ def test_all_pinned_slots_report_no_free_slot():
     finally:
         cache.close()
         layer.close()
+
+
+def test_streamed_steps_with_pinned_experts_follow_the_reference():
+    """Pins cut the victims a chunk's misses can take; when the misses could outnumber them the
+    planner must make the reference's serial lookups (which may then evict the chunk's own
+    entries).  Every step is checked against the oracle."""
+    H, I, E, k, NS, T = 512, 256, 16, 4, 5, 24
+    rng = np.random.default_rng(11)
+    gate, up, down = _weights(rng, H, I, E, O.TYPE_Q4_K, O.TYPE_Q4_K, True)
+    layer = tb.MoeLayer(H, I, E, k, gate_type=O.TYPE_Q4_K, up_type=O.TYPE_Q4_K, down_type=O.TYPE_Q4_K,
+                        max_tokens=T)
+    resident = tb.ExpertWeights(cuda(gate), cuda(up), cuda(down))
+    store = tb.ExpertWeights(pinned(gate), pinned(up), pinned(down))
+    slots = tb.ExpertWeights(*(torch.zeros((NS,) + a.shape[1:], dtype=torch.uint8, device="cuda")
+                               for a in (gate, up, down)))
+    cache = tb.SlotCache(layer, slots, store)
+    ref = S.LayerSlots(E, NS)
+    try:
+        cache.set_hot_set([3, 9])
+        S.make_resident(ref, ref.set_hot_set([3, 9]))
+        for step in range(4):
+            x = rng.standard_normal((T, H)).astype(np.float32)
+            lg = zipf_logits(rng, T, E)
+            ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+            out = layer.moe_ffn_streamed(cuda(x), cache, logits=cuda(lg), ids_out=ids)
+            want_out = layer.moe_ffn(cuda(x), resident, logits=cuda(lg))
+            got_ids = ids.cpu().numpy()
+            try:
+                steps_ref = S.step(ref, got_ids.reshape(-1))
+            except RuntimeError:  # the oracle found every slot pinned: so must the device
+                with pytest.raises(tb.TmoeError, match="all pinned"):
+                    layer.check()
+                break
+            layer.check()
+            _check_plan(cache, ref, got_ids, steps_ref)
+            # the reference's make_resident makes plain lookups, so with pins a chunk's late miss can
+            # evict the chunk's own earlier entry (two experts then share a slot); only without that
+            # are the outputs those of the resident experts
+            shared = any(len(set(sl)) < len(sl) for _, sl, _, _ in steps_ref)
+            if not shared:
+                assert np.array_equal(out.cpu().numpy().view(np.uint32), want_out.cpu().numpy().view(np.uint32))
+    finally:
+        cache.close()
+        layer.close()

@@ -132,9 +132,10 @@ cudaError_t launch_prefill_gemm(bool swiglu, const __half *A, int n_rows, int K,
                                 int *tile_start, const int32_t *perm, float *out, int *err, int sm_count,
                                 cudaStream_t st);
 
-cudaError_t launch_prep_gateup_a(const float *x, int T, const int32_t *perm, int n_rows, int x_div, int K,
-                                 __half *aq_t, float *ad_t, __half *ab_t, __half *aq, float *ad, __half *ab,
-                                 cudaStream_t st);
+// n_valid (device, may be NULL): the dispatched pairs; sorted rows past it are not gathered.
+cudaError_t launch_prep_gateup_a(const float *x, int T, const int32_t *perm, int n_rows, const int32_t *n_valid,
+                                 int x_div, int K, __half *aq_t, float *ad_t, __half *ab_t, __half *aq, float *ad,
+                                 __half *ab, cudaStream_t st);
 cudaError_t launch_prefill_gateup(const __half *aq, const float *ad, const __half *ab, int n_rows, int K, int I,
                                   const uint8_t *gate, const uint8_t *up, size_t nb1, size_t nb2_gate,
                                   size_t nb2_up, const int4 *active, const int32_t *n_active, int max_active,

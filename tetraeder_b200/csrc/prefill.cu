@@ -172,6 +172,9 @@ __global__ void __launch_bounds__(256) dequant_f16_kernel(const uint8_t *__restr
         const int r = u / nb, b = u - r * nb;
         const uint8_t *blk = dq_rows + r * row_bytes + b * BB;
         __align__(16) __half h[8];
+        // Two elements per step: their quant bytes become the fp16 pair (1024 + q) by exponent magic
+        // (one byte permute), an exact half2 subtraction leaves the integers, and the value is
+        // formed in f32 and rounded to fp16 once, as (float)q would give it.
         if constexpr (WT == TMOE_WT_Q4K) {
             const int c = lane >> 2;  // sub-block of 32
             const float d = h2f(*reinterpret_cast<const uint16_t *>(blk)),
@@ -188,10 +191,17 @@ __global__ void __launch_bounds__(256) dequant_f16_kernel(const uint8_t *__restr
             const float d1 = __fmul_rn(d, (float)scale), m1 = __fmul_rn(dmin, (float)mn);
             const uint2 q = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * (c >> 1) + 8 * (lane & 3));
             const int sh = (c & 1) * 4;
+            const uint32_t qw[2] = {(q.x >> sh) & 0x0f0f0f0fu, (q.y >> sh) & 0x0f0f0f0fu};
+            const __half2 base = __float2half2_rn(1024.0f);
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int v = (((i < 4 ? q.x : q.y) >> (8 * (i & 3) + sh)) & 0x0f);
-                h[i] = __float2half_rn(__fsub_rn(__fmul_rn(d1, (float)v), m1));
+            for (int i = 0; i < 4; i++) {
+                const uint32_t bits = __byte_perm(qw[i >> 1], 0x64u, (i & 1) ? 0x4342u : 0x4140u);
+                __half2 v;
+                memcpy(&v, &bits, 4);
+                const float2 f = __half22float2(__hsub2(v, base));
+                const __half2 r2 =
+                    __floats2half2_rn(__fsub_rn(__fmul_rn(d1, f.x), m1), __fsub_rn(__fmul_rn(d1, f.y), m1));
+                memcpy(&h[2 * i], &r2, 4);
             }
         } else {
             const int hh = lane >> 4, rr = 8 * (lane & 15);  // element k = 128 hh + rr + i
@@ -200,11 +210,18 @@ __global__ void __launch_bounds__(256) dequant_f16_kernel(const uint8_t *__restr
             const int lsh = rr < 64 ? 0 : 4, hsh = 2 * (rr >> 5);
             const float d = h2f((uint16_t)(blk[208] | (blk[209] << 8)));
             const float ds = __fmul_rn(d, (float)reinterpret_cast<const int8_t *>(blk + 192)[(128 * hh + rr) >> 4]);
+            // the 6-bit quants of elements 0-3 and 4-7, one per byte
+            const uint32_t qw[2] = {((lo.x >> lsh) & 0x0f0f0f0fu) | (((hi.x >> hsh) & 0x03030303u) << 4),
+                                    ((lo.y >> lsh) & 0x0f0f0f0fu) | (((hi.y >> hsh) & 0x03030303u) << 4)};
+            const __half2 base = __float2half2_rn(1056.0f);  // 1024 + the Q6_K bias 32
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const uint32_t lw = i < 4 ? lo.x : lo.y, hw = i < 4 ? hi.x : hi.y;
-                const int q = (int)((lw >> (8 * (i & 3) + lsh)) & 0x0f) | (int)(((hw >> (8 * (i & 3) + hsh)) & 3) << 4);
-                h[i] = __float2half_rn(__fmul_rn(ds, (float)(q - 32)));
+            for (int i = 0; i < 4; i++) {
+                const uint32_t bits = __byte_perm(qw[i >> 1], 0x64u, (i & 1) ? 0x4342u : 0x4140u);
+                __half2 v;
+                memcpy(&v, &bits, 4);
+                const float2 f = __half22float2(__hsub2(v, base));  // q - 32, exact
+                const __half2 r2 = __floats2half2_rn(__fmul_rn(ds, f.x), __fmul_rn(ds, f.y));
+                memcpy(&h[2 * i], &r2, 4);
             }
         }
         *reinterpret_cast<uint4 *>(dst + ((int64_t)e * N + row0 + r) * K + b * TMOE_QK + 8 * lane) =
@@ -526,11 +543,11 @@ __global__ void prep_gateup_a_kernel(const float *__restrict__ x, const int32_t 
 // [K], d [K/256], block sums [K/256][16].  One warp per row, 16-byte copies.
 __global__ void gather_gateup_a_kernel(const __half *__restrict__ aq_t, const float *__restrict__ ad_t,
                                        const __half *__restrict__ ab_t, const int32_t *__restrict__ perm,
-                                       int n_rows, int x_div, int K, __half *__restrict__ aq, float *__restrict__ ad,
-                                       __half *__restrict__ ab) {
+                                       int n_rows, const int32_t *__restrict__ n_valid, int x_div, int K,
+                                       __half *__restrict__ aq, float *__restrict__ ad, __half *__restrict__ ab) {
     const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    if (r >= n_rows) return;
+    if (r >= n_rows || (n_valid && r >= n_valid[0])) return;  // past the dispatched pairs: no tile reads them
     int p = perm[r];
     if (p < 0) p = 0;
     const int64_t t = p / x_div;
@@ -963,16 +980,16 @@ cudaError_t launch_dequant_f16(int wt, const uint8_t *w, size_t nb2, int N, int 
 }
 
 // The Q8_K of the T token rows (token order), then their copies in expert-sorted pair order.
-cudaError_t launch_prep_gateup_a(const float *x, int T, const int32_t *perm, int n_rows, int x_div, int K,
-                                 __half *aq_t, float *ad_t, __half *ab_t, __half *aq, float *ad, __half *ab,
-                                 cudaStream_t st) {
+cudaError_t launch_prep_gateup_a(const float *x, int T, const int32_t *perm, int n_rows, const int32_t *n_valid,
+                                 int x_div, int K, __half *aq_t, float *ad_t, __half *ab_t, __half *aq, float *ad,
+                                 __half *ab, cudaStream_t st) {
     if (n_rows <= 0 || T <= 0) return cudaSuccess;
     const int64_t warps = (int64_t)T * (K / TMOE_QK);
     prep_gateup_a_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(x, nullptr, T, 1, K, aq_t, ad_t, ab_t);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    gather_gateup_a_kernel<<<(unsigned)((n_rows + 7) / 8), 256, 0, st>>>(aq_t, ad_t, ab_t, perm, n_rows, x_div, K, aq,
-                                                                         ad, ab);
+    gather_gateup_a_kernel<<<(unsigned)((n_rows + 7) / 8), 256, 0, st>>>(aq_t, ad_t, ab_t, perm, n_rows, n_valid,
+                                                                         x_div, K, aq, ad, ab);
     return cudaGetLastError();
 }
 

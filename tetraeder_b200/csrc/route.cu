@@ -5,6 +5,11 @@
 // The router dot is canonical so that the logits are bit-identical with the CPU oracle: lane l
 // of a warp accumulates the elements i with (i/4) % 32 == l in increasing i with fma, then a
 // butterfly over lane distances 16, 8, 4, 2, 1.  The rest of the canonical order is in route.cuh.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "q8k.cuh"
@@ -99,16 +104,26 @@ __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_kernel(const floa
     }
 }
 
-// Router logits for many tokens (H % 256 == 0): a CTA of 8 warps owns 32 tokens x 16 experts and
-// streams K in chunks of 256 columns through a ring of RT_STAGES shared-memory stages (one bulk copy
-// per 1 KB row chunk).  A warp holds 8 tokens x 8 experts; lane l keeps the canonical partial sums
-// of slice l for all 64 logits in registers (the same fma chain as router_logits_kernel), so every
-// shared-memory load feeds 32 FMAs.  The 32 partials of a logit are then summed over the lanes in
-// the butterfly's tree (pairs at lane distance 16, 8, 4, 2, 1), transposed so that 32 logits take
-// 31 shuffles instead of 160: bit-identical to butterfly_f32 since each add has the same operands.
-constexpr int RT_TOK = 32, RT_EXP = 16, RT_KC = 256, RT_STAGES = 4;
+// Router logits for many tokens (H % 128 == 0): persistent CTAs of 8 warps over tiles of 16 tokens
+// x 64 experts.  K streams in chunks of 128 columns through a ring of RT_STAGES shared-memory
+// stages (one bulk copy per 512-byte row chunk); the ring runs on across tiles, so the next tile's
+// chunks arrive while a tile finishes.  A warp holds 8 tokens x 16 experts; lane l keeps the
+// canonical partial sums of slice l for all 128 logits in registers (the same fma chain as
+// router_logits_kernel), so one shared-memory load feeds 32 (w) or 64 (x) FMAs.  The 32 partials
+// of a logit are then summed over the lanes in the butterfly's tree (pairs at lane distance 16, 8,
+// 4, 2, 1), transposed so that 32 logits take 31 shuffles instead of 160: bit-identical to
+// butterfly_f32 since each add has the same operands.
+constexpr int RT_TOK = 16, RT_EXP = 64, RT_KC = 128, RT_STAGES = 4;
 constexpr int RT_STAGE_FLOATS = (RT_TOK + RT_EXP) * RT_KC;
 constexpr size_t RT_SMEM = (size_t)RT_STAGES * RT_STAGE_FLOATS * 4;
+
+__device__ __forceinline__ void rt_tma_load_2d(void *dst, const CUtensorMap *m, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
 
 __device__ __forceinline__ float transposed_butterfly(float (&v)[32], int lane) {
 #pragma unroll
@@ -126,83 +141,97 @@ __device__ __forceinline__ float transposed_butterfly(float (&v)[32], int lane) 
 
 __global__ void __launch_bounds__(256, 1) router_logits_tiled_kernel(const float *__restrict__ xn,
                                                                      const float *__restrict__ rw, int64_t T, int H,
-                                                                     int E, float *__restrict__ logits, int *err) {
-    extern __shared__ __align__(128) float rt_smem[];  // [RT_STAGES][32 token rows + 16 expert rows][RT_KC]
+                                                                     int E, float *__restrict__ logits, int *err,
+                                                                     const __grid_constant__ CUtensorMap map_x,
+                                                                     const __grid_constant__ CUtensorMap map_w) {
+    extern __shared__ __align__(128) float rt_smem[];  // [RT_STAGES][16 token rows + 64 expert rows][RT_KC]
     __shared__ __align__(8) uint64_t full[RT_STAGES];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t t0 = (int64_t)blockIdx.y * RT_TOK;  // the expert tiles of a token tile run together:
-    const int e0 = blockIdx.x * RT_EXP;                // the tile's rows of xn are read from HBM once
-    const int nt = (int)min((int64_t)RT_TOK, T - t0), ne = min(RT_EXP, E - e0);
     const int n_ch = H / RT_KC;
+    const int tiles_e = (E + RT_EXP - 1) / RT_EXP;
+    const int64_t n_tiles = ((T + RT_TOK - 1) / RT_TOK) * tiles_e;
+    // the CTA's tiles: blockIdx.x + i * gridDim.x; the expert tiles of a token tile are adjacent
+    const int64_t my_tiles = n_tiles > blockIdx.x ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int64_t n_steps = my_tiles * n_ch;
     if (threadIdx.x == 0) {
         for (int s = 0; s < RT_STAGES; s++) mbar_init(&full[s], 1);
         fence_barrier_init();
     }
     __syncthreads();
-    auto issue = [&](int c) {  // warp 0: chunk c into stage c % RT_STAGES
-        float *st = rt_smem + (c % RT_STAGES) * RT_STAGE_FLOATS;
-        if (lane == 0) mbar_arrive_expect_tx(&full[c % RT_STAGES], (uint32_t)(nt + ne) * RT_KC * 4);
+    // step j (tile j / n_ch, chunk j % n_ch) into stage j % RT_STAGES: one 2D tensor copy of the
+    // token rows and one of the expert rows (rows past T or E are zero-filled, never stored)
+    auto issue = [&](int64_t j) {
+        const int64_t tile = blockIdx.x + (j / n_ch) * gridDim.x;
+        const int c = (int)(j % n_ch);
+        const int t0 = (int)((tile / tiles_e) * RT_TOK);
+        const int e0 = (int)(tile % tiles_e) * RT_EXP;
+        float *st = rt_smem + (j % RT_STAGES) * RT_STAGE_FLOATS;
+        uint64_t *bar = &full[j % RT_STAGES];
+        if (lane == 0) {
+            mbar_arrive_expect_tx(bar, (uint32_t)RT_STAGE_FLOATS * 4);
+            rt_tma_load_2d(st, &map_x, c * RT_KC, t0, bar);
+            rt_tma_load_2d(st + RT_TOK * RT_KC, &map_w, c * RT_KC, e0, bar);
+        }
         __syncwarp();
-        const int64_t col = (int64_t)c * RT_KC;
-        if (lane < nt) bulk_g2s(st + lane * RT_KC, xn + (t0 + lane) * H + col, RT_KC * 4, &full[c % RT_STAGES]);
-        if (lane < ne)
-            bulk_g2s(st + (RT_TOK + lane) * RT_KC, rw + (int64_t)(e0 + lane) * H + col, RT_KC * 4,
-                     &full[c % RT_STAGES]);
     };
     if (warp == 0)
-        for (int c = 0; c < RT_STAGES && c < n_ch; c++) issue(c);
-    const int wt = warp & 3, we = warp >> 2;
-    float acc[8][8];
+        for (int64_t j = 0; j < RT_STAGES && j < n_steps; j++) issue(j);
+    const int wt = warp & 1, we = warp >> 1;  // 2 token groups x 4 expert groups
+    float acc[8][16];
+    for (int64_t j = 0; j < n_steps; j++) {
+        const int c = (int)(j % n_ch);
+        if (c == 0) {
 #pragma unroll
-    for (int i = 0; i < 8; i++)
+            for (int i = 0; i < 8; i++)
 #pragma unroll
-        for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
-    for (int c = 0; c < n_ch; c++) {
-        const int s = c % RT_STAGES;
-        const bool ok = mbar_wait_bounded(&full[s], (uint32_t)(c / RT_STAGES) & 1u);
-        if (__syncthreads_or(!ok)) {  // every thread leaves together
+                for (int q = 0; q < 16; q++) acc[i][q] = 0.0f;
+        }
+        const int s = (int)(j % RT_STAGES);
+        const bool ok = mbar_wait_bounded(&full[s], (uint32_t)(j / RT_STAGES) & 1u);
+        // one block barrier per step: every thread leaves together on a timeout, and past it every
+        // warp is done with step j - 1, whose stage is then refilled (RT_STAGES - 1 steps ahead)
+        if (__syncthreads_or(!ok)) {
             if (threadIdx.x == 0) latch_error(err, TMOE_DEV_ERR_TIMEOUT);
             return;
         }
+        if (warp == 0 && j >= 1 && j - 1 + RT_STAGES < n_steps) issue(j - 1 + RT_STAGES);
         const float4 *xs = reinterpret_cast<const float4 *>(rt_smem + s * RT_STAGE_FLOATS) + wt * 8 * (RT_KC / 4);
         const float4 *ws =
-            reinterpret_cast<const float4 *>(rt_smem + s * RT_STAGE_FLOATS + RT_TOK * RT_KC) + we * 8 * (RT_KC / 4);
+            reinterpret_cast<const float4 *>(rt_smem + s * RT_STAGE_FLOATS + RT_TOK * RT_KC) + we * 16 * (RT_KC / 4);
 #pragma unroll
         for (int ms = 0; ms < RT_KC / 128; ms++) {
-            float4 wv[8], xv[8];
+            float4 wv[16];
 #pragma unroll
-            for (int ee = 0; ee < 8; ee++) wv[ee] = ws[ee * (RT_KC / 4) + ms * 32 + lane];
+            for (int ee = 0; ee < 16; ee++) wv[ee] = ws[ee * (RT_KC / 4) + ms * 32 + lane];
 #pragma unroll
-            for (int tt = 0; tt < 8; tt++) xv[tt] = xs[tt * (RT_KC / 4) + ms * 32 + lane];
-            // element order per accumulator: .x, .y, .z, .w; consecutive FMAs are independent
+            for (int tt = 0; tt < 8; tt++) {
+                const float4 xv = xs[tt * (RT_KC / 4) + ms * 32 + lane];
+                // element order per accumulator: .x, .y, .z, .w; consecutive FMAs are independent
 #pragma unroll
-            for (int tt = 0; tt < 8; tt++)
+                for (int ee = 0; ee < 16; ee++) acc[tt][ee] = __fmaf_rn(wv[ee].x, xv.x, acc[tt][ee]);
 #pragma unroll
-                for (int ee = 0; ee < 8; ee++) acc[tt][ee] = __fmaf_rn(wv[ee].x, xv[tt].x, acc[tt][ee]);
+                for (int ee = 0; ee < 16; ee++) acc[tt][ee] = __fmaf_rn(wv[ee].y, xv.y, acc[tt][ee]);
 #pragma unroll
-            for (int tt = 0; tt < 8; tt++)
+                for (int ee = 0; ee < 16; ee++) acc[tt][ee] = __fmaf_rn(wv[ee].z, xv.z, acc[tt][ee]);
 #pragma unroll
-                for (int ee = 0; ee < 8; ee++) acc[tt][ee] = __fmaf_rn(wv[ee].y, xv[tt].y, acc[tt][ee]);
-#pragma unroll
-            for (int tt = 0; tt < 8; tt++)
-#pragma unroll
-                for (int ee = 0; ee < 8; ee++) acc[tt][ee] = __fmaf_rn(wv[ee].z, xv[tt].z, acc[tt][ee]);
-#pragma unroll
-            for (int tt = 0; tt < 8; tt++)
-#pragma unroll
-                for (int ee = 0; ee < 8; ee++) acc[tt][ee] = __fmaf_rn(wv[ee].w, xv[tt].w, acc[tt][ee]);
+                for (int ee = 0; ee < 16; ee++) acc[tt][ee] = __fmaf_rn(wv[ee].w, xv.w, acc[tt][ee]);
+            }
         }
-        __syncthreads();  // stage s is free again
-        if (warp == 0 && c + RT_STAGES < n_ch) issue(c + RT_STAGES);
-    }
+        if (c == n_ch - 1) {  // the tile's logits
+            const int64_t tile = blockIdx.x + (j / n_ch) * gridDim.x;
+            const int64_t t0 = (tile / tiles_e) * RT_TOK;
+            const int e0 = (int)(tile % tiles_e) * RT_EXP;
 #pragma unroll
-    for (int g = 0; g < 2; g++) {
-        float v[32];
+            for (int g = 0; g < 4; g++) {  // 32 logits each: 4 tokens (4 (g & 1) ..) x 8 experts (8 (g >> 1) ..)
+                float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; j++) v[j] = acc[4 * g + j / 8][j % 8];
-        const float s = transposed_butterfly(v, lane);
-        const int tt = wt * 8 + 4 * g + lane / 8, ee = we * 8 + lane % 8;
-        if (tt < nt && ee < ne) logits[(t0 + tt) * E + e0 + ee] = s;
+                for (int q = 0; q < 32; q++) v[q] = acc[4 * (g & 1) + q / 8][8 * (g >> 1) + q % 8];
+                const float sum = transposed_butterfly(v, lane);
+                const int64_t t = t0 + wt * 8 + 4 * (g & 1) + lane / 8;
+                const int e = e0 + we * 16 + 8 * (g >> 1) + lane % 8;
+                if (t < T && e < E) logits[t * E + e] = sum;
+            }
+        }
     }
 }
 
@@ -271,12 +300,34 @@ cudaError_t launch_rms_norm(const float *x, const float *norm_w, float eps, int6
     return cudaGetLastError();
 }
 
-static bool router_tiled(int64_t T, int H) { return T >= 1024 && H % RT_KC == 0; }
+static bool router_tiled(int64_t T, int H) { return T >= 1024 && T < (1ll << 31) && H % RT_KC == 0; }
+
+// f32 [rows][H] with a box of RT_KC columns x box_rows rows, no swizzle (rows 512 bytes apart).
+static bool encode_f32_rows(CUtensorMap *m, const float *base, int64_t rows, int H, int box_rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 enc = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)H * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)RT_KC, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1u, 1u};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 cudaError_t launch_router_logits(const float *xn, const float *rw, int64_t T, int H, int E, float *logits,
                                  const Q8Rows *q8, int *err, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
-    if (!q8 && router_tiled(T, H) && ((uintptr_t)xn & 15) == 0 && ((uintptr_t)rw & 15) == 0) {
+    CUtensorMap map_x, map_w;
+    if (!q8 && router_tiled(T, H) && E >= RT_EXP && ((uintptr_t)xn & 15) == 0 && ((uintptr_t)rw & 15) == 0 &&
+        encode_f32_rows(&map_x, xn, T, H, RT_TOK) && encode_f32_rows(&map_w, rw, E, H, RT_EXP)) {
         static int set_tiled[64] = {};
         int dev = 0;
         cudaGetDevice(&dev);
@@ -287,9 +338,11 @@ cudaError_t launch_router_logits(const float *xn, const float *rw, int64_t T, in
             if (e != cudaSuccess) return e;
             set_tiled[dev] = 1;
         }
-        dim3 grid((unsigned)((E + RT_EXP - 1) / RT_EXP), (unsigned)((T + RT_TOK - 1) / RT_TOK));
-        if (grid.y > 65535) return cudaErrorInvalidValue;
-        router_logits_tiled_kernel<<<grid, 256, RT_SMEM, st>>>(xn, rw, T, H, E, logits, err);
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int64_t tiles = ((T + RT_TOK - 1) / RT_TOK) * ((E + RT_EXP - 1) / RT_EXP);
+        const unsigned grid = (unsigned)std::min<int64_t>(tiles, sms > 0 ? sms : 148);
+        router_logits_tiled_kernel<<<grid, 256, RT_SMEM, st>>>(xn, rw, T, H, E, logits, err, map_x, map_w);
         return cudaGetLastError();
     }
     constexpr int TT = 8;

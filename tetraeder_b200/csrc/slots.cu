@@ -23,81 +23,17 @@ __device__ __forceinline__ void lru_better(unsigned long long &bs, int &bi, unsi
     if (i >= 0 && (bi < 0 || s < bs || (s == bs && i < bi))) bs = s, bi = i;
 }
 
-__global__ void __launch_bounds__(SP_THREADS) slot_plan_kernel(const int32_t *__restrict__ ids, int n_pairs,
-                                                               SlotsDev s, int *err) {
-    __shared__ int first[SP_MAX_E], cnt[SP_MAX_E], order[SP_MAX_E], seq[SP_MAX_E];
-    __shared__ int slot_of[SP_MAX_E];
-    __shared__ unsigned char pinned[SP_MAX_E];
-    __shared__ int owner[SP_MAX_SLOTS];
-    __shared__ unsigned long long stamp[SP_MAX_SLOTS];
-    __shared__ int n_distinct, bad;
-    const int E = s.n_expert, tid = threadIdx.x, lane = tid & 31;
-    const int active = min(s.active[0], s.max_slots);
-    for (int e = tid; e < E; e += blockDim.x) {
-        first[e] = INT32_MAX, cnt[e] = 0;
-        slot_of[e] = s.slot_of[e], pinned[e] = s.pinned[e];
-    }
-    for (int i = tid; i < s.max_slots; i += blockDim.x) owner[i] = s.owner[i], stamp[i] = s.stamp[i];
-    for (int i = tid; i < s.max_chunks * E; i += blockDim.x) s.map[i] = -1;
-    for (int i = tid; i < s.max_chunks; i += blockDim.x) s.n_loads[i] = 0;
-    if (tid == 0) n_distinct = 0, bad = 0;
-    __syncthreads();
-    // first appearance and pair counts; lanes routed to the same expert are merged first
-    for (int base = 0; base < n_pairs; base += blockDim.x) {
-        const int p = base + tid;
-        int e = p < n_pairs ? ids[p] : -1;
-        if (p < n_pairs && (e < 0 || e >= E)) {
-            bad = 1;
-            e = -1;
-        }
-        const unsigned m = __match_any_sync(0xffffffffu, e);
-        if (e >= 0 && lane == __ffs(m) - 1) {
-            atomicMin(&first[e], p);  // the lowest lane holds the group's first pair
-            atomicAdd(&cnt[e], __popc(m));
-        }
-    }
-    __syncthreads();
-    if (bad) {  // the reference: "router chose expert {e}, out of range"
-        if (tid == 0) {
-            latch_error(err, TMOE_DEV_ERR_BADID);
-            s.n_chunks[0] = 0;
-        }
-        return;
-    }
-    for (int e = tid; e < E; e += blockDim.x) {
-        if (cnt[e]) {
-            s.counts[e] += (unsigned long long)cnt[e];
-            int r = 0;
-            for (int f = 0; f < E; f++) r += first[f] < first[e];
-            order[r] = e;
-            atomicAdd(&n_distinct, 1);
-        }
-    }
-    __syncthreads();
-    if (tid >= 32) return;
-    // warp 0: residents first, then misses, each in order of first appearance
-    const int nd = n_distinct;
-    int w = 0;
-    for (int pass = 0; pass < 2; pass++)
-        for (int i0 = 0; i0 < nd; i0 += 32) {
-            const int i = i0 + lane;
-            const bool take = i < nd && ((slot_of[order[i]] >= 0) == (pass == 0));
-            const unsigned b = __ballot_sync(0xffffffffu, take);
-            if (take) seq[w + __popc(b & ((1u << lane) - 1))] = order[i];
-            w += __popc(b);
-        }
-    __syncwarp();
-    const int n = max(active, 1);
-    const int n_chunks = (nd + n - 1) / n;
-    if (n_chunks > s.max_chunks) {
-        if (lane == 0) latch_error(err, TMOE_DEV_ERR_NOSLOT), s.n_chunks[0] = 0;
-        return;
-    }
-    unsigned long long clock = s.meta[0], hits = 0, misses = 0;
-    int failed = 0;
-    for (int q = 0; q < nd && !failed; q++) {  // make_resident of each chunk, in order
-        const int c = q / n, e = seq[q];
-        clock++;
+// One chunk's lookups by one warp, in order (LayerSlots::lookup, slots.rs:138-177): the general
+// path, used when a chunk's misses could run out of other victims (pinned residents outside the
+// chunk) and must then evict entries of the chunk itself exactly as the serial lookups do.
+// Returns the index of the lookup that found no slot, or -1.
+__device__ int chunk_serial(int c, int qa, int qb, const int *seq, int *slot_of, const unsigned char *pinned,
+                            int *owner, unsigned long long *stamp, int active, unsigned long long clock0,
+                            int *n_loads, unsigned long long &hits, unsigned long long &misses, const SlotsDev &s) {
+    const int lane = threadIdx.x & 31, E = s.n_expert;
+    for (int q = qa; q < qb; q++) {
+        const int e = seq[q];
+        const unsigned long long clock = clock0 + q + 1;
         int sl = slot_of[e];
         if (sl >= 0) {
             if (lane == 0) stamp[sl] = clock;
@@ -124,31 +60,198 @@ __global__ void __launch_bounds__(SP_THREADS) slot_plan_kernel(const int32_t *__
                 }
                 sl = bi;
             }
-            if (sl < 0) {  // every slot pinned: the reference's "no free expert slot (all pinned)"
-                failed = 1;
-                break;
-            }
+            if (sl < 0) return q;  // every slot pinned: "no free expert slot (all pinned)"
             if (lane == 0) {
                 const int ev = owner[sl];
                 if (ev >= 0) slot_of[ev] = -1;
                 owner[sl] = e, slot_of[e] = sl, stamp[sl] = clock;
-                const int li = s.n_loads[c];
-                s.loads[c * s.max_slots + li] = make_int2(e, sl);
-                s.n_loads[c] = li + 1;
+                s.loads[c * s.max_slots + n_loads[c]] = make_int2(e, sl);
+                n_loads[c]++;
             }
             misses++;
         }
         if (lane == 0) s.map[c * E + e] = sl;
         __syncwarp();
     }
-    if (lane == 0) {
-        s.meta[0] = clock, s.meta[1] += hits, s.meta[2] += misses;
+    return -1;
+}
+
+// The plan of a layer step (Streamer::plan + make_resident per chunk), one CTA:
+//  1. first appearance and pair count per expert, in per-group private tables (no atomics
+//     across groups), merged;
+//  2. the distinct experts ranked by first appearance, residents first;
+//  3. per chunk: the hits refresh their stamps; then, since the plan puts residents first, every
+//     chunk's hits precede its misses, so its misses take -- in order -- the free slots
+//     (ascending), then the unpinned residents outside the chunk by ascending stamp (ties: the
+//     lower slot), which is exactly what successive LRU lookups pick: one rank-by-count sort per
+//     chunk instead of one argmin per miss.  A chunk whose misses could outnumber those candidates
+//     (only possible with pinned residents outside it) makes the serial lookups instead.
+constexpr int SP_GROUP_WORDS = 8192;  // first + count tables of all groups: at most 32 KB
+
+__global__ void __launch_bounds__(SP_THREADS) slot_plan_kernel(const int32_t *__restrict__ ids, int n_pairs,
+                                                               SlotsDev s, int n_groups, int *err) {
+    extern __shared__ int sp_dyn[];  // [n_groups][E] first, then [n_groups][E] counts
+    __shared__ int first[SP_MAX_E], order[SP_MAX_E], seq[SP_MAX_E], slot_of[SP_MAX_E];
+    __shared__ unsigned char pinned[SP_MAX_E], in_chunk[SP_MAX_E];
+    __shared__ int owner[SP_MAX_SLOTS], cand[SP_MAX_SLOTS];
+    __shared__ unsigned long long stamp[SP_MAX_SLOTS];
+    __shared__ int n_loads[SP_MAX_E];
+    __shared__ int n_distinct, bad, n_free, n_cand, failed_at;
+    const int E = s.n_expert, S = s.max_slots, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int active = min(s.active[0], S);
+    int *gfirst = sp_dyn, *gcnt = sp_dyn + n_groups * E;
+    for (int i = tid; i < n_groups * E; i += blockDim.x) gfirst[i] = INT32_MAX, gcnt[i] = 0;
+    for (int e = tid; e < E; e += blockDim.x) slot_of[e] = s.slot_of[e], pinned[e] = s.pinned[e], in_chunk[e] = 0;
+    for (int i = tid; i < S; i += blockDim.x) owner[i] = s.owner[i], stamp[i] = s.stamp[i];
+    for (int i = tid; i < s.max_chunks * E; i += blockDim.x) s.map[i] = -1;
+    for (int i = tid; i < s.max_chunks; i += blockDim.x) n_loads[i] = 0;
+    if (tid == 0) n_distinct = 0, bad = 0, failed_at = -1;
+    __syncthreads();
+    {  // 1. group g of warps takes pairs [g * span, (g + 1) * span), 32 at a time per warp
+        const int nw = blockDim.x >> 5, wpg = nw / n_groups, g = warp / wpg, wi = warp % wpg;
+        const int span = (n_pairs + n_groups - 1) / n_groups;
+        const int p0 = g * span, p1 = min(n_pairs, p0 + span);
+        int *fg = gfirst + g * E, *cg = gcnt + g * E;
+        for (int base = p0 + 32 * wi; base < p1; base += 32 * wpg) {
+            const int p = base + lane;
+            if (p < p1) {
+                const int e = __ldg(ids + p);
+                if (e < 0 || e >= E) {
+                    bad = 1;
+                } else {
+                    atomicMin(&fg[e], p);
+                    atomicAdd(&cg[e], 1);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (bad) {  // the reference: "router chose expert {e}, out of range"
+        for (int i = tid; i < s.max_chunks; i += blockDim.x) s.n_loads[i] = 0;
+        if (tid == 0) latch_error(err, TMOE_DEV_ERR_BADID), s.n_chunks[0] = 0;
+        return;
+    }
+    for (int e = tid; e < E; e += blockDim.x) {
+        int f = INT32_MAX, n = 0;
+        for (int g = 0; g < n_groups; g++) f = min(f, gfirst[g * E + e]), n += gcnt[g * E + e];
+        first[e] = n ? f : INT32_MAX;
+        if (n) s.counts[e] += (unsigned long long)n;
+    }
+    __syncthreads();
+    // 2. rank by first appearance (first appearances are distinct pair indices)
+    for (int e = tid; e < E; e += blockDim.x) {
+        if (first[e] != INT32_MAX) {
+            int r = 0;
+            for (int f = 0; f < E; f++) r += first[f] < first[e];
+            order[r] = e;
+            atomicAdd(&n_distinct, 1);
+        }
+    }
+    __syncthreads();
+    const int nd = n_distinct;
+    if (warp == 0) {  // residents first, then misses, each in order of first appearance
+        int w = 0;
+        for (int pass = 0; pass < 2; pass++)
+            for (int i0 = 0; i0 < nd; i0 += 32) {
+                const int i = i0 + lane;
+                const bool take = i < nd && ((slot_of[order[i]] >= 0) == (pass == 0));
+                const unsigned b = __ballot_sync(0xffffffffu, take);
+                if (take) seq[w + __popc(b & ((1u << lane) - 1))] = order[i];
+                w += __popc(b);
+            }
+    }
+    __syncthreads();
+    const int n = max(active, 1);
+    const int n_chunks = (nd + n - 1) / n;
+    if (n_chunks > s.max_chunks) {
+        for (int i = tid; i < s.max_chunks; i += blockDim.x) s.n_loads[i] = 0;
+        if (tid == 0) latch_error(err, TMOE_DEV_ERR_NOSLOT), s.n_chunks[0] = 0;
+        return;
+    }
+    const unsigned long long clock0 = s.meta[0];
+    unsigned long long hits = 0, misses = 0;  // warp 0's counts on the serial path
+    int par_hits = 0, par_misses = 0;
+    for (int c = 0; c < n_chunks; c++) {
+        const int qa = c * n, qb = min(nd, qa + n);
+        // 3a. hits (residents at the start of the chunk) refresh their stamps
+        for (int q = qa + tid; q < qb; q += blockDim.x) {
+            const int e = seq[q];
+            in_chunk[e] = 1;
+            const int sl = slot_of[e];
+            if (sl >= 0) {
+                stamp[sl] = clock0 + q + 1;
+                s.map[c * E + e] = sl;
+            }
+        }
+        if (tid == 0) n_free = 0, n_cand = 0;
+        __syncthreads();
+        int h = 0;  // the chunk's hits: a prefix of it
+        for (int q = qa; q < qb && slot_of[seq[q]] >= 0; q++) h++;
+        const int m = (qb - qa) - h;
+        // 3b. victims: free slots (ascending), then unpinned residents outside the chunk by stamp
+        for (int i = tid; i < active; i += blockDim.x) {
+            const int o = owner[i];
+            if (o < 0) atomicAdd(&n_free, 1);
+            else if (!pinned[o] && !in_chunk[o]) atomicAdd(&n_cand, 1);
+        }
+        __syncthreads();
+        const int nf = n_free, nc = n_cand;
+        if (m > nf + nc) {  // only with pinned residents outside the chunk: the serial lookups
+            if (warp == 0) {
+                const int fq = chunk_serial(c, qa, qb, seq, slot_of, pinned, owner, stamp, active, clock0, n_loads,
+                                            hits, misses, s);
+                if (lane == 0) failed_at = fq;
+                __syncwarp();
+            }
+            __syncthreads();
+            for (int q = qa + tid; q < qb; q += blockDim.x) in_chunk[seq[q]] = 0;
+            __syncthreads();
+            if (failed_at >= 0) break;
+            continue;
+        }
+        for (int i = tid; i < active; i += blockDim.x) {
+            const int o = owner[i];
+            int r = -1;
+            if (o < 0) {  // rank among the free slots: by index
+                r = 0;
+                for (int j = 0; j < i; j++) r += owner[j] < 0;
+            } else if (!pinned[o] && !in_chunk[o]) {  // after the free slots: by (stamp, slot)
+                r = nf;
+                const unsigned long long si = stamp[i];
+                for (int j = 0; j < active; j++) {
+                    const int oj = owner[j];
+                    if (oj >= 0 && !pinned[oj] && !in_chunk[oj] && (stamp[j] < si || (stamp[j] == si && j < i))) r++;
+                }
+            }
+            if (r >= 0 && r < m) cand[r] = i;
+        }
+        __syncthreads();
+        // 3c. miss i takes cand[i]
+        for (int i = tid; i < m; i += blockDim.x) {
+            const int q = qa + h + i, e = seq[q], sl = cand[i];
+            const int ev = owner[sl];
+            if (ev >= 0) slot_of[ev] = -1;
+            owner[sl] = e, slot_of[e] = sl, stamp[sl] = clock0 + q + 1;
+            s.loads[c * S + i] = make_int2(e, sl);
+            s.map[c * E + e] = sl;
+        }
+        if (tid == 0) n_loads[c] = m, par_hits += h, par_misses += m;
+        __syncthreads();
+        for (int q = qa + tid; q < qb; q += blockDim.x) in_chunk[seq[q]] = 0;
+        __syncthreads();
+    }
+    if (tid == 0) {  // every lookup advances the clock, the failed one included (slots.rs:143)
+        const bool failed = failed_at >= 0;
+        s.meta[0] = clock0 + (unsigned long long)(failed ? failed_at + 1 : nd);
+        s.meta[1] += hits + (unsigned long long)par_hits;
+        s.meta[2] += misses + (unsigned long long)par_misses;
         if (failed) s.meta[3] += 1, latch_error(err, TMOE_DEV_ERR_NOSLOT);
         s.n_chunks[0] = failed ? 0 : n_chunks;
     }
-    __syncwarp();
-    for (int e = lane; e < E; e += 32) s.slot_of[e] = slot_of[e];
-    for (int i = lane; i < s.max_slots; i += 32) s.owner[i] = owner[i], s.stamp[i] = stamp[i];
+    __syncthreads();
+    for (int e = tid; e < E; e += blockDim.x) s.slot_of[e] = slot_of[e];
+    for (int i = tid; i < S; i += blockDim.x) s.owner[i] = owner[i], s.stamp[i] = stamp[i];
+    for (int i = tid; i < s.max_chunks; i += blockDim.x) s.n_loads[i] = n_loads[i];
 }
 
 // Copies the experts of chunk c's loads from the host store into their slots: blockIdx.y = load,
@@ -256,7 +359,20 @@ bool slots_fit(int n_expert, int max_slots) {
 }
 
 cudaError_t launch_slot_plan(const int32_t *ids, int n_pairs, const SlotsDev &s, int *err, cudaStream_t st) {
-    slot_plan_kernel<<<1, SP_THREADS, 0, st>>>(ids, n_pairs, s, err);
+    int groups = 32;  // a power of two dividing the 32 warps, its tables within SP_GROUP_WORDS
+    while (groups > 1 && groups * 2 * s.n_expert > SP_GROUP_WORDS) groups >>= 1;
+    const size_t smem = (size_t)groups * 2 * s.n_expert * 4;
+    static int set_bytes[64] = {};  // static + dynamic shared memory exceed the default 48 KB
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!set_bytes[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(slot_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   SP_GROUP_WORDS * 4);
+        if (e != cudaSuccess) return e;
+        set_bytes[dev] = 1;
+    }
+    slot_plan_kernel<<<1, SP_THREADS, smem, st>>>(ids, n_pairs, s, groups, err);
     return cudaGetLastError();
 }
 

@@ -258,7 +258,8 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
         // gate/up as exact grouped tcgen05 GEMMs (rows in expert-sorted order), then the down GEMM
         {
             PhaseMark pm(h, st, TMOE_PHASE_QUANT_X);
-            e = tmoe::launch_prep_gateup_a(xn, (int)T, h->perm, (int)P, k, H, h->aq16_t, h->ad16_t, h->ab16_t, h->aq16,
+            e = tmoe::launch_prep_gateup_a(xn, (int)T, h->perm, (int)P, h->offsets + t->n_slots, k, H, h->aq16_t,
+                                           h->ad16_t, h->ab16_t, h->aq16,
                                            h->ad16, h->ab16, st);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "prefill gate/up rows");
