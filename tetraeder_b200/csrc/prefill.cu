@@ -461,7 +461,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(const __gri
 //   main_b[t][n] = sum_{k in b} q_x[t][k] * (sc[n][s(k)] * q[n][k])   (q_x int8, sc*q <= 945)
 //   min_b[t][n]  = sum_s  B[t][b][s] * m[n][b][s]                       (B = 64 * hi + lo: K = 16)
 //   out[t][n]   += d_x[t][b] * (d[n][b] * main_b - dmin[n][b] * min_b)   (the ggml Q4_K x Q8_K dot)
-// The per-block accumulators live in TMEM (main and min, double-buffered: 4 x 128 columns) and
+// The min term shares the block's accumulator: acc = main_b - (dmin / d) * min_b, with the block
+// sums as [64 hi, lo] (exact) against c = -(dmin / d) * m as a high and a low fp16 part (two K = 16
+// MMAs; about 22 bits of c), and the epilogue folds out += d_x * d * acc: one TMEM value per output
+// and block instead of two.
+// The per-block accumulators live in TMEM (double-buffered: 2 x 128 columns) and
 // the epilogue warps fold them into per-thread running sums while the next block's MMAs run.  A
 // tile is 128 token rows x 64 features of gate and the same 64 of up (128 MMA columns); the
 // SwiGLU happens once per tile.  Warps: 0 TMA (q_x rows, block sums), 1 MMA, 2-5 dequantise the
@@ -474,7 +478,8 @@ constexpr int GU_RAW_BYTES = 128 * TMOE_Q4K_BYTES;  // one super-block of the ti
 constexpr int GU_RAWN = 3;  // raw prefetch buffers: two blocks ahead
 // shared memory: the rings, the scales, 512 bytes of barriers, then the tile tables; plus 1024 bytes
 // of alignment slack
-constexpr int GU_FIXED = GU_S * (2 * PF_A_BYTES) + 2 * 2 * GU_AP_BYTES + GU_RAWN * GU_RAW_BYTES + 2 * 128 * 8 + 512;
+constexpr int GU_FIXED = GU_S * (2 * PF_A_BYTES) + 6 * GU_AP_BYTES + GU_RAWN * GU_RAW_BYTES + 2 * 128 * 8 + 512;
+constexpr uint32_t GU_TMEM_COLS = 256;  // two accumulators of 128 columns (64 gate + 64 up features)
 static_assert((GU_S * 4 + 12) * 8 + 16 <= 512, "barrier room");
 
 // K-major, no swizzle: 8-row x 16-byte core matrices, rows 16 bytes apart, 8-row groups 128 bytes
@@ -532,8 +537,8 @@ __global__ void prep_gateup_a_kernel(const float *__restrict__ x, const int32_t 
     *reinterpret_cast<uint4 *>(aq + r * K + b * TMOE_QK + 8 * lane) = *reinterpret_cast<const uint4 *>(h);
     const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);  // lanes 4s hold sub-block s's sum
     if ((lane & 3) == 0) {
-        const int sb = lane >> 2, hi = s32 >> 6, lo = s32 - 64 * hi;
-        __half2 pr = __halves2half2(__int2half_rn(hi), __int2half_rn(lo));
+        const int sb = lane >> 2, hi = s32 >> 6, lo = s32 - 64 * hi;  // 64 hi in [-4096, 4032]: exact
+        __half2 pr = __halves2half2(__int2half_rn(64 * hi), __int2half_rn(lo));
         *reinterpret_cast<__half2 *>(ab + (r * nb + b) * 16 + 2 * sb) = pr;
     }
     if (lane == 0) ad[r * nb + b] = d;
@@ -616,9 +621,9 @@ __global__ void __launch_bounds__(GU_THREADS, 1) prefill_gateup_kernel(const __g
     uint8_t *sA = smem;                                  // [GU_S][128 x 64 fp16, sw128]
     uint8_t *sB = sA + GU_S * PF_A_BYTES;                // [GU_S][128 x 64 fp16, sw128]
     uint8_t *sAp = sB + GU_S * PF_A_BYTES;               // [2][min operand A]
-    uint8_t *sBp = sAp + 2 * GU_AP_BYTES;                // [2][min operand B]
-    uint8_t *sRaw = sBp + 2 * GU_AP_BYTES;               // [GU_RAWN][128 rows x 144 B], the dequant prefetch
-    float2 *scl = reinterpret_cast<float2 *>(sRaw + GU_RAWN * GU_RAW_BYTES);  // [2][128] {d, dmin}
+    uint8_t *sBp = sAp + 2 * GU_AP_BYTES;                // [2][hi, lo][min operand B]
+    uint8_t *sRaw = sBp + 4 * GU_AP_BYTES;               // [GU_RAWN][128 rows x 144 B], the dequant prefetch
+    float2 *scl = reinterpret_cast<float2 *>(sRaw + GU_RAWN * GU_RAW_BYTES);  // [2][128] {fold scale, 0}
     uint64_t *bars = reinterpret_cast<uint64_t *>(scl + 2 * 128);
     uint64_t *fa = bars, *ea = fa + GU_S, *fb = ea + GU_S, *eb = fb + GU_S;
     uint64_t *fap = eb + GU_S, *eap = fap + 2, *fbp = eap + 2, *ebp = fbp + 2, *fsc = ebp + 2, *esc = fsc + 2;
@@ -654,7 +659,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) prefill_gateup_kernel(const __g
         fence_barrier_init();
     }
     if (warp == 0) {
-        tmem_alloc(tmem_slot, PF_TMEM_COLS);
+        tmem_alloc(tmem_slot, GU_TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -696,7 +701,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) prefill_gateup_kernel(const __g
                     const int buf = it_b & 1;
                     if (it_b >= 2) GU_WAIT(&te[buf], ((it_b >> 1) - 1) & 1);
                     tc_fence_after();
-                    const uint32_t dmain = tmem_base + (uint32_t)(buf * 256), dmin = dmain + 128;
+                    const uint32_t dmain = tmem_base + (uint32_t)(buf * 128);
                     for (int st = 0; st < 4; st++, it_s++) {
                         const int s = it_s % GU_S;
                         GU_WAIT(&fa[s], (it_s / GU_S) & 1);
@@ -712,8 +717,12 @@ __global__ void __launch_bounds__(GU_THREADS, 1) prefill_gateup_kernel(const __g
                     GU_WAIT(&fap[buf], (it_b >> 1) & 1);
                     GU_WAIT(&fbp[buf], (it_b >> 1) & 1);
                     tc_fence_after();
-                    umma_f16(dmin, kmajor_plain_desc(smem_u32(sAp + buf * GU_AP_BYTES)),
-                             kmajor_plain_desc(smem_u32(sBp + buf * GU_AP_BYTES)), idesc, 0u);
+                    // the min term joins the block's accumulator: A' = [64 hi, lo] x B' = c split
+                    // exactly into two fp16 parts (c_hi, then c_lo), c = -(dmin / s) * m
+                    const uint64_t ap = kmajor_plain_desc(smem_u32(sAp + buf * GU_AP_BYTES));
+                    umma_f16(dmain, ap, kmajor_plain_desc(smem_u32(sBp + buf * 2 * GU_AP_BYTES)), idesc, 1u);
+                    umma_f16(dmain, ap, kmajor_plain_desc(smem_u32(sBp + buf * 2 * GU_AP_BYTES + GU_AP_BYTES)), idesc,
+                             1u);
                     umma_commit(&eap[buf]);
                     umma_commit(&ebp[buf]);
                     umma_commit(&tf[buf]);
@@ -756,6 +765,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) prefill_gateup_kernel(const __g
         prefetch();
         prefetch();
         const uint32_t EXP2 = 0x64006400u;  // fp16 1024 in both halves
+        float fn = 1.0f;                    // the current block's main-value factor (see below)
         while (tile < n_tiles && !*abort_flag) {
             const uint8_t *cur = my_raw + rb * GU_RAW_BYTES;
             prefetch();        // two blocks ahead
@@ -778,17 +788,32 @@ __global__ void __launch_bounds__(GU_THREADS, 1) prefill_gateup_kernel(const __g
                 GU_WAIT_WARP(&esc[i2], ((it_b >> 1) - 1) & 1);
                 GU_WAIT_WARP(&ebp[i2], ((it_b >> 1) - 1) & 1);
             }
-            scl[i2 * 128 + n] = make_float2(d, dmin);
-            {  // min operand row n: {64 m_s, m_s} for s = 0..7 at K 2s, 2s+1
-                uint32_t mw[8];
+            // The block's fold scale sn and the factor fn of its main values: normally sn = d and fn = 1
+            // (the main values sc * q stay exact integers).  Rows whose min scale dwarfs d (|dmin| >
+            // 1024 |d|, or d = 0) fold with sn = |dmin| / 1024 instead, so that c below stays within
+            // fp16; their main values, a tiny share of the dot there, are then rounded to fp16.
+            const bool normal = d != 0.0f && fabsf(dmin) <= 1024.0f * fabsf(d);
+            const float sn = normal ? d : (dmin != 0.0f ? fabsf(dmin) * (1.0f / 1024.0f) : 1.0f);
+            fn = normal ? 1.0f : __fdiv_rn(d, sn);
+            const float rm = -__fdiv_rn(dmin, sn);
+            scl[i2 * 128 + n] = make_float2(sn, 0.0f);
+            {  // min operand row n: c_s = rm * m_s at K 2s and 2s+1 (against 64 hi_s and lo_s), as
+               // c_hi (first operand) + c_lo (second), each fp16
+                uint32_t wh[8], wl[8];
 #pragma unroll
                 for (int sb = 0; sb < 8; sb++) {
                     const int mv = (int)((sb < 4 ? m_lo : m_hi) >> (8 * (sb & 3))) & 0xff;
-                    mw[sb] = h2_bits(__halves2half2(__int2half_rn(64 * mv), __int2half_rn(mv)));
+                    const float c = __fmul_rn(rm, (float)mv);
+                    const __half ch = __float2half_rn(c);
+                    const __half cl = __float2half_rn(__fsub_rn(c, __half2float(ch)));
+                    wh[sb] = h2_bits(__halves2half2(ch, ch));
+                    wl[sb] = h2_bits(__halves2half2(cl, cl));
                 }
-                uint8_t *bp = sBp + i2 * GU_AP_BYTES + n * 16;
-                *reinterpret_cast<uint4 *>(bp) = make_uint4(mw[0], mw[1], mw[2], mw[3]);
-                *reinterpret_cast<uint4 *>(bp + 2048) = make_uint4(mw[4], mw[5], mw[6], mw[7]);
+                uint8_t *bp = sBp + i2 * 2 * GU_AP_BYTES + n * 16;
+                *reinterpret_cast<uint4 *>(bp) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+                *reinterpret_cast<uint4 *>(bp + 2048) = make_uint4(wh[4], wh[5], wh[6], wh[7]);
+                *reinterpret_cast<uint4 *>(bp + GU_AP_BYTES) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+                *reinterpret_cast<uint4 *>(bp + GU_AP_BYTES + 2048) = make_uint4(wl[4], wl[5], wl[6], wl[7]);
             }
             fence_proxy_async_smem();
             __syncwarp();
@@ -807,10 +832,11 @@ __global__ void __launch_bounds__(GU_THREADS, 1) prefill_gateup_kernel(const __g
                 const uint4 qa = raw[1 + 2 * st], qb = raw[2 + 2 * st];
                 const int scl_l = (int)((st < 2 ? s_lo : s_hi) >> (16 * (st & 1))) & 0xff;
                 const int scl_h = (int)((st < 2 ? s_lo : s_hi) >> (16 * (st & 1) + 8)) & 0xff;
-                const __half2 ml = __half2half2(__int2half_rn(scl_l));
-                const __half2 al = __half2half2(__int2half_rn(-1024 * scl_l));
-                const __half2 mh = __half2half2(__hmul(__int2half_rn(scl_h), __float2half_rn(0.0625f)));
-                const __half2 ah = __half2half2(__int2half_rn(-64 * scl_h));
+                // (exact for fn = 1: sc, -1024 sc, sc / 16 and -64 sc are all fp16 integers/dyadics)
+                const __half ml1 = __float2half_rn(__fmul_rn(fn, (float)scl_l));
+                const __half mh1 = __float2half_rn(__fmul_rn(fn, __fmul_rn((float)scl_h, 0.0625f)));
+                const __half2 ml = __half2half2(ml1), al = __half2half2(__hmul(ml1, __float2half_rn(-1024.0f)));
+                const __half2 mh = __half2half2(mh1), ah = __half2half2(__hmul(mh1, __float2half_rn(-1024.0f)));
                 const uint32_t wq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
                 uint8_t *brow = sB + s * PF_A_BYTES + n * 128;
 #pragma unroll
@@ -862,11 +888,11 @@ __global__ void __launch_bounds__(GU_THREADS, 1) prefill_gateup_kernel(const __g
                 GU_WAIT_WARP(&tf[buf], (it_b >> 1) & 1);
                 GU_WAIT_WARP(&fsc[buf], (it_b >> 1) & 1);
                 tc_fence_after();
-                const uint32_t taddr = tmem_base + (uint32_t)(buf * 256) + ((uint32_t)(q * 32) << 16);
-                const float4 *sg = reinterpret_cast<const float4 *>(scl + buf * 128 + 32 * h);  // {d, dmin} x 2
+                const uint32_t taddr = tmem_base + (uint32_t)(buf * 128) + ((uint32_t)(q * 32) << 16);
+                const float4 *sg = reinterpret_cast<const float4 *>(scl + buf * 128 + 32 * h);  // {sn, 0} x 2
                 const float4 *su = sg + 32;
                 float v[32];
-                tmem_ld32(taddr + 32 * h, v);  // main, gate features
+                tmem_ld32(taddr + 32 * h, v);  // gate features 32h ..
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
@@ -874,29 +900,13 @@ __global__ void __launch_bounds__(GU_THREADS, 1) prefill_gateup_kernel(const __g
                     tg[i] = __fmaf_rn(dx * s4.x, v[i], tg[i]);
                     tg[i + 1] = __fmaf_rn(dx * s4.z, v[i + 1], tg[i + 1]);
                 }
-                tmem_ld32(taddr + 128 + 32 * h, v);  // min, gate
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const float4 s4 = sg[i >> 1];
-                    tg[i] = __fmaf_rn(-dx * s4.y, v[i], tg[i]);
-                    tg[i + 1] = __fmaf_rn(-dx * s4.w, v[i + 1], tg[i + 1]);
-                }
-                tmem_ld32(taddr + 64 + 32 * h, v);  // main, up
+                tmem_ld32(taddr + 64 + 32 * h, v);  // up features 32h ..
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
                     const float4 s4 = su[i >> 1];
                     tu[i] = __fmaf_rn(dx * s4.x, v[i], tu[i]);
                     tu[i + 1] = __fmaf_rn(dx * s4.z, v[i + 1], tu[i + 1]);
-                }
-                tmem_ld32(taddr + 192 + 32 * h, v);  // min, up
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const float4 s4 = su[i >> 1];
-                    tu[i] = __fmaf_rn(-dx * s4.y, v[i], tu[i]);
-                    tu[i + 1] = __fmaf_rn(-dx * s4.w, v[i + 1], tu[i + 1]);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -920,7 +930,7 @@ done:
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, PF_TMEM_COLS);
+        tmem_dealloc(tmem_base, GU_TMEM_COLS);
     }
 }
 #undef GU_WAIT
