@@ -66,6 +66,9 @@ def parse():
                    help="decode: C2 at T tokens (the metric's config); prefill: C2-shaped layer at T=8192 "
                         "(tensor roofline); streamed: config 5, skewed routing over 64 device slots of 128 experts")
     p.add_argument("--slots", type=int, default=64)
+    p.add_argument("--ep", choices=["a2a", "allreduce"], default="a2a",
+                   help="N > 1: a2a = each rank its own --tokens, dispatched to the experts' ranks (all-to-all); "
+                        "allreduce = the reference's EP mode, the same tokens on every rank, outputs summed")
     a = p.parse_args()
     if a.mode != "decode" and a.tokens == 64:
         a.tokens = 8192
@@ -168,16 +171,18 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     T, L = args.tokens, args.layers
     ep = world > 1
+    a2a = ep and args.ep == "a2a"
     # N = 1: the layer on one GPU.  N > 1: the reference's EP mode, experts split contiguously over
     # the ranks, the same tokens on every rank, partial outputs summed with NCCL (strong scaling)
     layers = make_layers(torch, moe, L, args.seed, dev, world, rank)
     log(f"{L} layers generated ({E // world} experts each on this rank)")
     gen = torch.Generator(device=dev)
-    gen.manual_seed(args.seed + 1)
+    gen.manual_seed(args.seed + 1 + (rank if a2a else 0))  # a2a: every rank has tokens of its own
     x_dev = torch.randn((T, H), generator=gen, device=dev)
     x_host = x_dev.cpu().pin_memory()
     out_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
-    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=Q6K, max_tokens=T, device=local_rank)
+    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=Q6K,
+                        max_tokens=world * T if a2a else T, device=local_rank)
     outs = [torch.empty((T, H), device=dev) for _ in range(L)]
     ids = [torch.empty((T, K_USED), dtype=torch.int32, device=dev) for _ in range(L)]
     ws = [torch.empty((T, K_USED), dtype=torch.float32, device=dev) for _ in range(L)]
@@ -190,7 +195,9 @@ def run_ours(args, rank, world, local_rank):
 
     def call(li, x):
         rw, wts = layers[li]
-        if ep:
+        if a2a:
+            moe.ep_a2a_moe_ffn(layer, comm, x, wts, router_w=rw, out=outs[li], ids_out=ids[li], w_out=ws[li])
+        elif ep:
             moe.ep_moe_ffn(layer, comm, x, wts, table, router_w=rw, out=outs[li], ids_out=ids[li], w_out=ws[li])
         else:
             layer.moe_ffn(x, wts, router_w=rw, out=outs[li], ids_out=ids[li], w_out=ws[li])
@@ -247,7 +254,8 @@ def run_ours(args, rank, world, local_rank):
     clocks = clk.summary()
     layer.check()
     log(f"graph timed: {ms / args.steps:.3f} ms/step")
-    units = (1 if ep else world) * args.steps * L * T  # EP: the ranks process the same tokens jointly
+    # all-reduce EP: the ranks process the same tokens jointly; a2a and replicas: T tokens per rank
+    units = (1 if ep and not a2a else world) * args.steps * L * T
     value = units / (ms / 1e3)
 
     def e2e_step():
@@ -259,11 +267,19 @@ def run_ours(args, rank, world, local_rank):
     e2e_value = units / (e2e_ms / 1e3)
     log(f"e2e timed: {e2e_ms / args.steps:.3f} ms/step")
 
-    # distinct experts per layer (the D of the roofline bytes)
-    distinct = [int(torch.unique(ids[li]).numel()) for li in range(L)]
+    # distinct experts per layer (the D of the roofline bytes); a2a: over every rank's tokens
+    if a2a:
+        all_ids = []
+        for li in range(L):
+            parts = [torch.empty_like(ids[li]) for _ in range(world)]
+            dist.all_gather(parts, ids[li])
+            all_ids.append(torch.cat(parts))
+    else:
+        all_ids = ids
+    distinct = [int(torch.unique(all_ids[li]).numel()) for li in range(L)]
     if ep:  # this rank's GEMVs read only the experts it holds
         lo, hi = rank * (E // world), (rank + 1) * (E // world)
-        local = [int(((u >= lo) & (u < hi)).sum()) for u in (torch.unique(ids[li]) for li in range(L))]
+        local = [int(((u >= lo) & (u < hi)).sum()) for u in (torch.unique(all_ids[li]) for li in range(L))]
     else:
         local = distinct
 
@@ -334,7 +350,10 @@ def run_ours(args, rank, world, local_rank):
                 "path": "tmoe_layer C-ABI calls (ctypes) x 48 + pinned H2D/D2H"},
         "gpu_launches": int(launches_per_call * L * args.steps), "clocks": clocks,
     }
-    if ep:
+    if a2a:
+        result["config"]["parallelism"] = (f"ep{world} all-to-all (experts split contiguously, {T} tokens per rank "
+                                           "dispatched to the experts' ranks and combined back over NCCL)")
+    elif ep:
         result["config"]["parallelism"] = f"ep{world} (experts split contiguously, tokens replicated, NCCL all-reduce)"
         result["scaling"] = "strong"
     if args.sweep and rank == 0 and not ep:
@@ -380,7 +399,8 @@ def run_streamed(args, local_rank):
     gen.manual_seed(args.seed + 1)
     x = torch.randn((T, H), generator=gen, device=dev)
     lg = torch.randn((T, E), generator=gen, device=dev) + bias.to(dev)
-    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=Q6K, max_tokens=T, device=local_rank)
+    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=Q6K,
+                        max_tokens=world * T if a2a else T, device=local_rank)
     cache = tb.SlotCache(layer, slots, store)
     cache.make_resident([int(e) for e in perm[:NS]])
     out = torch.empty((T, H), device=dev)
@@ -592,8 +612,21 @@ def run_reference(args):
                     "here; the oracle/ C restatement of its semantics is timed instead"}
 
 
+_JSON_FD = None  # the original stdout: it carries only the JSON line
+
+
+def emit(obj):
+    os.write(_JSON_FD if _JSON_FD is not None else 1, (json.dumps(obj) + "\n").encode())
+
+
 def main():
+    global _JSON_FD
     args = parse()
+    # stdout carries the one JSON line; anything else written to file descriptor 1 (NCCL's version
+    # banner, library output) goes to stderr
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     faulthandler.dump_traceback_later(int(os.environ.get("TMOE_BENCH_WATCHDOG_S", "420")), exit=False)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -601,7 +634,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0
-        print(json.dumps(run_reference(args)), flush=True)
+        emit(run_reference(args))
         return 0
     if world > 1:
         import torch
@@ -613,7 +646,7 @@ def main():
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(args)
-        print(json.dumps(res), flush=True)
+        emit(res)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
