@@ -400,7 +400,7 @@ def run_streamed(args, local_rank):
     x = torch.randn((T, H), generator=gen, device=dev)
     lg = torch.randn((T, E), generator=gen, device=dev) + bias.to(dev)
     layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=Q6K,
-                        max_tokens=world * T if a2a else T, device=local_rank)
+                        max_tokens=T, device=local_rank)
     cache = tb.SlotCache(layer, slots, store)
     cache.make_resident([int(e) for e in perm[:NS]])
     out = torch.empty((T, H), device=dev)
