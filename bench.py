@@ -44,10 +44,24 @@ def log(msg):
 
 H, I, E, K_USED = 2048, 768, 128, 8
 Q4K, Q6K = 12, 14
+DOWN_T = Q6K                                                      # Q4_K_M promotes ffn_down to Q6_K
 EXPERT_BYTES = 2 * I * (H // 256) * 144 + H * (I // 256) * 210  # 3,059,712
 GATE_UP_BYTES = 2 * I * (H // 256) * 144                          # 1,769,472
 DOWN_BYTES = H * (I // 256) * 210                                 # 1,290,240
 ROUTER_BYTES = E * H * 4                                          # 1,048,576
+
+
+def set_shape(name):
+    """c2: the Qwen3-30B-A3B layer (the metric's config); 235b: the Qwen3-235B-A22B layer of config 4
+    (hidden 4096, moe_intermediate 1536, 128 experts, top-8, all Q4_K)."""
+    global H, I, DOWN_T, EXPERT_BYTES, GATE_UP_BYTES, DOWN_BYTES, ROUTER_BYTES
+    if name == "235b":
+        H, I, DOWN_T = 4096, 1536, Q4K
+    down_block = 210 if DOWN_T == Q6K else 144
+    GATE_UP_BYTES = 2 * I * (H // 256) * 144
+    DOWN_BYTES = H * (I // 256) * down_block
+    EXPERT_BYTES = GATE_UP_BYTES + DOWN_BYTES
+    ROUTER_BYTES = E * H * 4
 
 
 def parse():
@@ -66,10 +80,13 @@ def parse():
                    help="decode: C2 at T tokens (the metric's config); prefill: C2-shaped layer at T=8192 "
                         "(tensor roofline); streamed: config 5, skewed routing over 64 device slots of 128 experts")
     p.add_argument("--slots", type=int, default=64)
+    p.add_argument("--shape", choices=["c2", "235b"], default="c2",
+                   help="c2: the Qwen3-30B-A3B layer (the metric's config); 235b: config 4's layer shape")
     p.add_argument("--ep", choices=["a2a", "allreduce"], default="a2a",
                    help="N > 1: a2a = each rank its own --tokens, dispatched to the experts' ranks (all-to-all); "
                         "allreduce = the reference's EP mode, the same tokens on every rank, outputs summed")
     a = p.parse_args()
+    set_shape(a.shape)
     if a.mode != "decode" and a.tokens == 64:
         a.tokens = 8192
     if a.mode == "prefill" and a.layers == 48:
@@ -78,6 +95,15 @@ def parse():
 
 
 def workload(args, n_gpus):
+    if args.shape == "235b":
+        name = {"decode": "C4 Qwen3-235B-A22B-shaped MoE layer, decode",
+                "prefill": "C4 Qwen3-235B-A22B-shaped MoE layer, prefill",
+                "streamed": "C4-shaped layer, streamed"}[args.mode]
+        return {"workload": name, "tokens_per_layer_call": args.tokens, "n_embd": H, "n_ff": I, "n_expert": E,
+                "n_expert_used": K_USED, "types": "gate/up/down Q4_K (this repo's quantiser)",
+                "layers_per_step": args.layers,
+                "l2": f"inputs larger than L2: {args.layers} distinct resident layers rotated each step",
+                "parallelism": f"replicas x{n_gpus}" if n_gpus > 1 else "single GPU", "seed": args.seed}
     name = {"decode": "C2 Qwen3-30B-A3B MoE layer, decode",
             "prefill": "C2-shaped Qwen3-30B-A3B MoE layer, prefill (north-star tensor target)",
             "streamed": "C5 skewed large-batch stress, 64 of 128 experts in device slots"}[args.mode]
@@ -154,7 +180,7 @@ def make_layers(torch, moe, n_layers, seed, device, world=1, rank=0):
         rw = torch.randn((E, H), generator=g, device=device) * 0.02
         gate = moe.quantize(Q4K, torch.randn((per, I, H), generator=ge, device=device) * 0.02)
         up = moe.quantize(Q4K, torch.randn((per, I, H), generator=ge, device=device) * 0.02)
-        down = moe.quantize(Q6K, torch.randn((per, H, I), generator=ge, device=device) * 0.02)
+        down = moe.quantize(DOWN_T, torch.randn((per, H, I), generator=ge, device=device) * 0.02)
         layers.append((rw, moe.ExpertWeights(gate, up, down)))
     torch.cuda.synchronize()
     return layers
@@ -181,7 +207,7 @@ def run_ours(args, rank, world, local_rank):
     x_dev = torch.randn((T, H), generator=gen, device=dev)
     x_host = x_dev.cpu().pin_memory()
     out_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
-    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=Q6K,
+    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=DOWN_T,
                         max_tokens=world * T if a2a else T, device=local_rank)
     outs = [torch.empty((T, H), device=dev) for _ in range(L)]
     ids = [torch.empty((T, K_USED), dtype=torch.int32, device=dev) for _ in range(L)]
@@ -313,7 +339,8 @@ def run_ours(args, rank, world, local_rank):
     layer_ms = ms / (args.steps * L)
     roofline = {"bound": "hbm", "kernel": f"gemv_kernel ({dom})", "achieved": round(achieved, 1),
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                "peak_source": peaks["source"], "traffic": None if ep else traffic_from_profiles(dom),
+                "peak_source": peaks["source"],
+                "traffic": None if ep or args.shape != "c2" else traffic_from_profiles(dom),
                 "algorithmic_bytes_per_launch": int(dom_bytes), "avg_launch_us": round(phase_ms[dom] * 1e3, 2)}
     layer_roof = {"bytes_per_layer_call": int(layer_bytes), "distinct_experts_mean": round(d_mean, 2),
                   "us_per_layer_call": round(layer_ms * 1e3, 2),
@@ -399,7 +426,7 @@ def run_streamed(args, local_rank):
     gen.manual_seed(args.seed + 1)
     x = torch.randn((T, H), generator=gen, device=dev)
     lg = torch.randn((T, E), generator=gen, device=dev) + bias.to(dev)
-    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=Q6K,
+    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=DOWN_T,
                         max_tokens=T, device=local_rank)
     cache = tb.SlotCache(layer, slots, store)
     cache.make_resident([int(e) for e in perm[:NS]])
@@ -485,7 +512,7 @@ def sweep_tokens(torch, tb, layers, dev):
     res = {}
     for T in (1, 4, 16, 64):
         log(f"sweep T={T}")
-        layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=Q6K, max_tokens=T,
+        layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=DOWN_T, max_tokens=T,
                             device=dev.index)
         x = torch.randn((T, H), device=dev)
         out = torch.empty((T, H), device=dev)
@@ -553,7 +580,7 @@ def host_layer(seed, T):
     rng = np.random.default_rng(seed)
     gate = O.quantize(O.TYPE_Q4_K, (rng.standard_normal((E, I, H), dtype=np.float32) * 0.02))
     up = O.quantize(O.TYPE_Q4_K, (rng.standard_normal((E, I, H), dtype=np.float32) * 0.02))
-    down = O.quantize(O.TYPE_Q6_K, (rng.standard_normal((E, H, I), dtype=np.float32) * 0.02))
+    down = O.quantize(DOWN_T, (rng.standard_normal((E, H, I), dtype=np.float32) * 0.02))
     rw = (rng.standard_normal((E, H), dtype=np.float32) * 0.02)
     x = rng.standard_normal((T, H), dtype=np.float32)
     return gate, up, down, rw, x
@@ -573,12 +600,12 @@ def cpu_baseline(args):
     gate, up, down, rw, x = host_layer(args.seed, T)
     threads = cpu_threads()
     t0 = time.perf_counter()
-    O.layer(x, K_USED, gate, up, down, H, I, E, router_w=rw, down_type=O.TYPE_Q6_K, nthreads=threads)
+    O.layer(x, K_USED, gate, up, down, H, I, E, router_w=rw, down_type=DOWN_T, nthreads=threads)
     first = time.perf_counter() - t0
     n = max(1, int(args.cpu_sample_s / max(first, 1e-3)))
     t0 = time.perf_counter()
     for _ in range(n):
-        O.layer(x, K_USED, gate, up, down, H, I, E, router_w=rw, down_type=O.TYPE_Q6_K, nthreads=threads)
+        O.layer(x, K_USED, gate, up, down, H, I, E, router_w=rw, down_type=DOWN_T, nthreads=threads)
     dt = time.perf_counter() - t0
     return {"value": round(n * T / dt, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
             "sample": f"{n} C2 layer calls of T={T} tokens (router, Q8_K expert dots, combine), one layer's weights"}
@@ -593,10 +620,10 @@ def run_reference(args):
     gate, up, down, rw, x = host_layer(args.seed, T)
     threads = cpu_threads()
     for _ in range(args.warmup):
-        O.layer(x, K_USED, gate, up, down, H, I, E, router_w=rw, down_type=O.TYPE_Q6_K, nthreads=threads)
+        O.layer(x, K_USED, gate, up, down, H, I, E, router_w=rw, down_type=DOWN_T, nthreads=threads)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        O.layer(x, K_USED, gate, up, down, H, I, E, router_w=rw, down_type=O.TYPE_Q6_K, nthreads=threads)
+        O.layer(x, K_USED, gate, up, down, H, I, E, router_w=rw, down_type=DOWN_T, nthreads=threads)
     dt = time.perf_counter() - t0
     value = args.steps * T / dt
     sample = f"{args.steps} C2 layer calls of T={T} tokens, one layer's weights, {threads} threads"

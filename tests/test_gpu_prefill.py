@@ -40,6 +40,7 @@ PREFILL_CASES = [
     # (name, H, I, E, k, T, gate/up type, down type, exact quantiser)
     ("tiny T=1024", 512, 256, 16, 4, 1024, O.TYPE_Q4_K, O.TYPE_Q4_K, True),
     ("C2 30B T=512", 2048, 768, 128, 8, 512, O.TYPE_Q4_K, O.TYPE_Q6_K, False),
+    ("C4 235B shape T=512", 4096, 1536, 16, 8, 512, O.TYPE_Q4_K, O.TYPE_Q4_K, False),
 ]
 
 
