@@ -103,6 +103,21 @@ def test_dispatch_bit_exact(T, E, k, neg):
     assert np.array_equal(host(perm)[: o[-1]], p)
 
 
+def test_dispatch_bit_exact_under_skew():
+    """A few experts take most pairs (ids drawn with replacement, Zipf-like): the many-CTA sort must
+    still give the one-CTA order."""
+    T, E, k = 8192, 128, 8
+    rng = np.random.default_rng(5)
+    wts = 1.0 / np.arange(1, E + 1) ** 1.2
+    ids = rng.choice(E, size=(T, k), p=wts / wts.sum()).astype(np.int32)
+    ids[rng.random(ids.shape) < 0.05] = -1
+    layer = tb.MoeLayer(2048, 768, E, k, max_tokens=T)
+    counts, offsets, perm = layer.dispatch(cuda(ids), E)
+    c, o, p = O.sort_pairs(ids, E)
+    assert np.array_equal(host(counts), c) and np.array_equal(host(offsets), o)
+    assert np.array_equal(host(perm)[: o[-1]], p)
+
+
 # ------------------------------------------------------------------------------------ quantiser
 @pytest.mark.parametrize("qt", [O.TYPE_Q4_K, O.TYPE_Q6_K])
 def test_device_quantiser_bytes_equal_oracle(qt):

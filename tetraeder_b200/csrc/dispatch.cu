@@ -111,6 +111,122 @@ __global__ void __launch_bounds__(1024) sort_pairs_kernel(const int32_t *__restr
                                err, sh);
 }
 
+// The same dispatch for many pairs, over CTAs of SORT_CHUNK consecutive pairs: each chunk counts its
+// pairs per expert; one CTA turns the counts into offsets (and the active list) and each chunk's
+// first slot per expert; each chunk then scatters its pairs in order, ranked per warp as in
+// sort_pairs_cta.  Pairs of an expert end up in increasing pair order, exactly as one CTA sorts
+// them.  scratch: n_chunks * n_slots ints.
+constexpr int SORT_CHUNK = 2048;  // 64 pairs per warp
+
+__global__ void __launch_bounds__(1024) sort_hist_kernel(const int32_t *__restrict__ ids, int n_pairs, int n_slots,
+                                                         int32_t *__restrict__ chunk, int *err) {
+    extern __shared__ int32_t hc[];  // [n_slots]
+    for (int e = threadIdx.x; e < n_slots; e += blockDim.x) hc[e] = 0;
+    __syncthreads();
+    const int p0 = blockIdx.x * SORT_CHUNK, p1 = min(n_pairs, p0 + SORT_CHUNK);
+    bool bad = false;
+    for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+        const int e = ids[p];
+        if (e >= n_slots) bad = true;
+        if (e >= 0 && e < n_slots) atomicAdd(&hc[e], 1);
+    }
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) latch_error(err, TMOE_DEV_ERR_BADID);
+    __syncthreads();
+    for (int e = threadIdx.x; e < n_slots; e += blockDim.x) chunk[(int64_t)blockIdx.x * n_slots + e] = hc[e];
+}
+
+__global__ void __launch_bounds__(1024) sort_scan_kernel(int n_chunks, int n_slots, int32_t *__restrict__ chunk,
+                                                         int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
+                                                         int4 *__restrict__ active, int32_t *__restrict__ n_active,
+                                                         int *counters, int n_counters) {
+    extern __shared__ int32_t offs[];  // [n_slots + 1]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (counters && (int)threadIdx.x < n_counters) counters[threadIdx.x] = 0;  // work counters of the GEMVs
+    for (int e = threadIdx.x; e < n_slots; e += blockDim.x) {  // each chunk's first slot within its expert
+        int run = 0;
+        for (int c = 0; c < n_chunks; c++) {
+            const int v = chunk[(int64_t)c * n_slots + e];
+            chunk[(int64_t)c * n_slots + e] = run;
+            run += v;
+        }
+        counts[e] = run;
+        offs[e] = run;
+    }
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of the counts, 32 experts per step
+        int carry = 0;
+        for (int base = 0; base < n_slots; base += 32) {
+            const int e = base + lane;
+            const int c = e < n_slots ? offs[e] : 0;
+            int inc = c;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int o = __shfl_up_sync(0xffffffffu, inc, off);
+                if (lane >= off) inc += o;
+            }
+            if (e < n_slots) offs[e] = carry + inc - c;
+            carry += __shfl_sync(0xffffffffu, inc, 31);
+        }
+        if (lane == 0) offs[n_slots] = carry;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e <= n_slots; e += blockDim.x) offsets[e] = offs[e];
+    if (warp == 0) {
+        int na = 0;
+        for (int base = 0; base < n_slots; base += 32) {
+            const int e = base + lane;
+            const bool has = e < n_slots && (offs[e + 1] - offs[e]) > 0;
+            const unsigned m = __ballot_sync(0xffffffffu, has);
+            if (has) active[na + __popc(m & ((1u << lane) - 1u))] = make_int4(e, offs[e], offs[e + 1], 0);
+            na += __popc(m);
+        }
+        if (lane == 0) n_active[0] = na;
+    }
+    for (int e = threadIdx.x; e < n_slots; e += blockDim.x)
+        for (int c = 0; c < n_chunks; c++) chunk[(int64_t)c * n_slots + e] += offs[e];
+}
+
+__global__ void __launch_bounds__(1024) sort_scatter_kernel(const int32_t *__restrict__ ids, int n_pairs, int n_slots,
+                                                            const int32_t *__restrict__ chunk,
+                                                            int32_t *__restrict__ perm) {
+    extern __shared__ int32_t hw[];  // [32 warps][n_slots]
+    constexpr int NW = 32, SEG = SORT_CHUNK / NW;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < NW * n_slots; i += blockDim.x) hw[i] = 0;
+    __syncthreads();
+    const int c0 = blockIdx.x * SORT_CHUNK;
+    const int p0 = c0 + warp * SEG, p1 = min(n_pairs, p0 + SEG);
+    for (int p = p0 + lane; p < p1; p += 32) {
+        const int e = ids[p];
+        if (e >= 0 && e < n_slots) atomicAdd(&hw[warp * n_slots + e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < n_slots; e += blockDim.x) {  // warp w's first slot: the chunk's + earlier warps'
+        int run = chunk[(int64_t)blockIdx.x * n_slots + e];
+        for (int w = 0; w < NW; w++) {
+            const int v = hw[w * n_slots + e];
+            hw[w * n_slots + e] = run;
+            run += v;
+        }
+    }
+    __syncthreads();
+    const unsigned lt = (1u << lane) - 1u;
+    for (int base = p0; base < p1; base += 32) {
+        const int p = base + lane;
+        const int e = p < p1 ? ids[p] : -1;
+        const bool ok = e >= 0 && e < n_slots;
+        const unsigned peers = __match_any_sync(0xffffffffu, ok ? e : -1);
+        if (ok) perm[hw[warp * n_slots + e] + __popc(peers & lt)] = p;
+        __syncwarp();
+        if (ok && (peers & lt) == 0) hw[warp * n_slots + e] += __popc(peers);
+        __syncwarp();
+    }
+}
+
+size_t sort_scratch_ints(int64_t n_pairs, int n_slots) {
+    return (size_t)((n_pairs + SORT_CHUNK - 1) / SORT_CHUNK) * (size_t)n_slots;
+}
+
 // Decode regime (T*k <= ROUTE_FUSED_MAX_PAIRS): softmax/top-k of every token, the optional EP
 // map, and the dispatch of the (mapped) ids, in one CTA of 1024 threads.  ids_out / w_out get the
 // router's choices; mapped gets the ids the experts see (= ids_out without a table).
@@ -344,7 +460,19 @@ static cudaError_t set_smem_once(KernT kern, size_t smem, int *cache) {
 
 cudaError_t launch_sort_pairs(const int32_t *ids, int n_pairs, int n_slots, int32_t *counts, int32_t *offsets,
                               int32_t *perm, int4 *active, int32_t *n_active, int *counters, int n_counters,
-                              int *err, cudaStream_t st) {
+                              int *err, cudaStream_t st, int32_t *scratch, size_t scratch_ints) {
+    const int n_chunks = (n_pairs + SORT_CHUNK - 1) / SORT_CHUNK;
+    if (scratch && n_chunks >= 4 && scratch_ints >= sort_scratch_ints(n_pairs, n_slots)) {
+        static int cache_s[64] = {};
+        const size_t smem_s = (size_t)32 * n_slots * 4;
+        cudaError_t e = set_smem_once(sort_scatter_kernel, smem_s, cache_s);
+        if (e != cudaSuccess) return e;
+        sort_hist_kernel<<<n_chunks, 1024, (size_t)n_slots * 4, st>>>(ids, n_pairs, n_slots, scratch, err);
+        sort_scan_kernel<<<1, 1024, (size_t)(n_slots + 1) * 4, st>>>(n_chunks, n_slots, scratch, counts, offsets,
+                                                                      active, n_active, counters, n_counters);
+        sort_scatter_kernel<<<n_chunks, 1024, smem_s, st>>>(ids, n_pairs, n_slots, scratch, perm);
+        return cudaGetLastError();
+    }
     const size_t smem = sort_pairs_smem(n_slots);
     static int cache[64] = {};
     cudaError_t e = set_smem_once(sort_pairs_kernel, smem, cache);

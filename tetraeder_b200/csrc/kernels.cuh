@@ -60,9 +60,12 @@ cudaError_t launch_quantize_q8k(const float *x, int64_t rows, int K, const int32
 size_t sort_pairs_smem(int n_slots);
 // The dispatch also zeroes `counters` (n_counters ints: the GEMV work counters; may be NULL).
 // active: the experts with pairs, {e, offsets[e], offsets[e + 1], 0} each, n_active[0] of them.
+// With scratch (sort_scratch_ints(n_pairs, n_slots) ints) and many pairs the sort runs over many CTAs
+// (the same permutation); otherwise in one CTA.
+size_t sort_scratch_ints(int64_t n_pairs, int n_slots);
 cudaError_t launch_sort_pairs(const int32_t *ids, int n_pairs, int n_slots, int32_t *counts, int32_t *offsets,
                               int32_t *perm, int4 *active, int32_t *n_active, int *counters, int n_counters,
-                              int *err, cudaStream_t st);
+                              int *err, cudaStream_t st, int32_t *scratch = nullptr, size_t scratch_ints = 0);
 // Fused softmax/top-k + optional EP map + dispatch for T*k <= ROUTE_FUSED_MAX_PAIRS.
 #define ROUTE_FUSED_MAX_PAIRS 4096
 bool route_dispatch_fits(int64_t T, int k, int E, int n_slots);

@@ -53,6 +53,8 @@ struct tmoe_handle {
     float *ad16 = nullptr, *ad16_t = nullptr;  // d of the A rows' Q8_K blocks (sorted rows, token rows)
     int *tile_start = nullptr, *tile_start2 = nullptr;
     int *counters = nullptr;    // GEMV work counters
+    int32_t *sort_scratch = nullptr;  // per-chunk expert counts of the many-CTA dispatch
+    size_t sort_scratch_ints = 0;
     int *route_done = nullptr;  // the fused routing kernel's tile counters (zero between calls)
     int *err = nullptr;
     // exchange buffers of the all-to-all EP mode (allocated on its first call; see tmoe_ep_a2a_layer)
@@ -190,6 +192,8 @@ size_t carve(tmoe_handle *h, char *base) {
         h->ab16_t = (__half *)take(T * (H / 256) * 16 * 2);
     }
     h->counters = (int *)take(kCounters * 4);
+    h->sort_scratch_ints = tmoe::sort_scratch_ints(P, kMaxSlots);
+    h->sort_scratch = (int32_t *)take(h->sort_scratch_ints * 4);
     h->route_done = (int *)take((T / 4 + 2) * 4);
     h->err = (int *)take(4);
     return off;
@@ -248,7 +252,8 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
         {
             PhaseMark pm(h, st, TMOE_PHASE_DISPATCH);
             e = tmoe::launch_sort_pairs(ids, (int)P, t->n_slots, h->counts, h->offsets, h->perm, h->active,
-                                        h->n_active, h->counters, kCounters, h->err, st);
+                                        h->n_active, h->counters, kCounters, h->err, st, h->sort_scratch,
+                                        h->sort_scratch_ints);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "sort_pairs");
     }
@@ -878,7 +883,8 @@ int tmoe_dispatch(tmoe_handle *h, void *stream, const int32_t *ids, int64_t T, i
     if (!ids || !counts || !offsets || !perm) return fail(h, TMOE_E_INVALID, "null tensor");
     DeviceGuard dg(c.device);
     cudaError_t e = tmoe::launch_sort_pairs(ids, (int)(T * c.n_expert_used), n_slots, counts, offsets, perm,
-                                            h->active, h->n_active, nullptr, 0, h->err, (cudaStream_t)stream);
+                                            h->active, h->n_active, nullptr, 0, h->err, (cudaStream_t)stream,
+                                            h->sort_scratch, h->sort_scratch_ints);
     if (e != cudaSuccess) return cuda_fail(h, e, "sort_pairs");
     return TMOE_OK;
 }
