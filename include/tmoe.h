@@ -188,7 +188,9 @@ TMOE_API int tmoe_ep_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const 
  * `slots`: device slot tensors (n_slots = the slot count); `store`: the layer's E experts in pinned
  * host memory (cudaHostAlloc / cudaHostRegister, i.e. device-mapped), the same row layout
  * (nb1) as the slots.  The cache keeps both pointers; neither is copied.  One cache per layer;
- * calls on a cache are stream-ordered like the handle's. */
+ * calls on a cache are stream-ordered like the handle's.  With more experts than slots the cache
+ * also owns a staging area of (slot count) experts of device memory and a side stream: the misses
+ * of chunks after the first are paged in there while the earlier chunk computes. */
 typedef struct tmoe_slots tmoe_slots;
 TMOE_API int tmoe_slots_create(tmoe_handle *h, const tmoe_expert_tensors *slots, const tmoe_expert_tensors *store,
                                tmoe_slots **out);
@@ -210,9 +212,11 @@ TMOE_API int tmoe_slots_state(tmoe_slots *s, void *stream, int32_t *owner, int64
  * chunk's misses; n_loads [max_chunks]; any may be NULL. */
 TMOE_API int tmoe_slots_last_plan(tmoe_slots *s, void *stream, int32_t *n_chunks, int32_t *map, int32_t *loads,
                                   int32_t *n_loads);
-/* The streamed layer step: tmoe_route, the device plan, then per chunk: page its misses in, compute
- * its pairs from the slot tensors (dout rows of the chunk's pairs), and finally one combine of all
- * pairs in choice order -- the same per-pair arithmetic as tmoe_layer on resident experts. */
+/* The streamed layer step: tmoe_route, the device plan, then per chunk: page its misses in (chunk 0
+ * straight into its slots; later chunks into the staging area on the side stream, overlapping the
+ * previous chunk's compute, then moved into their slots), compute its pairs from the slot tensors
+ * (dout rows of the chunk's pairs), and finally one combine of all pairs in choice order -- the same
+ * per-pair arithmetic as tmoe_layer on resident experts. */
 TMOE_API int tmoe_streamed_layer(tmoe_handle *h, void *stream, tmoe_slots *s, const float *x, int64_t T,
                                  int32_t use_norm, const float *norm_w, const float *router_w, const float *logits,
                                  float *out, int32_t *ids_out, float *w_out);

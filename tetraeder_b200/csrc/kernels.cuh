@@ -170,6 +170,12 @@ bool slots_fit(int n_expert, int max_slots);
 cudaError_t launch_slot_plan(const int32_t *ids, int n_pairs, const SlotsDev &s, int *err, cudaStream_t st);
 cudaError_t launch_slot_lookup_list(const int32_t *list, int n, const SlotsDev &s, int *err, cudaStream_t st);
 cudaError_t launch_slot_page(const SlotsDev &s, int chunk, const SlotCopy &cp, int sm_count, cudaStream_t st);
+// The overlapped miss path (see slots.cu): host store -> staging (load index order, ebytes per
+// expert), and staging -> the loads' slots.
+cudaError_t launch_slot_stage(const SlotsDev &s, int chunk, const SlotCopy &cp, uint8_t *staging, size_t ebytes,
+                              cudaStream_t st);
+cudaError_t launch_slot_unstage(const SlotsDev &s, int chunk, const SlotCopy &cp, const uint8_t *staging,
+                                size_t ebytes, int sm_count, cudaStream_t st);
 
 // Rows per work item of the GEMV for K columns and N rows per expert; 0 if N does not fit.
 int gemv_rows_per_item(int wt, int K, int N);

@@ -353,6 +353,54 @@ __global__ void slot_lookup_list_kernel(const int32_t *__restrict__ list, int n,
     for (int i = lane; i < s.max_slots; i += 32) s.owner[i] = owner[i], s.stamp[i] = stamp[i];
 }
 
+// The overlapped miss path: the loads of chunk c >= 1 go first into a staging area (one expert
+// of gate, up and down bytes back to back per load index), paged in from the host store on a side
+// stream while earlier chunks compute, by a lean kernel (128 threads, few registers, few CTAs) that
+// can share SMs with the compute kernels; right before chunk c computes, a device copy moves them
+// into their slots (after chunk c - 1, whose slots they may replace, has finished).
+__device__ __forceinline__ void copy16_x4(uint4 *dst, const uint4 *src, size_t n16, size_t i, size_t step) {
+    for (; i + 3 * step < n16; i += 4 * step) {
+        const uint4 a = src[i], b = src[i + step], c2 = src[i + 2 * step], d = src[i + 3 * step];
+        dst[i] = a, dst[i + step] = b, dst[i + 2 * step] = c2, dst[i + 3 * step] = d;
+    }
+    for (; i < n16; i += step) dst[i] = src[i];
+}
+
+__global__ void __launch_bounds__(128, 16) slot_stage_kernel(SlotsDev s, int c, SlotCopy cp, uint8_t *staging,
+                                                             size_t ebytes) {
+    const int nl = s.n_loads[c];
+    const size_t step = (size_t)gridDim.x * blockDim.x, i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (int li = 0; li < nl; li++) {
+        const int e = s.loads[c * s.max_slots + li].x;
+        uint8_t *dst = staging + (size_t)li * ebytes;
+#pragma unroll 1
+        for (int m = 0; m < 3; m++) {
+            const uint8_t *sb = m == 0 ? cp.src[0] : m == 1 ? cp.src[1] : cp.src[2];
+            const size_t snb = m == 0 ? cp.src_nb2[0] : m == 1 ? cp.src_nb2[1] : cp.src_nb2[2];
+            const size_t nbytes = m == 0 ? cp.bytes[0] : m == 1 ? cp.bytes[1] : cp.bytes[2];
+            copy16_x4(reinterpret_cast<uint4 *>(dst), reinterpret_cast<const uint4 *>(sb + (size_t)e * snb),
+                      nbytes >> 4, i0, step);
+            dst += nbytes;
+        }
+    }
+}
+
+// blockIdx.y = load, blockIdx.z = matrix: staging -> the load's slot.
+__global__ void __launch_bounds__(256) slot_unstage_kernel(SlotsDev s, int c, SlotCopy cp, const uint8_t *staging,
+                                                           size_t ebytes) {
+    const int li = blockIdx.y;
+    if (li >= s.n_loads[c]) return;
+    const int slot = s.loads[c * s.max_slots + li].y;
+    const int m = blockIdx.z;
+    uint8_t *db = m == 0 ? cp.dst[0] : m == 1 ? cp.dst[1] : cp.dst[2];
+    const size_t dnb = m == 0 ? cp.dst_nb2[0] : m == 1 ? cp.dst_nb2[1] : cp.dst_nb2[2];
+    const size_t nbytes = m == 0 ? cp.bytes[0] : m == 1 ? cp.bytes[1] : cp.bytes[2];
+    const size_t off = m == 0 ? 0 : m == 1 ? cp.bytes[0] : cp.bytes[0] + cp.bytes[1];
+    copy16_x4(reinterpret_cast<uint4 *>(db + (size_t)slot * dnb),
+              reinterpret_cast<const uint4 *>(staging + (size_t)li * ebytes + off), nbytes >> 4,
+              (size_t)blockIdx.x * blockDim.x + threadIdx.x, (size_t)gridDim.x * blockDim.x);
+}
+
 bool slots_fit(int n_expert, int max_slots) {
     return n_expert >= 1 && n_expert <= SP_MAX_E && max_slots >= 1 && max_slots <= SP_MAX_SLOTS &&
            max_slots <= 65535;
@@ -386,6 +434,20 @@ cudaError_t launch_slot_page(const SlotsDev &s, int chunk, const SlotCopy &cp, i
     const int per_load = 3 * s.max_slots;
     const int gx = max(1, min(64, (2 * sm_count + per_load - 1) / per_load));
     slot_page_kernel<<<dim3(gx, s.max_slots, 3), 256, 0, st>>>(s, chunk, cp);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_slot_stage(const SlotsDev &s, int chunk, const SlotCopy &cp, uint8_t *staging, size_t ebytes,
+                              cudaStream_t st) {
+    slot_stage_kernel<<<32, 128, 0, st>>>(s, chunk, cp, staging, ebytes);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_slot_unstage(const SlotsDev &s, int chunk, const SlotCopy &cp, const uint8_t *staging,
+                                size_t ebytes, int sm_count, cudaStream_t st) {
+    const int per_load = 3 * s.max_slots;
+    const int gx = max(1, min(64, (4 * sm_count + per_load - 1) / per_load));
+    slot_unstage_kernel<<<dim3(gx, s.max_slots, 3), 256, 0, st>>>(s, chunk, cp, staging, ebytes);
     return cudaGetLastError();
 }
 

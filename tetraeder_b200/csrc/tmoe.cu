@@ -88,6 +88,13 @@ struct tmoe_slots {
     void *mem = nullptr;
     int32_t *list = nullptr;  // device copy of a make_resident list
     int active = 0;           // host mirror of the slots in use (LayerSlots::active)
+    // the overlapped miss path: staging for one chunk's loads, the side stream that pages them in,
+    // and per chunk the events of "staged" (side -> main) and "moved into the slots" (main -> side)
+    uint8_t *staging = nullptr;
+    size_t ebytes = 0;
+    cudaStream_t side = nullptr;
+    std::vector<cudaEvent_t> ev_staged, ev_moved;
+    cudaEvent_t ev_plan = nullptr;
 };
 
 namespace {
@@ -1022,6 +1029,21 @@ int tmoe_slots_create(tmoe_handle *h, const tmoe_expert_tensors *slots, const tm
         return cuda_fail(h, e, "slot tables init");
     }
     sl->active = S;
+    if (MC > 1) {  // chunks after the first are paged in on a side stream while the first computes
+        sl->ebytes = bytes[0] + bytes[1] + bytes[2];
+        bool ok = cudaMalloc(&sl->staging, (size_t)S * sl->ebytes) == cudaSuccess &&
+                  cudaStreamCreateWithFlags(&sl->side, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaEventCreateWithFlags(&sl->ev_plan, cudaEventDisableTiming) == cudaSuccess;
+        sl->ev_staged.assign(MC, nullptr), sl->ev_moved.assign(MC, nullptr);
+        for (int i = 0; ok && i < MC; i++)
+            ok = cudaEventCreateWithFlags(&sl->ev_staged[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&sl->ev_moved[i], cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) {
+            cudaGetLastError();
+            tmoe_slots_destroy(sl);
+            return fail(h, TMOE_E_NOMEM, "staging of the miss path (%zu bytes)", (size_t)S * sl->ebytes);
+        }
+    }
     *out = sl;
     return TMOE_OK;
 }
@@ -1029,6 +1051,14 @@ int tmoe_slots_create(tmoe_handle *h, const tmoe_expert_tensors *slots, const tm
 void tmoe_slots_destroy(tmoe_slots *s) {
     if (!s) return;
     DeviceGuard dg(s->h->cfg.device);
+    if (s->side) cudaStreamSynchronize(s->side);
+    for (cudaEvent_t ev : s->ev_staged)
+        if (ev) cudaEventDestroy(ev);
+    for (cudaEvent_t ev : s->ev_moved)
+        if (ev) cudaEventDestroy(ev);
+    if (s->ev_plan) cudaEventDestroy(s->ev_plan);
+    if (s->side) cudaStreamDestroy(s->side);
+    if (s->staging) cudaFree(s->staging);
     cudaFree(s->mem);
     delete s;
 }
@@ -1132,10 +1162,35 @@ int tmoe_streamed_layer(tmoe_handle *h, void *stream, tmoe_slots *s, const float
         e = tmoe::launch_slot_plan(ids, (int)P, s->dev, h->err, st);
     }
     if (e != cudaSuccess) return cuda_fail(h, e, "slot plan");
-    for (int ch = 0; ch < s->dev.max_chunks; ch++) {
-        {
+    // Chunk 0's misses are paged straight into their slots.  Chunk c >= 1 is paged from the host
+    // store into the staging area on the side stream while chunk c - 1 computes, then moved into
+    // its slots right before it computes (its slots may be chunk c - 1's).  The events are enqueued
+    // in dependency order, so the schedule holds under stream capture too.
+    const int MC = s->dev.max_chunks;
+    const bool overlap = s->side != nullptr;
+    if (overlap) {
+        if ((e = cudaEventRecord(s->ev_plan, st)) == cudaSuccess &&
+            (e = cudaStreamWaitEvent(s->side, s->ev_plan, 0)) == cudaSuccess &&
+            (e = tmoe::launch_slot_stage(s->dev, 1, s->copy, s->staging, s->ebytes, s->side)) == cudaSuccess)
+            e = cudaEventRecord(s->ev_staged[1], s->side);
+        if (e != cudaSuccess) return cuda_fail(h, e, "staging");
+    }
+    for (int ch = 0; ch < MC; ch++) {
+        if (ch == 0 || !overlap) {
             PhaseMark pm(h, st, TMOE_PHASE_SLOT_PAGE);
             e = tmoe::launch_slot_page(s->dev, ch, s->copy, h->sm_count, st);
+        } else {
+            if ((e = cudaStreamWaitEvent(st, s->ev_staged[ch], 0)) == cudaSuccess) {
+                PhaseMark pm(h, st, TMOE_PHASE_SLOT_PAGE);
+                e = tmoe::launch_slot_unstage(s->dev, ch, s->copy, s->staging, s->ebytes, h->sm_count, st);
+            }
+            if (e == cudaSuccess && ch + 1 < MC) {  // the staging is free again: the next chunk's pages
+                if ((e = cudaEventRecord(s->ev_moved[ch], st)) == cudaSuccess &&
+                    (e = cudaStreamWaitEvent(s->side, s->ev_moved[ch], 0)) == cudaSuccess &&
+                    (e = tmoe::launch_slot_stage(s->dev, ch + 1, s->copy, s->staging, s->ebytes, s->side)) ==
+                        cudaSuccess)
+                    e = cudaEventRecord(s->ev_staged[ch + 1], s->side);
+            }
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "slot paging");
         {
