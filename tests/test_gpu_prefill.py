@@ -1,4 +1,4 @@
-"""The large-batch regime (T * k >= 4096 pairs): gate/up on the integer MMA path (exact Q8_K block
+"""The large-batch regime (T * k >= 6144 pairs): gate/up on the integer MMA path (exact Q8_K block
 sums, as on the reference CPU path) and the down product as a grouped tcgen05 GEMM with fp16
 operands (the SwiGLU activations through the same Q8_K round trip as on the reference path, then
 fp16; the down weights dequantised to fp16), checked against the CPU oracle on the same inputs.
@@ -38,9 +38,9 @@ def _case(H, I, E, T, gt, dt, seed, exact):
 
 PREFILL_CASES = [
     # (name, H, I, E, k, T, gate/up type, down type, exact quantiser)
-    ("tiny T=1024", 512, 256, 16, 4, 1024, O.TYPE_Q4_K, O.TYPE_Q4_K, True),
-    ("C2 30B T=512", 2048, 768, 128, 8, 512, O.TYPE_Q4_K, O.TYPE_Q6_K, False),
-    ("C4 235B shape T=512", 4096, 1536, 16, 8, 512, O.TYPE_Q4_K, O.TYPE_Q4_K, False),
+    ("tiny T=1536", 512, 256, 16, 4, 1536, O.TYPE_Q4_K, O.TYPE_Q4_K, True),
+    ("C2 30B T=768", 2048, 768, 128, 8, 768, O.TYPE_Q4_K, O.TYPE_Q6_K, False),
+    ("C4 235B shape T=768", 4096, 1536, 16, 8, 768, O.TYPE_Q4_K, O.TYPE_Q4_K, False),
 ]
 
 
@@ -52,7 +52,12 @@ def test_prefill_layer_parity(case):
     wts = tb.ExpertWeights(cuda(gate), cuda(up), cuda(down))
     ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
     w = torch.empty((T, k), dtype=torch.float32, device="cuda")
+    layer.profile(True)
     out = layer.moe_ffn(cuda(x), wts, router_w=cuda(rw), ids_out=ids, w_out=w)
+    phases = layer.profile_collect()
+    layer.profile(False)
+    # the grouped GEMMs ran, not the decode GEMV (whose activations take a separate Q8_K pass)
+    assert "gate_up" in phases and "quant_act" not in phases, f"{name}: phases {sorted(phases)}"
     out2 = layer.moe_ffn(cuda(x), wts, router_w=cuda(rw))  # again: tiles and buffers are reused
     layer.check()
     want_ids, want_w, _, _ = O.route(x, k, router_w=rw)

@@ -57,7 +57,7 @@ def _check_plan(cache, ref_layer, ids, steps_ref):
 CASES = [
     # name, H, I, E, k, slots, T, gate/up type, down type, exact, zipf
     ("tiny 6 slots T=32", 512, 256, 16, 4, 6, 32, O.TYPE_Q4_K, O.TYPE_Q4_K, True, False),
-    ("tiny 5 slots prefill T=1024", 512, 256, 16, 4, 5, 1024, O.TYPE_Q4_K, O.TYPE_Q4_K, True, True),
+    ("tiny 5 slots prefill T=1536", 512, 256, 16, 4, 5, 1536, O.TYPE_Q4_K, O.TYPE_Q4_K, True, True),
     ("30B 64 slots T=64", 2048, 768, 128, 8, 64, 64, O.TYPE_Q4_K, O.TYPE_Q6_K, False, True),
 ]
 

@@ -111,6 +111,30 @@ struct TokCols {
     int pp0, pp1;
 };
 
+// The same group's activation data as this thread's base pointers, set once per pass (super-block
+// kb then sits at a fixed stride from each): the B-operand row of column g at the thread's k
+// offset, that row's sub-block sum words (2 per super-block for Q4_K, 4 for Q6_K, the thread's
+// one), and the super-block scales of columns 2*t4 and 2*t4+1.
+struct XBase {
+    const int8_t *q;
+    const uint32_t *bl, *bh;
+    const float *d0, *d1;
+};
+
+template <int WT>
+__device__ __forceinline__ XBase x_base(const GemvArgs &a, const TokCols &c, int nb) {
+    const int t4 = threadIdx.x & 3;
+    constexpr int NBW = WT == TMOE_WT_Q4K ? 2 : 4;
+    const int64_t sw = (int64_t)c.xg * nb * NBW + (WT == TMOE_WT_Q4K ? (t4 & 1) : t4);
+    XBase p;
+    p.q = a.xq + (int64_t)c.xg * a.K + (WT == TMOE_WT_Q4K ? 8 : 4) * t4;
+    p.bl = a.xbl + sw;
+    p.bh = a.xbh + sw;
+    p.d0 = a.xd + (int64_t)c.x0 * nb;
+    p.d1 = a.xd + (int64_t)c.x1 * nb;
+    return p;
+}
+
 // ------------------------------------------------------------------ Q4_K
 // Per super-block and 8-token group: a thread's B operands.  Inside a sub-block the k order is
 // permuted identically for both operands (thread t4 holds elements 8*t4 .. 8*t4+7 of the 32),
@@ -122,6 +146,7 @@ struct XQ4 {
     float d0, d1;
 };
 
+// From the token columns directly (two-group passes: fewer live registers than kept bases).
 __device__ __forceinline__ void load_xq4(const GemvArgs &a, const TokCols &c, int kb, int nb, XQ4 &o) {
     const int t4 = threadIdx.x & 3;
     const int8_t *q = a.xq + (int64_t)c.xg * a.K + TMOE_QK * kb + 8 * t4;
@@ -137,6 +162,21 @@ __device__ __forceinline__ void load_xq4(const GemvArgs &a, const TokCols &c, in
     o.d1 = __ldg(a.xd + (int64_t)c.x1 * nb + kb);
 }
 
+// From kept bases; lo: t4 < 2 (the threads whose B operand of the min MMAs holds the 8 sub-block
+// sums).
+__device__ __forceinline__ void load_xq4(const XBase &p, int kb, bool lo, XQ4 &o) {
+    const int8_t *q = p.q + TMOE_QK * kb;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        o.l[j] = ldg64(q + 64 * j);
+        o.h[j] = ldg64(q + 64 * j + 32);
+    }
+    o.bl = lo ? __ldg(p.bl + 2 * kb) : 0u;
+    o.bh = lo ? __ldg(p.bh + 2 * kb) : 0u;
+    o.d0 = __ldg(p.d0 + kb);
+    o.d1 = __ldg(p.d1 + kb);
+}
+
 // One super-block of MMA rows g (at ra) and g+8 (at rb) against NGR token groups.
 //  - The high nibbles go to the MMA in place (byte & 0xf0 = 16 * q, unsigned): those products
 //    are 16 times too large and the super-block's sum of them is shifted right by 4, exactly.
@@ -145,7 +185,7 @@ __device__ __forceinline__ void load_xq4(const GemvArgs &a, const TokCols &c, in
 //    mins x lo bytes + 64 * (mins x hi bytes), B_s = 64 * hi + lo.
 template <int NGR>
 __device__ __forceinline__ void q4_block(const uint8_t *ra, const uint8_t *rb, const XQ4 (&x)[NGR],
-                                         float (&acc)[2][4]) {
+                                         float (*acc)[4]) {
     const int t4 = threadIdx.x & 3;
     const uint4 ha = *reinterpret_cast<const uint4 *>(ra);
     const uint4 hb = *reinterpret_cast<const uint4 *>(rb);
@@ -230,6 +270,16 @@ __device__ __forceinline__ void load_xq6(const GemvArgs &a, const TokCols &c, in
     o.d1 = __ldg(a.xd + (int64_t)c.x1 * nb + kb);
 }
 
+__device__ __forceinline__ void load_xq6(const XBase &p, int kb, XQ6 &o) {
+    const int8_t *q = p.q + TMOE_QK * kb;
+#pragma unroll
+    for (int s = 0; s < 16; s++) o.w[s] = ldg32(q + 16 * s);
+    o.bl = __ldg(p.bl + 4 * kb);
+    o.bh = __ldg(p.bh + 4 * kb);
+    o.d0 = __ldg(p.d0 + kb);
+    o.d1 = __ldg(p.d1 + kb);
+}
+
 // 32-bit word at p (2-byte aligned); MIS 0: p is word aligned, 1: p is 2 bytes off, 2: either.
 template <int MIS>
 __device__ __forceinline__ uint32_t ld32(const uint8_t *p) {
@@ -268,7 +318,7 @@ __device__ __forceinline__ uint32_t q6_vals(const Q6Half &q, int sl8) {
 
 template <int NGR, int MA, int MB>
 __device__ __forceinline__ void q6_block(const uint8_t *ba, const uint8_t *bb, const XQ6 (&x)[NGR],
-                                         float (&acc)[2][4]) {
+                                         float (*acc)[4]) {
     const int t4 = threadIdx.x & 3;
     int isum[NGR][4];
 #pragma unroll
@@ -392,6 +442,7 @@ __device__ __forceinline__ void fetch_next(const GemvArgs &a, Feed &f, const Gro
     }
 }
 
+template <int NG>
 __device__ __forceinline__ void next_item(const GemvArgs &a, Feed &f, const GroupQueue &q, int n_items) {
     const int lane = threadIdx.x & 31;
     for (;;) {
@@ -414,15 +465,15 @@ __device__ __forceinline__ void next_item(const GemvArgs &a, Feed &f, const Grou
         f.beg = beg;
         f.end = end;
         f.pass = 0;
-        f.npass = (end - beg + 2 * TOKG - 1) / (2 * TOKG);
+        f.npass = (end - beg + NG * TOKG - 1) / (NG * TOKG);
         f.chunk = 0;
         return;
     }
 }
 
 // Issues the next fill into `slot` (record, expect_tx, the copies) from lane 0 and advances the
-// feed.  With no items left the fill is an end marker (no copies).
-template <int WT, bool GATEUP>
+// feed.  With no items left the fill is an end marker (no copies).  A pass covers NG token groups.
+template <int WT, bool GATEUP, int NG>
 __device__ __forceinline__ void fill(const GemvArgs &a, const GemvMaps &tm, Feed &f, uint64_t *bar, SlotRec *rec,
                                      uint8_t *slot, const GroupQueue &q, int n_items) {
     const int lane = threadIdx.x & 31;
@@ -436,7 +487,7 @@ __device__ __forceinline__ void fill(const GemvArgs &a, const GemvMaps &tm, Feed
             uint32_t pbytes = 0;
             int poff = 0;
             if (f.chunk == 0) {  // the pass's pair indices, rounded out to 16 bytes
-                const int t0 = f.beg + f.pass * 2 * TOKG, nt = min(2 * TOKG, f.end - t0);
+                const int t0 = f.beg + f.pass * NG * TOKG, nt = min(NG * TOKG, f.end - t0);
                 const uintptr_t src = reinterpret_cast<uintptr_t>(a.perm + t0);
                 ps = src & ~(uintptr_t)15;
                 pbytes = (uint32_t)(((src + 4u * (uint32_t)nt + 15) & ~(uintptr_t)15) - ps);
@@ -470,12 +521,14 @@ __device__ __forceinline__ void fill(const GemvArgs &a, const GemvMaps &tm, Feed
     if (f.item < 0) return;
     if (++f.chunk == a.n_chunks) {
         f.chunk = 0;
-        if (++f.pass == f.npass) next_item(a, f, q, n_items);
+        if (++f.pass == f.npass) next_item<NG>(a, f, q, n_items);
     }
 }
 
 // ------------------------------------------------------------------ kernel
-template <int WT, bool GATEUP, int MINB>
+// NG: token groups per pass (1: decode batches of a few tokens per expert, where the second
+// group's registers would only cost occupancy of the scheduler; 2: larger batches).
+template <int WT, bool GATEUP, int MINB, int NG>
 __global__ void __launch_bounds__(GEMV_THREADS, MINB)
     gemv_kernel(const GemvArgs a, const __grid_constant__ GemvMaps tm) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -510,13 +563,14 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
     f.gi = 0;
     f.n_item = -1;
     fetch_next(a, f, q, n_items);
-    next_item(a, f, q, n_items);
+    next_item<NG>(a, f, q, n_items);
     for (int s = 0; s < D; s++)
-        fill<WT, GATEUP>(a, tm, f, &bars[s], &recs[s], slots + (size_t)s * a.slot_bytes, q, n_items);
+        fill<WT, GATEUP, NG>(a, tm, f, &bars[s], &recs[s], slots + (size_t)s * a.slot_bytes, q, n_items);
 
-    TokCols tc[2];
+    TokCols tc[NG];
+    XBase xb0;  // NG == 1: the group's bases, kept for the pass (two-group passes address from tc)
     int ng = 1;
-    float acc[2][4];
+    float acc[NG][4];
     int s = 0;
     uint32_t ph = 0;
     for (;;) {
@@ -541,12 +595,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
         const uint8_t *sl = slots + (size_t)s * a.slot_bytes;
         if (chunk == 0) {  // a new pass: the token columns of its (up to) two groups
             const int4 bv = *reinterpret_cast<const int4 *>(&recs[s].beg);
-            const int t0 = bv.x + pass * 2 * TOKG;
-            const int nt = min(2 * TOKG, bv.y - t0);
+            const int t0 = bv.x + pass * NG * TOKG;
+            const int nt = min(NG * TOKG, bv.y - t0);
             const int *pp = reinterpret_cast<const int *>(sl + a.wbytes) + bv.z;  // the pass's pairs
             ng = nt > TOKG ? 2 : 1;
 #pragma unroll
-            for (int G = 0; G < 2; G++) {
+            for (int G = 0; G < NG; G++) {
                 const int ntok = min(TOKG, nt - G * TOKG);
                 // past the group's end the group's first token stands in (never written)
                 int pg = ntok > 0 ? pp[G * TOKG + (g < ntok ? g : 0)] : 0;
@@ -563,11 +617,49 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
                 tc[G].pp0 = v0 ? p0 : -1;
                 tc[G].pp1 = v1 ? p1 : -1;
             }
+            if constexpr (NG == 1) xb0 = x_base<WT>(a, tc[0], nb);
 #pragma unroll
-            for (int G = 0; G < 2; G++) acc[G][0] = acc[G][1] = acc[G][2] = acc[G][3] = 0.0f;
+            for (int G = 0; G < NG; G++) acc[G][0] = acc[G][1] = acc[G][2] = acc[G][3] = 0.0f;
         }
         const int S = a.row_stride;
-        if constexpr (WT == TMOE_WT_Q4K) {
+        if constexpr (NG == 1) {
+            if constexpr (WT == TMOE_WT_Q4K) {
+                const uint8_t *ra = sl + (size_t)g * S, *rb = sl + (size_t)(g + 8) * S;
+                const bool lo = t4 < 2;
+                if (nblk == 2) {  // both super-blocks' activations in flight before the MMAs
+                    XQ4 x0[1], x1[1];
+                    load_xq4(xb0, b0, lo, x0[0]);
+                    load_xq4(xb0, b0 + 1, lo, x1[0]);
+                    q4_block<1>(ra, rb, x0, acc);
+                    q4_block<1>(ra + TMOE_Q4K_BYTES, rb + TMOE_Q4K_BYTES, x1, acc);
+                } else {
+                    for (int bi = 0; bi < nblk; bi++) {
+                        XQ4 x[1];
+                        load_xq4(xb0, b0 + bi, lo, x[0]);
+                        q4_block<1>(ra + bi * TMOE_Q4K_BYTES, rb + bi * TMOE_Q4K_BYTES, x, acc);
+                    }
+                }
+            } else if constexpr (GATEUP) {
+                const uint8_t *ra = sl + (size_t)g * S, *rb = sl + (size_t)(g + 8) * S;
+                for (int kb = 0; kb < nb; kb++) {
+                    XQ6 x[1];
+                    load_xq6(xb0, kb, x[0]);
+                    q6_block<1, 2, 2>(ra + kb * TMOE_Q6K_BYTES, rb + kb * TMOE_Q6K_BYTES, x, acc);
+                }
+            } else {
+                const uint8_t *ra = sl + (size_t)(2 * g) * S, *rb = sl + (size_t)(2 * g + 1) * S;
+                for (int kb = 0; kb < nb; kb++) {
+                    const int ma = kb & 1, mb = (nb + kb) & 1;
+                    const uint8_t *pa = ra + kb * TMOE_Q6K_BYTES, *pb = rb + kb * TMOE_Q6K_BYTES;
+                    XQ6 x[1];
+                    load_xq6(xb0, kb, x[0]);
+                    if (ma == 0 && mb == 0) q6_block<1, 0, 0>(pa, pb, x, acc);
+                    else if (ma == 0) q6_block<1, 0, 1>(pa, pb, x, acc);
+                    else if (mb == 0) q6_block<1, 1, 0>(pa, pb, x, acc);
+                    else q6_block<1, 1, 1>(pa, pb, x, acc);
+                }
+            }
+        } else if constexpr (WT == TMOE_WT_Q4K) {
             const uint8_t *ra = sl + (size_t)g * S, *rb = sl + (size_t)(g + 8) * S;
             for (int bi = 0; bi < nblk; bi++) {
                 const int kb = b0 + bi;
@@ -578,7 +670,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
                 } else {
                     XQ4 x[2];
                     load_xq4(a, tc[0], kb, nb, x[0]);
-                    load_xq4(a, tc[1], kb, nb, x[1]);
+                    load_xq4(a, tc[NG - 1], kb, nb, x[1]);
                     q4_block<2>(ra + bi * TMOE_Q4K_BYTES, rb + bi * TMOE_Q4K_BYTES, x, acc);
                 }
             }
@@ -592,7 +684,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
                 } else {
                     XQ6 x[2];
                     load_xq6(a, tc[0], kb, nb, x[0]);
-                    load_xq6(a, tc[1], kb, nb, x[1]);
+                    load_xq6(a, tc[NG - 1], kb, nb, x[1]);
                     q6_block<2, 2, 2>(ra + kb * TMOE_Q6K_BYTES, rb + kb * TMOE_Q6K_BYTES, x, acc);
                 }
             }
@@ -611,7 +703,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
                 } else {
                     XQ6 x[2];
                     load_xq6(a, tc[0], kb, nb, x[0]);
-                    load_xq6(a, tc[1], kb, nb, x[1]);
+                    load_xq6(a, tc[NG - 1], kb, nb, x[1]);
                     if (ma == 0 && mb == 0) q6_block<2, 0, 0>(pa, pb, x, acc);
                     else if (ma == 0) q6_block<2, 0, 1>(pa, pb, x, acc);
                     else if (mb == 0) q6_block<2, 1, 0>(pa, pb, x, acc);
@@ -620,7 +712,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
             }
         }
         __syncwarp();  // every lane's reads of the slot are done (their values are consumed)
-        fill<WT, GATEUP>(a, tm, f, &bars[s], &recs[s], slots + (size_t)s * a.slot_bytes, q, n_items);
+        fill<WT, GATEUP, NG>(a, tm, f, &bars[s], &recs[s], slots + (size_t)s * a.slot_bytes, q, n_items);
         if (chunk == a.n_chunks - 1) {  // this pass's sums are complete
             // output rows of MMA rows g and g+8
             int row_a, row_b;
@@ -634,7 +726,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
                 row_b = row_a + 1;
             }
 #pragma unroll
-            for (int G = 0; G < 2; G++) {
+            for (int G = 0; G < NG; G++) {
                 if (G >= ng) break;
                 const int q0 = tc[G].pp0, q1 = tc[G].pp1;
                 if constexpr (GATEUP) {
@@ -750,15 +842,24 @@ static cudaError_t launch_t(const GemvArgs &args_in, int max_items, int sm_count
     const int slots = sm_count * pl.ctas_per_sm;
     if (grid > slots) grid = slots;
     if (grid < 1) return cudaSuccess;
-    static int cache1[64] = {}, cache2[64] = {};
+    // One token group per pass when the batch averages at most 4 pairs per active expert (decode):
+    // an expert with more tokens then takes more passes over rows that L2 still holds.
+    const bool one = (int64_t)a.n_pairs <= 4 * (int64_t)max_items;
+    static int cache[4][64] = {};
     cudaError_t e;
+#define TMOE_GEMV_LAUNCH(MINB, NG, CI)                                                                      \
+    do {                                                                                                 \
+        if ((e = set_smem_once(gemv_kernel<WT, GATEUP, MINB, NG>, smem, cache[CI])) != cudaSuccess) return e; \
+        gemv_kernel<WT, GATEUP, MINB, NG><<<grid, GEMV_THREADS, smem, st>>>(a, tm);                       \
+    } while (0)
     if (pl.ctas_per_sm == 2) {
-        if ((e = set_smem_once(gemv_kernel<WT, GATEUP, 2>, smem, cache2)) != cudaSuccess) return e;
-        gemv_kernel<WT, GATEUP, 2><<<grid, GEMV_THREADS, smem, st>>>(a, tm);
+        if (one) TMOE_GEMV_LAUNCH(2, 1, 0);
+        else TMOE_GEMV_LAUNCH(2, 2, 1);
     } else {
-        if ((e = set_smem_once(gemv_kernel<WT, GATEUP, 1>, smem, cache1)) != cudaSuccess) return e;
-        gemv_kernel<WT, GATEUP, 1><<<grid, GEMV_THREADS, smem, st>>>(a, tm);
+        if (one) TMOE_GEMV_LAUNCH(1, 1, 2);
+        else TMOE_GEMV_LAUNCH(1, 2, 3);
     }
+#undef TMOE_GEMV_LAUNCH
     return cudaGetLastError();
 }
 
