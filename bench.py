@@ -76,9 +76,10 @@ def parse():
     p.add_argument("--cpu-sample-s", type=float, default=15.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--sweep", action="store_true", help="also time T in {1,4,16,64}")
-    p.add_argument("--mode", choices=["decode", "prefill", "streamed"], default="decode",
+    p.add_argument("--mode", choices=["decode", "prefill", "streamed", "gguf"], default="decode",
                    help="decode: C2 at T tokens (the metric's config); prefill: C2-shaped layer at T=8192 "
-                        "(tensor roofline); streamed: config 5, skewed routing over 64 device slots of 128 experts")
+                        "(tensor roofline); streamed: config 5, skewed routing over 64 device slots of 128 experts; "
+                        "gguf: loading the expert tensors of a C2-shaped GGUF file into HBM")
     p.add_argument("--slots", type=int, default=64)
     p.add_argument("--shape", choices=["c2", "235b"], default="c2",
                    help="c2: the Qwen3-30B-A3B layer (the metric's config); 235b: config 4's layer shape")
@@ -509,6 +510,105 @@ def run_streamed(args, local_rank):
     return res
 
 
+def run_gguf(args, local_rank):
+    """Expert loading from a GGUF file (load_weights, qwen3moe.rs:2498-2584): a synthetic C2-shaped
+    file of --layers layers (128 experts of random bytes per layer; default 4 layers, 1.57 GB of
+    experts) is written to a temporary directory, then each step loads every layer's three stacked
+    expert tensors into preallocated HBM through tmoe_gguf_load (pinned double buffering).  Page
+    cache warm (the file was just written); `cold_gbs` is the same load after
+    posix_fadvise(DONTNEED) on the file (no effect where the directory is RAM-backed).
+    `reference_pattern_gbs`: the reference's loop for the same bytes (16 MB reads into a pageable
+    buffer, each copied to the device synchronously), in this process."""
+    import shutil
+    import tempfile
+
+    import torch
+
+    from tests.gguf_fixture import write_moe_gguf
+    from tetraeder_b200.gguf import EXPERT_TENSORS, GgufFile
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    L = args.layers if args.layers != 48 else 4
+    tmp = tempfile.mkdtemp(prefix="tmoe_gguf_")
+    try:
+        path = os.path.join(tmp, "c2.gguf")
+        log(f"writing a {L}-layer C2-shaped GGUF")
+        write_moe_gguf(path, n_layer=L, n_embd=H, n_ff=I, n_expert=E, n_used=K_USED, gate_type=Q4K,
+                       down_type=DOWN_T, quantise=False, extra_kv=False, n_vocab=256, seed=args.seed)
+        f = GgufFile(path)
+        names = [f"blk.{il}.{n}.weight" for il in range(L) for n in EXPERT_TENSORS]
+        outs = [torch.empty(f.tensor(n).nbytes, dtype=torch.uint8, device=dev) for n in names]
+        step_bytes = sum(o.numel() for o in outs)
+
+        def step():
+            for n, o in zip(names, outs):
+                f.load(n, o)
+
+        def timed(fn, n_steps, before=None):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ms = 0.0
+            for _ in range(n_steps):
+                if before:
+                    before()
+                torch.cuda.synchronize()
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                ms += e0.elapsed_time(e1)
+            return ms / n_steps
+
+        for _ in range(max(args.warmup, 3)):
+            step()
+        with Clocks(local_rank) as clk:
+            ms = timed(step, args.steps)
+
+        def drop():
+            fd = os.open(path, os.O_RDONLY)
+            os.posix_fadvise(fd, 0, 0, os.POSIX_FADV_DONTNEED)
+            os.close(fd)
+
+        cold_ms = timed(step, 1, before=drop)
+        buf = bytearray(16 << 20)
+
+        def reference_pattern():
+            with open(path, "rb") as fh:
+                for n, o in zip(names, outs):
+                    t = f.tensor(n)
+                    fh.seek(t.offset)
+                    done = 0
+                    while done < t.nbytes:
+                        k = min(len(buf), t.nbytes - done)
+                        fh.readinto(memoryview(buf)[:k])
+                        o[done:done + k].copy_(torch.frombuffer(buf, dtype=torch.uint8, count=k))
+                        done += k
+
+        ref_ms = timed(reference_pattern, 1)
+        checks = [torch.equal(outs[i][:4096].cpu(), torch.from_numpy(f.read(names[i], 0, 4096)))
+                  for i in (0, len(names) - 1)]
+        if not all(checks):
+            raise RuntimeError("loaded bytes differ from the file")
+        f.close()
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    gbs = step_bytes / (ms / 1e3) / 1e9
+    return {
+        "metric": "gguf_expert_load_gbs", "value": round(gbs, 2), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": {"workload": f"C2-shaped GGUF, {L} layers x {E} experts (gate/up Q4_K, down Q6_K shapes, random "
+                               "bytes), every expert tensor into HBM", "bytes_per_step": step_bytes,
+                   "page_cache": "warm", "loader": "tmoe_gguf_load: pread into two pinned 64 MB buffers, "
+                                                   "cudaMemcpyAsync per chunk"},
+        "cold_gbs": round(step_bytes / (cold_ms / 1e3) / 1e9, 2),
+        "reference_pattern_gbs": round(step_bytes / (ref_ms / 1e3) / 1e9, 2),
+        "e2e": {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": step_bytes, "d2h_bytes_per_step": 0,
+                "path": "GgufFile.load -> tmoe_gguf_load (file -> HBM is the whole path)"},
+        "gpu_launches": 0, "clocks": clk.summary(),
+    }
+
+
 def sweep_tokens(torch, tb, layers, dev):
     """tokens/s and layer roofline fraction at T in {1, 4, 16, 64} (graph of 48 layer calls)."""
     peaks = load_peaks()
@@ -672,6 +772,11 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
+    if args.mode == "gguf":
+        if world > 1:
+            raise SystemExit("--mode gguf runs on one GPU")
+        emit(run_gguf(args, local_rank))
+        return 0
     res = run_streamed(args, local_rank) if args.mode == "streamed" else run_ours(args, rank, world, local_rank)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:

@@ -66,6 +66,7 @@ extern "C" {
 #define TMOE_E_UNSUPPORTED -4
 #define TMOE_E_DEVICE -5    /* a kernel reported an error (timeout of a bounded wait) */
 #define TMOE_E_COMM -6      /* NCCL failure */
+#define TMOE_E_NOTFOUND -7  /* a GGUF key or tensor that the file does not have */
 
 #define TMOE_TYPE_Q4_K 12
 #define TMOE_TYPE_Q6_K 14
@@ -253,6 +254,47 @@ TMOE_API int tmoe_quantize(int32_t type, const float *x, int64_t nrows, int64_t 
                            void *stream);
 /* quant::to_f32 (crates/ggml-sys/src/quant.rs:19) for Q4_K / Q6_K: n values (n % 256 == 0). */
 TMOE_API int tmoe_dequantize(int32_t type, const void *in, int64_t n, float *out, void *stream);
+
+/* GGUF model files (crates/model/src/gguf.rs; the loader of load_weights, qwen3moe.rs:2498-2584).
+ *   tmoe_gguf_open        <- Gguf::open (gguf.rs:236-296): the header, metadata and tensor index of a
+ *                            file, or of every shard of a split model opened from its first shard
+ *                            (<prefix>-00001-of-0000N.gguf); GGUF version 3 only
+ *   tmoe_gguf_kv          <- Gguf::get/str/u64/f32 (gguf.rs:409-450): integers widen to u64 / i64,
+ *                            floats to f64, arrays keep their length only
+ *   tmoe_gguf_tensor_info <- Gguf::tensor (gguf.rs:452): name, ggml type, ne[4], shard, absolute
+ *                            byte offset in the shard file, bytes
+ *   tmoe_gguf_read/load   <- the reads of load_weights: bytes [offset, offset + nbytes) of a tensor
+ *                            (an expert slab is nbytes / ne[2] long, TensorInfo::slab gguf.rs:76-86)
+ *                            into host memory, or into device memory of `device` through pinned
+ *                            bounce buffers on `stream` (returns when the copies are done)
+ * Errors: TMOE_E_INVALID (bad file, bad range), TMOE_E_UNSUPPORTED (version), TMOE_E_NOTFOUND
+ * (missing key), TMOE_E_CUDA; the message is tmoe_gguf_last_error() (per thread).  Strings
+ * returned stay valid until tmoe_gguf_close. */
+typedef struct tmoe_gguf tmoe_gguf;
+#define TMOE_GGUF_U64 0
+#define TMOE_GGUF_I64 1
+#define TMOE_GGUF_F64 2
+#define TMOE_GGUF_BOOL 3 /* in u: 0 or 1 */
+#define TMOE_GGUF_STR 4
+#define TMOE_GGUF_ARRAY 5 /* in n: the length */
+TMOE_API int tmoe_gguf_open(const char *path, tmoe_gguf **out);
+TMOE_API void tmoe_gguf_close(tmoe_gguf *g);
+TMOE_API const char *tmoe_gguf_last_error(void);
+TMOE_API int32_t tmoe_gguf_n_shards(const tmoe_gguf *g);
+TMOE_API int64_t tmoe_gguf_n_kv(const tmoe_gguf *g);
+TMOE_API int tmoe_gguf_kv_key(const tmoe_gguf *g, int64_t i, const char **key);
+TMOE_API int tmoe_gguf_kv(const tmoe_gguf *g, const char *key, int32_t *kind, uint64_t *u, int64_t *i, double *f,
+                          const char **s, uint64_t *n);
+TMOE_API int64_t tmoe_gguf_n_tensors(const tmoe_gguf *g);
+/* index of the tensor, or -1 */
+TMOE_API int64_t tmoe_gguf_find_tensor(const tmoe_gguf *g, const char *name);
+TMOE_API int tmoe_gguf_tensor_info(const tmoe_gguf *g, int64_t i, const char **name, int32_t *type, int64_t *ne,
+                                   int32_t *shard, uint64_t *offset, uint64_t *nbytes);
+/* ggml's block size (elements) and bytes per block of a type id */
+TMOE_API int tmoe_gguf_type_size(int32_t type, int32_t *block_elems, int32_t *block_bytes);
+TMOE_API int tmoe_gguf_read(const tmoe_gguf *g, int64_t tensor, uint64_t offset, uint64_t nbytes, void *dst);
+TMOE_API int tmoe_gguf_load(const tmoe_gguf *g, int64_t tensor, uint64_t offset, uint64_t nbytes, void *dst,
+                            int32_t device, void *stream);
 
 /* Per-kernel device timing of this handle's calls (the StepProfile phase timers of
  * crates/model/src/qwen3moe.rs:69-107, narrowed to the layer's kernels).  While enabled, every

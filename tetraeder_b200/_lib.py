@@ -12,7 +12,8 @@ HEADER = os.path.join(HERE, "..", "include", "tmoe.h")
 
 TMOE_OK = 0
 ERRORS = {-1: "TMOE_E_INVALID", -2: "TMOE_E_CUDA", -3: "TMOE_E_NOMEM", -4: "TMOE_E_UNSUPPORTED",
-          -5: "TMOE_E_DEVICE", -6: "TMOE_E_COMM"}
+          -5: "TMOE_E_DEVICE", -6: "TMOE_E_COMM", -7: "TMOE_E_NOTFOUND"}
+TMOE_E_INVALID, TMOE_E_UNSUPPORTED, TMOE_E_NOTFOUND = -1, -4, -7
 TYPE_Q4_K, TYPE_Q6_K = 12, 14
 
 
@@ -73,6 +74,19 @@ SIGNATURES = {
     "tmoe_slots_state": ([P, P, P, P, P], C.c_int),
     "tmoe_slots_last_plan": ([P, P, P, P, P, P], C.c_int),
     "tmoe_streamed_layer": ([P, P, P, P, I64, I32, P, P, P, P, P, P], C.c_int),
+    "tmoe_gguf_open": ([C.c_char_p, C.POINTER(C.c_void_p)], C.c_int),
+    "tmoe_gguf_close": ([P], None),
+    "tmoe_gguf_last_error": ([], C.c_char_p),
+    "tmoe_gguf_n_shards": ([P], I32),
+    "tmoe_gguf_n_kv": ([P], I64),
+    "tmoe_gguf_kv_key": ([P, I64, C.POINTER(C.c_char_p)], C.c_int),
+    "tmoe_gguf_kv": ([P, C.c_char_p, P, P, P, P, C.POINTER(C.c_char_p), P], C.c_int),
+    "tmoe_gguf_n_tensors": ([P], I64),
+    "tmoe_gguf_find_tensor": ([P, C.c_char_p], I64),
+    "tmoe_gguf_tensor_info": ([P, I64, C.POINTER(C.c_char_p), P, P, P, P, P], C.c_int),
+    "tmoe_gguf_type_size": ([I32, P, P], C.c_int),
+    "tmoe_gguf_read": ([P, I64, C.c_uint64, C.c_uint64, P], C.c_int),
+    "tmoe_gguf_load": ([P, I64, C.c_uint64, C.c_uint64, P, I32, P], C.c_int),
 }
 COMM_ID_BYTES = 128
 PHASES = ["rms_norm", "router_logits", "topk", "map_ids", "dispatch", "quant_x", "gate_up", "quant_act",

@@ -126,8 +126,9 @@ struct GemvArgs {
 };
 // prefill.cu: the grouped tcgen05 GEMMs of the large-batch regime (see prefill.cu)
 bool prefill_fits(int H, int I);
-cudaError_t launch_prep_rows(const float *src, const int32_t *perm, int n_rows, int x_div, int K, __half *dst,
-                             cudaStream_t st);
+// n_valid (device, may be NULL): rows past it (no dispatched pair) are skipped.
+cudaError_t launch_prep_rows(const float *src, const int32_t *perm, int n_rows, const int32_t *n_valid, int x_div,
+                             int K, __half *dst, cudaStream_t st);
 cudaError_t launch_dequant_f16(int wt, const uint8_t *w, size_t nb2, int N, int K, const int4 *active,
                                const int32_t *n_active, int max_active, __half *dst, cudaStream_t st);
 cudaError_t launch_prefill_gemm(bool swiglu, const __half *A, int n_rows, int K, const __half *b0, const __half *b1,
@@ -136,9 +137,10 @@ cudaError_t launch_prefill_gemm(bool swiglu, const __half *A, int n_rows, int K,
                                 cudaStream_t st);
 
 // n_valid (device, may be NULL): the dispatched pairs; sorted rows past it are not gathered.
+// tokens_ready: aq_t / ad_t / ab_t already hold these T tokens (an earlier chunk of the same call).
 cudaError_t launch_prep_gateup_a(const float *x, int T, const int32_t *perm, int n_rows, const int32_t *n_valid,
                                  int x_div, int K, __half *aq_t, float *ad_t, __half *ab_t, __half *aq, float *ad,
-                                 __half *ab, cudaStream_t st);
+                                 __half *ab, bool tokens_ready, cudaStream_t st);
 cudaError_t launch_prefill_gateup(const __half *aq, const float *ad, const __half *ab, int n_rows, int K, int I,
                                   const uint8_t *gate, const uint8_t *up, size_t nb1, size_t nb2_gate,
                                   size_t nb2_up, const int4 *active, const int32_t *n_active, int max_active,

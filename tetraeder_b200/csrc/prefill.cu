@@ -110,15 +110,16 @@ __device__ __forceinline__ float silu_mul_pf(float g, float u) { return (g / (1.
 
 // ------------------------------------------------------------------ preparation kernels
 // A rows of the GEMM: row r of `rows` (expert-sorted pairs; src row = perm[r] / x_div) through the
-// Q8_K round trip, as fp16.  One warp per (row, 256-block).
+// Q8_K round trip, as fp16.  One warp per (row, 256-block); rows from n_valid[0] on (no dispatched
+// pair: no tile reads them) are skipped.
 __global__ void prep_rows_kernel(const float *__restrict__ src, const int32_t *__restrict__ perm, int n_rows,
-                                 int x_div, int K, __half *__restrict__ dst) {
+                                 const int32_t *__restrict__ n_valid, int x_div, int K, __half *__restrict__ dst) {
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int nb = K / TMOE_QK;
     const int64_t r = gw / nb;
     const int b = (int)(gw % nb);
-    if (r >= n_rows) return;
+    if (r >= n_rows || (n_valid && r >= n_valid[0])) return;
     int p = perm ? perm[r] : (int)r;
     if (p < 0) p = 0;
     const float *xr = src + (int64_t)(p / x_div) * K + b * TMOE_QK + 8 * lane;
@@ -962,11 +963,11 @@ static bool encode_f16_rows(CUtensorMap *m, const void *base, int64_t rows, int 
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-cudaError_t launch_prep_rows(const float *src, const int32_t *perm, int n_rows, int x_div, int K, __half *dst,
-                             cudaStream_t st) {
+cudaError_t launch_prep_rows(const float *src, const int32_t *perm, int n_rows, const int32_t *n_valid, int x_div,
+                             int K, __half *dst, cudaStream_t st) {
     if (n_rows <= 0) return cudaSuccess;
     const int64_t warps = (int64_t)n_rows * (K / TMOE_QK);
-    prep_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(src, perm, n_rows, x_div, K, dst);
+    prep_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(src, perm, n_rows, n_valid, x_div, K, dst);
     return cudaGetLastError();
 }
 
@@ -992,12 +993,14 @@ cudaError_t launch_dequant_f16(int wt, const uint8_t *w, size_t nb2, int N, int 
 // The Q8_K of the T token rows (token order), then their copies in expert-sorted pair order.
 cudaError_t launch_prep_gateup_a(const float *x, int T, const int32_t *perm, int n_rows, const int32_t *n_valid,
                                  int x_div, int K, __half *aq_t, float *ad_t, __half *ab_t, __half *aq, float *ad,
-                                 __half *ab, cudaStream_t st) {
+                                 __half *ab, bool tokens_ready, cudaStream_t st) {
     if (n_rows <= 0 || T <= 0) return cudaSuccess;
-    const int64_t warps = (int64_t)T * (K / TMOE_QK);
-    prep_gateup_a_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(x, nullptr, T, 1, K, aq_t, ad_t, ab_t);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (!tokens_ready) {
+        const int64_t warps = (int64_t)T * (K / TMOE_QK);
+        prep_gateup_a_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(x, nullptr, T, 1, K, aq_t, ad_t, ab_t);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
     gather_gateup_a_kernel<<<(unsigned)((n_rows + 7) / 8), 256, 0, st>>>(aq_t, ad_t, ab_t, perm, n_rows, n_valid,
                                                                          x_div, K, aq, ad, ab);
     return cudaGetLastError();

@@ -228,9 +228,6 @@ int check_tensors(tmoe_handle *h, const tmoe_expert_tensors *t) {
     return TMOE_OK;
 }
 
-// a4-a8 on `ids` (already slot ids) and `w`.  dispatched: the dispatch buffers (counts, offsets,
-// perm, active, zeroed work counters) already hold this call's dispatch; x_quantized: the Q8_K
-// rows of xn are already in h->xq/xd/xbl/xbh.
 // The down product of the large-batch regime as a grouped tcgen05 GEMM: A2 = Q8_K round trip of
 // the SwiGLU activations in expert-sorted order, as fp16; fp16 copies of the active experts'
 // down rows; dout[pair] = A2 . down^T.  (gate/up stay on the integer MMA path: their outputs feed
@@ -240,7 +237,8 @@ cudaError_t prefill_down(tmoe_handle *h, cudaStream_t st, int64_t P, const tmoe_
                          bool act_sorted) {
     const tmoe_config &c = h->cfg;
     const int H = c.n_embd, I = c.n_ff;
-    cudaError_t e = tmoe::launch_prep_rows(h->act, act_sorted ? nullptr : h->perm, (int)P, 1, I, h->a2, st);
+    cudaError_t e = tmoe::launch_prep_rows(h->act, act_sorted ? nullptr : h->perm, (int)P, h->offsets + t->n_slots, 1,
+                                           I, h->a2, st);
     if (e == cudaSuccess)
         e = tmoe::launch_dequant_f16(wt_of(c.down_type), (const uint8_t *)t->down, t->down_nb2, H, I, h->active,
                                      h->n_active, max_active, h->w16_down, st);
@@ -251,8 +249,14 @@ cudaError_t prefill_down(tmoe_handle *h, cudaStream_t st, int64_t P, const tmoe_
     return e;
 }
 
+// a4-a8 on `ids` (already slot ids) and `w`.  dispatched: the dispatch buffers (counts, offsets,
+// perm, active, zeroed work counters) already hold this call's dispatch; x_quantized: the Q8_K
+// rows of xn are already in h->xq/xd/xbl/xbh; combine: fold the pair rows into `out` (else they
+// stay in h->dout); a16_ready: the large-batch regime's per-token fp16 Q8_K rows of xn
+// (h->aq16_t/ad16_t/ab16_t) are already there, from an earlier chunk of the same layer call.
 int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, const int32_t *ids, const float *w,
-                const tmoe_expert_tensors *t, float *out, bool dispatched, bool x_quantized, bool combine = true) {
+                const tmoe_expert_tensors *t, float *out, bool dispatched, bool x_quantized, bool combine = true,
+                bool a16_ready = false) {
     const tmoe_config &c = h->cfg;
     const int k = c.n_expert_used, H = c.n_embd, I = c.n_ff;
     const int64_t P = T * k;
@@ -274,8 +278,7 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
         {
             PhaseMark pm(h, st, TMOE_PHASE_QUANT_X);
             e = tmoe::launch_prep_gateup_a(xn, (int)T, h->perm, (int)P, h->offsets + t->n_slots, k, H, h->aq16_t,
-                                           h->ad16_t, h->ab16_t, h->aq16,
-                                           h->ad16, h->ab16, st);
+                                           h->ad16_t, h->ab16_t, h->aq16, h->ad16, h->ab16, a16_ready, st);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "prefill gate/up rows");
         {
@@ -1168,7 +1171,8 @@ int tmoe_streamed_layer(tmoe_handle *h, void *stream, tmoe_slots *s, const float
     // Chunk 0's misses are paged straight into their slots.  Chunk c >= 1 is paged from the host
     // store into the staging area on the side stream while chunk c - 1 computes, then moved into
     // its slots right before it computes (its slots may be chunk c - 1's).  The events are enqueued
-    // in dependency order, so the schedule holds under stream capture too.
+    // in dependency order, so the schedule holds under stream capture too.  Chunks >= 1 reuse
+    // chunk 0's Q8_K rows of xn.
     const int MC = s->dev.max_chunks;
     const bool overlap = s->side != nullptr;
     if (overlap) {
@@ -1201,7 +1205,7 @@ int tmoe_streamed_layer(tmoe_handle *h, void *stream, tmoe_slots *s, const float
             e = tmoe::launch_map_ids(ids, P, s->dev.map + (size_t)ch * E, E, h->mapped, st);
         }
         if (e != cudaSuccess) return cuda_fail(h, e, "chunk map");
-        rc = run_experts(h, st, xn, T, h->mapped, w, &s->slot_wts, out, false, ch > 0, false);
+        rc = run_experts(h, st, xn, T, h->mapped, w, &s->slot_wts, out, false, ch > 0, false, ch > 0);
         if (rc) return rc;
     }
     {
