@@ -81,6 +81,12 @@ def parse():
                         "(tensor roofline); streamed: config 5, skewed routing over 64 device slots of 128 experts; "
                         "gguf: loading the expert tensors of a C2-shaped GGUF file into HBM")
     p.add_argument("--slots", type=int, default=64)
+    p.add_argument("--routing", default=None,
+                   help="streamed mode: replay the layer steps of this tetraeder-routing v1 trace instead of the "
+                        "Zipf routing (cyclically, one recorded step per bench step)")
+    p.add_argument("--routing-layer", type=int, default=-1, help="the trace layer to replay (-1: the first one)")
+    p.add_argument("--record-trace", default=None,
+                   help="streamed mode: also write the routing of --steps steps as a tetraeder-routing v1 trace")
     p.add_argument("--shape", choices=["c2", "235b"], default="c2",
                    help="c2: the Qwen3-30B-A3B layer (the metric's config); 235b: config 4's layer shape")
     p.add_argument("--ep", choices=["a2a", "allreduce"], default="a2a",
@@ -425,8 +431,23 @@ def run_streamed(args, local_rank):
     bias, perm = zipf_bias(torch, E, args.seed + 5)
     gen = torch.Generator(device=dev)
     gen.manual_seed(args.seed + 1)
+    replay = None
+    if args.routing:  # recorded routing: the logits of each step reproduce its recorded choice
+        from tetraeder_b200.trace import LayerStep, TraceReader
+        with TraceReader(args.routing) as tr:
+            if tr.header.n_expert != E or tr.header.n_used != K_USED:
+                raise SystemExit(f"{args.routing}: {tr.header.n_expert} experts, top-{tr.header.n_used}; "
+                                 f"the bench layer has {E}, top-{K_USED}")
+            steps = [r for r in tr if isinstance(r, LayerStep)]
+        layer_id = args.routing_layer if args.routing_layer >= 0 else (steps[0].layer if steps else 0)
+        steps = [r for r in steps if r.layer == layer_id]
+        if not steps:
+            raise SystemExit(f"{args.routing}: no steps of layer {layer_id}")
+        T = args.tokens = steps[0].n_tokens
+        steps = [r for r in steps if r.n_tokens == T]
+        replay = [torch.from_numpy(r.logits(E)).to(dev) for r in steps]
     x = torch.randn((T, H), generator=gen, device=dev)
-    lg = torch.randn((T, E), generator=gen, device=dev) + bias.to(dev)
+    lg = replay[0] if replay else torch.randn((T, E), generator=gen, device=dev) + bias.to(dev)
     layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=DOWN_T,
                         max_tokens=T, device=local_rank)
     cache = tb.SlotCache(layer, slots, store)
@@ -434,8 +455,14 @@ def run_streamed(args, local_rank):
     out = torch.empty((T, H), device=dev)
     x_host, out_host = x.cpu().pin_memory(), torch.empty((T, H)).pin_memory()
 
+    cursor = [0]
+
     def step():
-        layer.moe_ffn_streamed(x, cache, logits=lg, out=out)
+        logits = lg
+        if replay:
+            logits = replay[cursor[0] % len(replay)]
+            cursor[0] += 1
+        layer.moe_ffn_streamed(x, cache, logits=logits, out=out)
 
     step()
     layer.check()
@@ -475,6 +502,16 @@ def run_streamed(args, local_rank):
     layer.profile(False)
     n_chunks, _, loads = cache.last_plan()
     phase_ms = {k: v[0] for k, v in prof.items()}
+    if args.record_trace:  # the routing of --steps further steps, as a trace (untimed)
+        from tetraeder_b200.trace import TraceHeader, TraceWriter
+        th = TraceHeader(1, E, K_USED, model="bench streamed C5", vram_slots=NS, ram_slots=E, ubatch=T,
+                         hot_source="profile", expert_bytes=[EXPERT_BYTES])
+        ids = torch.empty((T, K_USED), dtype=torch.int32, device=dev)
+        with TraceWriter(args.record_trace, th) as tw:
+            for i in range(args.steps):
+                logits = replay[(cursor[0] + i) % len(replay)] if replay else lg
+                layer.moe_ffn_streamed(x, cache, logits=logits, out=out, ids_out=ids)
+                tw.layer_step(i, 0, ids.cpu().numpy())
     peaks = load_peaks()
     gu_flops = 2 * T * K_USED * 2 * H * I
     ach = gu_flops / (phase_ms["gate_up"] / 1e3) / 1e12
@@ -485,8 +522,11 @@ def run_streamed(args, local_rank):
         "steps": args.steps, "warmup": W, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None,
         "dtype": "gate/up exact Q8_K x Q4_K on tcgen05 (fp16-carried integers), down fp16 tcgen05", "data": "synthetic",
-        "config": dict(workload(args, 1), slots=NS, routing="logits ~N(0,1) + Zipf(1.2) bias over a seeded "
-                       "permutation", store="all 128 experts in pinned host memory, paged in by a copy kernel"),
+        "config": dict(workload(args, 1), slots=NS,
+                       routing=(f"recorded: {os.path.basename(args.routing)}, {len(replay)} steps of one layer, "
+                                "replayed in order" if replay else
+                                "logits ~N(0,1) + Zipf(1.2) bias over a seeded permutation"),
+                       store="all 128 experts in pinned host memory, paged in by a copy kernel"),
         "roofline": {"bound": "tensor", "kernel": "prefill_gateup_kernel (all chunks)", "achieved": round(ach, 1),
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4),
                      "peak_source": peaks["source"] + ", burst bf16", "traffic": None,

@@ -296,6 +296,47 @@ TMOE_API int tmoe_gguf_read(const tmoe_gguf *g, int64_t tensor, uint64_t offset,
 TMOE_API int tmoe_gguf_load(const tmoe_gguf *g, int64_t tensor, uint64_t offset, uint64_t nbytes, void *dst,
                             int32_t device, void *stream);
 
+/* Routing traces, the tetraeder-routing v1 format (crates/memory/src/replay/trace.rs): a JSON
+ * header line (TraceHeader), then records of a layer step's routed ids (and optional predictions)
+ * or of a hot-set refresh.  For replaying recorded routing into the layer.
+ *   tmoe_trace_open/next/ids <- TraceReader (trace.rs:225-330): the header is parsed and checked
+ *     (format and version, id_bytes = 1 for n_expert <= 256 else 2, n_used > 0, one expert_bytes
+ *     entry per layer); tmoe_trace_next returns 1 with a record, 0 at a clean end of file, a
+ *     negative code on a truncated or corrupt record (more than 2^20 tokens, an id >= n_expert, an
+ *     unknown kind), after which the reader stays failed; tmoe_trace_ids copies the current step's
+ *     routed (which = 0), predicted (1) or depth-2 predicted (2) ids, n_tokens * n_used int32
+ *     token-major
+ *   tmoe_trace_create/write_step/write_refresh/finish <- TraceWriter (trace.rs:120-200): the header
+ *     is given as JSON, checked and written back as serde_json writes it; ids outside
+ *     [0, n_expert) are an error and nothing of that record is written
+ * Errors: TMOE_E_INVALID, TMOE_E_NOTFOUND (no profile / no predictions); message:
+ * tmoe_trace_last_error() (per thread). */
+typedef struct tmoe_trace tmoe_trace;
+typedef struct tmoe_trace_writer tmoe_trace_writer;
+typedef struct {
+    uint32_t version, n_layer, n_expert, n_used, id_bytes, vram_slots, ram_slots, prefetch_depth, ubatch;
+    int32_t has_profile;
+} tmoe_trace_info;
+#define TMOE_TRACE_STEP 0
+#define TMOE_TRACE_REFRESH 1
+TMOE_API int tmoe_trace_open(const char *path, tmoe_trace **out);
+TMOE_API void tmoe_trace_close(tmoe_trace *t);
+TMOE_API const char *tmoe_trace_last_error(void);
+TMOE_API int tmoe_trace_header(const tmoe_trace *t, tmoe_trace_info *info);
+/* the header line as read; the string fields format, model, hot_source, prompt_hash */
+TMOE_API const char *tmoe_trace_header_json(const tmoe_trace *t);
+TMOE_API const char *tmoe_trace_header_str(const tmoe_trace *t, const char *field);
+TMOE_API int tmoe_trace_expert_bytes(const tmoe_trace *t, uint64_t *out);
+TMOE_API int tmoe_trace_profile(const tmoe_trace *t, int64_t *rows, int64_t *cols, uint64_t *out);
+TMOE_API int tmoe_trace_next(tmoe_trace *t, int32_t *kind, uint32_t *step, int32_t *layer, uint32_t *n_tokens,
+                             int32_t *flags);
+TMOE_API int tmoe_trace_ids(const tmoe_trace *t, int32_t which, int32_t *out);
+TMOE_API int tmoe_trace_create(const char *path, const char *header_json, tmoe_trace_writer **out);
+TMOE_API int tmoe_trace_write_step(tmoe_trace_writer *w, uint32_t step, int32_t layer, uint32_t n_tokens,
+                                   const int32_t *ids, const int32_t *predicted, const int32_t *predicted2);
+TMOE_API int tmoe_trace_write_refresh(tmoe_trace_writer *w, uint32_t step);
+TMOE_API int tmoe_trace_finish(tmoe_trace_writer *w);
+
 /* Per-kernel device timing of this handle's calls (the StepProfile phase timers of
  * crates/model/src/qwen3moe.rs:69-107, narrowed to the layer's kernels).  While enabled, every
  * kernel launch is bracketed by CUDA events on its stream; tmoe_profile_collect synchronises,

@@ -205,3 +205,45 @@ def test_streamed_steps_with_pinned_experts_follow_the_reference():
     finally:
         cache.close()
         layer.close()
+
+
+def test_replayed_routing_trace_routes_as_recorded(tmp_path):
+    """Recorded routing (a tetraeder-routing v1 trace) replayed through the streamed layer: the
+    logits of each recorded step make the layer's own top-k pick exactly the recorded ids, the
+    planner follows the reference's LRU over them, and the output matches the oracle."""
+    from tetraeder_b200.trace import LayerStep, TraceHeader, TraceReader, TraceWriter
+    H, I, E, k, NS, T = 512, 256, 16, 4, 6, 32
+    rng = np.random.default_rng(11)
+    gate, up, down = _weights(rng, H, I, E, O.TYPE_Q4_K, O.TYPE_Q4_K, True)
+    path = tmp_path / "routing.bin"
+    with TraceWriter(path, TraceHeader(2, E, k, vram_slots=NS, ram_slots=E)) as w:
+        for step in range(4):
+            for il in range(2):
+                lg = zipf_logits(rng, T, E)
+                w.layer_step(step, il, O.softmax_topk(lg, k)[0])
+            if step == 1:
+                w.hot_refresh(step)
+    with TraceReader(path) as r:
+        recorded = [s for s in r if isinstance(s, LayerStep) and s.layer == 1]
+    assert len(recorded) == 4
+    layer = tb.MoeLayer(H, I, E, k, gate_type=O.TYPE_Q4_K, up_type=O.TYPE_Q4_K, down_type=O.TYPE_Q4_K, max_tokens=T)
+    store = tb.ExpertWeights(pinned(gate), pinned(up), pinned(down))
+    slots = tb.ExpertWeights(*(torch.zeros((NS,) + a.shape[1:], dtype=torch.uint8, device="cuda")
+                               for a in (gate, up, down)))
+    cache = tb.SlotCache(layer, slots, store)
+    ref = S.LayerSlots(E, NS)
+    try:
+        for s in recorded:
+            x = rng.standard_normal((T, H)).astype(np.float32)
+            lg = s.logits(E)
+            ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+            out = layer.moe_ffn_streamed(cuda(x), cache, logits=cuda(lg), ids_out=ids)
+            layer.check()
+            assert np.array_equal(ids.cpu().numpy(), s.ids), f"step {s.step}: routing differs from the trace"
+            _check_plan(cache, ref, s.ids, S.step(ref, s.ids.reshape(-1)))
+            want_ids, want_w, _ = O.softmax_topk(lg, k)
+            want = O.experts(x, want_ids, want_w, gate, up, down, H, I, E, O.TYPE_Q4_K, O.TYPE_Q4_K, O.TYPE_Q4_K)
+            assert nrms(out.cpu().numpy(), want) < 1e-3
+    finally:
+        cache.close()
+        layer.close()

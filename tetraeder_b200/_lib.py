@@ -87,6 +87,20 @@ SIGNATURES = {
     "tmoe_gguf_type_size": ([I32, P, P], C.c_int),
     "tmoe_gguf_read": ([P, I64, C.c_uint64, C.c_uint64, P], C.c_int),
     "tmoe_gguf_load": ([P, I64, C.c_uint64, C.c_uint64, P, I32, P], C.c_int),
+    "tmoe_trace_open": ([C.c_char_p, C.POINTER(C.c_void_p)], C.c_int),
+    "tmoe_trace_close": ([P], None),
+    "tmoe_trace_last_error": ([], C.c_char_p),
+    "tmoe_trace_header": ([P, P], C.c_int),
+    "tmoe_trace_header_json": ([P], C.c_char_p),
+    "tmoe_trace_header_str": ([P, C.c_char_p], C.c_char_p),
+    "tmoe_trace_expert_bytes": ([P, P], C.c_int),
+    "tmoe_trace_profile": ([P, P, P, P], C.c_int),
+    "tmoe_trace_next": ([P, P, P, P, P, P], C.c_int),
+    "tmoe_trace_ids": ([P, I32, P], C.c_int),
+    "tmoe_trace_create": ([C.c_char_p, C.c_char_p, C.POINTER(C.c_void_p)], C.c_int),
+    "tmoe_trace_write_step": ([P, C.c_uint32, I32, C.c_uint32, P, P, P], C.c_int),
+    "tmoe_trace_write_refresh": ([P, C.c_uint32], C.c_int),
+    "tmoe_trace_finish": ([P], C.c_int),
 }
 COMM_ID_BYTES = 128
 PHASES = ["rms_norm", "router_logits", "topk", "map_ids", "dispatch", "quant_x", "gate_up", "quant_act",
