@@ -76,10 +76,12 @@ def parse():
     p.add_argument("--cpu-sample-s", type=float, default=15.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--sweep", action="store_true", help="also time T in {1,4,16,64}")
-    p.add_argument("--mode", choices=["decode", "prefill", "streamed", "gguf"], default="decode",
+    p.add_argument("--ctx", type=int, default=4096, help="model mode: the context each sequence decodes at")
+    p.add_argument("--mode", choices=["decode", "prefill", "streamed", "gguf", "model"], default="decode",
                    help="decode: C2 at T tokens (the metric's config); prefill: C2-shaped layer at T=8192 "
                         "(tensor roofline); streamed: config 5, skewed routing over 64 device slots of 128 experts; "
-                        "gguf: loading the expert tensors of a C2-shaped GGUF file into HBM")
+                        "gguf: loading the expert tensors of a C2-shaped GGUF file into HBM; model: config 3, the "
+                        "whole Qwen3-30B-A3B-shaped model decoding --tokens sequences at --ctx context")
     p.add_argument("--slots", type=int, default=64)
     p.add_argument("--routing", default=None,
                    help="streamed mode: replay the layer steps of this tetraeder-routing v1 trace instead of the "
@@ -94,7 +96,7 @@ def parse():
                         "allreduce = the reference's EP mode, the same tokens on every rank, outputs summed")
     a = p.parse_args()
     set_shape(a.shape)
-    if a.mode != "decode" and a.tokens == 64:
+    if a.mode in ("prefill", "streamed") and a.tokens == 64:
         a.tokens = 8192
     if a.mode == "prefill" and a.layers == 48:
         a.layers = 4
@@ -649,6 +651,90 @@ def run_gguf(args, local_rank):
     }
 
 
+def run_model(args, local_rank):
+    """Config 3: decode steps of the whole Qwen3-30B-A3B-shaped model (48 layers, 32 query / 4 KV
+    heads of 128, 128 experts top-8 of 768, vocabulary 151936), synthetic Q4_K_M-typed weights
+    (attention q/k/o and experts gate/up Q4_K, v and expert down Q6_K, token embedding Q4_K, output
+    Q6_K), B = --tokens sequences each at --ctx positions of context (the F16 KV caches filled with
+    random values up to there: the step's cost does not depend on them).  One step = one CUDA graph
+    replay: every sequence gets one token (the previous step's greedy token) at its next position."""
+    import torch
+
+    from tetraeder_b200.gguf import Hparams
+    from tetraeder_b200.model import Qwen3MoeModel
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    B, ctx = args.tokens, args.ctx
+    W = max(args.warmup, 3)
+    hp = Hparams(name="Qwen3-30B-A3B-shaped", n_layer=48, n_ctx_train=40960, n_embd=2048, n_head=32, n_head_kv=4,
+                 head_dim=128, n_rot=128, n_expert=128, n_expert_used=8, n_ff_exp=768, n_vocab=151936, rms_eps=1e-6,
+                 rope_freq_base=1e6, tied_output=False)
+    n_ctx = ctx + W + args.steps + 1
+    log(f"model: synthetic weights, B={B}, context {ctx}")
+    m = Qwen3MoeModel.synthetic(hp, max_batch=B, n_ctx=n_ctx, device=local_rank, seed=args.seed)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed + 3)
+    for c in m.kc + m.vc:
+        c[:, :ctx].normal_(0.0, 1.0, generator=gen)
+    tokens = torch.randint(0, hp.n_vocab, (B,), dtype=torch.int32, device=dev, generator=gen)
+    pos = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    m.decode(tokens, pos)
+    m.check()
+    g = m.graph(tokens, pos)
+
+    def step():
+        g.replay()
+        tokens.copy_(m.next_tokens[:B])
+        pos.add_(1)
+
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local_rank) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    m.check()
+    # bytes a step must read: every weight it touches (all experts at this B: about 126 of 128 per
+    # layer for B >= 64, fewer below; counted from the expected distinct experts), the KV caches up
+    # to the positions, the output matrix
+    exp_d = hp.n_expert * (1 - (1 - hp.n_expert_used / hp.n_expert) ** B)
+    w = m.w
+    attn = sum(w[f"blk.0.{n}.weight"].data.numel() for n in ("attn_q", "attn_k", "attn_v", "attn_output"))
+    expert = sum(w[f"blk.0.{n}.weight"].data.numel() for n in ("ffn_gate_exps", "ffn_up_exps", "ffn_down_exps"))
+    expert //= hp.n_expert
+    kv = B * (ctx + W + args.steps // 2) * hp.n_head_kv * hp.head_dim * 2 * 2
+    per_layer = attn + exp_d * expert + hp.n_expert * hp.n_embd * 4 + kv
+    step_bytes = hp.n_layer * per_layer + w["output.weight"].data.numel()
+    peaks = load_peaks()
+    achieved = step_bytes / (ms / 1e3) / 1e9
+    g = None
+    m.close()
+    return {
+        "metric": "decode_tokens_per_s", "value": round(B / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": W, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "Q4_K/Q6_K weights x Q8_K activations (integer MMA), f32 attention over an F16 "
+                                  "KV cache", "data": "synthetic",
+        "config": {"workload": "C3 Qwen3-30B-A3B-shaped model, batched decode", "sequences": B, "context": ctx,
+                   "n_layer": hp.n_layer, "n_embd": hp.n_embd, "n_head": hp.n_head, "n_head_kv": hp.n_head_kv,
+                   "head_dim": hp.head_dim, "n_expert": hp.n_expert, "n_expert_used": hp.n_expert_used,
+                   "n_ff_exp": hp.n_ff_exp, "n_vocab": hp.n_vocab, "types": "Q4_K_M-like (attn q/k/o, experts gate/up, "
+                   "token_embd Q4_K; attn v, experts down, output Q6_K)", "seed": args.seed,
+                   "l2": "inputs larger than L2: every step reads all weights and the KV caches"},
+        "roofline": {"bound": "hbm", "kernel": "the whole decode step", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": peaks["source"], "traffic": None,
+                     "algorithmic_bytes_per_step": int(step_bytes),
+                     "note": "weights touched (expected distinct experts) + KV caches + output matrix"},
+        "gpu_launches": None, "clocks": clk.summary(),
+    }
+
+
 def sweep_tokens(torch, tb, layers, dev):
     """tokens/s and layer roofline fraction at T in {1, 4, 16, 64} (graph of 48 layer calls)."""
     peaks = load_peaks()
@@ -812,10 +898,10 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
-    if args.mode == "gguf":
+    if args.mode in ("gguf", "model"):
         if world > 1:
-            raise SystemExit("--mode gguf runs on one GPU")
-        emit(run_gguf(args, local_rank))
+            raise SystemExit(f"--mode {args.mode} runs on one GPU")
+        emit(run_gguf(args, local_rank) if args.mode == "gguf" else run_model(args, local_rank))
         return 0
     res = run_streamed(args, local_rank) if args.mode == "streamed" else run_ours(args, rank, world, local_rank)
     if rank == 0:

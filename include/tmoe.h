@@ -255,6 +255,44 @@ TMOE_API int tmoe_quantize(int32_t type, const float *x, int64_t nrows, int64_t 
 /* quant::to_f32 (crates/ggml-sys/src/quant.rs:19) for Q4_K / Q6_K: n values (n % 256 == 0). */
 TMOE_API int tmoe_dequantize(int32_t type, const void *in, int64_t n, float *out, void *stream);
 
+/* The decode step around the MoE layer (config 3: the full Qwen3-MoE model, attention() of
+ * crates/model/src/attn.rs:246-405 and build_step of qwen3moe.rs:2777-2870), as stream-ordered
+ * ops on a handle (its error flag and SM count); the projections are tmoe_mul_mat_id with one
+ * expert.  Device pointers throughout.
+ *   tmoe_get_rows    <- Context::get_rows (context.rs:231): out[i] = row rows[i] of W as f32 (ggml
+ *                       type 0 F32, 1 F16, 12 Q4_K, 14 Q6_K; rows nb1 apart); a row outside
+ *                       [0, n_rows_w) gives zeros and latches the device error (tmoe_check)
+ *   tmoe_rms_norm    <- rms_norm (:274) times w (NULL: none), over `rows` rows of n
+ *   tmoe_rope_neox   <- rope_ext (:343) in NeoX mode, in place on x [n_tok][n_head][head_dim],
+ *                       token t at position pos[t], the first n_rot dims rotated
+ *   tmoe_attn_decode <- set_rows (:238) of the new K/V rows into F16 caches [B][n_ctx][n_kv]
+ *                       [head_dim] at pos[b], then flash_attn_ext (:368) of one query per sequence
+ *                       over its positions 0..pos[b]: q [B][n_head][head_dim] (n_head a multiple
+ *                       of n_kv, at most 8 query heads per KV head; head_dim 64 or 128), k/v
+ *                       [B][n_kv][head_dim], out [B][n_head][head_dim]; scratch of
+ *                       tmoe_attn_decode_scratch_bytes
+ *   tmoe_add         <- add (:243);  tmoe_argmax: the first index of each row's maximum */
+/* Context::mul_mat (context.rs) of one Q4_K/Q6_K matrix W [N rows of K] and x f32 [T][K] ->
+ * out [T][N], on the decode GEMV.  reuse_x != 0: x is the activations of the previous
+ * tmoe_mul_mat call on this handle with the same K, T and weight family (Q4_K or Q6_K), whose Q8_K
+ * rows are reused (the Q, K and V projections of one normalised input).  The workspace is sized on
+ * first use: make a first call outside a stream capture. */
+TMOE_API int tmoe_mul_mat(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1, int64_t K, int64_t N,
+                          const float *x, int64_t T, int32_t reuse_x, float *out);
+TMOE_API int tmoe_get_rows(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1, int64_t K,
+                           int64_t n_rows_w, const int32_t *rows, int64_t n, float *out);
+TMOE_API int tmoe_rms_norm(tmoe_handle *h, void *stream, const float *x, const float *w, float eps, int64_t rows,
+                           int64_t n, float *out);
+TMOE_API int tmoe_rope_neox(tmoe_handle *h, void *stream, float *x, const int32_t *pos, int64_t n_tok, int32_t n_head,
+                            int32_t head_dim, int32_t n_rot, float freq_base);
+TMOE_API int64_t tmoe_attn_decode_scratch_bytes(tmoe_handle *h, int32_t B, int32_t n_head, int32_t n_kv,
+                                                int32_t head_dim, int32_t n_ctx);
+TMOE_API int tmoe_attn_decode(tmoe_handle *h, void *stream, const float *q, const float *k, const float *v,
+                              void *k_cache, void *v_cache, const int32_t *pos, int32_t B, int32_t n_head,
+                              int32_t n_kv, int32_t head_dim, int32_t n_ctx, float scale, void *scratch, float *out);
+TMOE_API int tmoe_add(tmoe_handle *h, void *stream, const float *a, const float *b, float *out, int64_t n);
+TMOE_API int tmoe_argmax(tmoe_handle *h, void *stream, const float *x, int64_t rows, int64_t n, int32_t *out);
+
 /* GGUF model files (crates/model/src/gguf.rs; the loader of load_weights, qwen3moe.rs:2498-2584).
  *   tmoe_gguf_open        <- Gguf::open (gguf.rs:236-296): the header, metadata and tensor index of a
  *                            file, or of every shard of a split model opened from its first shard

@@ -24,7 +24,7 @@ def _expert_bytes(rng, qtype, E, rows, cols, quantise):
 
 def write_moe_gguf(path, *, n_layer=2, n_embd=256, n_head=4, n_head_kv=2, head_dim=64, n_expert=4, n_used=2,
                    n_ff=256, n_vocab=300, gate_type=12, down_type=14, seed=7, quantise=True, tied=False,
-                   split_max_tensors=0, extra_kv=True):
+                   split_max_tensors=0, extra_kv=True, attn_types=(1, 1, 1, 1), embd_type=1, out_type=1):
     """Writes the file(s) and returns {tensor name: (ggml type, numpy data as written)}."""
     import gguf
     rng = np.random.default_rng(seed)
@@ -72,20 +72,29 @@ def write_moe_gguf(path, *, n_layer=2, n_embd=256, n_head=4, n_head_kv=2, head_d
     def f16(*shape, std=0.1):
         return (rng.standard_normal(shape) * std).astype(np.float16)
 
+    def matrix(name, qtype, rows, cols, std=0.1):
+        """F16, or Q4_K/Q6_K bytes of N(0, std) values (the oracle's quantiser)."""
+        if qtype in QUANT_BYTES:
+            import oracle as O
+            w_ = (rng.standard_normal((rows, cols)) * std).astype(np.float32)
+            add(name, np.ascontiguousarray(O.quantize(qtype, w_)).reshape(rows, -1), qt(qtype))
+        else:
+            add(name, f16(rows, cols, std=std))
+
     def f32(*shape):
         return (1.0 + 0.1 * rng.standard_normal(shape)).astype(np.float32)
 
-    add("token_embd.weight", f16(n_vocab, n_embd))
+    matrix("token_embd.weight", embd_type, n_vocab, n_embd, std=0.5)
     add("output_norm.weight", f32(n_embd))
     if not tied:
-        add("output.weight", f16(n_vocab, n_embd))
+        matrix("output.weight", out_type, n_vocab, n_embd)
     for il in range(n_layer):
         p = f"blk.{il}."
         add(p + "attn_norm.weight", f32(n_embd))
-        add(p + "attn_q.weight", f16(n_head * head_dim, n_embd))
-        add(p + "attn_k.weight", f16(n_head_kv * head_dim, n_embd))
-        add(p + "attn_v.weight", f16(n_head_kv * head_dim, n_embd))
-        add(p + "attn_output.weight", f16(n_embd, n_head * head_dim))
+        matrix(p + "attn_q.weight", attn_types[0], n_head * head_dim, n_embd)
+        matrix(p + "attn_k.weight", attn_types[1], n_head_kv * head_dim, n_embd)
+        matrix(p + "attn_v.weight", attn_types[2], n_head_kv * head_dim, n_embd)
+        matrix(p + "attn_output.weight", attn_types[3], n_embd, n_head * head_dim)
         add(p + "attn_q_norm.weight", f32(head_dim))
         add(p + "attn_k_norm.weight", f32(head_dim))
         add(p + "ffn_norm.weight", f32(n_embd))

@@ -1,0 +1,161 @@
+"""The decode step of the whole Qwen3-MoE model (tetraeder_b200.model) against the CPU oracle of the
+same step (oracle/model.py), on a tiny qwen3moe GGUF written by gguf-py with Q4_K/Q6_K matrices:
+several sequences decoded over several positions (the F16 KV cache grows step by step), eager and
+replayed from a CUDA graph; plus the attention op alone against a float64 softmax over a random
+cache, at both head sizes and with a long context (many splits)."""
+import numpy as np
+import pytest
+import torch
+
+gguf = pytest.importorskip("gguf")
+
+import oracle as O  # noqa: E402
+from oracle.model import Matrix, ModelOracle  # noqa: E402
+import tetraeder_b200 as tb  # noqa: E402
+from tests.common import nrms  # noqa: E402
+from tests.gguf_fixture import write_moe_gguf  # noqa: E402
+from tetraeder_b200.gguf import GgufFile  # noqa: E402
+from tetraeder_b200.model import Qwen3MoeModel  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _oracle_weights(written, hp):
+    w = {}
+    for name, (t, arr) in written.items():
+        if t == O.TYPE_F32 and (arr.ndim == 1 or name.endswith("ffn_gate_inp.weight")):
+            w[name] = arr
+        elif name.endswith("_exps.weight"):
+            w[name] = Matrix(t, arr, arr.shape[0] * arr.shape[1], 0)
+        else:
+            rows = arr.shape[0]
+            cols = arr.shape[1] if t in (O.TYPE_F16, O.TYPE_F32) else hp.n_embd if not name.endswith(
+                "attn_output.weight") else hp.n_head * hp.head_dim
+            w[name] = Matrix(t, arr, rows, cols)
+    return w
+
+
+@pytest.fixture(scope="module")
+def tiny_model(tmp_path_factory):
+    p = tmp_path_factory.mktemp("model") / "tiny-qwen3moe.gguf"
+    written = write_moe_gguf(p, n_layer=2, n_embd=512, n_head=4, n_head_kv=2, head_dim=128, n_expert=8, n_used=2,
+                             n_ff=256, n_vocab=512, gate_type=12, down_type=14, attn_types=(12, 12, 14, 12),
+                             embd_type=12, out_type=14, extra_kv=False)
+    return p, written
+
+
+def test_decode_steps_match_the_oracle(tiny_model):
+    path, written = tiny_model
+    B, steps, n_ctx = 3, 6, 64
+    with GgufFile(path) as f:
+        hp = f.hparams
+        model = Qwen3MoeModel.from_gguf(f, max_batch=B, n_ctx=n_ctx)
+    ref = ModelOracle(hp, _oracle_weights(written, hp), B, n_ctx)
+    rng = np.random.default_rng(5)
+    start = np.array([0, 3, 17], dtype=np.int32)  # sequences at different lengths
+    try:
+        for s in range(steps):
+            toks = rng.integers(0, hp.n_vocab, B).astype(np.int32)
+            pos = (start + s).astype(np.int32)
+            got = model.decode(torch.from_numpy(toks).cuda(), torch.from_numpy(pos).cuda()).cpu().numpy()
+            model.check()
+            want = ref.decode(toks, pos)  # positions never written read as zeros on both sides
+            n = nrms(got, want)
+            assert n < 1e-2, f"step {s}: logits nrms {n:.2e}"
+        nt = model.next_tokens.cpu().numpy()
+        assert np.array_equal(nt, np.argmax(got, axis=1)), "argmax"
+    finally:
+        model.close()
+
+
+def test_graph_replay_matches_eager(tiny_model):
+    path, _ = tiny_model
+    B, n_ctx = 2, 32
+    with GgufFile(path) as f:
+        a = Qwen3MoeModel.from_gguf(f, max_batch=B, n_ctx=n_ctx)
+        b = Qwen3MoeModel.from_gguf(f, max_batch=B, n_ctx=n_ctx)
+    toks = torch.tensor([5, 9], dtype=torch.int32, device="cuda")
+    pos = torch.tensor([0, 0], dtype=torch.int32, device="cuda")
+    try:
+        b.decode(toks, pos)  # sizes the projections' workspace, fills position 0
+        a.decode(toks, pos)
+        torch.cuda.synchronize()
+        g = b.graph(toks, pos)
+        for step in range(1, 4):
+            toks.copy_(torch.tensor([step * 7 % 512, step * 11 % 512], dtype=torch.int32))
+            pos.fill_(step)
+            want = a.decode(toks, pos).clone()
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(b.logits[:B], want), f"step {step}"
+        b.check()
+        del g
+    finally:
+        a.close()
+        b.close()
+
+
+@pytest.mark.parametrize("hd,nh,nkv,ctx", [(128, 32, 4, 4096), (64, 4, 2, 100), (128, 8, 8, 1)])
+def test_attention_op_against_float64(hd, nh, nkv, ctx):
+    B = 3
+    layer = tb.MoeLayer(512, 256, 8, 2, gate_type=12, up_type=12, down_type=12, max_tokens=4)
+    lib, h = layer.lib, layer.h
+    rng = np.random.default_rng(hd + nh)
+    kc = (rng.standard_normal((B, ctx, nkv, hd)) * 0.5).astype(np.float16)
+    vc = rng.standard_normal((B, ctx, nkv, hd)).astype(np.float16)
+    q = rng.standard_normal((B, nh, hd)).astype(np.float32)
+    k = rng.standard_normal((B, nkv, hd)).astype(np.float32)
+    v = rng.standard_normal((B, nkv, hd)).astype(np.float32)
+    pos = np.array([ctx - 1, ctx // 2, 0], dtype=np.int32)
+    d_kc, d_vc = torch.from_numpy(kc).cuda(), torch.from_numpy(vc).cuda()
+    out = torch.empty((B, nh, hd), device="cuda")
+    nbytes = lib.tmoe_attn_decode_scratch_bytes(h, B, nh, nkv, hd, ctx)
+    scratch = torch.empty(nbytes // 4 + 1, device="cuda")
+    import ctypes as C
+    dq, dk, dv, dp = (torch.from_numpy(a).cuda() for a in (q, k, v, pos))
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    scale = 1.0 / np.sqrt(hd)
+    assert lib.tmoe_attn_decode(h, None, P(dq), P(dk), P(dv), P(d_kc), P(d_vc), P(dp), B, nh, nkv, hd, ctx, scale,
+                                P(scratch), P(out)) == 0
+    layer.check()
+    got = out.cpu().numpy()
+    G = nh // nkv
+    for b in range(B):
+        kc[b, pos[b]] = k[b].astype(np.float16)
+        vc[b, pos[b]] = v[b].astype(np.float16)
+        K, V = kc[b, :pos[b] + 1].astype(np.float64), vc[b, :pos[b] + 1].astype(np.float64)
+        for hh in range(nh):
+            s = K[:, hh // G] @ q[b, hh].astype(np.float64) * scale
+            e = np.exp(s - s.max())
+            want = e @ V[:, hh // G] / e.sum()
+            assert np.abs(got[b, hh] - want).max() < 2e-3 * max(1.0, np.abs(want).max()), (b, hh)
+    # the new rows landed in the caches
+    assert np.array_equal(d_kc.cpu().numpy()[np.arange(B), pos], k.astype(np.float16))
+    layer.close()
+
+
+@pytest.mark.parametrize("qtype,K,N,T", [(12, 2048, 4096, 64), (14, 2048, 512, 3), (12, 512, 151936 // 64 * 16, 5)])
+def test_mul_mat_against_the_oracle(qtype, K, N, T):
+    """tmoe_mul_mat (one matrix, every row of x) against the oracle's mul_mat_id with one expert, and
+    reuse_x: a second matrix of the same family over the same x, and the guard on a mismatch."""
+    import ctypes as C
+    rng = np.random.default_rng(K + N + T)
+    W = np.ascontiguousarray(O.quantize(qtype, (rng.standard_normal((N, K)) * 0.05).astype(np.float32)))
+    W2 = np.ascontiguousarray(O.quantize(qtype, (rng.standard_normal((16, K)) * 0.05).astype(np.float32)))
+    x = rng.standard_normal((T, K)).astype(np.float32)
+    layer = tb.MoeLayer(512, 256, 8, 2, gate_type=12, up_type=12, down_type=12, max_tokens=4)
+    lib, h = layer.lib, layer.h
+    dW, dW2, dx = (torch.from_numpy(a).cuda() for a in (W, W2, x))
+    out, out2 = torch.empty((T, N), device="cuda"), torch.empty((T, 16), device="cuda")
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    nb1 = W.shape[1] if W.ndim == 2 else W.shape[-1]
+    assert lib.tmoe_mul_mat(h, None, qtype, P(dW), nb1, K, N, P(dx), T, 0, P(out)) == 0
+    assert lib.tmoe_mul_mat(h, None, qtype, P(dW2), nb1, K, 16, P(dx), T, 1, P(out2)) == 0
+    other = 14 if qtype == 12 else 12
+    assert lib.tmoe_mul_mat(h, None, other, P(dW2), nb1, K, 16, P(dx), T, 1, P(out2)) != 0  # another family
+    layer.check()
+    for w_, o_, n_ in ((W, out, N), (W2, out2, 16)):
+        want = O.mul_mat_id(qtype, w_.reshape(1, n_, -1), K, n_, 1, x[:, None, :], np.zeros((T, 1), np.int32))[:, 0]
+        got = o_.cpu().numpy()
+        assert np.abs(got - want).max() <= 1e-4 * max(1.0, np.abs(want).max())
+    layer.close()

@@ -87,6 +87,14 @@ SIGNATURES = {
     "tmoe_gguf_type_size": ([I32, P, P], C.c_int),
     "tmoe_gguf_read": ([P, I64, C.c_uint64, C.c_uint64, P], C.c_int),
     "tmoe_gguf_load": ([P, I64, C.c_uint64, C.c_uint64, P, I32, P], C.c_int),
+    "tmoe_mul_mat": ([P, P, I32, P, C.c_size_t, I64, I64, P, I64, I32, P], C.c_int),
+    "tmoe_get_rows": ([P, P, I32, P, C.c_size_t, I64, I64, P, I64, P], C.c_int),
+    "tmoe_rms_norm": ([P, P, P, P, C.c_float, I64, I64, P], C.c_int),
+    "tmoe_rope_neox": ([P, P, P, P, I64, I32, I32, I32, C.c_float], C.c_int),
+    "tmoe_attn_decode_scratch_bytes": ([P, I32, I32, I32, I32, I32], I64),
+    "tmoe_attn_decode": ([P, P, P, P, P, P, P, P, I32, I32, I32, I32, I32, C.c_float, P, P], C.c_int),
+    "tmoe_add": ([P, P, P, P, P, I64], C.c_int),
+    "tmoe_argmax": ([P, P, P, I64, I64, P], C.c_int),
     "tmoe_trace_open": ([C.c_char_p, C.POINTER(C.c_void_p)], C.c_int),
     "tmoe_trace_close": ([P], None),
     "tmoe_trace_last_error": ([], C.c_char_p),

@@ -92,6 +92,22 @@ cudaError_t launch_combine(const float *dout, const int32_t *ids, const float *w
 // quant.cu
 cudaError_t launch_quantize(int wt, const float *x, int64_t nblocks, uint8_t *out, cudaStream_t st);
 cudaError_t launch_dequantize(int wt, const uint8_t *in, int64_t n, float *out, cudaStream_t st);
+// out[i][:K] = row rows[i] of W (ggml type 0 F32, 1 F16, 12 Q4_K, 14 Q6_K; n_rows_w rows nb1 apart);
+// a row outside [0, n_rows_w) gives zeros and latches TMOE_DEV_ERR_BADID in err.
+cudaError_t launch_get_rows(int32_t type, const uint8_t *W, size_t nb1, int K, int64_t n_rows_w, const int32_t *rows,
+                            int64_t n, float *out, int *err, cudaStream_t st);
+// model.cu: the decode step around the MoE layer
+cudaError_t launch_rope_neox(float *x, const int32_t *pos, int64_t n_tok, int n_head, int head_dim, int n_rot,
+                             float freq_base, cudaStream_t st);
+int attn_splits(int B, int n_kv, int n_ctx, int sm_count);
+size_t attn_scratch_floats(int B, int n_head, int head_dim, int n_kv, int n_ctx, int sm_count);
+cudaError_t launch_attn_decode(const float *q, const float *k, const float *v, __half *kc, __half *vc,
+                               const int32_t *pos, int B, int n_head, int n_kv, int head_dim, int n_ctx, float scale,
+                               float *part, float *out, int sm_count, int *err, cudaStream_t st);
+cudaError_t launch_add(const float *a, const float *b, float *out, int64_t n, cudaStream_t st);
+cudaError_t launch_dense_prep(int T, int4 *active, int32_t *n_active, int32_t *perm, int *counters, int n_counters,
+                              cudaStream_t st);
+cudaError_t launch_argmax(const float *x, int64_t rows, int64_t n, int32_t *out, cudaStream_t st);
 
 // gemv.cu
 struct GemvArgs {

@@ -113,15 +113,9 @@ __global__ void quantize_q6k_kernel(const float *__restrict__ x, int64_t nblocks
     }
 }
 
-// One thread per 32 outputs (one Q4_K sub-block or two Q6_K sub-blocks).
-__global__ void dequantize_kernel(int wt, const uint8_t *__restrict__ in, int64_t n, float *__restrict__ out) {
-    int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (g * 32 >= n) return;
-    int64_t b = g / 8;
-    int c = (int)(g % 8);  // 32-element chunk in the super-block
-    float *o = out + g * 32;
+// Elements 32c .. 32c+31 of the super-block at `blk` (one Q4_K sub-block or two Q6_K sub-blocks).
+__device__ void dequant32(int wt, const uint8_t *__restrict__ blk, int c, float *__restrict__ o) {
     if (wt == TMOE_WT_Q4K) {
-        const uint8_t *blk = in + b * TMOE_Q4K_BYTES;
         float d = h2f((uint16_t)(blk[0] | (blk[1] << 8))), dmin = h2f((uint16_t)(blk[2] | (blk[3] << 8)));
         const uint8_t *sc = blk + 4;
         int s = c, scale, mn;
@@ -139,7 +133,6 @@ __global__ void dequantize_kernel(int wt, const uint8_t *__restrict__ in, int64_
             o[l] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
         }
     } else {
-        const uint8_t *blk = in + b * TMOE_Q6K_BYTES;
         const uint8_t *ql = blk, *qh = blk + 128;
         const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192);
         float d = h2f((uint16_t)(blk[208] | (blk[209] << 8)));
@@ -152,6 +145,39 @@ __global__ void dequantize_kernel(int wt, const uint8_t *__restrict__ in, int64_
     }
 }
 
+// One thread per 32 outputs.
+__global__ void dequantize_kernel(int wt, const uint8_t *__restrict__ in, int64_t n, float *__restrict__ out) {
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (g * 32 >= n) return;
+    const int64_t b = g / 8;
+    const uint8_t *blk = in + b * (wt == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES);
+    dequant32(wt, blk, (int)(g % 8), out + g * 32);
+}
+
+// get_rows: out[i][:] = row rows[i] of W (F32, F16, Q4_K or Q6_K rows of K elements, nb1 bytes
+// apart).  One CTA per output row.
+__global__ void get_rows_kernel(int32_t type, const uint8_t *__restrict__ W, size_t nb1, int K, int64_t n_rows_w,
+                                const int32_t *__restrict__ rows, float *__restrict__ out, int *err) {
+    const int64_t i = blockIdx.x;
+    const int32_t r = rows[i];
+    float *o = out + i * K;
+    if (r < 0 || r >= n_rows_w) {  // an out-of-range row: zeros and the error flag
+        for (int c = threadIdx.x; c < K; c += blockDim.x) o[c] = 0.0f;
+        if (threadIdx.x == 0 && err) atomicCAS(err, 0, TMOE_DEV_ERR_BADID);
+        return;
+    }
+    const uint8_t *row = W + (size_t)r * nb1;
+    if (type == 0) {
+        for (int c = threadIdx.x; c < K; c += blockDim.x) o[c] = reinterpret_cast<const float *>(row)[c];
+    } else if (type == 1) {
+        for (int c = threadIdx.x; c < K; c += blockDim.x) o[c] = h2f(reinterpret_cast<const uint16_t *>(row)[c]);
+    } else {
+        const int wt = type == 12 ? TMOE_WT_Q4K : TMOE_WT_Q6K;
+        const int bb = wt == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES;
+        for (int g = threadIdx.x; g < K / 32; g += blockDim.x) dequant32(wt, row + (size_t)(g / 8) * bb, g % 8, o + g * 32);
+    }
+}
+
 cudaError_t launch_quantize(int wt, const float *x, int64_t nblocks, uint8_t *out, cudaStream_t st) {
     if (nblocks <= 0) return cudaSuccess;
     unsigned grid = (unsigned)((nblocks + 127) / 128);
@@ -159,6 +185,14 @@ cudaError_t launch_quantize(int wt, const float *x, int64_t nblocks, uint8_t *ou
         quantize_q4k_kernel<<<grid, 128, 0, st>>>(x, nblocks, out);
     else
         quantize_q6k_kernel<<<grid, 128, 0, st>>>(x, nblocks, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_get_rows(int32_t type, const uint8_t *W, size_t nb1, int K, int64_t n_rows_w, const int32_t *rows,
+                            int64_t n, float *out, int *err, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    if (n > 0x7fffffff) return cudaErrorInvalidValue;
+    get_rows_kernel<<<(unsigned)n, 128, 0, st>>>(type, W, nb1, K, n_rows_w, rows, out, err);
     return cudaGetLastError();
 }
 

@@ -34,6 +34,12 @@ struct tmoe_handle {
     int sm_count = 0;
     void *ws = nullptr;
     size_t ws_bytes = 0;
+    // tmoe_mul_mat: its workspace, and which activations its Q8_K rows hold (for reuse_x)
+    void *dense_ws = nullptr;
+    size_t dense_ws_bytes = 0;
+    const float *dense_x = nullptr;
+    int dense_wt = -1;
+    int64_t dense_k = 0, dense_t = 0;
     // routing
     float *logits = nullptr;
     int32_t *ids = nullptr;
@@ -421,6 +427,7 @@ void tmoe_destroy(tmoe_handle *h) {
     DeviceGuard dg(h->cfg.device);
     if (h->ws) cudaFree(h->ws);
     if (h->op_ws) cudaFree(h->op_ws);
+    if (h->dense_ws) cudaFree(h->dense_ws);
     if (h->a2a.mem) cudaFree(h->a2a.mem);
     for (auto &ev : h->prof.ev)
         if (ev) cudaEventDestroy(ev);
@@ -789,6 +796,73 @@ int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, s
     return TMOE_OK;
 }
 
+int tmoe_mul_mat(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1, int64_t K, int64_t N,
+                 const float *x, int64_t T, int32_t reuse_x, float *out) {
+    if (!h) return TMOE_E_INVALID;
+    if (!is_kquant(type)) return fail(h, TMOE_E_UNSUPPORTED, "mul_mat type %d (need Q4_K or Q6_K)", type);
+    if (K <= 0 || K % 256 || N <= 0 || T < 0 || T > (1 << 24)) return fail(h, TMOE_E_INVALID, "bad mul_mat shape");
+    if (T == 0) return TMOE_OK;
+    if (!W || !x || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    if (!aligned16(x)) return fail(h, TMOE_E_INVALID, "x must be 16-byte aligned");
+    const int wt = wt_of(type);
+    if (nb1 != row_size(type, K)) return fail(h, TMOE_E_UNSUPPORTED, "rows must be contiguous (nb1 == row size)");
+    if ((uintptr_t)W & 15u) return fail(h, TMOE_E_INVALID, "W must be 16-byte aligned");
+    if (!tmoe::gemv_rows_per_item(wt, (int)K, (int)N))
+        return fail(h, TMOE_E_UNSUPPORTED, "N=%lld rows fit no GEMV row tile (multiples of 16)", (long long)N);
+    const bool reuse = reuse_x != 0;
+    if (reuse && (h->dense_x != x || h->dense_wt != wt || h->dense_k != K || h->dense_t != T))
+        return fail(h, TMOE_E_INVALID, "reuse_x: the last quantised activations are not these (x, K, T, weight family)");
+    DeviceGuard dg(h->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    size_t need = 0;
+    auto lay = [&](size_t bytes) {
+        size_t o = need;
+        need = align_up(need + bytes, 256);
+        return o;
+    };
+    const size_t nbw = (size_t)tmoe::q8_nbw(wt);
+    const size_t o_q = lay((size_t)T * K), o_d = lay((size_t)T * (K / 256) * 4);
+    const size_t o_bl = lay((size_t)T * (K / 256) * nbw * 4), o_bh = lay((size_t)T * (K / 256) * nbw * 4);
+    const size_t o_act = lay(16), o_na = lay(4), o_perm = lay((size_t)T * 4 + 16), o_work = lay(kCounters * 4);
+    cudaError_t e;
+    if (need > h->dense_ws_bytes) {  // grows on first use (outside any stream capture)
+        if (reuse) return fail(h, TMOE_E_INVALID, "reuse_x before the workspace exists");
+        if (h->dense_ws) {
+            cudaStreamSynchronize(st);
+            cudaFree(h->dense_ws);
+            h->dense_ws = nullptr;
+            h->dense_ws_bytes = 0;
+        }
+        if ((e = cudaMalloc(&h->dense_ws, need)) != cudaSuccess)
+            return fail(h, TMOE_E_NOMEM, "cudaMalloc(%zu): %s", need, cudaGetErrorString(e));
+        h->dense_ws_bytes = need;
+    }
+    char *base = (char *)h->dense_ws;
+    int8_t *q = (int8_t *)(base + o_q);
+    float *d = (float *)(base + o_d);
+    uint32_t *bl = (uint32_t *)(base + o_bl), *bh = (uint32_t *)(base + o_bh);
+    int4 *act = (int4 *)(base + o_act);
+    int32_t *na = (int32_t *)(base + o_na), *perm = (int32_t *)(base + o_perm);
+    int *work = (int *)(base + o_work);
+    if (!reuse) {
+        if ((e = tmoe::launch_quantize_q8k(x, T, (int)K, nullptr, tmoe::Q8Rows{q, d, bl, bh, wt}, st)) != cudaSuccess)
+            return cuda_fail(h, e, "quantize x");
+        h->dense_x = x, h->dense_wt = wt, h->dense_k = K, h->dense_t = T;
+    }
+    if ((e = tmoe::launch_dense_prep((int)T, act, na, perm, work, kCounters, st)) != cudaSuccess)
+        return cuda_fail(h, e, "mul_mat prep");
+    tmoe::GemvArgs g{};
+    g.w0 = (const uint8_t *)W;
+    g.nb1_0 = nb1, g.nb2_0 = align_up(nb1 * (size_t)N, 16);
+    g.K = (int)K, g.N = (int)N;
+    g.xq = q, g.xd = d, g.xbl = bl, g.xbh = bh, g.x_div = 1;
+    g.perm = perm, g.active = act, g.n_active = na;
+    g.n_slots = 1, g.max_active = 1, g.n_pairs = (int)T, g.work = work;
+    g.out = out, g.err = h->err;
+    if ((e = tmoe::launch_gemv(wt, false, g, 1, h->sm_count, st)) != cudaSuccess) return cuda_fail(h, e, "mul_mat gemv");
+    return TMOE_OK;
+}
+
 }  // extern "C"
 
 namespace {
@@ -920,6 +994,89 @@ int tmoe_dequantize(int32_t type, const void *in, int64_t n, float *out, void *s
     cudaError_t e = tmoe::launch_dequantize(wt_of(type), (const uint8_t *)in, n, out, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(nullptr, e, "dequantize");
     return TMOE_OK;
+}
+
+// ---------------------------------------------------------------- the decode step's other ops
+int tmoe_get_rows(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1, int64_t K, int64_t n_rows_w,
+                  const int32_t *rows, int64_t n, float *out) {
+    if (!h) return TMOE_E_INVALID;
+    if (type != 0 && type != 1 && !is_kquant(type)) return fail(h, TMOE_E_UNSUPPORTED, "get_rows type %d", type);
+    if (K <= 0 || K > (1 << 30) || (is_kquant(type) && K % 256) || n < 0 || n_rows_w <= 0)
+        return fail(h, TMOE_E_INVALID, "bad get_rows shape");
+    const size_t rb = type == 0 ? (size_t)K * 4 : type == 1 ? (size_t)K * 2 : row_size(type, K);
+    if (nb1 < rb) return fail(h, TMOE_E_INVALID, "row stride %zu below the row size %zu", nb1, rb);
+    if (n == 0) return TMOE_OK;
+    if (!W || !rows || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    DeviceGuard dg(h->cfg.device);
+    cudaError_t e = tmoe::launch_get_rows(type, (const uint8_t *)W, nb1, (int)K, n_rows_w, rows, n, out, h->err,
+                                          (cudaStream_t)stream);
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "get_rows");
+}
+
+int tmoe_rms_norm(tmoe_handle *h, void *stream, const float *x, const float *w, float eps, int64_t rows, int64_t n,
+                  float *out) {
+    if (!h) return TMOE_E_INVALID;
+    if (rows < 0 || n <= 0 || n > (1 << 30)) return fail(h, TMOE_E_INVALID, "bad rms_norm shape");
+    if (rows == 0) return TMOE_OK;
+    if (!x || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    DeviceGuard dg(h->cfg.device);
+    cudaError_t e = tmoe::launch_rms_norm(x, w, eps, rows, (int)n, out, (cudaStream_t)stream);
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "rms_norm");
+}
+
+int tmoe_rope_neox(tmoe_handle *h, void *stream, float *x, const int32_t *pos, int64_t n_tok, int32_t n_head,
+                   int32_t head_dim, int32_t n_rot, float freq_base) {
+    if (!h) return TMOE_E_INVALID;
+    if (n_tok < 0 || n_head <= 0 || head_dim <= 0 || n_rot <= 0 || n_rot > head_dim || n_rot % 2 || freq_base <= 0)
+        return fail(h, TMOE_E_INVALID, "bad rope shape");
+    if (n_tok == 0) return TMOE_OK;
+    if (!x || !pos) return fail(h, TMOE_E_INVALID, "null tensor");
+    DeviceGuard dg(h->cfg.device);
+    cudaError_t e = tmoe::launch_rope_neox(x, pos, n_tok, n_head, head_dim, n_rot, freq_base, (cudaStream_t)stream);
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "rope");
+}
+
+int64_t tmoe_attn_decode_scratch_bytes(tmoe_handle *h, int32_t B, int32_t n_head, int32_t n_kv, int32_t head_dim,
+                                       int32_t n_ctx) {
+    if (!h || B < 0 || n_head <= 0 || n_kv <= 0 || head_dim <= 0 || n_ctx <= 0) return TMOE_E_INVALID;
+    return (int64_t)(tmoe::attn_scratch_floats(B, n_head, head_dim, n_kv, n_ctx, h->sm_count) * 4);
+}
+
+int tmoe_attn_decode(tmoe_handle *h, void *stream, const float *q, const float *k, const float *v, void *k_cache,
+                     void *v_cache, const int32_t *pos, int32_t B, int32_t n_head, int32_t n_kv, int32_t head_dim,
+                     int32_t n_ctx, float scale, void *scratch, float *out) {
+    if (!h) return TMOE_E_INVALID;
+    if (B < 0 || n_kv <= 0 || n_head % n_kv || n_head / n_kv > 8 || (head_dim != 64 && head_dim != 128) || n_ctx <= 0)
+        return fail(h, TMOE_E_UNSUPPORTED, "attention shape: %d heads over %d KV heads of %d (up to 8 heads per KV "
+                                           "head, head_dim 64 or 128)", n_head, n_kv, head_dim);
+    if (B == 0) return TMOE_OK;
+    if (!q || !k || !v || !k_cache || !v_cache || !pos || !scratch || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    if (((uintptr_t)k_cache | (uintptr_t)v_cache) & 15u) return fail(h, TMOE_E_INVALID, "caches must be 16-byte aligned");
+    DeviceGuard dg(h->cfg.device);
+    cudaError_t e = tmoe::launch_attn_decode(q, k, v, (__half *)k_cache, (__half *)v_cache, pos, B, n_head, n_kv,
+                                             head_dim, n_ctx, scale, (float *)scratch, out, h->sm_count, h->err,
+                                             (cudaStream_t)stream);
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "attention");
+}
+
+int tmoe_add(tmoe_handle *h, void *stream, const float *a, const float *b, float *out, int64_t n) {
+    if (!h) return TMOE_E_INVALID;
+    if (n < 0) return fail(h, TMOE_E_INVALID, "bad add size");
+    if (n == 0) return TMOE_OK;
+    if (!a || !b || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    DeviceGuard dg(h->cfg.device);
+    cudaError_t e = tmoe::launch_add(a, b, out, n, (cudaStream_t)stream);
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "add");
+}
+
+int tmoe_argmax(tmoe_handle *h, void *stream, const float *x, int64_t rows, int64_t n, int32_t *out) {
+    if (!h) return TMOE_E_INVALID;
+    if (rows < 0 || n <= 0 || n > 0x7fffffff) return fail(h, TMOE_E_INVALID, "bad argmax shape");
+    if (rows == 0) return TMOE_OK;
+    if (!x || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    DeviceGuard dg(h->cfg.device);
+    cudaError_t e = tmoe::launch_argmax(x, rows, n, out, (cudaStream_t)stream);
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "argmax");
 }
 
 int tmoe_profile_enable(tmoe_handle *h, int32_t enable) {
