@@ -285,6 +285,12 @@ TMOE_API int tmoe_rms_norm(tmoe_handle *h, void *stream, const float *x, const f
                            int64_t n, float *out);
 TMOE_API int tmoe_rope_neox(tmoe_handle *h, void *stream, float *x, const int32_t *pos, int64_t n_tok, int32_t n_head,
                             int32_t head_dim, int32_t n_rot, float freq_base);
+/* The two per-head norms and the two RoPEs of attention() (attn.rs:320-325) in one launch:
+ * q [T][n_head][head_dim] = rope(rms_norm(q) * q_norm), k [T][n_kv][head_dim] likewise with k_norm
+ * (head_dim a multiple of 32, at most 128). */
+TMOE_API int tmoe_qk_norm_rope(tmoe_handle *h, void *stream, float *q, float *k, const float *q_norm,
+                               const float *k_norm, const int32_t *pos, int64_t T, int32_t n_head, int32_t n_kv,
+                               int32_t head_dim, int32_t n_rot, float freq_base, float eps);
 TMOE_API int64_t tmoe_attn_decode_scratch_bytes(tmoe_handle *h, int32_t B, int32_t n_head, int32_t n_kv,
                                                 int32_t head_dim, int32_t n_ctx);
 TMOE_API int tmoe_attn_decode(tmoe_handle *h, void *stream, const float *q, const float *k, const float *v,

@@ -91,6 +91,7 @@ SIGNATURES = {
     "tmoe_get_rows": ([P, P, I32, P, C.c_size_t, I64, I64, P, I64, P], C.c_int),
     "tmoe_rms_norm": ([P, P, P, P, C.c_float, I64, I64, P], C.c_int),
     "tmoe_rope_neox": ([P, P, P, P, I64, I32, I32, I32, C.c_float], C.c_int),
+    "tmoe_qk_norm_rope": ([P, P, P, P, P, P, P, I64, I32, I32, I32, I32, C.c_float, C.c_float], C.c_int),
     "tmoe_attn_decode_scratch_bytes": ([P, I32, I32, I32, I32, I32], I64),
     "tmoe_attn_decode": ([P, P, P, P, P, P, P, P, I32, I32, I32, I32, I32, C.c_float, P, P], C.c_int),
     "tmoe_add": ([P, P, P, P, P, I64], C.c_int),

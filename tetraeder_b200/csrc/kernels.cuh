@@ -99,6 +99,8 @@ cudaError_t launch_get_rows(int32_t type, const uint8_t *W, size_t nb1, int K, i
 // model.cu: the decode step around the MoE layer
 cudaError_t launch_rope_neox(float *x, const int32_t *pos, int64_t n_tok, int n_head, int head_dim, int n_rot,
                              float freq_base, cudaStream_t st);
+cudaError_t launch_qk_norm_rope(float *q, float *k, const float *qw, const float *kw, const int32_t *pos, int64_t T,
+                                int n_head, int n_kv, int d, int n_rot, float freq_base, float eps, cudaStream_t st);
 int attn_splits(int B, int n_kv, int n_ctx, int sm_count);
 size_t attn_scratch_floats(int B, int n_head, int head_dim, int n_kv, int n_ctx, int sm_count);
 cudaError_t launch_attn_decode(const float *q, const float *k, const float *v, __half *kc, __half *vc,

@@ -8,9 +8,10 @@
 //                         of one KV head share its K/V reads.  Split over the context, each split
 //                         keeping an online softmax (max, sum, weighted V); attn_merge_kernel joins
 //                         the splits
+//   qk_norm_rope_kernel   the per-head norms of Q and K and their RoPE in one launch (attn.rs:320-325)
 //   add_kernel, argmax_kernel   the residual adds and greedy sampling
-// The projections are the GEMV of gemv.cu (tmoe_mul_mat_id with one expert), the norms
-// rms_norm_kernel (route.cu), the token embedding get_rows_kernel (quant.cu).
+// The projections are the GEMV of gemv.cu (tmoe_mul_mat: dense_prep_kernel's dispatch of one
+// matrix), the norms rms_norm_kernel (route.cu), the token embedding get_rows_kernel (quant.cu).
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -37,6 +38,44 @@ __global__ void rope_neox_kernel(float *__restrict__ x, const int32_t *__restric
     }
 }
 
+// The per-head RMS norms of Q and K times q_norm / k_norm, then NeoX RoPE, in one launch: a CTA per
+// row (token, head) of q [T][n_head][d] and k [T][n_kv][d], one thread per element (d <= 128).  The
+// mean square is summed in f64, as rms_norm_kernel does.
+__global__ void qk_norm_rope_kernel(float *__restrict__ q, float *__restrict__ k, const float *__restrict__ qw,
+                                    const float *__restrict__ kw, const int32_t *__restrict__ pos, int n_head,
+                                    int n_kv, int d, int n_rot, float freq_base, float eps) {
+    __shared__ float row[128];
+    __shared__ double part[4];
+    const int r = blockIdx.x, per_tok = n_head + n_kv;
+    const int t = r / per_tok, hh = r % per_tok;
+    float *x = hh < n_head ? q + ((size_t)t * n_head + hh) * d : k + ((size_t)t * n_kv + (hh - n_head)) * d;
+    const float *w = hh < n_head ? qw : kw;
+    const int i = threadIdx.x;
+    const float v = i < d ? x[i] : 0.0f;
+    double sq = (double)__fmul_rn(v, v);
+    for (int o = 16; o >= 1; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if ((i & 31) == 0) part[i >> 5] = sq;
+    __syncthreads();
+    double sum = 0.0;
+    for (int j = 0; j < (int)(blockDim.x >> 5); j++) sum += part[j];
+    const float mean = __double2float_rn(__ddiv_rn(sum, (double)d));
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    const float nv = i < d ? __fmul_rn(__fmul_rn(v, scale), w[i]) : 0.0f;
+    if (i < d) row[i] = nv;
+    __syncthreads();
+    const int half = n_rot / 2;
+    if (i < half) {
+        const float theta = (float)pos[t] * powf(freq_base, -2.0f * (float)i / (float)n_rot);
+        float sn, cs;
+        sincosf(theta, &sn, &cs);
+        const float x0 = row[i], x1 = row[i + half];
+        x[i] = x0 * cs - x1 * sn;
+        x[i + half] = x0 * sn + x1 * cs;
+    } else if (i >= n_rot && i < d) {
+        x[i] = nv;
+    }
+}
+
 // cache[b][pos[b]][:] = rows[b][:] (n_kv * head_dim values, as F16) for K and V.
 __global__ void kv_store_kernel(const float *__restrict__ k, const float *__restrict__ v, __half *__restrict__ kc,
                                 __half *__restrict__ vc, const int32_t *__restrict__ pos, int n_ctx, int width,
@@ -54,14 +93,60 @@ __global__ void kv_store_kernel(const float *__restrict__ k, const float *__rest
     }
 }
 
-// One CTA per (split, KV head, sequence), 128 threads.  G query heads share the KV head.  Tiles of
-// AT_TILE positions: K and V staged in shared memory (K rows padded by one word so that the 32
-// positions of a warp hit distinct banks); warp w scores heads w, w+4, ... (lane = position);
-// the online softmax per head lives in its warp; thread t accumulates output dimensions t (and
-// t + 128 for larger heads) of every head.
-constexpr int AT_TILE = 32;
-constexpr int AT_THREADS = 128;
+// One CTA per (split, KV head, sequence), 4 warps, on the tensor cores (mma.sync m16n8k16, f16
+// operands, f32 accumulators).  The G <= 8 query heads of the KV head are the 16-row A operand
+// (rows past G zero); each warp takes tiles of AT_TILE = 16 positions of the CTA's split (warp w:
+// tiles w, w + 4, ...), staged by cp.async into its own two padded shared-memory stages (rows past
+// the split's end zero-filled and masked to -inf):
+//   S = Q K^T   (2 position blocks x HD/16 dim blocks; K rows through ldmatrix: a K row is a
+//               column of the col-major B operand);
+//   online softmax of each head (row) over the tile, in the S fragments (a quad of lanes shares a
+//               row);
+//   O += P V    (the S fragments, as f16, are P's A fragments; V through ldmatrix.trans).
+// At the end the four warps' (max, sum, O) are merged in shared memory and written as the split's
+// partial for attn_merge_kernel.
+constexpr int AT_TILE = 16;
+constexpr int AT_WARPS = 4;
+constexpr int AT_THREADS = 32 * AT_WARPS;
 constexpr int AT_MAX_G = 8;
+
+template <int HD>
+struct AttnSmem {
+    static constexpr int ROW = HD + 8;  // halfs per staged row: 16 bytes of padding, conflict-free ldmatrix
+    static constexpr int STAGE = 2 * AT_TILE * ROW;  // K then V
+    static constexpr size_t BYTES = (size_t)AT_WARPS * 2 * STAGE * 2;
+};
+
+__device__ __forceinline__ void at_cp16(uint32_t dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void at_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void at_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
 
 template <int HD>
 __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const float *__restrict__ q,
@@ -70,110 +155,150 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const float *__
                                                                  const int32_t *__restrict__ pos, int n_head,
                                                                  int n_kv, int n_ctx, float scale,
                                                                  float *__restrict__ part) {
-    constexpr int KW = HD / 2 + 1;  // words per staged K row (half2 + one pad word)
-    __shared__ float qs[AT_MAX_G][HD];
-    __shared__ uint32_t ks[AT_TILE][KW];
-    __shared__ __align__(16) __half vs[AT_TILE][HD];
-    __shared__ float ps[AT_MAX_G][AT_TILE];
-    __shared__ float alpha_s[AT_MAX_G];
+    using SM = AttnSmem<HD>;
+    constexpr int KB = HD / 16;  // dim blocks of the QK^T product
+    constexpr int NB = HD / 8;   // dim blocks of the output
+    extern __shared__ __align__(16) __half at_smem[];
     const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z, S = gridDim.x;
     const int G = n_head / n_kv;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gr = lane >> 2, t4 = lane & 3;
     const int len = min(pos[b] + 1, n_ctx);
     const int per = ((len + S - 1) / S + AT_TILE - 1) / AT_TILE * AT_TILE;
-    const int p0 = s * per, p1 = min(len, p0 + per);
-    for (int i = tid; i < G * HD; i += AT_THREADS)
-        qs[i / HD][i % HD] = q[((size_t)b * n_head + (size_t)g * G + i / HD) * HD + i % HD] * scale;
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};  // per head of this warp (w, w + 4)
-    constexpr int DPT = HD >= AT_THREADS ? HD / AT_THREADS : 1;  // output dims per thread
-    float acc[AT_MAX_G][DPT];
-#pragma unroll
-    for (int h = 0; h < AT_MAX_G; h++)
-#pragma unroll
-        for (int j = 0; j < DPT; j++) acc[h][j] = 0.0f;
+    const int p0 = min(len, s * per), p1 = min(len, p0 + per);
     const size_t row_stride = (size_t)n_kv * HD;
     const __half *kb = kc + (size_t)b * n_ctx * row_stride + (size_t)g * HD;
     const __half *vb = vc + (size_t)b * n_ctx * row_stride + (size_t)g * HD;
+    __half *stage0 = at_smem + (size_t)warp * 2 * SM::STAGE;
+
+    // Q fragments (rows = heads of this KV head, scaled), f16
+    uint32_t qa[KB][4];
+    {
+        const float *qb = q + ((size_t)b * n_head + (size_t)g * G) * HD;
+#pragma unroll
+        for (int k = 0; k < KB; k++) {
+            const int c0 = 16 * k + 2 * t4;
+            float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            if (gr < G) {
+                v[0] = qb[gr * HD + c0] * scale, v[1] = qb[gr * HD + c0 + 1] * scale;
+                v[4] = qb[gr * HD + c0 + 8] * scale, v[5] = qb[gr * HD + c0 + 9] * scale;
+            }
+            qa[k][0] = pack_h2(v[0], v[1]);
+            qa[k][1] = 0u;  // rows 8..15: no head
+            qa[k][2] = pack_h2(v[4], v[5]);
+            qa[k][3] = 0u;
+        }
+    }
+    float o[NB][4];
+#pragma unroll
+    for (int n = 0; n < NB; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f;  // of row gr (the rows gr + 8 hold no head)
+
+    const int n_tiles = (p1 - p0 + AT_TILE - 1) / AT_TILE;
+    auto issue = [&](int i, int st) {  // tile i of this warp into stage st
+        const int t0 = p0 + (warp + i * AT_WARPS) * AT_TILE;
+        __half *ks = stage0 + st * SM::STAGE, *vs = ks + AT_TILE * SM::ROW;
+        constexpr int CH = HD / 8;  // 16-byte chunks per row
+        for (int c = lane; c < AT_TILE * CH; c += 32) {
+            const int r = c / CH, col = 8 * (c % CH);
+            const bool ok = t0 + r < p1;
+            const size_t off = (size_t)(ok ? t0 + r : p0) * row_stride + col;
+            at_cp16(smem_u32(ks + r * SM::ROW + col), kb + off, ok);
+            at_cp16(smem_u32(vs + r * SM::ROW + col), vb + off, ok);
+        }
+        at_commit();
+    };
+    const int mine = n_tiles > warp ? (n_tiles - warp + AT_WARPS - 1) / AT_WARPS : 0;
+    if (mine > 0) issue(0, 0);
+    for (int i = 0; i < mine; i++) {
+        if (i + 1 < mine) {
+            issue(i + 1, (i + 1) & 1);
+            at_wait<1>();
+        } else {
+            at_wait<0>();
+        }
+        __syncwarp();
+        const __half *ks = stage0 + (i & 1) * SM::STAGE, *vs = ks + AT_TILE * SM::ROW;
+        const int t0 = p0 + (warp + i * AT_WARPS) * AT_TILE;
+        // S = Q K^T: 16 heads x 16 positions
+        float sc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+#pragma unroll
+        for (int nb = 0; nb < 2; nb++)
+#pragma unroll
+            for (int k = 0; k < KB; k += 2) {
+                // matrices: positions 8nb + 0..7 x dims 16k + {0, 8}, 16(k+1) + {0, 8}
+                const int r = 8 * nb + (lane & 7), cblk = 16 * k + 8 * (lane >> 3);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(smem_u32(ks + r * SM::ROW + cblk), b0, b1, b2, b3);
+                mma_f16(sc[nb], qa[k][0], qa[k][1], qa[k][2], qa[k][3], b0, b1);
+                if (k + 1 < KB) mma_f16(sc[nb], qa[k + 1][0], qa[k + 1][1], qa[k + 1][2], qa[k + 1][3], b2, b3);
+            }
+        // mask positions past the split, then the online softmax of row gr
+#pragma unroll
+        for (int nb = 0; nb < 2; nb++)
+#pragma unroll
+            for (int j = 0; j < 2; j++)
+                if (t0 + 8 * nb + 2 * t4 + j >= p1) sc[nb][j] = -INFINITY;
+        float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);  // finite: every tile holds at least one position
+        const float alpha = m_run == -INFINITY ? 0.0f : __expf(m_run - m_new);
+        float pr[2][2];
+        float sum = 0.0f;
+#pragma unroll
+        for (int nb = 0; nb < 2; nb++)
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                pr[nb][j] = __expf(sc[nb][j] - m_new);
+                sum += pr[nb][j];
+            }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        l_run = l_run * alpha + sum;
+        m_run = m_new;
+        // P as the A operand (k = the 16 positions): rows gr (heads), rows gr + 8 zero
+        const uint32_t pa0 = pack_h2(pr[0][0], pr[0][1]), pa2 = pack_h2(pr[1][0], pr[1][1]);
+#pragma unroll
+        for (int n = 0; n < NB; n++) o[n][0] *= alpha, o[n][1] *= alpha;
+#pragma unroll
+        for (int n = 0; n < NB; n += 2) {
+            // matrices: positions 0..7 / 8..15 x dims 8n + 0..7, then 8(n+1) + 0..7, transposed
+            const int r = (lane & 7) + 8 * ((lane >> 3) & 1), cblk = 8 * n + 8 * (lane >> 4);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(smem_u32(vs + r * SM::ROW + cblk), b0, b1, b2, b3);
+            mma_f16(o[n], pa0, 0u, pa2, 0u, b0, b1);
+            mma_f16(o[n + 1], pa0, 0u, pa2, 0u, b2, b3);
+        }
+        __syncwarp();  // every lane's ldmatrix of this stage is done before it is refilled
+    }
+    at_wait<0>();
     __syncthreads();
-    for (int t0 = p0; t0 < p1; t0 += AT_TILE) {
-        const int nt = min(AT_TILE, p1 - t0);
-        // stage K and V of the tile (16-byte loads: HD / 8 per row)
-        for (int i = tid; i < AT_TILE * (HD / 8); i += AT_THREADS) {
-            const int r = i / (HD / 8), c = i % (HD / 8);
-            uint4 kv4 = make_uint4(0, 0, 0, 0), vv4 = make_uint4(0, 0, 0, 0);
-            if (r < nt) {
-                kv4 = *reinterpret_cast<const uint4 *>(kb + (size_t)(t0 + r) * row_stride + 8 * c);
-                vv4 = *reinterpret_cast<const uint4 *>(vb + (size_t)(t0 + r) * row_stride + 8 * c);
-            }
-            ks[r][4 * c] = kv4.x, ks[r][4 * c + 1] = kv4.y, ks[r][4 * c + 2] = kv4.z, ks[r][4 * c + 3] = kv4.w;
-            *reinterpret_cast<uint4 *>(&vs[r][8 * c]) = vv4;
-        }
-        __syncthreads();
-        // scores and the online softmax of heads warp, warp + 4
+    // merge the warps: row gr of each warp -> shared memory, then the CTA combines them
+    float *red = reinterpret_cast<float *>(at_smem);  // [warp][8 rows][2 + HD]
+    constexpr int RW = 2 + HD;
+    if (gr < AT_MAX_G) {
+        float *rr = red + ((size_t)warp * AT_MAX_G + gr) * RW;
+        if (t4 == 0) rr[0] = m_run, rr[1] = l_run;
 #pragma unroll
-        for (int hh = 0; hh < 2; hh++) {
-            const int h = warp + 4 * hh;
-            if (h >= G) break;
-            float sc = -INFINITY;
-            if (lane < nt) {
-                float d = 0.0f;
-#pragma unroll 8
-                for (int j = 0; j < HD / 2; j++) {
-                    const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(&ks[lane][j]));
-                    d = fmaf(qs[h][2 * j], kf.x, d);
-                    d = fmaf(qs[h][2 * j + 1], kf.y, d);
-                }
-                sc = d;
-            }
-            float mx = sc;
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            const float m_new = fmaxf(m[hh], mx);
-            const float pe = lane < nt ? __expf(sc - m_new) : 0.0f;
-            float sum = pe;
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            const float a = m[hh] == -INFINITY ? 0.0f : __expf(m[hh] - m_new);
-            l[hh] = l[hh] * a + sum;
-            m[hh] = m_new;
-            ps[h][lane] = pe;
-            if (lane == 0) alpha_s[h] = a;
-        }
-        __syncthreads();
-        // P . V
-#pragma unroll
-        for (int j = 0; j < DPT; j++) {
-            const int d = tid + j * AT_THREADS;
-            if (d >= HD) break;
-#pragma unroll
-            for (int h = 0; h < AT_MAX_G; h++)
-                if (h < G) acc[h][j] *= alpha_s[h];
-            for (int r = 0; r < nt; r++) {
-                const float vv = __half2float(vs[r][d]);
-#pragma unroll
-                for (int h = 0; h < AT_MAX_G; h++)
-                    if (h < G) acc[h][j] = fmaf(ps[h][r], vv, acc[h][j]);
-            }
-        }
-        __syncthreads();
+        for (int n = 0; n < NB; n++) rr[2 + 8 * n + 2 * t4] = o[n][0], rr[2 + 8 * n + 2 * t4 + 1] = o[n][1];
     }
-    // partials: [b][head][s] = {m, l, acc[HD]}
+    __syncthreads();
     const size_t pstride = (size_t)HD + 2;
-#pragma unroll
-    for (int hh = 0; hh < 2; hh++) {
-        const int h = warp + 4 * hh;
-        if (h < G && lane == 0) {
-            float *pp = part + (((size_t)b * n_head + (size_t)g * G + h) * S + s) * pstride;
-            pp[0] = m[hh], pp[1] = l[hh];
+    for (int i = threadIdx.x; i < G * HD; i += AT_THREADS) {
+        const int h = i / HD, d = i % HD;
+        float M = -INFINITY;
+        for (int w = 0; w < AT_WARPS; w++) M = fmaxf(M, red[((size_t)w * AT_MAX_G + h) * RW]);
+        float L = 0.0f, acc = 0.0f;
+        for (int w = 0; w < AT_WARPS; w++) {
+            const float *rr = red + ((size_t)w * AT_MAX_G + h) * RW;
+            if (rr[0] == -INFINITY) continue;
+            const float f = __expf(rr[0] - M);
+            L += f * rr[1];
+            acc += f * rr[2 + d];
         }
-    }
-#pragma unroll
-    for (int j = 0; j < DPT; j++) {
-        const int d = tid + j * AT_THREADS;
-        if (d >= HD) break;
-#pragma unroll
-        for (int h = 0; h < AT_MAX_G; h++)
-            if (h < G) part[(((size_t)b * n_head + (size_t)g * G + h) * S + s) * pstride + 2 + d] = acc[h][j];
+        float *pp = part + (((size_t)b * n_head + (size_t)g * G + h) * S + s) * pstride;
+        if (d == 0) pp[0] = M, pp[1] = L;
+        pp[2 + d] = acc;
     }
 }
 
@@ -254,6 +379,16 @@ cudaError_t launch_dense_prep(int T, int4 *active, int32_t *n_active, int32_t *p
     return cudaGetLastError();
 }
 
+cudaError_t launch_qk_norm_rope(float *q, float *k, const float *qw, const float *kw, const int32_t *pos, int64_t T,
+                                int n_head, int n_kv, int d, int n_rot, float freq_base, float eps, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if (d <= 0 || d > 128 || d % 32 || n_rot <= 0 || n_rot > d || n_rot % 2 || T * (n_head + n_kv) > 0x7fffffff)
+        return cudaErrorInvalidValue;
+    qk_norm_rope_kernel<<<(unsigned)(T * (n_head + n_kv)), d, 0, st>>>(q, k, qw, kw, pos, n_head, n_kv, d, n_rot,
+                                                                       freq_base, eps);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_rope_neox(float *x, const int32_t *pos, int64_t n_tok, int n_head, int head_dim, int n_rot,
                              float freq_base, cudaStream_t st) {
     if (n_tok <= 0) return cudaSuccess;
@@ -285,10 +420,27 @@ cudaError_t launch_attn_decode(const float *q, const float *k, const float *v, _
     if (e != cudaSuccess) return e;
     const int S = attn_splits(B, n_kv, n_ctx, sm_count);
     const dim3 grid(S, n_kv, B);
-    if (head_dim == 128)
-        attn_decode_kernel<128><<<grid, AT_THREADS, 0, st>>>(q, kc, vc, pos, n_head, n_kv, n_ctx, scale, part);
-    else
-        attn_decode_kernel<64><<<grid, AT_THREADS, 0, st>>>(q, kc, vc, pos, n_head, n_kv, n_ctx, scale, part);
+    static int set128[64] = {}, set64[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (head_dim == 128) {
+        constexpr size_t smem = AttnSmem<128>::BYTES;
+        if (!set128[dev] &&
+            (e = cudaFuncSetAttribute(attn_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem)) != cudaSuccess)
+            return e;
+        set128[dev] = 1;
+        attn_decode_kernel<128><<<grid, AT_THREADS, smem, st>>>(q, kc, vc, pos, n_head, n_kv, n_ctx, scale, part);
+    } else {
+        constexpr size_t smem = AttnSmem<64>::BYTES;
+        if (!set64[dev] &&
+            (e = cudaFuncSetAttribute(attn_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem)) != cudaSuccess)
+            return e;
+        set64[dev] = 1;
+        attn_decode_kernel<64><<<grid, AT_THREADS, smem, st>>>(q, kc, vc, pos, n_head, n_kv, n_ctx, scale, part);
+    }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     attn_merge_kernel<<<B * n_head, 128, 0, st>>>(part, S, head_dim, out);
     return cudaGetLastError();

@@ -1036,6 +1036,21 @@ int tmoe_rope_neox(tmoe_handle *h, void *stream, float *x, const int32_t *pos, i
     return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "rope");
 }
 
+int tmoe_qk_norm_rope(tmoe_handle *h, void *stream, float *q, float *k, const float *q_norm, const float *k_norm,
+                      const int32_t *pos, int64_t T, int32_t n_head, int32_t n_kv, int32_t head_dim, int32_t n_rot,
+                      float freq_base, float eps) {
+    if (!h) return TMOE_E_INVALID;
+    if (T < 0 || n_head <= 0 || n_kv <= 0 || head_dim <= 0 || head_dim > 128 || head_dim % 32 || n_rot <= 0 ||
+        n_rot > head_dim || n_rot % 2 || freq_base <= 0)
+        return fail(h, TMOE_E_INVALID, "bad qk_norm_rope shape (head_dim a multiple of 32 up to 128)");
+    if (T == 0) return TMOE_OK;
+    if (!q || !k || !q_norm || !k_norm || !pos) return fail(h, TMOE_E_INVALID, "null tensor");
+    DeviceGuard dg(h->cfg.device);
+    cudaError_t e = tmoe::launch_qk_norm_rope(q, k, q_norm, k_norm, pos, T, n_head, n_kv, head_dim, n_rot, freq_base,
+                                              eps, (cudaStream_t)stream);
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "qk_norm_rope");
+}
+
 int64_t tmoe_attn_decode_scratch_bytes(tmoe_handle *h, int32_t B, int32_t n_head, int32_t n_kv, int32_t head_dim,
                                        int32_t n_ctx) {
     if (!h || B < 0 || n_head <= 0 || n_kv <= 0 || head_dim <= 0 || n_ctx <= 0) return TMOE_E_INVALID;

@@ -2,7 +2,7 @@
 build_step (crates/model/src/qwen3moe.rs:2777-2826) with attention() (crates/model/src/attn.rs:
 246-405), one new token for each of B sequences, over F16 KV caches.  Every op is a libtmoe call:
 tmoe_get_rows, tmoe_rms_norm, tmoe_mul_mat (the projections, on the decode GEMV),
-tmoe_rope_neox, tmoe_attn_decode, tmoe_add, the MoE layer (tmoe_layer with the FFN norm) and
+tmoe_qk_norm_rope, tmoe_attn_decode, tmoe_add, the MoE layer (tmoe_layer with the FFN norm) and
 tmoe_argmax; a step is stream-ordered and allocation-free, so it can be captured in a CUDA graph
 (Qwen3MoeModel.graph).
 
@@ -165,12 +165,17 @@ class Qwen3MoeModel:
             # the Q8_K rows of cur are reused by a projection of the same type as the previous one
             self._mm(wk, self.cur, self.k, B, st, reuse=wk.type == wq.type)
             self._mm(wv, self.cur, self.v, B, st, reuse=wv.type == wk.type)
-            chk(L.tmoe_rms_norm(h, st, _ptr(self.q), _ptr(w[p + "attn_q_norm.weight"]), hp.rms_eps, B * nh, d,
-                                _ptr(self.q)))
-            chk(L.tmoe_rms_norm(h, st, _ptr(self.k), _ptr(w[p + "attn_k_norm.weight"]), hp.rms_eps, B * nkv, d,
-                                _ptr(self.k)))
-            chk(L.tmoe_rope_neox(h, st, _ptr(self.q), _ptr(pos), B, nh, d, hp.n_rot, hp.rope_freq_base))
-            chk(L.tmoe_rope_neox(h, st, _ptr(self.k), _ptr(pos), B, nkv, d, hp.n_rot, hp.rope_freq_base))
+            if d % 32 == 0 and d <= 128:  # the two norms and the two RoPEs in one launch
+                chk(L.tmoe_qk_norm_rope(h, st, _ptr(self.q), _ptr(self.k), _ptr(w[p + "attn_q_norm.weight"]),
+                                        _ptr(w[p + "attn_k_norm.weight"]), _ptr(pos), B, nh, nkv, d, hp.n_rot,
+                                        hp.rope_freq_base, hp.rms_eps))
+            else:
+                chk(L.tmoe_rms_norm(h, st, _ptr(self.q), _ptr(w[p + "attn_q_norm.weight"]), hp.rms_eps, B * nh, d,
+                                    _ptr(self.q)))
+                chk(L.tmoe_rms_norm(h, st, _ptr(self.k), _ptr(w[p + "attn_k_norm.weight"]), hp.rms_eps, B * nkv, d,
+                                    _ptr(self.k)))
+                chk(L.tmoe_rope_neox(h, st, _ptr(self.q), _ptr(pos), B, nh, d, hp.n_rot, hp.rope_freq_base))
+                chk(L.tmoe_rope_neox(h, st, _ptr(self.k), _ptr(pos), B, nkv, d, hp.n_rot, hp.rope_freq_base))
             chk(L.tmoe_attn_decode(h, st, _ptr(self.q), _ptr(self.k), _ptr(self.v), _ptr(self.kc[il]),
                                    _ptr(self.vc[il]), _ptr(pos), B, nh, nkv, d, self.n_ctx, 1.0 / d ** 0.5,
                                    _ptr(self.scratch), _ptr(self.att)))
