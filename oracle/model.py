@@ -8,7 +8,8 @@ Restates, per decode step of B sequences (one new token each):
     (ggml mul_mat: the Q8_K dot of the activations, as on the reference CPU path, here through the
     layer oracle's mul_mat_id with one expert); rms_norm per head times q_norm / k_norm; NeoX RoPE
     (attn.rs:225-236); K and V stored as F16 (set_rows into the F16 cache); softmax(q k^T / sqrt(d)) v
-    over the sequence's positions 0..pos (the causal mask of attn.rs:425); Wo; plus x;
+    over the sequence's positions 0..pos (the causal mask of attn.rs:425), with q converted to F16 as
+    flash_attn_ext does for an F16 cache; Wo; plus x;
   head (qwen3moe.rs:2809-2826): rms_norm * output_norm, then `output` (or the tied token_embd).
 Parity with ggml itself is not pinned (ggml is absent from the reference tree); the arithmetic
 follows the published ops, in float32 with float64 where noted.
@@ -92,13 +93,15 @@ class ModelOracle:
         k = rope_neox(rms_norm(k, w[p + "attn_k_norm.weight"], hp.rms_eps), pos, hp.n_rot, hp.rope_freq_base)
         out = np.zeros((B, nh, d), np.float32)
         G = nh // nkv
+        # flash_attn_ext over an F16 cache converts Q to F16 and scales the Q.K dot (ggml's CPU and CUDA paths)
+        q16 = q.astype(np.float16).astype(np.float64)
         for b in range(B):
             self.kc[il][b, pos[b]] = k[b].reshape(-1).astype(np.float16)
             self.vc[il][b, pos[b]] = v[b].astype(np.float16)
             K = self.kc[il][b, :pos[b] + 1].astype(np.float64).reshape(-1, nkv, d)
             V = self.vc[il][b, :pos[b] + 1].astype(np.float64).reshape(-1, nkv, d)
             for h in range(nh):
-                s = K[:, h // G, :] @ q[b, h].astype(np.float64) / np.sqrt(d)
+                s = (K[:, h // G, :] @ q16[b, h]) * np.float64(np.float32(1.0 / np.sqrt(d)))
                 e = np.exp(s - s.max())
                 out[b, h] = (e @ V[:, h // G, :] / e.sum()).astype(np.float32)
         o = w[p + "attn_output.weight"].matmul(out.reshape(B, nh * d))

@@ -61,7 +61,11 @@ def test_decode_steps_match_the_oracle(tiny_model):
             model.check()
             want = ref.decode(toks, pos)  # positions never written read as zeros on both sides
             n = nrms(got, want)
-            assert n < 1e-2, f"step {s}: logits nrms {n:.2e}"
+            # Attention's probabilities enter the tensor cores as f16 (as in ggml's flash attention); the
+            # next projection re-quantises its input to Q8_K, which turns those last-bit differences into
+            # a few flipped 8-bit roundings per step: about 1.5e-2 of the logits over two layers here.
+            # The ops themselves are held tighter below.
+            assert n < 5e-2, f"step {s}: logits nrms {n:.2e}"
         nt = model.next_tokens.cpu().numpy()
         assert np.array_equal(nt, np.argmax(got, axis=1)), "argmax"
     finally:
@@ -120,12 +124,13 @@ def test_attention_op_against_float64(hd, nh, nkv, ctx):
     layer.check()
     got = out.cpu().numpy()
     G = nh // nkv
+    q16 = q.astype(np.float16)  # the Q operand as flash attention takes it over an F16 cache
     for b in range(B):
         kc[b, pos[b]] = k[b].astype(np.float16)
         vc[b, pos[b]] = v[b].astype(np.float16)
         K, V = kc[b, :pos[b] + 1].astype(np.float64), vc[b, :pos[b] + 1].astype(np.float64)
         for hh in range(nh):
-            s = K[:, hh // G] @ q[b, hh].astype(np.float64) * scale
+            s = K[:, hh // G] @ q16[b, hh].astype(np.float64) * np.float64(np.float32(scale))
             e = np.exp(s - s.max())
             want = e @ V[:, hh // G] / e.sum()
             # Q, K, P and V enter the tensor cores as f16 (f32 accumulation), as in ggml's own flash attention

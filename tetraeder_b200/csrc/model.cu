@@ -170,7 +170,8 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const float *__
     const __half *vb = vc + (size_t)b * n_ctx * row_stride + (size_t)g * HD;
     __half *stage0 = at_smem + (size_t)warp * 2 * SM::STAGE;
 
-    // Q fragments (rows = heads of this KV head, scaled), f16
+    // Q fragments (rows = heads of this KV head), f16; the scale goes on the f32 scores, as ggml's
+    // flash attention over an F16 cache converts Q to F16 and scales the Q.K dot
     uint32_t qa[KB][4];
     {
         const float *qb = q + ((size_t)b * n_head + (size_t)g * G) * HD;
@@ -179,8 +180,8 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const float *__
             const int c0 = 16 * k + 2 * t4;
             float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
             if (gr < G) {
-                v[0] = qb[gr * HD + c0] * scale, v[1] = qb[gr * HD + c0 + 1] * scale;
-                v[4] = qb[gr * HD + c0 + 8] * scale, v[5] = qb[gr * HD + c0 + 9] * scale;
+                v[0] = qb[gr * HD + c0], v[1] = qb[gr * HD + c0 + 1];
+                v[4] = qb[gr * HD + c0 + 8], v[5] = qb[gr * HD + c0 + 9];
             }
             qa[k][0] = pack_h2(v[0], v[1]);
             qa[k][1] = 0u;  // rows 8..15: no head
@@ -232,12 +233,12 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const float *__
                 mma_f16(sc[nb], qa[k][0], qa[k][1], qa[k][2], qa[k][3], b0, b1);
                 if (k + 1 < KB) mma_f16(sc[nb], qa[k + 1][0], qa[k + 1][1], qa[k + 1][2], qa[k + 1][3], b2, b3);
             }
-        // mask positions past the split, then the online softmax of row gr
+        // scale; mask positions past the split; then the online softmax of row gr
 #pragma unroll
         for (int nb = 0; nb < 2; nb++)
 #pragma unroll
             for (int j = 0; j < 2; j++)
-                if (t0 + 8 * nb + 2 * t4 + j >= p1) sc[nb][j] = -INFINITY;
+                sc[nb][j] = t0 + 8 * nb + 2 * t4 + j >= p1 ? -INFINITY : sc[nb][j] * scale;
         float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
