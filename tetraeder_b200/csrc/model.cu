@@ -363,20 +363,24 @@ __global__ void argmax_kernel(const float *__restrict__ x, int64_t n, int32_t *_
     }
 }
 
-// The dispatch of a dense product (one matrix, every row of x): active = {0, 0, T}, one active
-// expert, pairs in order, the GEMV's work counters zeroed.
-__global__ void dense_prep_kernel(int T, int4 *__restrict__ active, int32_t *__restrict__ n_active,
+// The dispatch of a dense product (one matrix, every row of x): the T rows in groups of `group`
+// tokens, each group an active entry of the same matrix (active[j] = {0, j * group, its end}), so
+// that the GEMV spreads the matrix's row tiles times the groups over the SMs (a group's second
+// read of the rows comes from L2); pairs in order; the GEMV's work counters zeroed.
+__global__ void dense_prep_kernel(int T, int group, int4 *__restrict__ active, int32_t *__restrict__ n_active,
                                   int32_t *__restrict__ perm, int *__restrict__ counters, int n_counters) {
+    const int ng = (T + group - 1) / group;
     for (int i = threadIdx.x; i < T; i += blockDim.x) perm[i] = i;
+    for (int j = threadIdx.x; j < ng; j += blockDim.x) active[j] = make_int4(0, j * group, min(T, (j + 1) * group), 0);
     if (threadIdx.x < n_counters) counters[threadIdx.x] = 0;
-    if (threadIdx.x == 0) active[0] = make_int4(0, 0, T, 0), n_active[0] = 1;
+    if (threadIdx.x == 0) n_active[0] = ng;
 }
 
 // ------------------------------------------------------------------ launchers
-cudaError_t launch_dense_prep(int T, int4 *active, int32_t *n_active, int32_t *perm, int *counters, int n_counters,
-                              cudaStream_t st) {
-    if (n_counters > 256) return cudaErrorInvalidValue;
-    dense_prep_kernel<<<1, 256, 0, st>>>(T, active, n_active, perm, counters, n_counters);
+cudaError_t launch_dense_prep(int T, int group, int4 *active, int32_t *n_active, int32_t *perm, int *counters,
+                              int n_counters, cudaStream_t st) {
+    if (n_counters > 256 || group < 1) return cudaErrorInvalidValue;
+    dense_prep_kernel<<<1, 256, 0, st>>>(T, group, active, n_active, perm, counters, n_counters);
     return cudaGetLastError();
 }
 
