@@ -189,3 +189,43 @@ def test_qk_norm_rope_against_the_oracle(d, n_rot):
         want = rope_neox(rms_norm(x, w, eps), pos, n_rot, base)
         assert np.abs(got.cpu().numpy() - want).max() < 1e-4 * max(1.0, np.abs(want).max())
     layer.close()
+
+
+@pytest.mark.parametrize("rows,H", [(3, 2048), (64, 2048), (2048, 4096), (4097, 2048), (64, 100)])
+def test_rms_norm_bit_exact(rows, H):
+    """tmoe_rms_norm against the oracle's rms_norm, bit for bit: a CTA per row (few long rows) and
+    a warp per row (many rows, or short ones), with and without the weight."""
+    import ctypes as C
+    from oracle.model import rms_norm
+    rng = np.random.default_rng(rows * 7 + H)
+    x = (rng.standard_normal((rows, H)) * rng.uniform(0.01, 30.0, (rows, 1))).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    layer = tb.MoeLayer(512, 256, 8, 2, gate_type=12, up_type=12, down_type=12, max_tokens=4)
+    dx, dw = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
+    out = torch.empty_like(dx)
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    for wt, wn in ((P(dw), w), (None, None)):
+        assert layer.lib.tmoe_rms_norm(layer.h, None, P(dx), wt, 1e-6, rows, H, P(out)) == 0
+        layer.check()
+        assert np.array_equal(out.cpu().numpy(), rms_norm(x, wn, 1e-6))
+    layer.close()
+
+
+@pytest.mark.parametrize("rows,n", [(64, 151936), (5, 151935), (2, 7)])
+def test_argmax_first_index(rows, n):
+    """tmoe_argmax against numpy's argmax (the first index of the maximum): planted ties on the same
+    row, a row of -inf, both the four-wide (n % 4 == 0) and the scalar path."""
+    import ctypes as C
+    rng = np.random.default_rng(rows + n)
+    x = rng.standard_normal((rows, n)).astype(np.float32)
+    x[0, n // 3] = x[0, n - 1] = x[0, 1] = 50.0  # three ties: index 1 wins
+    x[-1, :] = -np.inf
+    if rows > 2:
+        x[1, n - 1] = 99.0  # the maximum at the row's last element
+    layer = tb.MoeLayer(512, 256, 8, 2, gate_type=12, up_type=12, down_type=12, max_tokens=4)
+    dx = torch.from_numpy(x).cuda()
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    assert layer.lib.tmoe_argmax(layer.h, None, C.c_void_p(dx.data_ptr()), rows, n, C.c_void_p(out.data_ptr())) == 0
+    layer.check()
+    assert np.array_equal(out.cpu().numpy(), np.argmax(x, axis=1).astype(np.int32))
+    layer.close()

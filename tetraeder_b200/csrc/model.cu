@@ -332,13 +332,29 @@ __global__ void add_kernel(const float *__restrict__ a, const float *__restrict_
 }
 
 // out[r] = the first index of the largest value of row r.  One CTA per row.
-__global__ void argmax_kernel(const float *__restrict__ x, int64_t n, int32_t *__restrict__ out) {
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ x, int64_t n, bool vec4,
+                                                      int32_t *__restrict__ out) {
     const float *row = x + (int64_t)blockIdx.x * n;
     float best = -INFINITY;
     int64_t bi = 0x7fffffff;
-    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = row[i];
-        if (v > best || (v == best && i < bi)) best = v, bi = i;
+    if (vec4) {  // n % 4 == 0 and the rows 16-byte aligned: four elements a load, two loads in flight
+        const float4 *r4 = reinterpret_cast<const float4 *>(row);
+        const int64_t n4 = n / 4, step = blockDim.x;
+        for (int64_t j = threadIdx.x; j < n4; j += 2 * step) {
+            const float4 a = __ldcs(r4 + j);
+            const float4 b = j + step < n4 ? __ldcs(r4 + j + step) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            const float va[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const int64_t i = (c < 4 ? j : j + step) * 4 + (c & 3);
+                if (va[c] > best || (va[c] == best && i < bi)) best = va[c], bi = i;
+            }
+        }
+    } else {
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+            const float v = row[i];
+            if (v > best || (v == best && i < bi)) best = v, bi = i;
+        }
     }
     __shared__ float sv[32];
     __shared__ int64_t si[32];
@@ -460,7 +476,8 @@ cudaError_t launch_add(const float *a, const float *b, float *out, int64_t n, cu
 cudaError_t launch_argmax(const float *x, int64_t rows, int64_t n, int32_t *out, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
     if (rows > 0x7fffffff || n <= 0) return cudaErrorInvalidValue;
-    argmax_kernel<<<(unsigned)rows, 256, 0, st>>>(x, n, out);
+    const bool vec4 = n % 4 == 0 && ((uintptr_t)x & 15) == 0;
+    argmax_kernel<<<(unsigned)rows, 1024, 0, st>>>(x, n, vec4, out);
     return cudaGetLastError();
 }
 

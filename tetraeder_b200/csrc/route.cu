@@ -40,6 +40,30 @@ __global__ void rms_norm_kernel(const float *__restrict__ x, const float *__rest
     }
 }
 
+// The same norm with a CTA of 256 threads per row, for batches of few rows (one warp per row would
+// leave most SMs idle): per-thread f64 partial sums of the f32 squares, a butterfly per warp, the
+// warps' sums added in order; the same f32 mean, scale and products as rms_norm_kernel.
+__global__ void __launch_bounds__(256) rms_norm_row_kernel(const float *__restrict__ x, const float *__restrict__ norm_w,
+                                                          float eps, int H, float *__restrict__ out) {
+    __shared__ double part[8];
+    const int64_t row = blockIdx.x;
+    const float *xr = x + row * H;
+    double acc = 0.0;
+    for (int i = threadIdx.x; i < H; i += 256) acc = __dadd_rn(acc, (double)__fmul_rn(xr[i], xr[i]));
+    acc = butterfly_f64(acc);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    double sum = 0.0;
+    for (int w = 0; w < 8; w++) sum = __dadd_rn(sum, part[w]);
+    const float mean = __double2float_rn(__ddiv_rn(sum, (double)H));
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    float *o = out + row * H;
+    for (int i = threadIdx.x; i < H; i += 256) {
+        const float v = __fmul_rn(xr[i], scale);
+        o[i] = norm_w ? __fmul_rn(v, norm_w[i]) : v;
+    }
+}
+
 // Router logits, H % 512 == 0: a CTA of RL_WARPS warps (one expert each) and TT tokens.  The
 // tokens' rows are staged whole in shared memory with 16-byte loads; each warp then streams its
 // expert's row with all loads of an 512-element stretch in flight.  When q8 != NULL, the CTAs of
@@ -295,6 +319,10 @@ __global__ void quantize_q8k_kernel(const float *__restrict__ x, int64_t rows, i
 cudaError_t launch_rms_norm(const float *x, const float *norm_w, float eps, int64_t T, int H, float *out,
                             cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
+    if (T <= 2048 && H >= 1024) {  // few long rows: a CTA per row
+        rms_norm_row_kernel<<<(unsigned)T, 256, 0, st>>>(x, norm_w, eps, H, out);
+        return cudaGetLastError();
+    }
     const int warps = 8;
     rms_norm_kernel<<<(unsigned)((T + warps - 1) / warps), warps * 32, 0, st>>>(x, norm_w, eps, T, H, out);
     return cudaGetLastError();
