@@ -718,8 +718,8 @@ def run_model(args, local_rank):
     return {
         "metric": "decode_tokens_per_s", "value": round(B / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": 1,
         "steps": args.steps, "warmup": W, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "Q4_K/Q6_K weights x Q8_K activations (integer MMA), f32 attention over an F16 "
-                                  "KV cache", "data": "synthetic",
+        "vs_baseline": None, "dtype": "Q4_K/Q6_K weights x Q8_K activations (integer MMA); attention in f16 MMAs with "
+                                  "f32 accumulation over an F16 KV cache", "data": "synthetic",
         "config": {"workload": "C3 Qwen3-30B-A3B-shaped model, batched decode", "sequences": B, "context": ctx,
                    "n_layer": hp.n_layer, "n_embd": hp.n_embd, "n_head": hp.n_head, "n_head_kv": hp.n_head_kv,
                    "head_dim": hp.head_dim, "n_expert": hp.n_expert, "n_expert_used": hp.n_expert_used,

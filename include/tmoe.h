@@ -276,7 +276,8 @@ TMOE_API int tmoe_dequantize(int32_t type, const void *in, int64_t n, float *out
  * out [T][N], on the decode GEMV.  reuse_x != 0: x is the activations of the previous
  * tmoe_mul_mat call on this handle with the same K, T and weight family (Q4_K or Q6_K), whose Q8_K
  * rows are reused (the Q, K and V projections of one normalised input).  The workspace is sized on
- * first use: make a first call outside a stream capture. */
+ * first use: make a first call outside a stream capture.  It belongs to the handle, so calls that
+ * may run at the same time (on different streams) need a handle each. */
 TMOE_API int tmoe_mul_mat(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1, int64_t K, int64_t N,
                           const float *x, int64_t T, int32_t reuse_x, float *out);
 TMOE_API int tmoe_get_rows(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1, int64_t K,

@@ -49,6 +49,14 @@ class Qwen3MoeModel:
         self.moe = MoeLayer(hp.n_embd, hp.n_ff_exp, hp.n_expert, hp.n_expert_used, gate_type=gt, up_type=ut,
                             down_type=dt, max_tokens=max_batch, device=device, rms_eps=hp.rms_eps)
         self.lib, self.h = self.moe.lib, self.moe.h
+        # The K and V projections run beside Q, each on a stream of its own with a handle of its own
+        # (a handle's projection workspace serves one stream at a time): at decode batch sizes each
+        # projection is a few hundred GEMV items, too few to fill the SMs alone.
+        self._lanes = [MoeLayer(512, 256, 8, 2, gate_type=TYPE_Q4_K, up_type=TYPE_Q4_K, down_type=TYPE_Q4_K,
+                                max_tokens=4, device=device) for _ in range(2)]
+        self._side = [torch.cuda.Stream(device=self.device) for _ in range(2)]
+        self._fork = torch.cuda.Event()
+        self._join = [torch.cuda.Event() for _ in range(2)]
         self.experts = [ExpertWeights(*(self.w[f"blk.{il}.{n}.weight"].data.view(hp.n_expert, -1,
                                                                                   self.w[f"blk.{il}.{n}.weight"].nb1)
                                         for n in ("ffn_gate_exps", "ffn_up_exps", "ffn_down_exps")))
@@ -145,13 +153,15 @@ class Qwen3MoeModel:
         return cls(hp, w, max_batch, n_ctx, device)
 
     # -- the step ------------------------------------------------------------------------
-    def _mm(self, m: Matrix, x: torch.Tensor, out: torch.Tensor, B: int, st, reuse: bool = False):
-        _lib.check(self.lib.tmoe_mul_mat(self.h, st, m.type, C.c_void_p(m.data.data_ptr()), m.nb1, m.cols, m.rows,
-                                         _ptr(x), B, int(reuse), _ptr(out)), self.h)
+    def _mm(self, m: Matrix, x: torch.Tensor, out: torch.Tensor, B: int, st, reuse: bool = False, h=None):
+        h = self.h if h is None else h
+        _lib.check(self.lib.tmoe_mul_mat(h, st, m.type, C.c_void_p(m.data.data_ptr()), m.nb1, m.cols, m.rows,
+                                         _ptr(x), B, int(reuse), _ptr(out)), h)
 
     def _step(self, tokens: torch.Tensor, pos: torch.Tensor, B: int, stream):
         hp, w, L, h = self.hp, self.w, self.lib, self.h
         st = _stream(stream)
+        main = torch.cuda.current_stream(self.device) if stream is None else stream
         d, nh, nkv, H = hp.head_dim, hp.n_head, hp.n_head_kv, hp.n_embd
         chk = lambda rc: _lib.check(rc, h)  # noqa: E731
         emb = w["token_embd.weight"]
@@ -161,10 +171,14 @@ class Qwen3MoeModel:
             p = f"blk.{il}."
             chk(L.tmoe_rms_norm(h, st, _ptr(self.x), _ptr(w[p + "attn_norm.weight"]), hp.rms_eps, B, H, _ptr(self.cur)))
             wq, wk, wv = w[p + "attn_q.weight"], w[p + "attn_k.weight"], w[p + "attn_v.weight"]
+            self._fork.record(main)
+            for side, lane, wm, out, join in zip(self._side, self._lanes, (wk, wv), (self.k, self.v), self._join):
+                side.wait_event(self._fork)
+                self._mm(wm, self.cur, out, B, _stream(side), h=lane.h)
+                join.record(side)
             self._mm(wq, self.cur, self.q, B, st)
-            # the Q8_K rows of cur are reused by a projection of the same type as the previous one
-            self._mm(wk, self.cur, self.k, B, st, reuse=wk.type == wq.type)
-            self._mm(wv, self.cur, self.v, B, st, reuse=wv.type == wk.type)
+            for join in self._join:
+                main.wait_event(join)
             if d % 32 == 0 and d <= 128:  # the two norms and the two RoPEs in one launch
                 chk(L.tmoe_qk_norm_rope(h, st, _ptr(self.q), _ptr(self.k), _ptr(w[p + "attn_q_norm.weight"]),
                                         _ptr(w[p + "attn_k_norm.weight"]), _ptr(pos), B, nh, nkv, d, hp.n_rot,
@@ -212,6 +226,10 @@ class Qwen3MoeModel:
 
     def check(self):
         self.moe.check()
+        for lane in self._lanes:
+            lane.check()
 
     def close(self):
+        for lane in self._lanes:
+            lane.close()
         self.moe.close()
