@@ -876,10 +876,12 @@ cudaError_t launch_gemv(int wt, bool gateup, const GemvArgs &a, int max_items, i
     if (a.n_pairs < 0 || a.n_pairs >= (1 << 24) || a.x_div < 1 || a.x_div > (1 << 16) ||
         (int64_t)max_items * (a.N / (ITEM_ROWS / 2)) >= (1 << 24))
         return cudaErrorInvalidValue;
-    // contiguous rows, 16-byte aligned expert strides (the fills' alignment arithmetic rests on it)
+    // Q6_K: contiguous rows (whole-row fills); Q4_K: rows at least a row apart on 16-byte strides
+    // (tensor-map fills: a matrix's K slices as experts); 16-byte aligned expert strides
     const size_t rb = (size_t)(wt == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES) * (a.K / TMOE_QK);
-    if (a.nb1_0 != rb || (a.nb2_0 & 15u) || ((uintptr_t)a.w0 & 15u)) return cudaErrorInvalidValue;
-    if (gateup && (a.nb1_1 != rb || (a.nb2_1 & 15u) || ((uintptr_t)a.w1 & 15u))) return cudaErrorInvalidValue;
+    auto rows_ok = [&](size_t nb1) { return wt == TMOE_WT_Q4K ? nb1 >= rb && nb1 % 16 == 0 : nb1 == rb; };
+    if (!rows_ok(a.nb1_0) || (a.nb2_0 & 15u) || ((uintptr_t)a.w0 & 15u)) return cudaErrorInvalidValue;
+    if (gateup && (!rows_ok(a.nb1_1) || (a.nb2_1 & 15u) || ((uintptr_t)a.w1 & 15u))) return cudaErrorInvalidValue;
     if (wt == TMOE_WT_Q4K)
         return gateup ? launch_t<TMOE_WT_Q4K, true>(a, max_items, sm_count, st)
                       : launch_t<TMOE_WT_Q4K, false>(a, max_items, sm_count, st);

@@ -107,8 +107,9 @@ cudaError_t launch_attn_decode(const float *q, const float *k, const float *v, _
                                const int32_t *pos, int B, int n_head, int n_kv, int head_dim, int n_ctx, float scale,
                                float *part, float *out, int sm_count, int *err, cudaStream_t st);
 cudaError_t launch_add(const float *a, const float *b, float *out, int64_t n, cudaStream_t st);
-cudaError_t launch_dense_prep(int T, int group, int4 *active, int32_t *n_active, int32_t *perm, int *counters,
+cudaError_t launch_dense_prep(int T, int group, int ks, int4 *active, int32_t *n_active, int32_t *perm, int *counters,
                               int n_counters, cudaStream_t st);
+cudaError_t launch_splitk_sum(const float *part, int64_t T, int N, int ks, float *out, cudaStream_t st);
 cudaError_t launch_argmax(const float *x, int64_t rows, int64_t n, int32_t *out, cudaStream_t st);
 
 // gemv.cu

@@ -380,23 +380,52 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
 }
 
 // The dispatch of a dense product (one matrix, every row of x): the T rows in groups of `group`
-// tokens, each group an active entry of the same matrix (active[j] = {0, j * group, its end}), so
-// that the GEMV spreads the matrix's row tiles times the groups over the SMs (a group's second
-// read of the rows comes from L2); pairs in order; the GEMV's work counters zeroed.
-__global__ void dense_prep_kernel(int T, int group, int4 *__restrict__ active, int32_t *__restrict__ n_active,
+// tokens, each group an active entry of the same matrix, so that the GEMV spreads the matrix's row
+// tiles times the groups over the SMs (a group's second read of the rows comes from L2); the GEMV's
+// work counters zeroed.  With ks > 1 the product is split along K into ks slices, slice s being
+// "expert" s of the GEMV (the matrix's columns s*K/ks.., an expert stride of one slice's bytes) and
+// token t's slice s its pair t*ks + s: the Q8_K rows of x [T][K] read as [T*ks][K/ks], the partial
+// outputs as [T][ks][N].  Entry j = s * ng + g holds slice s of group g; perm[s*T + t] = t*ks + s.
+__global__ void dense_prep_kernel(int T, int group, int ks, int4 *__restrict__ active, int32_t *__restrict__ n_active,
                                   int32_t *__restrict__ perm, int *__restrict__ counters, int n_counters) {
     const int ng = (T + group - 1) / group;
-    for (int i = threadIdx.x; i < T; i += blockDim.x) perm[i] = i;
-    for (int j = threadIdx.x; j < ng; j += blockDim.x) active[j] = make_int4(0, j * group, min(T, (j + 1) * group), 0);
+    for (int i = threadIdx.x; i < T * ks; i += blockDim.x) perm[i] = (i % T) * ks + i / T;
+    for (int j = threadIdx.x; j < ng * ks; j += blockDim.x) {
+        const int s = j / ng, g = j % ng;
+        active[j] = make_int4(s, s * T + g * group, s * T + min(T, (g + 1) * group), 0);
+    }
     if (threadIdx.x < n_counters) counters[threadIdx.x] = 0;
-    if (threadIdx.x == 0) n_active[0] = ng;
+    if (threadIdx.x == 0) n_active[0] = ng * ks;
+}
+
+// out[t][n] = sum over s of part[t][s][n], the slices added in order (the same sums every call).
+__global__ void splitk_sum_kernel(const float *__restrict__ part, int64_t T, int N, int ks, float *__restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // a group of 4 outputs
+    const int64_t n4 = (int64_t)N / 4;
+    if (i >= T * n4) return;
+    const int64_t t = i / n4, c = i % n4;
+    const float4 *p = reinterpret_cast<const float4 *>(part + t * ks * (int64_t)N) + c;
+    float4 a = __ldcs(p);
+    for (int s = 1; s < ks; s++) {
+        const float4 b = __ldcs(p + s * n4);
+        a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+    }
+    reinterpret_cast<float4 *>(out + t * (int64_t)N)[c] = a;
 }
 
 // ------------------------------------------------------------------ launchers
-cudaError_t launch_dense_prep(int T, int group, int4 *active, int32_t *n_active, int32_t *perm, int *counters,
+cudaError_t launch_dense_prep(int T, int group, int ks, int4 *active, int32_t *n_active, int32_t *perm, int *counters,
                               int n_counters, cudaStream_t st) {
-    if (n_counters > 256 || group < 1) return cudaErrorInvalidValue;
-    dense_prep_kernel<<<1, 256, 0, st>>>(T, group, active, n_active, perm, counters, n_counters);
+    if (n_counters > 256 || group < 1 || ks < 1 || (int64_t)T * ks >= (1 << 24)) return cudaErrorInvalidValue;
+    dense_prep_kernel<<<1, 256, 0, st>>>(T, group, ks, active, n_active, perm, counters, n_counters);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_splitk_sum(const float *part, int64_t T, int N, int ks, float *out, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if (N % 4 || ks < 1 || ((uintptr_t)part & 15) || ((uintptr_t)out & 15)) return cudaErrorInvalidValue;
+    const int64_t n = T * (N / 4);
+    splitk_sum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, T, N, ks, out);
     return cudaGetLastError();
 }
 

@@ -40,6 +40,7 @@ struct tmoe_handle {
     const float *dense_x = nullptr;
     int dense_wt = -1;
     int64_t dense_k = 0, dense_t = 0;
+    bool dense_nosplit = false;  // the GEMV took no tensor map over a matrix's K slices
     // routing
     float *logits = nullptr;
     int32_t *ids = nullptr;
@@ -828,8 +829,16 @@ int tmoe_mul_mat(tmoe_handle *h, void *stream, int32_t type, const void *W, size
     // (C3 decode at 16 sequences: 10.7 ms per step against 12.0 with one group)
     const int kGroup = T >= 64 ? 16 : T >= 16 ? 4 : 1;
     const int n_groups = (int)((T + kGroup - 1) / kGroup);
-    const size_t o_act = lay((size_t)n_groups * 16), o_na = lay(4), o_perm = lay((size_t)T * 4 + 16),
-                 o_work = lay(kCounters * 4);
+    // Q4_K: split K in ks slices (each at least one two-super-block fill) while the items (row tiles x
+    // groups x slices) would leave warps idle; the slices' partial outputs are then added in order.
+    const int nb = (int)(K / 256);
+    int ks = 1;
+    if (wt == TMOE_WT_Q4K && N % 4 == 0 && !h->dense_nosplit)
+        while (nb % (2 * ks) == 0 && nb / (2 * ks) >= 2 && (N / 16) * n_groups * ks < 8LL * h->sm_count &&
+               T * 2 * ks < (1 << 24))
+            ks *= 2;
+    const size_t o_act = lay((size_t)n_groups * ks * 16), o_na = lay(4), o_perm = lay((size_t)T * ks * 4 + 16),
+                 o_work = lay(kCounters * 4), o_part = ks > 1 ? lay((size_t)T * ks * N * 4) : 0;
     cudaError_t e;
     if (need > h->dense_ws_bytes) {  // grows on first use (outside any stream capture)
         if (reuse) return fail(h, TMOE_E_INVALID, "reuse_x before the workspace exists");
@@ -850,23 +859,35 @@ int tmoe_mul_mat(tmoe_handle *h, void *stream, int32_t type, const void *W, size
     int4 *act = (int4 *)(base + o_act);
     int32_t *na = (int32_t *)(base + o_na), *perm = (int32_t *)(base + o_perm);
     int *work = (int *)(base + o_work);
+    float *part = (float *)(base + o_part);
     if (!reuse) {
         if ((e = tmoe::launch_quantize_q8k(x, T, (int)K, nullptr, tmoe::Q8Rows{q, d, bl, bh, wt}, st)) != cudaSuccess)
             return cuda_fail(h, e, "quantize x");
         h->dense_x = x, h->dense_wt = wt, h->dense_k = K, h->dense_t = T;
     }
-    if ((e = tmoe::launch_dense_prep((int)T, kGroup, act, na, perm, work, kCounters, st)) != cudaSuccess)
-        return cuda_fail(h, e, "mul_mat prep");
-    tmoe::GemvArgs g{};
-    g.w0 = (const uint8_t *)W;
-    g.nb1_0 = nb1, g.nb2_0 = align_up(nb1 * (size_t)N, 16);
-    g.K = (int)K, g.N = (int)N;
-    g.xq = q, g.xd = d, g.xbl = bl, g.xbh = bh, g.x_div = 1;
-    g.perm = perm, g.active = act, g.n_active = na;
-    g.n_slots = 1, g.max_active = n_groups, g.n_pairs = (int)T, g.work = work;
-    g.out = out, g.err = h->err;
-    if ((e = tmoe::launch_gemv(wt, false, g, n_groups, h->sm_count, st)) != cudaSuccess)
-        return cuda_fail(h, e, "mul_mat gemv");
+    for (;;) {
+        if ((e = tmoe::launch_dense_prep((int)T, kGroup, ks, act, na, perm, work, kCounters, st)) != cudaSuccess)
+            return cuda_fail(h, e, "mul_mat prep");
+        tmoe::GemvArgs g{};
+        g.w0 = (const uint8_t *)W;
+        g.nb1_0 = nb1, g.nb2_0 = ks > 1 ? nb1 / ks : align_up(nb1 * (size_t)N, 16);
+        g.K = (int)(K / ks), g.N = (int)N;
+        g.xq = q, g.xd = d, g.xbl = bl, g.xbh = bh, g.x_div = 1;
+        g.perm = perm, g.active = act, g.n_active = na;
+        g.n_slots = ks, g.max_active = n_groups * ks, g.n_pairs = (int)(T * ks), g.work = work;
+        g.out = ks > 1 ? part : out, g.err = h->err;
+        e = tmoe::launch_gemv(wt, false, g, n_groups * ks, h->sm_count, st);
+        if (e == cudaErrorInvalidValue && ks > 1) {  // no tensor map over the slices: unsplit from now on
+            cudaGetLastError();
+            h->dense_nosplit = true;
+            ks = 1;
+            continue;
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "mul_mat gemv");
+        break;
+    }
+    if (ks > 1 && (e = tmoe::launch_splitk_sum(part, T, (int)N, ks, out, st)) != cudaSuccess)
+        return cuda_fail(h, e, "mul_mat split-K sum");
     return TMOE_OK;
 }
 
