@@ -141,7 +141,8 @@ def test_attention_op_against_float64(hd, nh, nkv, ctx):
 
 
 @pytest.mark.parametrize("qtype,K,N,T", [(12, 2048, 4096, 64), (14, 2048, 512, 3), (12, 512, 151936 // 64 * 16, 5),
-                                         (12, 4096, 2048, 64), (12, 2048, 512, 50), (12, 1024, 256, 1)])
+                                         (12, 4096, 2048, 64), (12, 2048, 512, 50), (12, 1024, 256, 1),
+                                         (14, 2048, 512, 64)])
 def test_mul_mat_against_the_oracle(qtype, K, N, T):
     """tmoe_mul_mat (one matrix, every row of x) against the oracle's mul_mat_id with one expert, and
     reuse_x: a second matrix of the same family over the same x, and the guard on a mismatch.  The
