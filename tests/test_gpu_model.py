@@ -232,3 +232,33 @@ def test_argmax_first_index(rows, n):
     layer.check()
     assert np.array_equal(out.cpu().numpy(), np.argmax(x, axis=1).astype(np.int32))
     layer.close()
+
+
+def test_mul_mat_beyond_l2_matches_row_slices():
+    """A matrix larger than L2 (here 67.7 MB of Q4_K) takes the batch as one entry, its token passes
+    over each row tile back to back; its rows must equal, bit for bit, those of the same matrix
+    multiplied in two halves below the threshold (16-token groups: the same token columns per
+    pass, the same per-row sums).  The halves' path is held to the oracle by the tests above."""
+    import ctypes as C
+    K, N, T = 256, 470016, 64
+    layer = tb.MoeLayer(512, 256, 8, 2, gate_type=12, up_type=12, down_type=12, max_tokens=4)
+    lib, h = layer.lib, layer.h
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    w32 = torch.randn((N, K), device="cuda", generator=g) * 0.05
+    W = torch.empty((N, 144), dtype=torch.uint8, device="cuda")
+    assert lib.tmoe_quantize(12, C.c_void_p(w32.data_ptr()), N, K, C.c_void_p(W.data_ptr()),
+                             C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    del w32
+    x = torch.randn((T, K), device="cuda", generator=g)
+    full = torch.empty((T, N), device="cuda")
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    assert lib.tmoe_mul_mat(h, None, 12, P(W), 144, K, N, P(x), T, 0, P(full)) == 0
+    halves = []
+    for r0, r1 in ((0, N // 2), (N // 2, N)):
+        o = torch.empty((T, r1 - r0), device="cuda")
+        assert lib.tmoe_mul_mat(h, None, 12, P(W[r0:r1]), 144, K, r1 - r0, P(x), T, 0, P(o)) == 0
+        halves.append(o)
+    layer.check()
+    assert torch.equal(full, torch.cat(halves, dim=1))
+    layer.close()

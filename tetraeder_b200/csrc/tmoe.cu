@@ -827,7 +827,10 @@ int tmoe_mul_mat(tmoe_handle *h, void *stream, int32_t type, const void *W, size
     // token groups, each an active entry of the matrix: 16 tokens (one pass of the GEMV's two-group
     // kernel) from 64 tokens on, fewer below, so that small batches still spread over the SMs
     // (C3 decode at 16 sequences: 10.7 ms per step against 12.0 with one group)
-    const int kGroup = T >= 64 ? 16 : T >= 16 ? 4 : 1;
+    // A matrix well beyond L2 (the output head) takes the batch as one entry instead: its token
+    // passes over a row tile then follow one another and re-read the tile from L2, where separate
+    // groups would each stream the whole matrix from HBM.
+    const int kGroup = (size_t)N * nb1 > (64u << 20) ? (int)T : T >= 64 ? 16 : T >= 16 ? 4 : 1;
     const int n_groups = (int)((T + kGroup - 1) / kGroup);
     // Q4_K: split K in ks slices (each at least one two-super-block fill) while the items (row tiles x
     // groups x slices) would leave warps idle; the slices' partial outputs are then added in order.
