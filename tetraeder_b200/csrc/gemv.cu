@@ -196,6 +196,36 @@ __device__ __forceinline__ void q4_block(const uint8_t *ra, const uint8_t *rb, c
     for (int G = 0; G < NGR; G++)
 #pragma unroll
         for (int i = 0; i < 4; i++) il[G][i] = ih[G][i] = 0;
+    if constexpr (NGR == 1) {  // one group: both sub-block pairs' MMAs before their scale multiply-adds
+#pragma unroll
+        for (int jj = 0; jj < 4; jj += 2) {
+            int dl[2][4], dh[2][4];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int j = jj + u;
+                const uint2 wa = *reinterpret_cast<const uint2 *>(ra + 16 + 32 * j + 8 * t4);
+                const uint2 wb = *reinterpret_cast<const uint2 *>(rb + 16 + 32 * j + 8 * t4);
+                mma_k32_u8s8(dl[u], wa.x & NIB, wb.x & NIB, wa.y & NIB, wb.y & NIB, x[0].l[j].x, x[0].l[j].y);
+                mma_k32_u8s8(dh[u], wa.x & ~NIB, wb.x & ~NIB, wa.y & ~NIB, wb.y & ~NIB, x[0].h[j].x, x[0].h[j].y);
+            }
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int j = jj + u;
+                const uint32_t sa = j < 2 ? sca0 : sca1, sb = j < 2 ? scb0 : scb1;
+                const int bi = 2 * (j & 1);
+                const int sla = ubyte(sa, bi), sha = ubyte(sa, bi + 1);
+                const int slb = ubyte(sb, bi), shb = ubyte(sb, bi + 1);
+                il[0][0] += sla * dl[u][0];
+                il[0][1] += sla * dl[u][1];
+                il[0][2] += slb * dl[u][2];
+                il[0][3] += slb * dl[u][3];
+                ih[0][0] += sha * dh[u][0];
+                ih[0][1] += sha * dh[u][1];
+                ih[0][2] += shb * dh[u][2];
+                ih[0][3] += shb * dh[u][3];
+            }
+        }
+    } else
 #pragma unroll
     for (int j = 0; j < 4; j++) {
         const uint2 wa = *reinterpret_cast<const uint2 *>(ra + 16 + 32 * j + 8 * t4);
