@@ -23,6 +23,7 @@ from __future__ import annotations
 import argparse
 import datetime
 import faulthandler
+import hashlib
 import json
 import os
 import statistics
@@ -214,8 +215,10 @@ def run_ours(args, rank, world, local_rank):
     gen = torch.Generator(device=dev)
     gen.manual_seed(args.seed + 1 + (rank if a2a else 0))  # a2a: every rank has tokens of its own
     x_dev = torch.randn((T, H), generator=gen, device=dev)
-    x_host = x_dev.cpu().pin_memory()
-    out_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    # e2e: every layer call takes its own input from pinned host memory and returns its output there
+    x_host = torch.randn((L, T, H), generator=torch.Generator().manual_seed(args.seed + 2)).pin_memory()
+    out_host = torch.empty((L, T, H), dtype=torch.float32).pin_memory()
+    x_call = [torch.empty((T, H), device=dev) for _ in range(L)]
     layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=DOWN_T,
                         max_tokens=world * T if a2a else T, device=local_rank)
     outs = [torch.empty((T, H), device=dev) for _ in range(L)]
@@ -293,10 +296,33 @@ def run_ours(args, rank, world, local_rank):
     units = (1 if ep and not a2a else world) * args.steps * L * T
     value = units / (ms / 1e3)
 
+    # e2e: per layer call, the H2D of its input and the D2H of its output, on two copy streams
+    # pipelined with the calls (call l+1's input lands while call l computes; call l's output leaves
+    # while call l+1 computes); events keep each buffer's reuse in order across steps
+    h2d_s, d2h_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    ev_in, ev_done, ev_out = [ev() for _ in range(L)], [ev() for _ in range(L)], [ev() for _ in range(L)]
+    for li in range(L):  # recorded once, so the first step's waits are satisfied
+        ev_done[li].record()
+        ev_out[li].record()
+
     def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        one_step(x_dev)
-        out_host.copy_(outs[-1], non_blocking=True)
+        main = torch.cuda.current_stream()
+        for li in range(L):
+            with torch.cuda.stream(h2d_s):
+                h2d_s.wait_event(ev_done[li])  # the last step's call li no longer reads x_call[li]
+                x_call[li].copy_(x_host[li], non_blocking=True)
+                ev_in[li].record(h2d_s)
+        for li in range(L):
+            main.wait_event(ev_in[li])
+            main.wait_event(ev_out[li])  # the last step's output li has left the device
+            call(li, x_call[li])
+            ev_done[li].record(main)
+            with torch.cuda.stream(d2h_s):
+                d2h_s.wait_event(ev_done[li])
+                out_host[li].copy_(outs[li], non_blocking=True)
+                ev_out[li].record(d2h_s)
+        main.wait_stream(d2h_s)
 
     e2e_ms = timed(e2e_step, args.steps, max(args.warmup, 3))
     e2e_value = units / (e2e_ms / 1e3)
@@ -381,9 +407,10 @@ def run_ours(args, rank, world, local_rank):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": dtype, "data": "synthetic",
         "config": workload(args, world), "roofline": roofline, "layer_roofline": layer_roof,
-        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
-                "d2h_bytes_per_step": T * H * 4, "ms_per_step": round(e2e_ms / args.steps, 4),
-                "path": "tmoe_layer C-ABI calls (ctypes) x 48 + pinned H2D/D2H"},
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": L * T * H * 4,
+                "d2h_bytes_per_step": L * T * H * 4, "ms_per_step": round(e2e_ms / args.steps, 4),
+                "path": f"{L} tmoe_layer C-ABI calls (ctypes, eager) per step, each with its own pinned H2D input "
+                        "and D2H output, copies pipelined with the calls on two copy streams"},
         "gpu_launches": int(launches_per_call * L * args.steps), "clocks": clocks,
     }
     if a2a:
@@ -787,18 +814,28 @@ def load_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback (profiling recipe)"}
 
 
+def gemv_source_sha16():
+    """The first 16 hex digits of sha256(csrc/gemv.cu): the source the committed ncu figures are of."""
+    with open(os.path.join(ROOT, "tetraeder_b200", "csrc", "gemv.cu"), "rb") as f:
+        return hashlib.sha256(f.read()).hexdigest()[:16]
+
+
 def traffic_from_profiles(kernel):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, used only when
+    the summary was taken of the gemv.cu that is built now (its `source_sha16` line); else None."""
     path = os.path.join(ROOT, "profiles", "gemv_decode_c2.md")
     if not os.path.exists(path):
         return None
+    traffic, sha = None, None
     for line in open(path):
         if line.startswith(f"traffic_bytes_per_launch[{kernel}]:"):
             try:
-                return int(float(line.split(":", 1)[1].strip()))
+                traffic = int(float(line.split(":", 1)[1].strip()))
             except ValueError:
                 return None
-    return None
+        elif line.startswith("source_sha16[gemv.cu]:"):
+            sha = line.split(":", 1)[1].strip()
+    return traffic if sha == gemv_source_sha16() else None
 
 
 # ---------------------------------------------------------------------------------------- CPU

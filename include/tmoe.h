@@ -108,9 +108,23 @@ TMOE_API const char *tmoe_last_error(const tmoe_handle *h);
 /* Synchronises `stream`, then reads and clears the device error flag. */
 TMOE_API int tmoe_check(tmoe_handle *h, void *stream);
 
+/* Holds `stream` until *flag == value, on the device, under the kernels' bounded-wait rule: after
+ * limit_ns nanoseconds (<= 0 or above one second: one second) the wait gives up, latches the
+ * handle's device error flag and lets the stream go on, so the next tmoe_check returns
+ * TMOE_E_DEVICE and the context stays usable.  `flag` is a device address: a word in device
+ * memory or in pinned, device-mapped host memory that the host writes (a host watchdog's gate on
+ * a step).  It must not be a word that another kernel on the same device is to set: kernels that
+ * wait on one another are not guaranteed to run at the same time.  No counterpart in the
+ * reference, whose executor waits on the host (crates/executor/src/exec.rs:164-177); this is the
+ * device side of the same rule, and the way to see a bounded device wait run out without a fault. */
+TMOE_API int tmoe_wait_flag(tmoe_handle *h, void *stream, const int32_t *flag, int32_t value, int64_t limit_ns);
+
 /* ggml mul_mat_id: out[t][j][:] = W[ids[t][j]] . b[t][b1 == 1 ? 0 : j][:]  (f32 [T][n_used][N]).
  * W: [K, N, n_w] of `type` (Q4_K or Q6_K, K % 256 == 0) with strides nb1/nb2;
- * b: f32 [T][b1][K], b1 == 1 or n_used; activations go through Q8_K as on ggml's CPU path. */
+ * b: f32 [T][b1][K], b1 == 1 or n_used; activations go through Q8_K as on ggml's CPU path.
+ * Its scratch is the handle's, allocated by tmoe_create for T * b1 and T * n_used up to
+ * max_tokens * n_expert_used and K up to max(n_embd, n_ff); a call beyond that returns
+ * TMOE_E_INVALID.  The call allocates nothing and does not synchronise. */
 TMOE_API int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1,
                     size_t nb2, int64_t K, int64_t N, int64_t n_w, const float *b, int64_t b1,
                     const int32_t *ids, int64_t n_used, int64_t T, float *out);
@@ -120,12 +134,16 @@ TMOE_API int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const v
  * budget, or where a cudaMalloc would synchronise the device in the middle of a step).  The same
  * arguments, arithmetic and results as tmoe_mul_mat_id; its scratch (the Q8_K rows of b, the
  * dispatch buffers) lives in a 2 MiB module-global device array instead of the handle's growable
- * buffer.  Limit: about T * b1 * K bytes of Q8_K rows plus T * n_used * 4 bytes of pair indices
- * must fit in 2 MiB (e.g. T * b1 <= 128 rows at K = 8192 with n_used = 8); larger calls return
- * TMOE_E_INVALID.  The first call on a device looks the array up (cudaGetSymbolAddress), so make
- * it before any stream capture.  The array is shared by every handle of the process on that
- * device: overlapping calls (on different streams, or from different threads) race on it and
- * must be ordered by the caller. */
+ * buffer.  Limit: with rows = T * b1, P = T * n_used and nbw = 2 for Q4_K, 4 for Q6_K, the scratch
+ * is rows*K*(1 + (4 + 8*nbw)/256) + 4*P + 16 bytes in five parts, each rounded up to 256 bytes,
+ * plus 25,344 bytes of per-slot tables and counters, and it must fit in 2 MiB (2,097,152 bytes);
+ * e.g. T <= 233 at K = 8192 for Q4_K with b1 = 1 and n_used = 8.  Larger calls return
+ * TMOE_E_INVALID.
+ * The first call on a device looks the array up (cudaGetSymbolAddress), so make it before any
+ * stream capture; the address is then cached per device, and a cudaDeviceReset invalidates it
+ * (do not use this entry point after resetting the device in the same process).  The array is
+ * shared by every handle of the process on that device: overlapping calls (on different
+ * streams, or from different threads) race on it and must be ordered by the caller. */
 TMOE_API int tmoe_mul_mat_id_noalloc(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1,
                                      size_t nb2, int64_t K, int64_t N, int64_t n_w, const float *b, int64_t b1,
                                      const int32_t *ids, int64_t n_used, int64_t T, float *out);

@@ -179,6 +179,32 @@ def test_mul_mat_id_30b_gate_up_shape():
     assert float(np.abs(got - want).max()) / scale <= 1e-4
 
 
+def test_mul_mat_id_allocates_nothing_within_the_create_bound():
+    """The handle's mul_mat_id scratch is sized by tmoe_create (T*b1 and T*n_used up to
+    max_tokens*n_expert_used, K up to max(n_embd, n_ff)): calls within it leave the device's free
+    memory as it was, and a call beyond it is refused before any launch."""
+    H, I, E, used, T = 2048, 768, 32, 8, 64
+    rng = np.random.default_rng(11)
+    W = cuda(quantized_experts(rng, O.TYPE_Q6_K, E, H, I, exact=False))
+    b = cuda(rng.uniform(-1, 1, (T, used, I)).astype(np.float32))
+    ids = cuda(np.stack([rng.permutation(E)[:used] for _ in range(T)]).astype(np.int32))
+    layer = tb.MoeLayer(H, I, E, used, max_tokens=T)
+    out = torch.empty((T, used, H), device="cuda")
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        layer.mul_mat_id(O.TYPE_Q6_K, W, b, ids, out=out)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0, "mul_mat_id allocated device memory"
+    layer.check()
+    want = O.mul_mat_id(O.TYPE_Q6_K, host(W), I, H, E, host(b), host(ids))
+    assert float(np.abs(host(out) - want).max()) / float(np.abs(want).max()) <= 1e-4
+    big = torch.zeros((2 * T, used, I), device="cuda")
+    with pytest.raises(tb.TmoeError, match="TMOE_E_INVALID"):
+        layer.mul_mat_id(O.TYPE_Q6_K, W, big, cuda(np.zeros((2 * T, used), np.int32)))
+    layer.close()
+
+
 # ------------------------------------------------------------------------------------ layer
 def _layer_case(H, I, E, k, T, gate_t, down_t, seed, exact):
     rng = np.random.default_rng(seed)

@@ -59,3 +59,39 @@ def test_noalloc_rejects_calls_beyond_its_scratch():
     assert tb._lib.ERRORS.get(rc) == "TMOE_E_INVALID"
     assert b"scratch" in layer.lib.tmoe_last_error(layer.h)
     layer.close()
+
+
+def _scratch_bytes(rows, K, P, qt):
+    """The scratch size the header states for one call (five parts rounded up to 256 bytes, plus
+    25,344 bytes of per-slot tables and counters)."""
+    al = lambda v: (v + 255) // 256 * 256
+    nbw = 2 if qt == O.TYPE_Q4_K else 4
+    nb = K // 256
+    return al(rows * K) + al(rows * nb * 4) + 2 * al(rows * nb * nbw * 4) + al(P * 4 + 16) + 25344
+
+
+def test_noalloc_accepts_the_largest_call_that_fits_and_rejects_the_next():
+    K, N, E, used = 2048, 16, 16, 8
+    T = 1
+    while _scratch_bytes(T + 1, K, (T + 1) * used, O.TYPE_Q4_K) <= 2 << 20:
+        T += 1
+    rng = XorShift(0xB0B)
+    W = torch.from_numpy(O.quantize(O.TYPE_Q4_K, rng.f32(E * N * K).reshape(E, N, K))).cuda()
+    layer = tb.MoeLayer(K, 768, E, used, max_tokens=T + 1)
+    b = torch.from_numpy(rng.f32((T + 1) * K).reshape(T + 1, 1, K)).cuda()
+    ids = torch.from_numpy(make_ids(rng, E, used, T + 1, 10)).cuda()
+    for call in range(2):
+        want = torch.full((T, used, N), float("nan"), device="cuda")
+        got = torch.full((T, used, N), float("nan"), device="cuda")
+        assert _call(layer, "tmoe_mul_mat_id", O.TYPE_Q4_K, W, b[:T], ids[:T], want) == 0
+        rc = _call(layer, "tmoe_mul_mat_id_noalloc", O.TYPE_Q4_K, W, b[:T], ids[:T], got)
+        assert rc == 0, layer.lib.tmoe_last_error(layer.h)
+        layer.check()
+        g, w = got.cpu().numpy(), want.cpu().numpy()
+        assert float(np.abs(g - w).max()) / max(float(np.abs(w).max()), 1e-6) <= 1e-4, f"call {call} at T={T}"
+    out = torch.empty((T + 1, used, N), device="cuda")
+    rc = _call(layer, "tmoe_mul_mat_id_noalloc", O.TYPE_Q4_K, W, b, ids, out)
+    assert tb._lib.ERRORS.get(rc) == "TMOE_E_INVALID", f"T={T + 1} must not fit"
+    assert f"needs {_scratch_bytes(T + 1, K, (T + 1) * used, O.TYPE_Q4_K)} bytes".encode() in \
+        layer.lib.tmoe_last_error(layer.h)
+    layer.close()

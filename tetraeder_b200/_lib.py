@@ -46,6 +46,7 @@ SIGNATURES = {
     "tmoe_destroy": ([P], None),
     "tmoe_last_error": ([P], C.c_char_p),
     "tmoe_check": ([P, P], C.c_int),
+    "tmoe_wait_flag": ([P, P, P, I32, I64], C.c_int),
     "tmoe_mul_mat_id": ([P, P, I32, P, C.c_size_t, C.c_size_t, I64, I64, I64, P, I64, P, I64, I64, P],
                         C.c_int),
     "tmoe_mul_mat_id_noalloc": ([P, P, I32, P, C.c_size_t, C.c_size_t, I64, I64, I64, P, I64, P, I64, I64, P],

@@ -2,6 +2,7 @@
 one in-tree shared library (it travels with the repository; no JIT cache)."""
 from __future__ import annotations
 
+import concurrent.futures
 import glob
 import os
 import shutil
@@ -36,13 +37,16 @@ def build(force: bool = False, verbose: bool = False) -> str:
         return LIB
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
-    objs = []
     extra = ["-Xptxas", "-v"] if verbose else []
-    for src in sources():
-        obj = os.path.join(objdir, os.path.basename(src) + ".o")
-        cmd = [NVCC, *ARCH, *FLAGS, *extra, "-c", src, "-o", obj]
-        subprocess.run(cmd, check=True)
-        objs.append(obj)
+    objs = [os.path.join(objdir, os.path.basename(src) + ".o") for src in sources()]
+
+    def compile_one(src_obj):
+        src, obj = src_obj
+        subprocess.run([NVCC, *ARCH, *FLAGS, *extra, "-c", src, "-o", obj], check=True)
+
+    # one nvcc per source, as many at once as there are host cores
+    with concurrent.futures.ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as pool:
+        list(pool.map(compile_one, zip(sources(), objs)))
     tmp = LIB + ".tmp"
     cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-cudart", "static", "-lnccl"]
     subprocess.run(cmd, check=True)

@@ -585,6 +585,29 @@ cudaError_t launch_zero_invalid_rows(const int32_t *ids, int64_t n_pairs, int n_
     return cudaGetLastError();
 }
 
+// One thread holds the stream until *flag == value (a flag the host writes into pinned, device-mapped
+// memory, or a device word), with the kernels' bounded-wait rule: it gives up after limit_ns of
+// %globaltimer, latches TMOE_DEV_ERR_TIMEOUT and returns, so the stream moves on and the context
+// stays usable.  The backoff keeps the polling thread to a few loads per microsecond.
+__global__ void wait_flag_kernel(const volatile int32_t *flag, int32_t value, uint64_t limit_ns, int *err) {
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t nap = 32;
+    while (*flag != value) {
+        if (globaltimer_ns() - t0 > limit_ns) {
+            latch_error(err, TMOE_DEV_ERR_TIMEOUT);
+            return;
+        }
+        __nanosleep(nap);
+        if (nap < 2048) nap *= 2;
+    }
+    __threadfence_system();  // what the writer stored before the flag is visible to later kernels
+}
+
+cudaError_t launch_wait_flag(const int32_t *flag, int32_t value, uint64_t limit_ns, int *err, cudaStream_t st) {
+    wait_flag_kernel<<<1, 1, 0, st>>>(flag, value, limit_ns, err);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_combine(const float *dout, const int32_t *ids, const float *w, int64_t T, int k, int H,
                            int n_slots, float *out, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;

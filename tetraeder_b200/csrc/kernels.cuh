@@ -88,6 +88,7 @@ cudaError_t launch_zero_invalid_rows(const int32_t *ids, int64_t n_pairs, int n_
                                      cudaStream_t st);
 cudaError_t launch_combine(const float *dout, const int32_t *ids, const float *w, int64_t T, int k, int H,
                            int n_slots, float *out, cudaStream_t st);
+cudaError_t launch_wait_flag(const int32_t *flag, int32_t value, uint64_t limit_ns, int *err, cudaStream_t st);
 
 // quant.cu
 cudaError_t launch_quantize(int wt, const float *x, int64_t nblocks, uint8_t *out, cudaStream_t st);

@@ -3,6 +3,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -74,7 +75,8 @@ struct tmoe_handle {
         int32_t *row_of = nullptr, *s_ids = nullptr, *r_ids = nullptr, *s_tok = nullptr, *counts = nullptr;
         float *s_w = nullptr, *r_w = nullptr, *s_x = nullptr, *r_x = nullptr, *part = nullptr, *ret = nullptr;
     } a2a;
-    // growable scratch of tmoe_mul_mat_id
+    // scratch of tmoe_mul_mat_id, sized at create for max_tokens * n_expert_used rows of
+    // K = max(n_embd, n_ff) in the larger (Q6_K) Q8_K layout
     void *op_ws = nullptr;
     size_t op_ws_bytes = 0;
     std::string last_error;
@@ -370,6 +372,79 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
     return TMOE_OK;
 }
 
+// Scratch of one mul_mat_id call: the Q8_K rows of b (qs, d, the split sub-block sums) and the
+// dispatch buffers, each part rounded up to 256 bytes.  In bytes, with nbw = 2 (Q4_K) or 4 (Q6_K):
+// rows*K*(1 + (4 + 8*nbw)/256) + 4*P + about 25 KiB of per-slot tables, plus the rounding.
+struct MmidLayout {
+    size_t q = 0, d = 0, bl = 0, bh = 0, cnt = 0, off = 0, act = 0, na = 0, perm = 0, work = 0, need = 0;
+    MmidLayout(int wt, int64_t rows, int64_t K, int64_t P) {
+        auto lay = [&](size_t bytes) {
+            const size_t o = need;
+            need = align_up(need + bytes, 256);
+            return o;
+        };
+        const size_t nbw = (size_t)tmoe::q8_nbw(wt), nb = (size_t)(K / 256);
+        q = lay((size_t)rows * (size_t)K), d = lay((size_t)rows * nb * 4);
+        bl = lay((size_t)rows * nb * nbw * 4), bh = lay((size_t)rows * nb * nbw * 4);
+        cnt = lay(kMaxSlots * 4), off = lay((kMaxSlots + 1) * 4), act = lay(kMaxSlots * 16), na = lay(4);
+        perm = lay((size_t)P * 4 + 16), work = lay(kCounters * 4);
+    }
+};
+
+// The argument checks of both mul_mat_id entry points.  T, n_used and K are bounded before any
+// size is formed from them, so no product below can wrap.
+int check_mmid(tmoe_handle *h, int32_t type, const void *W, size_t nb1, size_t nb2, int64_t K, int64_t N,
+               int64_t n_w, const float *b, int64_t b1, const int32_t *ids, int64_t n_used, int64_t T,
+               const float *out) {
+    if (!is_kquant(type)) return fail(h, TMOE_E_UNSUPPORTED, "mul_mat_id type %d (need Q4_K or Q6_K)", type);
+    if (K <= 0 || K % 256 || K > (1 << 20) || N <= 0 || N > (1 << 20) || n_w <= 0 || n_w > kMaxSlots ||
+        n_used <= 0 || n_used > kMaxSlots || T < 0 || T > (1 << 24) || T * n_used > (1 << 30) ||
+        (b1 != 1 && b1 != n_used))
+        return fail(h, TMOE_E_INVALID, "bad mul_mat_id shape");
+    if (!W || !b || !ids || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    if (!aligned16(b)) return fail(h, TMOE_E_INVALID, "b must be 16-byte aligned");
+    if (nb1 != row_size(type, K)) return fail(h, TMOE_E_UNSUPPORTED, "rows must be contiguous (nb1 == row size)");
+    if (((uintptr_t)W & 15u) || (nb2 & 15u)) return fail(h, TMOE_E_INVALID, "W and nb2 must be 16-byte aligned");
+    if (!tmoe::gemv_rows_per_item(wt_of(type), (int)K, (int)N))
+        return fail(h, TMOE_E_UNSUPPORTED, "N=%lld rows per expert fit no GEMV row tile (multiples of 16 or 32)",
+                    (long long)N);
+    return TMOE_OK;
+}
+
+// The launches of a checked mul_mat_id call, its scratch (layout L) at `base`.
+int run_mmid(tmoe_handle *h, cudaStream_t st, int wt, const void *W, size_t nb1, size_t nb2, int64_t K, int64_t N,
+             int64_t n_w, const float *b, int64_t b1, const int32_t *ids, int64_t n_used, int64_t T, float *out,
+             const MmidLayout &L, char *base) {
+    const int64_t P = T * n_used, rows = T * b1;
+    int8_t *q = (int8_t *)(base + L.q);
+    float *d = (float *)(base + L.d);
+    uint32_t *bl = (uint32_t *)(base + L.bl), *bh = (uint32_t *)(base + L.bh);
+    int32_t *cnt = (int32_t *)(base + L.cnt), *offs = (int32_t *)(base + L.off), *na = (int32_t *)(base + L.na),
+            *perm = (int32_t *)(base + L.perm);
+    int4 *act = (int4 *)(base + L.act);
+    int *work = (int *)(base + L.work);
+    cudaError_t e;
+    if ((e = tmoe::launch_sort_pairs(ids, (int)P, (int)n_w, cnt, offs, perm, act, na, work, kCounters, h->err, st)) !=
+        cudaSuccess)
+        return cuda_fail(h, e, "sort_pairs");
+    if ((e = tmoe::launch_quantize_q8k(b, rows, (int)K, nullptr, tmoe::Q8Rows{q, d, bl, bh, wt}, st)) != cudaSuccess)
+        return cuda_fail(h, e, "quantize b");
+    if ((e = tmoe::launch_zero_invalid_rows(ids, P, (int)n_w, (int)N, out, st)) != cudaSuccess)
+        return cuda_fail(h, e, "zero rows");
+    tmoe::GemvArgs g{};
+    g.w0 = (const uint8_t *)W;
+    g.nb1_0 = nb1, g.nb2_0 = nb2;
+    g.K = (int)K, g.N = (int)N;
+    g.xq = q, g.xd = d, g.xbl = bl, g.xbh = bh, g.x_div = b1 == 1 ? (int)n_used : 1;
+    const int max_active = (int)(P < n_w ? P : n_w);
+    g.perm = perm, g.active = act, g.n_active = na;
+    g.n_slots = (int)n_w, g.max_active = max_active, g.n_pairs = (int)P, g.work = work;
+    g.out = out, g.err = h->err;
+    if ((e = tmoe::launch_gemv(wt, false, g, max_active, h->sm_count, st)) != cudaSuccess)
+        return cuda_fail(h, e, "mul_mat_id gemv");
+    return TMOE_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -412,10 +487,21 @@ int tmoe_create(const tmoe_config *cfg, tmoe_handle **out) {
         return fail(nullptr, TMOE_E_NOMEM, "cudaMalloc(%zu) failed: %s", h->ws_bytes, cudaGetErrorString(e));
     }
     carve(h, (char *)h->ws);
+    {
+        const int64_t P = (int64_t)c.max_tokens * c.n_expert_used;
+        const MmidLayout L(TMOE_WT_Q6K, P, c.n_embd > c.n_ff ? c.n_embd : c.n_ff, P);
+        if ((e = cudaMalloc(&h->op_ws, L.need)) != cudaSuccess) {
+            cudaFree(h->ws);
+            delete h;
+            return fail(nullptr, TMOE_E_NOMEM, "cudaMalloc(%zu) failed: %s", L.need, cudaGetErrorString(e));
+        }
+        h->op_ws_bytes = L.need;
+    }
     e = cudaMemset(h->ws, 0, h->ws_bytes);  // the error flag and the routing counters start at zero
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaFree(h->ws);
+        cudaFree(h->op_ws);
         delete h;
         return fail(nullptr, TMOE_E_CUDA, "cudaMemset: %s", cudaGetErrorString(e));
     }
@@ -433,6 +519,27 @@ void tmoe_destroy(tmoe_handle *h) {
     for (auto &ev : h->prof.ev)
         if (ev) cudaEventDestroy(ev);
     delete h;
+}
+
+int tmoe_wait_flag(tmoe_handle *h, void *stream, const int32_t *flag, int32_t value, int64_t limit_ns) {
+    if (!h) return TMOE_E_INVALID;
+    if (!flag || ((uintptr_t)flag & 3u)) return fail(h, TMOE_E_INVALID, "flag must be a 4-byte aligned pointer");
+    const uint64_t lim = limit_ns <= 0 || (uint64_t)limit_ns > TMOE_WAIT_LIMIT_NS ? TMOE_WAIT_LIMIT_NS
+                                                                                  : (uint64_t)limit_ns;
+    DeviceGuard dg(h->cfg.device);
+    // a pinned host word is read through its device-mapped address; pageable memory is refused
+    cudaPointerAttributes at{};
+    cudaError_t e = cudaPointerGetAttributes(&at, flag);
+    if (e != cudaSuccess) return cuda_fail(h, e, "wait flag: pointer attributes");
+    const int32_t *dflag = flag;
+    if (at.type == cudaMemoryTypeHost) {
+        if (!at.devicePointer) return fail(h, TMOE_E_INVALID, "wait flag: the host word is not device-mapped");
+        dflag = (const int32_t *)at.devicePointer;
+    } else if (at.type != cudaMemoryTypeDevice && at.type != cudaMemoryTypeManaged) {
+        return fail(h, TMOE_E_INVALID, "wait flag: the word must be device memory or pinned host memory");
+    }
+    e = tmoe::launch_wait_flag(dflag, value, lim, h->err, (cudaStream_t)stream);
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "wait flag");
 }
 
 const char *tmoe_last_error(const tmoe_handle *h) {
@@ -728,73 +835,19 @@ int tmoe_mul_mat_id(tmoe_handle *h, void *stream, int32_t type, const void *W, s
                     int64_t K, int64_t N, int64_t n_w, const float *b, int64_t b1, const int32_t *ids,
                     int64_t n_used, int64_t T, float *out) {
     if (!h) return TMOE_E_INVALID;
-    if (!is_kquant(type)) return fail(h, TMOE_E_UNSUPPORTED, "mul_mat_id type %d (need Q4_K or Q6_K)", type);
-    if (K <= 0 || K % 256 || N <= 0 || n_w <= 0 || n_w > kMaxSlots || n_used <= 0 || T < 0 ||
-        (b1 != 1 && b1 != n_used))
-        return fail(h, TMOE_E_INVALID, "bad mul_mat_id shape");
-    if (!W || !b || !ids || !out) return fail(h, TMOE_E_INVALID, "null tensor");
-    if (!aligned16(b)) return fail(h, TMOE_E_INVALID, "b must be 16-byte aligned");
-    const int wt = wt_of(type);
-    if (nb1 != row_size(type, K)) return fail(h, TMOE_E_UNSUPPORTED, "rows must be contiguous (nb1 == row size)");
-    if (((uintptr_t)W & 15u) || (nb2 & 15u)) return fail(h, TMOE_E_INVALID, "W and nb2 must be 16-byte aligned");
-    if (!tmoe::gemv_rows_per_item(wt, (int)K, (int)N))
-        return fail(h, TMOE_E_UNSUPPORTED, "N=%lld rows per expert fit no GEMV row tile (multiples of 16 or 32)",
-                    (long long)N);
+    const int rc = check_mmid(h, type, W, nb1, nb2, K, N, n_w, b, b1, ids, n_used, T, out);
+    if (rc != TMOE_OK) return rc;
+    const MmidLayout L(wt_of(type), T * b1, K, T * n_used);
+    if (L.need > h->op_ws_bytes)
+        return fail(h, TMOE_E_INVALID,
+                    "mul_mat_id needs %zu bytes of scratch for T=%lld, b1=%lld, K=%lld, n_used=%lld; the handle's "
+                    "holds %zu (sized at create for T*b1 and T*n_used up to max_tokens*n_expert_used and K up to "
+                    "max(n_embd, n_ff))",
+                    L.need, (long long)T, (long long)b1, (long long)K, (long long)n_used, h->op_ws_bytes);
     if (T == 0) return TMOE_OK;
     DeviceGuard dg(h->cfg.device);
-    cudaStream_t st = (cudaStream_t)stream;
-    const int64_t P = T * n_used, rows = T * b1;
-    // scratch: Q8_K of b, sort buffers
-    size_t need = 0;
-    auto lay = [&](size_t bytes) {
-        size_t o = need;
-        need = align_up(need + bytes, 256);
-        return o;
-    };
-    const size_t nbw = (size_t)tmoe::q8_nbw(wt);
-    size_t o_q = lay((size_t)rows * K), o_d = lay((size_t)rows * (K / 256) * 4);
-    size_t o_bl = lay((size_t)rows * (K / 256) * nbw * 4), o_bh = lay((size_t)rows * (K / 256) * nbw * 4);
-    size_t o_cnt = lay(kMaxSlots * 4), o_off = lay((kMaxSlots + 1) * 4), o_act = lay(kMaxSlots * 16), o_na = lay(4);
-    size_t o_perm = lay((size_t)P * 4 + 16), o_work = lay(kCounters * 4);
-    cudaError_t e;
-    if (need > h->op_ws_bytes) {
-        if (h->op_ws) {
-            cudaStreamSynchronize(st);
-            cudaFree(h->op_ws);
-            h->op_ws = nullptr;
-            h->op_ws_bytes = 0;
-        }
-        if ((e = cudaMalloc(&h->op_ws, need)) != cudaSuccess)
-            return fail(h, TMOE_E_NOMEM, "cudaMalloc(%zu): %s", need, cudaGetErrorString(e));
-        h->op_ws_bytes = need;
-    }
-    char *base = (char *)h->op_ws;
-    int8_t *q = (int8_t *)(base + o_q);
-    float *d = (float *)(base + o_d);
-    uint32_t *bl = (uint32_t *)(base + o_bl), *bh = (uint32_t *)(base + o_bh);
-    int32_t *cnt = (int32_t *)(base + o_cnt), *offs = (int32_t *)(base + o_off), *na = (int32_t *)(base + o_na),
-            *perm = (int32_t *)(base + o_perm);
-    int4 *act = (int4 *)(base + o_act);
-    int *work = (int *)(base + o_work);
-    if ((e = tmoe::launch_sort_pairs(ids, (int)P, (int)n_w, cnt, offs, perm, act, na, work, kCounters, h->err, st)) !=
-        cudaSuccess)
-        return cuda_fail(h, e, "sort_pairs");
-    if ((e = tmoe::launch_quantize_q8k(b, rows, (int)K, nullptr, tmoe::Q8Rows{q, d, bl, bh, wt}, st)) != cudaSuccess)
-        return cuda_fail(h, e, "quantize b");
-    if ((e = tmoe::launch_zero_invalid_rows(ids, P, (int)n_w, (int)N, out, st)) != cudaSuccess)
-        return cuda_fail(h, e, "zero rows");
-    tmoe::GemvArgs g{};
-    g.w0 = (const uint8_t *)W;
-    g.nb1_0 = nb1, g.nb2_0 = nb2;
-    g.K = (int)K, g.N = (int)N;
-    g.xq = q, g.xd = d, g.xbl = bl, g.xbh = bh, g.x_div = b1 == 1 ? (int)n_used : 1;
-    const int max_active = (int)(P < n_w ? P : n_w);
-    g.perm = perm, g.active = act, g.n_active = na;
-    g.n_slots = (int)n_w, g.max_active = max_active, g.n_pairs = (int)P, g.work = work;
-    g.out = out, g.err = h->err;
-    if ((e = tmoe::launch_gemv(wt, false, g, max_active, h->sm_count, st)) != cudaSuccess)
-        return cuda_fail(h, e, "mul_mat_id gemv");
-    return TMOE_OK;
+    return run_mmid(h, (cudaStream_t)stream, wt_of(type), W, nb1, nb2, K, N, n_w, b, b1, ids, n_used, T, out, L,
+                    (char *)h->op_ws);
 }
 
 int tmoe_mul_mat(tmoe_handle *h, void *stream, int32_t type, const void *W, size_t nb1, int64_t K, int64_t N,
@@ -903,18 +956,22 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = 2u << 20;  // 2 MiB
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of g_noalloc_scratch on the current device (cached per device; the first call on
-// a device looks the symbol up, which may load the module there).
+// Device address of g_noalloc_scratch on the current device, looked up once per device (the
+// lookup may load the module there).  The cache entries are atomics, so threads making their first
+// call on a device at the same time only repeat the lookup.  A cudaDeviceReset unloads the module
+// and leaves the cached address stale; the header says not to use the entry point after one.
 cudaError_t noalloc_scratch(int dev, char **out) {
-    static char *addr[64] = {};
+    static std::atomic<char *> addr[64];
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!addr[dev]) {
-        void *p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    char *p = addr[dev].load(std::memory_order_acquire);
+    if (!p) {
+        void *q = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&q, g_noalloc_scratch);
         if (e != cudaSuccess) return e;
-        addr[dev] = (char *)p;
+        p = (char *)q;
+        addr[dev].store(p, std::memory_order_release);
     }
-    *out = addr[dev];
+    *out = p;
     return cudaSuccess;
 }
 
@@ -926,70 +983,24 @@ int tmoe_mul_mat_id_noalloc(tmoe_handle *h, void *stream, int32_t type, const vo
                             int64_t K, int64_t N, int64_t n_w, const float *b, int64_t b1, const int32_t *ids,
                             int64_t n_used, int64_t T, float *out) {
     if (!h) return TMOE_E_INVALID;
-    if (!is_kquant(type)) return fail(h, TMOE_E_UNSUPPORTED, "mul_mat_id type %d (need Q4_K or Q6_K)", type);
-    if (K <= 0 || K % 256 || N <= 0 || n_w <= 0 || n_w > kMaxSlots || n_used <= 0 || T < 0 ||
-        (b1 != 1 && b1 != n_used))
-        return fail(h, TMOE_E_INVALID, "bad mul_mat_id shape");
-    if (!W || !b || !ids || !out) return fail(h, TMOE_E_INVALID, "null tensor");
-    if (!aligned16(b)) return fail(h, TMOE_E_INVALID, "b must be 16-byte aligned");
-    const int wt = wt_of(type);
-    if (nb1 != row_size(type, K)) return fail(h, TMOE_E_UNSUPPORTED, "rows must be contiguous (nb1 == row size)");
-    if (((uintptr_t)W & 15u) || (nb2 & 15u)) return fail(h, TMOE_E_INVALID, "W and nb2 must be 16-byte aligned");
-    if (!tmoe::gemv_rows_per_item(wt, (int)K, (int)N))
-        return fail(h, TMOE_E_UNSUPPORTED, "N=%lld rows per expert fit no GEMV row tile (multiples of 16)",
-                    (long long)N);
-    const int64_t P = T * n_used, rows = T * b1;
+    const int rc = check_mmid(h, type, W, nb1, nb2, K, N, n_w, b, b1, ids, n_used, T, out);
+    if (rc != TMOE_OK) return rc;
     // the same layout as tmoe_mul_mat_id's scratch, placed in the static array
-    size_t need = 0;
-    auto lay = [&](size_t bytes) {
-        size_t o = need;
-        need = align_up(need + bytes, 256);
-        return o;
-    };
-    const size_t nbw = (size_t)tmoe::q8_nbw(wt);
-    size_t o_q = lay((size_t)rows * K), o_d = lay((size_t)rows * (K / 256) * 4);
-    size_t o_bl = lay((size_t)rows * (K / 256) * nbw * 4), o_bh = lay((size_t)rows * (K / 256) * nbw * 4);
-    size_t o_cnt = lay(kMaxSlots * 4), o_off = lay((kMaxSlots + 1) * 4), o_act = lay(kMaxSlots * 16), o_na = lay(4);
-    size_t o_perm = lay((size_t)P * 4 + 16), o_work = lay(kCounters * 4);
-    if (need > kNoAllocScratchBytes)
+    const MmidLayout L(wt_of(type), T * b1, K, T * n_used);
+    if (L.need > kNoAllocScratchBytes)
         return fail(h, TMOE_E_INVALID,
                     "mul_mat_id_noalloc needs %zu bytes of scratch for T=%lld, b1=%lld, K=%lld, n_used=%lld; the static "
                     "scratch holds %zu (use tmoe_mul_mat_id)",
-                    need, (long long)T, (long long)b1, (long long)K, (long long)n_used, kNoAllocScratchBytes);
+                    L.need, (long long)T, (long long)b1, (long long)K, (long long)n_used, kNoAllocScratchBytes);
     if (T == 0) return TMOE_OK;
     DeviceGuard dg(h->cfg.device);
-    cudaStream_t st = (cudaStream_t)stream;
     char *base = nullptr;
-    cudaError_t e = noalloc_scratch(h->cfg.device, &base);
+    const cudaError_t e = noalloc_scratch(h->cfg.device, &base);
     if (e != cudaSuccess) return cuda_fail(h, e, "cudaGetSymbolAddress(noalloc scratch)");
-    int8_t *q = (int8_t *)(base + o_q);
-    float *d = (float *)(base + o_d);
-    uint32_t *bl = (uint32_t *)(base + o_bl), *bh = (uint32_t *)(base + o_bh);
-    int32_t *cnt = (int32_t *)(base + o_cnt), *offs = (int32_t *)(base + o_off), *na = (int32_t *)(base + o_na),
-            *perm = (int32_t *)(base + o_perm);
-    int4 *act = (int4 *)(base + o_act);
-    int *work = (int *)(base + o_work);
     // nothing in the scratch needs to start at zero: the dispatch kernel writes counts, offsets,
     // the active list and perm, and zeroes the GEMV work counters, before the GEMV reads them
-    if ((e = tmoe::launch_sort_pairs(ids, (int)P, (int)n_w, cnt, offs, perm, act, na, work, kCounters, h->err, st)) !=
-        cudaSuccess)
-        return cuda_fail(h, e, "sort_pairs");
-    if ((e = tmoe::launch_quantize_q8k(b, rows, (int)K, nullptr, tmoe::Q8Rows{q, d, bl, bh, wt}, st)) != cudaSuccess)
-        return cuda_fail(h, e, "quantize b");
-    if ((e = tmoe::launch_zero_invalid_rows(ids, P, (int)n_w, (int)N, out, st)) != cudaSuccess)
-        return cuda_fail(h, e, "zero rows");
-    tmoe::GemvArgs g{};
-    g.w0 = (const uint8_t *)W;
-    g.nb1_0 = nb1, g.nb2_0 = nb2;
-    g.K = (int)K, g.N = (int)N;
-    g.xq = q, g.xd = d, g.xbl = bl, g.xbh = bh, g.x_div = b1 == 1 ? (int)n_used : 1;
-    const int max_active = (int)(P < n_w ? P : n_w);
-    g.perm = perm, g.active = act, g.n_active = na;
-    g.n_slots = (int)n_w, g.max_active = max_active, g.n_pairs = (int)P, g.work = work;
-    g.out = out, g.err = h->err;
-    if ((e = tmoe::launch_gemv(wt, false, g, max_active, h->sm_count, st)) != cudaSuccess)
-        return cuda_fail(h, e, "mul_mat_id gemv");
-    return TMOE_OK;
+    return run_mmid(h, (cudaStream_t)stream, wt_of(type), W, nb1, nb2, K, N, n_w, b, b1, ids, n_used, T, out, L,
+                    base);
 }
 
 int tmoe_dispatch(tmoe_handle *h, void *stream, const int32_t *ids, int64_t T, int32_t n_slots,

@@ -128,6 +128,14 @@ class MoeLayer:
         """Synchronises and raises if a kernel latched a device error."""
         _lib.check(self.lib.tmoe_check(self.h, _stream(stream)), self.h)
 
+    def wait_flag(self, flag: torch.Tensor, value: int, limit_ns: int = 0, stream=None):
+        """Holds the stream until flag[0] == value (an int32 word in device memory or in pinned host
+        memory that the host writes); after limit_ns (<= 0: one second) the wait gives up and the
+        next check() raises TMOE_E_DEVICE."""
+        if flag.dtype != torch.int32:
+            raise ValueError("the flag is an int32 word")
+        _lib.check(self.lib.tmoe_wait_flag(self.h, _stream(stream), _ptr(flag), int(value), int(limit_ns)), self.h)
+
     def router(self, ffn_inp: torch.Tensor, router_w: torch.Tensor | None = None,
                logits: torch.Tensor | None = None, ffn_norm: torch.Tensor | None = None,
                use_norm: bool = False, stream=None, want_logits: bool = False):
