@@ -199,9 +199,9 @@ def test_mul_mat_id_allocates_nothing_within_the_create_bound():
     layer.check()
     want = O.mul_mat_id(O.TYPE_Q6_K, host(W), I, H, E, host(b), host(ids))
     assert float(np.abs(host(out) - want).max()) / float(np.abs(want).max()) <= 1e-4
-    big = torch.zeros((2 * T, used, I), device="cuda")
+    big = torch.zeros((16 * T, used, I), device="cuda")
     with pytest.raises(tb.TmoeError, match="TMOE_E_INVALID"):
-        layer.mul_mat_id(O.TYPE_Q6_K, W, big, cuda(np.zeros((2 * T, used), np.int32)))
+        layer.mul_mat_id(O.TYPE_Q6_K, W, big, cuda(np.zeros((16 * T, used), np.int32)))
     layer.close()
 
 
