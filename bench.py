@@ -78,6 +78,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--sweep", action="store_true", help="also time T in {1,4,16,64}")
     p.add_argument("--ctx", type=int, default=4096, help="model mode: the context each sequence decodes at")
+    p.add_argument("--prefill", type=int, default=2048,
+                   help="model mode: also time the prefill of one prompt of this many random tokens (0: skip)")
     p.add_argument("--mode", choices=["decode", "prefill", "streamed", "gguf", "model"], default="decode",
                    help="decode: C2 at T tokens (the metric's config); prefill: C2-shaped layer at T=8192 "
                         "(tensor roofline); streamed: config 5, skewed routing over 64 device slots of 128 experts; "
@@ -697,11 +699,41 @@ def run_model(args, local_rank):
     hp = Hparams(name="Qwen3-30B-A3B-shaped", n_layer=48, n_ctx_train=40960, n_embd=2048, n_head=32, n_head_kv=4,
                  head_dim=128, n_rot=128, n_expert=128, n_expert_used=8, n_ff_exp=768, n_vocab=151936, rms_eps=1e-6,
                  rope_freq_base=1e6, tied_output=False)
-    n_ctx = ctx + W + args.steps + 1
+    n_ctx = max(ctx + W + args.steps + 1, args.prefill)
     log(f"model: synthetic weights, B={B}, context {ctx}")
     m = Qwen3MoeModel.synthetic(hp, max_batch=B, n_ctx=n_ctx, device=local_rank, seed=args.seed)
     gen = torch.Generator(device=dev)
     gen.manual_seed(args.seed + 3)
+    prefill = None
+    if args.prefill > 0:  # pp: one prompt of random token ids into sequence 0, then its first token
+        S = args.prefill
+        prompt = torch.randint(0, hp.n_vocab, (S,), dtype=torch.int32, device=dev, generator=gen)
+        m.prefill(prompt, seq=0)
+        m.check()
+        for _ in range(W):
+            m.prefill(prompt, seq=0)
+        torch.cuda.synchronize()
+        n_pp = max(2, min(args.steps, 5))
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local_rank) as pclk:
+            p0.record()
+            for _ in range(n_pp):
+                m.prefill(prompt, seq=0)
+            p1.record()
+            torch.cuda.synchronize()
+        pms = p0.elapsed_time(p1) / n_pp
+        m.check()
+        # routed FLOPs of one prompt: projections (q, k, v, o), router, experts, causal attention
+        d_, nh_, nkv_, H_ = hp.head_dim, hp.n_head, hp.n_head_kv, hp.n_embd
+        per_tok = (2 * H_ * (nh_ * d_ + 2 * nkv_ * d_) + 2 * nh_ * d_ * H_ + 2 * H_ * hp.n_expert
+                   + 2 * hp.n_expert_used * 3 * H_ * hp.n_ff_exp)
+        attn_fl = 4 * nh_ * d_ * S * (S + 1) / 2
+        fl = hp.n_layer * (S * per_tok + attn_fl)
+        prefill = {"tokens": S, "ms": round(pms, 3), "tokens_per_s": round(S / (pms / 1e3), 1), "runs": n_pp,
+                   "flops": int(fl), "tflops": round(fl / (pms / 1e3) / 1e12, 1), "clocks": pclk.summary(),
+                   "path": "Qwen3MoeModel.prefill: one multi-token step per run (eager C-ABI calls), the head on the "
+                           "last row"}
+        log(f"prefill of {S} tokens: {pms:.2f} ms ({S / (pms / 1e3):.0f} tokens/s)")
     for c in m.kc + m.vc:
         c[:, :ctx].normal_(0.0, 1.0, generator=gen)
     tokens = torch.randint(0, hp.n_vocab, (B,), dtype=torch.int32, device=dev, generator=gen)
@@ -758,7 +790,7 @@ def run_model(args, local_rank):
                      "peak_source": peaks["source"], "traffic": None,
                      "algorithmic_bytes_per_step": int(step_bytes),
                      "note": "weights touched (expected distinct experts) + KV caches + output matrix"},
-        "gpu_launches": None, "clocks": clk.summary(),
+        "gpu_launches": None, "clocks": clk.summary(), "prefill": prefill,
     }
 
 

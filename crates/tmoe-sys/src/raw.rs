@@ -386,6 +386,25 @@ extern "C" {
         scratch: *mut c_void,
         out: *mut f32,
     ) -> c_int;
+    pub fn tmoe_attn_prefill(
+        h: *mut tmoe_handle,
+        stream: *mut c_void,
+        q: *const f32,
+        k: *const f32,
+        v: *const f32,
+        k_cache: *mut c_void,
+        v_cache: *mut c_void,
+        seq: i32,
+        n_seq: i32,
+        pos0: i32,
+        S: i32,
+        n_head: i32,
+        n_kv: i32,
+        head_dim: i32,
+        n_ctx: i32,
+        scale: f32,
+        out: *mut f32,
+    ) -> c_int;
     pub fn tmoe_add(
         h: *mut tmoe_handle,
         stream: *mut c_void,

@@ -289,6 +289,12 @@ TMOE_API int tmoe_dequantize(int32_t type, const void *in, int64_t n, float *out
  *                       of n_kv, at most 8 query heads per KV head; head_dim 64 or 128), k/v
  *                       [B][n_kv][head_dim], out [B][n_head][head_dim]; scratch of
  *                       tmoe_attn_decode_scratch_bytes
+ *   tmoe_attn_prefill <- the multi-token form of the same two ops (attention_seqs, attn.rs:269-302,
+ *                       one sequence): the S new K/V rows k/v [S][n_kv][head_dim] go to positions
+ *                       pos0 .. pos0+S-1 of sequence `seq` of the caches [n_seq][n_ctx][n_kv]
+ *                       [head_dim], then query i of q [S][n_head][head_dim] attends to positions
+ *                       0 .. pos0+i (the causal mask of a prefill) -> out [S][n_head][head_dim];
+ *                       no scratch
  *   tmoe_add         <- add (:243);  tmoe_argmax: the first index of each row's maximum */
 /* Context::mul_mat (context.rs) of one Q4_K/Q6_K matrix W [N rows of K] and x f32 [T][K] ->
  * out [T][N], on the decode GEMV.  reuse_x != 0: x is the activations of the previous
@@ -315,6 +321,9 @@ TMOE_API int64_t tmoe_attn_decode_scratch_bytes(tmoe_handle *h, int32_t B, int32
 TMOE_API int tmoe_attn_decode(tmoe_handle *h, void *stream, const float *q, const float *k, const float *v,
                               void *k_cache, void *v_cache, const int32_t *pos, int32_t B, int32_t n_head,
                               int32_t n_kv, int32_t head_dim, int32_t n_ctx, float scale, void *scratch, float *out);
+TMOE_API int tmoe_attn_prefill(tmoe_handle *h, void *stream, const float *q, const float *k, const float *v,
+                               void *k_cache, void *v_cache, int32_t seq, int32_t n_seq, int32_t pos0, int32_t S,
+                               int32_t n_head, int32_t n_kv, int32_t head_dim, int32_t n_ctx, float scale, float *out);
 TMOE_API int tmoe_add(tmoe_handle *h, void *stream, const float *a, const float *b, float *out, int64_t n);
 TMOE_API int tmoe_argmax(tmoe_handle *h, void *stream, const float *x, int64_t rows, int64_t n, int32_t *out);
 

@@ -1,4 +1,4 @@
-"""CPU oracle of the Qwen3-MoE decode step around the MoE layer (config 3).  TEST INFRASTRUCTURE
+"""CPU oracle of the Qwen3-MoE decode and prefill steps around the MoE layer (config 3).  TEST INFRASTRUCTURE
 ONLY: imported by tests/ as the checker of tetraeder_b200.model, never by the product.
 
 Restates, per decode step of B sequences (one new token each):
@@ -81,8 +81,13 @@ class ModelOracle:
         self.kc = [np.zeros((max_batch, n_ctx, kv), np.float16) for _ in range(hp.n_layer)]
         self.vc = [np.zeros((max_batch, n_ctx, kv), np.float16) for _ in range(hp.n_layer)]
 
-    def attention(self, il, x, pos):
+    def attention(self, il, x, pos, seq=None):
+        """Row b of x is the token of sequence seq[b] (default: b) at position pos[b]; its K/V row is
+        stored, then it attends to that sequence's positions 0..pos[b] -- one token per sequence in
+        a decode step, or the S tokens of one sequence in a prefill (rows in position order, so each
+        row's keys are stored before it reads them: the causal mask)."""
         hp, w = self.hp, self.w
+        seq = np.arange(x.shape[0]) if seq is None else np.asarray(seq)
         B, d, nh, nkv = x.shape[0], hp.head_dim, hp.n_head, hp.n_head_kv
         p = f"blk.{il}."
         cur = rms_norm(x, w[p + "attn_norm.weight"], hp.rms_eps)
@@ -96,10 +101,11 @@ class ModelOracle:
         # flash_attn_ext over an F16 cache converts Q to F16 and scales the Q.K dot (ggml's CPU and CUDA paths)
         q16 = q.astype(np.float16).astype(np.float64)
         for b in range(B):
-            self.kc[il][b, pos[b]] = k[b].reshape(-1).astype(np.float16)
-            self.vc[il][b, pos[b]] = v[b].astype(np.float16)
-            K = self.kc[il][b, :pos[b] + 1].astype(np.float64).reshape(-1, nkv, d)
-            V = self.vc[il][b, :pos[b] + 1].astype(np.float64).reshape(-1, nkv, d)
+            sb = seq[b]
+            self.kc[il][sb, pos[b]] = k[b].reshape(-1).astype(np.float16)
+            self.vc[il][sb, pos[b]] = v[b].astype(np.float16)
+            K = self.kc[il][sb, :pos[b] + 1].astype(np.float64).reshape(-1, nkv, d)
+            V = self.vc[il][sb, :pos[b] + 1].astype(np.float64).reshape(-1, nkv, d)
             for h in range(nh):
                 s = (K[:, h // G, :] @ q16[b, h]) * np.float64(np.float32(1.0 / np.sqrt(d)))
                 e = np.exp(s - s.max())
@@ -108,17 +114,26 @@ class ModelOracle:
         return (x + o).astype(np.float32)
 
     def decode(self, tokens, pos):
+        return self._step(tokens, pos, None)
+
+    def prefill(self, tokens, seq, pos0=0):
+        """The S tokens of sequence `seq` at positions pos0 .. pos0+S-1 in one step (build_step over a
+        prompt); returns the logits of the last token [1, n_vocab]."""
+        S = len(tokens)
+        return self._step(tokens, pos0 + np.arange(S, dtype=np.int32), np.full(S, seq), last_only=True)
+
+    def _step(self, tokens, pos, seq, last_only=False):
         hp, w = self.hp, self.w
         x = w["token_embd.weight"].rows_f32(np.asarray(tokens))
         for il in range(hp.n_layer):
             p = f"blk.{il}."
-            ffn_inp = self.attention(il, x, np.asarray(pos))
+            ffn_inp = self.attention(il, x, np.asarray(pos), seq)
             ids, wt, xn, _ = route(ffn_inp, hp.n_expert_used, router_w=w[p + "ffn_gate_inp.weight"], norm=True,
                                    norm_w=w[p + "ffn_norm.weight"], eps=hp.rms_eps)
             g, u, dn = (w[p + n + ".weight"] for n in ("ffn_gate_exps", "ffn_up_exps", "ffn_down_exps"))
             moe = experts(xn, ids, wt, g.data, u.data, dn.data, hp.n_embd, hp.n_ff_exp, hp.n_expert, g.type, u.type,
                           dn.type)
             x = (ffn_inp + moe).astype(np.float32)
-        h = rms_norm(x, w["output_norm.weight"], hp.rms_eps)
+        h = rms_norm(x[-1:] if last_only else x, w["output_norm.weight"], hp.rms_eps)
         head = w["token_embd.weight"] if hp.tied_output else w["output.weight"]
         return head.matmul(h)

@@ -262,3 +262,104 @@ def test_mul_mat_beyond_l2_matches_row_slices():
     layer.check()
     assert torch.equal(full, torch.cat(halves, dim=1))
     layer.close()
+
+
+@pytest.mark.parametrize("hd,nh,nkv,S,pos0", [(128, 32, 4, 200, 37), (128, 4, 2, 64, 0), (64, 4, 2, 1, 5),
+                                             (128, 8, 8, 130, 900)])
+def test_prefill_attention_op_against_float64(hd, nh, nkv, S, pos0):
+    """tmoe_attn_prefill: S new rows of one sequence (its third of three) after pos0 cached ones;
+    each query i attends to positions 0 .. pos0 + i.  Against float64 attention over the
+    f16-rounded operands; partial 64-query blocks, GQA up to 8 heads per KV head, a single query."""
+    import ctypes as C
+    n_seq, seq, ctx = 3, 2, pos0 + S + 10
+    layer = tb.MoeLayer(512, 256, 8, 2, gate_type=12, up_type=12, down_type=12, max_tokens=4)
+    lib, h = layer.lib, layer.h
+    rng = np.random.default_rng(hd + nh + S)
+    kc = (rng.standard_normal((n_seq, ctx, nkv, hd)) * 0.5).astype(np.float16)
+    vc = rng.standard_normal((n_seq, ctx, nkv, hd)).astype(np.float16)
+    q = rng.standard_normal((S, nh, hd)).astype(np.float32)
+    k = (rng.standard_normal((S, nkv, hd)) * 0.5).astype(np.float32)
+    v = rng.standard_normal((S, nkv, hd)).astype(np.float32)
+    d_kc, d_vc = torch.from_numpy(kc).cuda(), torch.from_numpy(vc).cuda()
+    dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    out = torch.full((S, nh, hd), float("nan"), device="cuda")
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    scale = 1.0 / np.sqrt(hd)
+    assert lib.tmoe_attn_prefill(h, None, P(dq), P(dk), P(dv), P(d_kc), P(d_vc), seq, n_seq, pos0, S, nh, nkv, hd,
+                                 ctx, scale, P(out)) == 0
+    layer.check()
+    got = out.cpu().numpy()
+    kc[seq, pos0:pos0 + S] = k.astype(np.float16)
+    vc[seq, pos0:pos0 + S] = v.astype(np.float16)
+    G = nh // nkv
+    q16 = q.astype(np.float16).astype(np.float64)
+    for i in range(S):
+        n = pos0 + i + 1
+        K, V = kc[seq, :n].astype(np.float64), vc[seq, :n].astype(np.float64)
+        for hh in range(nh):
+            s = K[:, hh // G] @ q16[i, hh] * np.float64(np.float32(scale))
+            e = np.exp(s - s.max())
+            want = e @ V[:, hh // G] / e.sum()
+            assert np.abs(got[i, hh] - want).max() < 5e-3 * max(1.0, np.abs(want).max()), (i, hh)
+    # the new rows landed in this sequence's cache, and only there
+    assert np.array_equal(d_kc.cpu().numpy(), kc) and np.array_equal(d_vc.cpu().numpy(), vc)
+    with pytest.raises(tb.TmoeError, match="TMOE_E_INVALID"):
+        _lib_check(lib, h, lib.tmoe_attn_prefill(h, None, P(dq), P(dk), P(dv), P(d_kc), P(d_vc), seq, n_seq,
+                                                 ctx - S + 1, S, nh, nkv, hd, ctx, scale, P(out)))
+    layer.close()
+
+
+def _lib_check(lib, h, rc):
+    from tetraeder_b200 import _lib
+    _lib.check(rc, h)
+
+
+def test_prefill_then_decode_matches_the_oracle(tiny_model):
+    """A prompt of 45 tokens in one prefill step (three 16-token projection groups, a partial
+    64-query attention block), then three decode steps of the same sequence; the oracle runs the
+    same prompt row by row with the causal mask."""
+    path, written = tiny_model
+    S, n_ctx = 45, 64
+    with GgufFile(path) as f:
+        hp = f.hparams
+        model = Qwen3MoeModel.from_gguf(f, max_batch=1, n_ctx=n_ctx)
+    ref = ModelOracle(hp, _oracle_weights(written, hp), 1, n_ctx)
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, hp.n_vocab, S).astype(np.int32)
+    try:
+        got = model.prefill(torch.from_numpy(prompt).cuda(), seq=0).cpu().numpy()
+        model.check()
+        want = ref.prefill(prompt, 0)
+        assert nrms(got, want) < 5e-2, f"prefill logits nrms {nrms(got, want):.2e}"
+        assert int(model.next_tokens[0]) == int(np.argmax(got[0]))
+        for s in range(3):
+            tok = rng.integers(0, hp.n_vocab, 1).astype(np.int32)
+            pos = np.array([S + s], dtype=np.int32)
+            got = model.decode(torch.from_numpy(tok).cuda(), torch.from_numpy(pos).cuda()).cpu().numpy()
+            model.check()
+            want = ref.decode(tok, pos)
+            assert nrms(got, want) < 5e-2, f"decode step {s} after the prefill: nrms {nrms(got, want):.2e}"
+    finally:
+        model.close()
+
+
+def test_chunked_prefill_equals_one_prefill(tiny_model):
+    """The same prompt as one prefill step and as two chunks (the second at pos0 = 30 reads the
+    first chunk's keys from the cache): the last logits agree to the f16 rounding of the cached
+    keys, and both caches hold the same rows."""
+    path, _ = tiny_model
+    S, cut, n_ctx = 50, 30, 64
+    with GgufFile(path) as f:
+        one = Qwen3MoeModel.from_gguf(f, max_batch=2, n_ctx=n_ctx)
+    prompt = torch.from_numpy(np.random.default_rng(3).integers(0, 512, S).astype(np.int32)).cuda()
+    try:
+        a = one.prefill(prompt, seq=1).clone()
+        one.prefill(prompt[:cut], seq=0)
+        b = one.prefill(prompt[cut:], seq=0, pos0=cut).clone()
+        one.check()
+        assert nrms(b.cpu().numpy(), a.cpu().numpy()) < 1e-2
+        for il in range(len(one.kc)):
+            assert torch.equal(one.kc[il][0, :S], one.kc[il][1, :S]) or \
+                float((one.kc[il][0, :S].float() - one.kc[il][1, :S].float()).abs().max()) < 5e-2
+    finally:
+        one.close()

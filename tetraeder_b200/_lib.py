@@ -95,6 +95,7 @@ SIGNATURES = {
     "tmoe_qk_norm_rope": ([P, P, P, P, P, P, P, I64, I32, I32, I32, I32, C.c_float, C.c_float], C.c_int),
     "tmoe_attn_decode_scratch_bytes": ([P, I32, I32, I32, I32, I32], I64),
     "tmoe_attn_decode": ([P, P, P, P, P, P, P, P, I32, I32, I32, I32, I32, C.c_float, P, P], C.c_int),
+    "tmoe_attn_prefill": ([P, P, P, P, P, P, P, I32, I32, I32, I32, I32, I32, I32, I32, C.c_float, P], C.c_int),
     "tmoe_add": ([P, P, P, P, P, I64], C.c_int),
     "tmoe_argmax": ([P, P, P, I64, I64, P], C.c_int),
     "tmoe_trace_open": ([C.c_char_p, C.POINTER(C.c_void_p)], C.c_int),

@@ -107,6 +107,9 @@ size_t attn_scratch_floats(int B, int n_head, int head_dim, int n_kv, int n_ctx,
 cudaError_t launch_attn_decode(const float *q, const float *k, const float *v, __half *kc, __half *vc,
                                const int32_t *pos, int B, int n_head, int n_kv, int head_dim, int n_ctx, float scale,
                                float *part, float *out, int sm_count, int *err, cudaStream_t st);
+cudaError_t launch_attn_prefill(const float *q, const float *k, const float *v, __half *kc, __half *vc, int seq,
+                                int pos0, int S, int n_head, int n_kv, int head_dim, int n_ctx, float scale, float *out,
+                                cudaStream_t st);
 cudaError_t launch_add(const float *a, const float *b, float *out, int64_t n, cudaStream_t st);
 cudaError_t launch_dense_prep(int T, int group, int ks, int4 *active, int32_t *n_active, int32_t *perm, int *counters,
                               int n_counters, cudaStream_t st);

@@ -325,6 +325,197 @@ __global__ void attn_merge_kernel(const float *__restrict__ part, int S, int HD,
     }
 }
 
+// ------------------------------------------------------------------ prefill attention
+// cache[seq][pos0 + i][:] = rows[i][:] (n_kv * head_dim values as F16) for K and V, i < S: the
+// set_rows of a multi-token step's new K/V rows.
+__global__ void kv_store_rows_kernel(const float *__restrict__ k, const float *__restrict__ v, __half *__restrict__ kc,
+                                     __half *__restrict__ vc, int seq, int pos0, int n_ctx, int width) {
+    const size_t i = blockIdx.x;
+    const size_t dst = ((size_t)seq * n_ctx + pos0 + i) * width;
+    const float4 *k4 = reinterpret_cast<const float4 *>(k + i * width);
+    const float4 *v4 = reinterpret_cast<const float4 *>(v + i * width);
+    for (int c = threadIdx.x; c < width / 4; c += blockDim.x) {
+        const float4 a = k4[c], b = v4[c];
+        reinterpret_cast<__half2 *>(kc + dst)[2 * c] = __floats2half2_rn(a.x, a.y);
+        reinterpret_cast<__half2 *>(kc + dst)[2 * c + 1] = __floats2half2_rn(a.z, a.w);
+        reinterpret_cast<__half2 *>(vc + dst)[2 * c] = __floats2half2_rn(b.x, b.y);
+        reinterpret_cast<__half2 *>(vc + dst)[2 * c + 1] = __floats2half2_rn(b.z, b.w);
+    }
+}
+
+// Causal attention of S new queries of one sequence (query i at position pos0 + i attends to the
+// cache's positions 0 .. pos0 + i), the masked flash attention of a prefill step.  One CTA per
+// (64-query block, query head), 4 warps of 16 query rows each; the query head's KV head (GQA:
+// head / (n_head / n_kv)) is read from the F16 cache in 64-position tiles, staged by cp.async into
+// two shared stages that all four warps read.  Per tile and warp, on the tensor cores (mma.sync
+// m16n8k16, f16 operands, f32 accumulators), as in the decode kernel:
+//   S = Q K^T (16 x 64: K rows through ldmatrix), scaled in f32, masked above the diagonal;
+//   online softmax of each row in the S fragments (a quad of lanes shares a row);
+//   O += P V  (the S fragments, as f16, are P's A fragments; V through ldmatrix.trans).
+// The longest query blocks (the last ones) are launched first.
+constexpr int AP_Q = 64;  // query rows per CTA
+constexpr int AP_K = 64;  // positions per staged tile
+constexpr int AP_WARPS = 4;
+constexpr int AP_THREADS = 32 * AP_WARPS;
+
+template <int HD>
+struct PrefillSmem {
+    static constexpr int ROW = HD + 8;                 // halfs per staged row (conflict-free ldmatrix)
+    static constexpr int STAGE = 2 * AP_K * ROW;       // K then V
+    static constexpr size_t BYTES = (size_t)2 * STAGE * 2;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(AP_THREADS) attn_prefill_kernel(const float *__restrict__ q,
+                                                                  const __half *__restrict__ kc,
+                                                                  const __half *__restrict__ vc, int seq, int pos0,
+                                                                  int S, int n_head, int n_kv, int n_ctx, float scale,
+                                                                  float *__restrict__ out) {
+    using SM = PrefillSmem<HD>;
+    constexpr int KB = HD / 16, NB = HD / 8, CH = HD / 8;  // CH: 16-byte chunks per row
+    extern __shared__ __align__(16) __half ap_smem[];
+    const int qb = gridDim.x - 1 - blockIdx.x, h = blockIdx.y;
+    const int kvh = h / (n_head / n_kv);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gr = lane >> 2, t4 = lane & 3;
+    const int r0 = qb * AP_Q + warp * 16;  // this warp's first query row
+    const int rA = r0 + gr, rB = r0 + gr + 8;
+    const int qpA = pos0 + rA, qpB = pos0 + rB;
+    const int warp_last = pos0 + min(r0 + 15, S - 1);  // the warp's last query position
+    const int kv_end = pos0 + min(S, (qb + 1) * AP_Q);  // keys 0 .. kv_end - 1 serve this CTA
+    const size_t row_stride = (size_t)n_kv * HD;
+    const __half *kb = kc + (size_t)seq * n_ctx * row_stride + (size_t)kvh * HD;
+    const __half *vb = vc + (size_t)seq * n_ctx * row_stride + (size_t)kvh * HD;
+
+    // Q fragments of rows rA and rB (f16, unscaled; rows past S read as zero and are not written)
+    uint32_t qa[KB][4];
+    {
+        const size_t qs = (size_t)n_head * HD;
+        const float *qa_row = q + (size_t)min(rA, S - 1) * qs + (size_t)h * HD;
+        const float *qb_row = q + (size_t)min(rB, S - 1) * qs + (size_t)h * HD;
+        const bool va = rA < S, vb_ = rB < S;
+#pragma unroll
+        for (int k = 0; k < KB; k++) {
+            const int c0 = 16 * k + 2 * t4;
+            const float2 a0 = va ? *reinterpret_cast<const float2 *>(qa_row + c0) : make_float2(0.f, 0.f);
+            const float2 a1 = va ? *reinterpret_cast<const float2 *>(qa_row + c0 + 8) : make_float2(0.f, 0.f);
+            const float2 b0 = vb_ ? *reinterpret_cast<const float2 *>(qb_row + c0) : make_float2(0.f, 0.f);
+            const float2 b1 = vb_ ? *reinterpret_cast<const float2 *>(qb_row + c0 + 8) : make_float2(0.f, 0.f);
+            qa[k][0] = pack_h2(a0.x, a0.y);
+            qa[k][1] = pack_h2(b0.x, b0.y);
+            qa[k][2] = pack_h2(a1.x, a1.y);
+            qa[k][3] = pack_h2(b1.x, b1.y);
+        }
+    }
+    float o[NB][4];
+#pragma unroll
+    for (int n = 0; n < NB; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float mA = -INFINITY, mB = -INFINITY, lA = 0.0f, lB = 0.0f;
+
+    const int n_tiles = (kv_end + AP_K - 1) / AP_K;
+    auto issue = [&](int t, int st) {  // tile t into stage st, all threads; rows past kv_end zero
+        __half *ks = ap_smem + st * SM::STAGE, *vs = ks + AP_K * SM::ROW;
+        const int p0 = t * AP_K;
+        for (int c = threadIdx.x; c < AP_K * CH; c += AP_THREADS) {
+            const int r = c / CH, col = 8 * (c % CH);
+            const bool ok = p0 + r < kv_end;
+            const size_t off = (size_t)(ok ? p0 + r : 0) * row_stride + col;
+            at_cp16(smem_u32(ks + r * SM::ROW + col), kb + off, ok);
+            at_cp16(smem_u32(vs + r * SM::ROW + col), vb + off, ok);
+        }
+        at_commit();
+    };
+    issue(0, 0);
+    for (int t = 0; t < n_tiles; t++) {
+        if (t + 1 < n_tiles) {
+            issue(t + 1, (t + 1) & 1);
+            at_wait<1>();
+        } else {
+            at_wait<0>();
+        }
+        __syncthreads();
+        const int p0 = t * AP_K;
+        if (p0 <= warp_last) {  // else every position of the tile is after this warp's queries
+            const __half *ks = ap_smem + (t & 1) * SM::STAGE, *vs = ks + AP_K * SM::ROW;
+            float sc[8][4];
+#pragma unroll
+            for (int nb = 0; nb < 8; nb++) sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.0f;
+#pragma unroll
+            for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+                for (int k = 0; k < KB; k += 2) {
+                    const int r = 8 * nb + (lane & 7), cblk = 16 * k + 8 * (lane >> 3);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(smem_u32(ks + r * SM::ROW + cblk), b0, b1, b2, b3);
+                    mma_f16(sc[nb], qa[k][0], qa[k][1], qa[k][2], qa[k][3], b0, b1);
+                    mma_f16(sc[nb], qa[k + 1][0], qa[k + 1][1], qa[k + 1][2], qa[k + 1][3], b2, b3);
+                }
+            // scale, the causal mask (and positions past kv_end), the row maxima
+            float xA = -INFINITY, xB = -INFINITY;
+#pragma unroll
+            for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const int kp = p0 + 8 * nb + 2 * t4 + j;
+                    sc[nb][j] = kp > qpA || kp >= kv_end ? -INFINITY : sc[nb][j] * scale;
+                    sc[nb][2 + j] = kp > qpB || kp >= kv_end ? -INFINITY : sc[nb][2 + j] * scale;
+                    xA = fmaxf(xA, sc[nb][j]);
+                    xB = fmaxf(xB, sc[nb][2 + j]);
+                }
+            xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, 1));
+            xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, 2));
+            xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, 1));
+            xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, 2));
+            // position 0 is in tile 0 for every row, so the running maxima are finite from there on
+            const float nA = fmaxf(mA, xA), nB = fmaxf(mB, xB);
+            const float aA = mA == -INFINITY ? 0.0f : __expf(mA - nA), aB = mB == -INFINITY ? 0.0f : __expf(mB - nB);
+            float sA = 0.0f, sB = 0.0f;
+#pragma unroll
+            for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    sc[nb][j] = __expf(sc[nb][j] - nA);
+                    sc[nb][2 + j] = __expf(sc[nb][2 + j] - nB);
+                    sA += sc[nb][j];
+                    sB += sc[nb][2 + j];
+                }
+            sA += __shfl_xor_sync(0xffffffffu, sA, 1);
+            sA += __shfl_xor_sync(0xffffffffu, sA, 2);
+            sB += __shfl_xor_sync(0xffffffffu, sB, 1);
+            sB += __shfl_xor_sync(0xffffffffu, sB, 2);
+            lA = lA * aA + sA, lB = lB * aB + sB;
+            mA = nA, mB = nB;
+#pragma unroll
+            for (int n = 0; n < NB; n++) o[n][0] *= aA, o[n][1] *= aA, o[n][2] *= aB, o[n][3] *= aB;
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {  // P V over the tile's 4 k16 position blocks
+                const uint32_t pa0 = pack_h2(sc[2 * kk][0], sc[2 * kk][1]);
+                const uint32_t pa1 = pack_h2(sc[2 * kk][2], sc[2 * kk][3]);
+                const uint32_t pa2 = pack_h2(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+                const uint32_t pa3 = pack_h2(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+#pragma unroll
+                for (int n = 0; n < NB; n += 2) {
+                    const int r = 16 * kk + (lane & 7) + 8 * ((lane >> 3) & 1), cblk = 8 * n + 8 * (lane >> 4);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(smem_u32(vs + r * SM::ROW + cblk), b0, b1, b2, b3);
+                    mma_f16(o[n], pa0, pa1, pa2, pa3, b0, b1);
+                    mma_f16(o[n + 1], pa0, pa1, pa2, pa3, b2, b3);
+                }
+            }
+        }
+        __syncthreads();  // every warp is done with this stage before it is refilled
+    }
+    const size_t os = (size_t)n_head * HD;
+    const float iA = lA > 0.0f ? 1.0f / lA : 0.0f, iB = lB > 0.0f ? 1.0f / lB : 0.0f;
+#pragma unroll
+    for (int n = 0; n < NB; n++) {
+        const int c = 8 * n + 2 * t4;
+        if (rA < S)
+            *reinterpret_cast<float2 *>(out + (size_t)rA * os + (size_t)h * HD + c) = make_float2(o[n][0] * iA, o[n][1] * iA);
+        if (rB < S)
+            *reinterpret_cast<float2 *>(out + (size_t)rB * os + (size_t)h * HD + c) = make_float2(o[n][2] * iB, o[n][3] * iB);
+    }
+}
+
 __global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ out,
                            int64_t n) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -493,6 +684,44 @@ cudaError_t launch_attn_decode(const float *q, const float *k, const float *v, _
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     attn_merge_kernel<<<B * n_head, 128, 0, st>>>(part, S, head_dim, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attn_prefill(const float *q, const float *k, const float *v, __half *kc, __half *vc, int seq,
+                                int pos0, int S, int n_head, int n_kv, int head_dim, int n_ctx, float scale, float *out,
+                                cudaStream_t st) {
+    if (S <= 0) return cudaSuccess;
+    if (n_kv <= 0 || n_head % n_kv || (head_dim != 64 && head_dim != 128) || n_head > 65535 || seq < 0 ||
+        pos0 < 0 || (int64_t)pos0 + S > n_ctx)
+        return cudaErrorInvalidValue;
+    const int width = n_kv * head_dim;
+    kv_store_rows_kernel<<<S, 128, 0, st>>>(k, v, kc, vc, seq, pos0, n_ctx, width);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const dim3 grid((S + AP_Q - 1) / AP_Q, n_head);
+    static int set128[64] = {}, set64[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (head_dim == 128) {
+        constexpr size_t smem = PrefillSmem<128>::BYTES;
+        if (!set128[dev] &&
+            (e = cudaFuncSetAttribute(attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem)) != cudaSuccess)
+            return e;
+        set128[dev] = 1;
+        attn_prefill_kernel<128><<<grid, AP_THREADS, smem, st>>>(q, kc, vc, seq, pos0, S, n_head, n_kv, n_ctx, scale,
+                                                                 out);
+    } else {
+        constexpr size_t smem = PrefillSmem<64>::BYTES;
+        if (!set64[dev] &&
+            (e = cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem)) != cudaSuccess)
+            return e;
+        set64[dev] = 1;
+        attn_prefill_kernel<64><<<grid, AP_THREADS, smem, st>>>(q, kc, vc, seq, pos0, S, n_head, n_kv, n_ctx, scale,
+                                                                out);
+    }
     return cudaGetLastError();
 }
 

@@ -1116,6 +1116,26 @@ int tmoe_attn_decode(tmoe_handle *h, void *stream, const float *q, const float *
     return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "attention");
 }
 
+int tmoe_attn_prefill(tmoe_handle *h, void *stream, const float *q, const float *k, const float *v, void *k_cache,
+                      void *v_cache, int32_t seq, int32_t n_seq, int32_t pos0, int32_t S, int32_t n_head, int32_t n_kv,
+                      int32_t head_dim, int32_t n_ctx, float scale, float *out) {
+    if (!h) return TMOE_E_INVALID;
+    if (n_kv <= 0 || n_head <= 0 || n_head % n_kv || n_head > 65535 || (head_dim != 64 && head_dim != 128))
+        return fail(h, TMOE_E_UNSUPPORTED, "attention shape: %d heads over %d KV heads of %d (head_dim 64 or 128)",
+                    n_head, n_kv, head_dim);
+    if (S < 0 || n_seq <= 0 || seq < 0 || seq >= n_seq || pos0 < 0 || n_ctx <= 0 || (int64_t)pos0 + S > n_ctx)
+        return fail(h, TMOE_E_INVALID, "prefill of %d tokens at position %d of sequence %d: caches hold %d sequences "
+                                       "of %d positions", S, pos0, seq, n_seq, n_ctx);
+    if (S == 0) return TMOE_OK;
+    if (!q || !k || !v || !k_cache || !v_cache || !out) return fail(h, TMOE_E_INVALID, "null tensor");
+    if (((uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15u)
+        return fail(h, TMOE_E_INVALID, "q, k, v, out and the caches must be 16-byte aligned");
+    DeviceGuard dg(h->cfg.device);
+    const cudaError_t e = tmoe::launch_attn_prefill(q, k, v, (__half *)k_cache, (__half *)v_cache, seq, pos0, S, n_head,
+                                                    n_kv, head_dim, n_ctx, scale, out, (cudaStream_t)stream);
+    return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "prefill attention");
+}
+
 int tmoe_add(tmoe_handle *h, void *stream, const float *a, const float *b, float *out, int64_t n) {
     if (!h) return TMOE_E_INVALID;
     if (n < 0) return fail(h, TMOE_E_INVALID, "bad add size");

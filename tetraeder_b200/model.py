@@ -4,7 +4,8 @@ build_step (crates/model/src/qwen3moe.rs:2777-2826) with attention() (crates/mod
 tmoe_get_rows, tmoe_rms_norm, tmoe_mul_mat (the projections, on the decode GEMV),
 tmoe_qk_norm_rope, tmoe_attn_decode, tmoe_add, the MoE layer (tmoe_layer with the FFN norm) and
 tmoe_argmax; a step is stream-ordered and allocation-free, so it can be captured in a CUDA graph
-(Qwen3MoeModel.graph).
+(Qwen3MoeModel.graph).  Qwen3MoeModel.prefill runs the prompt of one sequence as one multi-token
+step (tmoe_attn_prefill for the causal attention).
 
 Weights come from a GGUF file (from_gguf: the reference's load_weights, qwen3moe.rs:2498-2584) or
 are synthetic (synthetic: seeded N(0, std) weights quantised on the device)."""
@@ -213,6 +214,79 @@ class Qwen3MoeModel:
         self._step(tokens, pos, B, stream)
         return self.logits[:B]
 
+    # -- prefill ---------------------------------------------------------------------------
+    def _prefill_buffers(self, S: int):
+        """Buffers and the MoE handle of a prefill of up to S tokens (made on first use)."""
+        if getattr(self, "_pf_cap", 0) >= S:
+            return
+        hp, f = self.hp, dict(dtype=torch.float32, device=self.device)
+        d, nh, nkv, H = hp.head_dim, hp.n_head, hp.n_head_kv, hp.n_embd
+        if getattr(self, "_pf_moe", None) is not None:
+            self._pf_moe.close()
+        self._pf_moe = MoeLayer(H, hp.n_ff_exp, hp.n_expert, hp.n_expert_used, gate_type=self.moe.cfg.gate_type,
+                                up_type=self.moe.cfg.up_type, down_type=self.moe.cfg.down_type, max_tokens=S,
+                                device=self.device.index, rms_eps=hp.rms_eps)
+        self._pf = {n: torch.empty((S, c), **f) for n, c in
+                    (("x", H), ("cur", H), ("q", nh * d), ("k", nkv * d), ("v", nkv * d), ("att", nh * d),
+                     ("o", H), ("ffn_inp", H), ("moe_out", H))}
+        self._pf_pos = torch.empty((S,), dtype=torch.int32, device=self.device)
+        self._pf_cap = S
+
+    def prefill(self, tokens: torch.Tensor, seq: int = 0, pos0: int = 0, stream=None) -> torch.Tensor:
+        """The prompt step of one sequence (build_step over S tokens, attention_seqs with the causal
+        mask, attn.rs:269-302): tokens int32 CUDA [S] go to positions pos0 .. pos0+S-1 of sequence
+        `seq`'s caches, every layer runs on all S rows at once (the projections on the GEMV with token
+        groups, the MoE layer on its large-batch path from S * k >= 6144 pairs, the causal attention
+        on the tensor cores), and the head runs on the last row.  Returns its logits [1, n_vocab]; the
+        greedy next token is next_tokens[0].  Decoding of the sequence then continues at pos0 + S."""
+        hp, w, L, h = self.hp, self.w, self.lib, self.h
+        S = tokens.shape[0]
+        if not 0 <= seq < self.max_batch or pos0 < 0 or pos0 + S > self.n_ctx:
+            raise ValueError(f"prefill of {S} tokens at {pos0} of sequence {seq}: the caches hold "
+                             f"{self.max_batch} sequences of {self.n_ctx} positions")
+        self._prefill_buffers(S)
+        b = {n: t[:S] for n, t in self._pf.items()}
+        st = _stream(stream)
+        main = torch.cuda.current_stream(self.device) if stream is None else stream
+        d, nh, nkv, H = hp.head_dim, hp.n_head, hp.n_head_kv, hp.n_embd
+        chk = lambda rc: _lib.check(rc, h)  # noqa: E731
+        pos = self._pf_pos[:S]
+        with torch.cuda.stream(main):
+            torch.arange(pos0, pos0 + S, dtype=torch.int32, device=self.device, out=pos)
+        emb = w["token_embd.weight"]
+        chk(L.tmoe_get_rows(h, st, emb.type, C.c_void_p(emb.data.data_ptr()), emb.nb1, H, emb.rows, _ptr(tokens), S,
+                            _ptr(b["x"])))
+        for il in range(hp.n_layer):
+            p = f"blk.{il}."
+            chk(L.tmoe_rms_norm(h, st, _ptr(b["x"]), _ptr(w[p + "attn_norm.weight"]), hp.rms_eps, S, H,
+                                _ptr(b["cur"])))
+            self._fork.record(main)
+            for side, lane, wm, out, join in zip(self._side, self._lanes, (w[p + "attn_k.weight"], w[p + "attn_v.weight"]),
+                                                 (b["k"], b["v"]), self._join):
+                side.wait_event(self._fork)
+                self._mm(wm, b["cur"], out, S, _stream(side), h=lane.h)
+                join.record(side)
+            self._mm(w[p + "attn_q.weight"], b["cur"], b["q"], S, st)
+            for join in self._join:
+                main.wait_event(join)
+            chk(L.tmoe_qk_norm_rope(h, st, _ptr(b["q"]), _ptr(b["k"]), _ptr(w[p + "attn_q_norm.weight"]),
+                                    _ptr(w[p + "attn_k_norm.weight"]), _ptr(pos), S, nh, nkv, d, hp.n_rot,
+                                    hp.rope_freq_base, hp.rms_eps))
+            chk(L.tmoe_attn_prefill(h, st, _ptr(b["q"]), _ptr(b["k"]), _ptr(b["v"]), _ptr(self.kc[il]),
+                                    _ptr(self.vc[il]), seq, self.max_batch, pos0, S, nh, nkv, d, self.n_ctx,
+                                    1.0 / d ** 0.5, _ptr(b["att"])))
+            self._mm(w[p + "attn_output.weight"], b["att"], b["o"], S, st)
+            chk(L.tmoe_add(h, st, _ptr(b["x"]), _ptr(b["o"]), _ptr(b["ffn_inp"]), S * H))
+            self._pf_moe.moe_ffn(b["ffn_inp"], self.experts[il], router_w=w[p + "ffn_gate_inp.weight"],
+                                 ffn_norm=w[p + "ffn_norm.weight"], use_norm=True, out=b["moe_out"], stream=stream)
+            chk(L.tmoe_add(h, st, _ptr(b["ffn_inp"]), _ptr(b["moe_out"]), _ptr(b["x"]), S * H))
+        last = b["x"][S - 1:]
+        chk(L.tmoe_rms_norm(h, st, _ptr(last), _ptr(w["output_norm.weight"]), hp.rms_eps, 1, H, _ptr(self.cur)))
+        head = w["token_embd.weight"] if hp.tied_output else w["output.weight"]
+        self._mm(head, self.cur, self.logits, 1, st)
+        chk(L.tmoe_argmax(h, st, _ptr(self.logits), 1, hp.n_vocab, _ptr(self.next_tokens)))
+        return self.logits[:1]
+
     def graph(self, tokens: torch.Tensor, pos: torch.Tensor):
         """A CUDA graph of decode(tokens, pos) for these (fixed) token and position buffers:
         update them in place, then replay.  Run decode once before capturing (the projections'
@@ -226,10 +300,14 @@ class Qwen3MoeModel:
 
     def check(self):
         self.moe.check()
+        if getattr(self, "_pf_moe", None) is not None:
+            self._pf_moe.check()
         for lane in self._lanes:
             lane.check()
 
     def close(self):
+        if getattr(self, "_pf_moe", None) is not None:
+            self._pf_moe.close()
         for lane in self._lanes:
             lane.close()
         self.moe.close()
