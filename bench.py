@@ -56,8 +56,7 @@ def set_shape(name):
     """c2: the Qwen3-30B-A3B layer (the metric's config); 235b: the Qwen3-235B-A22B layer of config 4
     (hidden 4096, moe_intermediate 1536, 128 experts, top-8, all Q4_K)."""
     global H, I, DOWN_T, EXPERT_BYTES, GATE_UP_BYTES, DOWN_BYTES, ROUTER_BYTES
-    if name == "235b":
-        H, I, DOWN_T = 4096, 1536, Q4K
+    H, I, DOWN_T = (4096, 1536, Q4K) if name == "235b" else (2048, 768, Q6K)
     down_block = 210 if DOWN_T == Q6K else 144
     GATE_UP_BYTES = 2 * I * (H // 256) * 144
     DOWN_BYTES = H * (I // 256) * down_block
@@ -94,6 +93,9 @@ def parse():
                    help="streamed mode: also write the routing of --steps steps as a tetraeder-routing v1 trace")
     p.add_argument("--shape", choices=["c2", "235b"], default="c2",
                    help="c2: the Qwen3-30B-A3B layer (the metric's config); 235b: config 4's layer shape")
+    p.add_argument("--no-c4", action="store_true",
+                   help="decode mode: skip the config-4 line (the 235B-shaped layer, expert-parallel over the ranks "
+                        "at N > 1) added to the C2 line")
     p.add_argument("--ep", choices=["a2a", "allreduce"], default="a2a",
                    help="N > 1: a2a = each rank its own --tokens, dispatched to the experts' ranks (all-to-all); "
                         "allreduce = the reference's EP mode, the same tokens on every rank, outputs summed")
@@ -428,6 +430,24 @@ def run_ours(args, rank, world, local_rank):
     if comm is not None:
         comm.close()
     return result
+
+
+def c4_line(args, rank, world, local_rank):
+    """Config 4 beside the C2 line: the Qwen3-235B-A22B-shaped layer (H 4096, I 1536, 128 experts
+    top-8, all Q4_K) at decode T = --tokens per rank, 16 distinct layers (21.7 GB of experts over the
+    ranks, above L2), the experts split contiguously over the ranks and the tokens dispatched
+    all-to-all at N > 1 (the same EP mode as the C2 line)."""
+    import copy
+    a = copy.copy(args)
+    a.shape, a.layers, a.sweep = "235b", 16, False
+    set_shape("235b")
+    try:
+        r = run_ours(a, rank, world, local_rank)
+    finally:
+        set_shape("c2")
+    keep = ("metric", "value", "unit", "n_gpus", "steps", "ms_per_step", "scaling", "config", "roofline",
+            "layer_roofline", "e2e", "gpu_launches", "clocks")
+    return {k: r[k] for k in keep if k in r}
 
 
 def zipf_bias(torch, E_, seed, s_=1.2):
@@ -973,6 +993,8 @@ def main():
         emit(run_gguf(args, local_rank) if args.mode == "gguf" else run_model(args, local_rank))
         return 0
     res = run_streamed(args, local_rank) if args.mode == "streamed" else run_ours(args, rank, world, local_rank)
+    if args.mode == "decode" and args.shape == "c2" and not args.no_c4:
+        res["c4"] = c4_line(args, rank, world, local_rank)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(args)

@@ -26,7 +26,9 @@ struct tmoe_comm {
 namespace tmoe {
 
 // Polls the communicator until its pending operation leaves ncclInProgress; after `timeout_s`
-// it aborts the communicator (which is then unusable: c->comm = NULL).
+// it aborts the communicator (which is then unusable: c->comm = NULL).  An enqueue of a step's
+// exchange normally completes within microseconds, so the first 200 us only yield the thread
+// between polls; longer waits (communicator setup, a slow peer) sleep 20 us at a time.
 static ncclResult_t nccl_wait(tmoe_comm *c) {
     const auto t0 = std::chrono::steady_clock::now();
     for (;;) {
@@ -40,7 +42,10 @@ static ncclResult_t nccl_wait(tmoe_comm *c) {
             c->comm = nullptr;
             return ncclInternalError;
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if (dt < 200e-6)
+            std::this_thread::yield();
+        else
+            std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
 }
 

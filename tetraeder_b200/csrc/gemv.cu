@@ -787,8 +787,11 @@ struct GemvPlan {
 };
 
 // Q4_K: a chunk of two super-blocks (a 288-byte row stride: the 8-byte fragment loads of rows
-// g = 0..7 hit distinct banks) with two CTAs per SM and as many slots as fit.  Q6_K: all of K;
-// two CTAs per SM if a slot per warp fits, else one.
+// g = 0..7 hit distinct banks) with two CTAs per SM and two slots per warp: a third slot fits but
+// was slower (C2 decode T = 64: gate/up 61.7 us against 60.5, the layer 129.7 against 126.4 us),
+// the 36 KB it takes per CTA being worth more as L1 for the activation rows.  Q6_K: all of K; two
+// CTAs per SM if a slot per warp fits, else one (one CTA with two slots per warp: down 71.6 us
+// against 56.7 with two CTAs of one slot).
 template <int WT>
 static GemvPlan plan_for(int K) {
     const int nb = K / TMOE_QK;
@@ -796,7 +799,8 @@ static GemvPlan plan_for(int K) {
     const int slot = (WT == TMOE_WT_Q4K ? ITEM_ROWS * TMOE_Q4K_BYTES * cb : ITEM_ROWS * TMOE_Q6K_BYTES * nb + 16) +
                      PERM_STAGE;
     const int d2 = (GEMV_SMEM_2CTA - GEMV_HDR) / (GEMV_NW * slot);
-    if (d2 >= (WT == TMOE_WT_Q4K ? 3 : 1)) return {cb, 2, d2 < GEMV_MAXD ? d2 : GEMV_MAXD};
+    if (WT == TMOE_WT_Q4K && d2 >= 2) return {cb, 2, 2};
+    if (d2 >= 1) return {cb, 2, d2 < GEMV_MAXD ? d2 : GEMV_MAXD};
     const int d1 = (GEMV_SMEM_1CTA - GEMV_HDR) / (GEMV_NW * slot);
     if (d1 >= 1) return {cb, 1, d1 < GEMV_MAXD ? d1 : GEMV_MAXD};
     return {0, 0, 0};
