@@ -520,8 +520,13 @@ static size_t route_fused_smem(int tt, int H, int T, int k, int n_slots) {
     return staged > sorting ? staged : sorting;
 }
 
+// Tokens per CTA: the batch itself below 8 tokens (rounded up to a power of two, so that a CTA
+// computes no dot products of empty token rows: at T = 1 a tile of 8 did eight times the work),
+// else 8, or 4 when 8 staged rows do not fit.
 static int route_fused_tt(int H, int T, int k, int n_slots) {
-    for (int tt = 8; tt >= 4; tt >>= 1)
+    int want = 8;
+    while (want > 1 && want / 2 >= T) want /= 2;
+    for (int tt = want; tt >= (want < 4 ? want : 4); tt >>= 1)
         if (route_fused_smem(tt, H, T, k, n_slots) <= 200 * 1024) return tt;
     return 0;
 }
@@ -546,7 +551,7 @@ cudaError_t launch_route_fused(const float *x, const float *rw, int T, int H, in
     const dim3 grid((E + FR_WARPS - 1) / FR_WARPS, (T + tt - 1) / tt);
     const Q8Rows none{nullptr, nullptr, nullptr, nullptr, 0};
     const Q8Rows qq = q8 ? *q8 : none;
-    static int cache[8][64] = {};
+    static int cache[16][64] = {};
 #define TMOE_RF(TTV, MP, CI)                                                                                   \
     do {                                                                                                       \
         cudaError_t e = set_smem_once(route_fused_kernel<TTV, MP>, smem, cache[CI]);                           \
@@ -556,17 +561,18 @@ cudaError_t launch_route_fused(const float *x, const float *rw, int T, int H, in
             perm, active, n_active, counters, n_counters, done, err);                                           \
     } while (0)
     const int mp = E <= 32 ? 1 : E <= 64 ? 2 : E <= 128 ? 4 : 8;
-    if (tt == 8) {
-        if (mp == 1) TMOE_RF(8, 1, 0);
-        else if (mp == 2) TMOE_RF(8, 2, 1);
-        else if (mp == 4) TMOE_RF(8, 4, 2);
-        else TMOE_RF(8, 8, 3);
-    } else {
-        if (mp == 1) TMOE_RF(4, 1, 4);
-        else if (mp == 2) TMOE_RF(4, 2, 5);
-        else if (mp == 4) TMOE_RF(4, 4, 6);
-        else TMOE_RF(4, 8, 7);
-    }
+#define TMOE_RF_TT(TTV, C0)                      \
+    do {                                         \
+        if (mp == 1) TMOE_RF(TTV, 1, C0);        \
+        else if (mp == 2) TMOE_RF(TTV, 2, C0 + 1); \
+        else if (mp == 4) TMOE_RF(TTV, 4, C0 + 2); \
+        else TMOE_RF(TTV, 8, C0 + 3);            \
+    } while (0)
+    if (tt == 8) TMOE_RF_TT(8, 0);
+    else if (tt == 4) TMOE_RF_TT(4, 4);
+    else if (tt == 2) TMOE_RF_TT(2, 8);
+    else TMOE_RF_TT(1, 12);
+#undef TMOE_RF_TT
 #undef TMOE_RF
     return cudaGetLastError();
 }
