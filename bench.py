@@ -75,7 +75,8 @@ def parse():
     p.add_argument("--seed", type=int, default=20261201)
     p.add_argument("--cpu-sample-s", type=float, default=15.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--sweep", action="store_true", help="also time T in {1,4,16,64}")
+    p.add_argument("--no-sweep", dest="sweep", action="store_false",
+                   help="decode mode at N = 1: skip the extra key that times T in {1, 4, 16, 64}")
     p.add_argument("--ctx", type=int, default=4096, help="model mode: the context each sequence decodes at")
     p.add_argument("--prefill", type=int, default=2048,
                    help="model mode: also time the prefill of one prompt of this many random tokens (0: skip)")
@@ -423,7 +424,7 @@ def run_ours(args, rank, world, local_rank):
     elif ep:
         result["config"]["parallelism"] = f"ep{world} (experts split contiguously, tokens replicated, NCCL all-reduce)"
         result["scaling"] = "strong"
-    if args.sweep and rank == 0 and not ep:
+    if args.sweep and args.mode == "decode" and rank == 0 and not ep:
         result["sweep"] = sweep_tokens(torch, tb, layers, dev)
     del graph
     torch.cuda.synchronize()
