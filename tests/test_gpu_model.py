@@ -363,3 +363,32 @@ def test_chunked_prefill_equals_one_prefill(tiny_model):
                 float((one.kc[il][0, :S].float() - one.kc[il][1, :S].float()).abs().max()) < 5e-2
     finally:
         one.close()
+
+
+@pytest.mark.parametrize("qtype,K,N,T", [(12, 2048, 4096, 512), (14, 2048, 512, 2048), (12, 4096, 2048, 700)])
+def test_mul_mat_prompt_batches_on_the_gemm(qtype, K, N, T):
+    """From 512 tokens tmoe_mul_mat runs as one tcgen05 GEMM over the fp16-dequantised matrix (x
+    through the Q8_K round trip, then fp16): held to the oracle's Q8_K mul_mat at the large-batch
+    bound of the MoE layer's down GEMM (normalised RMS 1e-3, max-abs 2.5e-2 x RMS); reuse_x takes
+    the same rows for a second matrix."""
+    import ctypes as C
+    from tests.common import maxabs_over_rms
+    rng = np.random.default_rng(K + N + T)
+    W = np.ascontiguousarray(O.quantize(qtype, (rng.standard_normal((N, K)) * 0.05).astype(np.float32)))
+    W2 = np.ascontiguousarray(O.quantize(qtype, (rng.standard_normal((256, K)) * 0.05).astype(np.float32)))
+    x = rng.standard_normal((T, K)).astype(np.float32)
+    layer = tb.MoeLayer(512, 256, 8, 2, gate_type=12, up_type=12, down_type=12, max_tokens=4)
+    lib, h = layer.lib, layer.h
+    dW, dW2, dx = (torch.from_numpy(a).cuda() for a in (W, W2, x))
+    out, out2 = torch.empty((T, N), device="cuda"), torch.empty((T, 256), device="cuda")
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    nb1 = W.shape[1]
+    assert lib.tmoe_mul_mat(h, None, qtype, P(dW), nb1, K, N, P(dx), T, 0, P(out)) == 0
+    assert lib.tmoe_mul_mat(h, None, qtype, P(dW2), nb1, K, 256, P(dx), T, 1, P(out2)) == 0
+    layer.check()
+    for w_, o_, n_ in ((W, out, N), (W2, out2, 256)):
+        want = O.mul_mat_id(qtype, w_.reshape(1, n_, -1), K, n_, 1, x[:, None, :], np.zeros((T, 1), np.int32))[:, 0]
+        got = o_.cpu().numpy()
+        assert nrms(got, want) <= 1e-3 and maxabs_over_rms(got, want) <= 2.5e-2, \
+            f"nrms {nrms(got, want):.2e} maxabs/rms {maxabs_over_rms(got, want):.2e}"
+    layer.close()

@@ -428,7 +428,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(const __gri
                     }
                 }
             } else {
-                const int p = valid ? __ldg(a.perm + r) : 0;
+                const int p = valid ? (a.perm ? __ldg(a.perm + r) : r) : 0;  // no perm: rows in place (dense)
                 float *orow = a.out + (int64_t)p * a.N + n * PF_BN;
 #pragma unroll 1
                 for (int c0 = 0; c0 < PF_BN; c0 += 32) {

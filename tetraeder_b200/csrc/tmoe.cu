@@ -24,6 +24,9 @@ constexpr int kCounters = 4;
 // few rows it has.  On a Qwen3-30B-shaped layer (128 experts, top-8) the two meet between
 // 4096 pairs (GEMV 470 us, GEMMs 583 us) and 8192 (GEMV 784 us, GEMMs 581 us).
 constexpr int64_t kPrefillMinPairs = 6144;
+// Tokens from which tmoe_mul_mat runs as one tcgen05 GEMM over fp16-dequantised weights instead of
+// the decode GEMV (a prompt's projections; decode batches stay on the GEMV's exact integer sums).
+constexpr int64_t kDenseGemmMinTokens = 512;
 thread_local std::string g_create_error;
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -42,6 +45,7 @@ struct tmoe_handle {
     int dense_wt = -1;
     int64_t dense_k = 0, dense_t = 0;
     bool dense_nosplit = false;  // the GEMV took no tensor map over a matrix's K slices
+    bool dense_a16 = false;      // the fp16 A rows of dense_x are in the workspace (the GEMM path)
     // routing
     float *logits = nullptr;
     int32_t *ids = nullptr;
@@ -874,6 +878,48 @@ int tmoe_mul_mat(tmoe_handle *h, void *stream, int32_t type, const void *W, size
         need = align_up(need + bytes, 256);
         return o;
     };
+    if (T >= kDenseGemmMinTokens && N % 256 == 0 && N <= (1 << 20)) {
+        // A prompt-sized batch: the matrix dequantised to fp16 once and one tcgen05 GEMM over all rows
+        // (x through the same Q8_K round trip, then fp16), the large-batch MoE path's down GEMM with
+        // one expert and the rows in place.  fp16 weights are its only departure from the GEMV's sums.
+        const size_t o_a = lay((size_t)T * K * 2), o_w = lay((size_t)N * K * 2), o_act = lay(16), o_na = lay(4),
+                     o_ts = lay(16), o_perm = lay((size_t)T * 4);
+        cudaError_t e;
+        if (need > h->dense_ws_bytes) {
+            if (reuse) return fail(h, TMOE_E_INVALID, "reuse_x before the workspace exists");
+            if (h->dense_ws) {
+                cudaStreamSynchronize(st);
+                cudaFree(h->dense_ws);
+                h->dense_ws = nullptr;
+                h->dense_ws_bytes = 0;
+                h->dense_x = nullptr;
+            }
+            if ((e = cudaMalloc(&h->dense_ws, need)) != cudaSuccess)
+                return fail(h, TMOE_E_NOMEM, "cudaMalloc(%zu): %s", need, cudaGetErrorString(e));
+            h->dense_ws_bytes = need;
+        }
+        char *base = (char *)h->dense_ws;
+        __half *a16 = (__half *)(base + o_a), *w16 = (__half *)(base + o_w);
+        int4 *act = (int4 *)(base + o_act);
+        int32_t *na = (int32_t *)(base + o_na);
+        int *ts = (int *)(base + o_ts);
+        int32_t *perm = (int32_t *)(base + o_perm);
+        if (!(reuse && h->dense_a16)) {
+            if ((e = tmoe::launch_prep_rows(x, nullptr, (int)T, nullptr, 1, (int)K, a16, st)) != cudaSuccess)
+                return cuda_fail(h, e, "mul_mat rows");
+            h->dense_x = x, h->dense_wt = wt, h->dense_k = K, h->dense_t = T, h->dense_a16 = true;
+        }
+        // one active "expert" (the matrix) over rows [0, T)
+        if ((e = tmoe::launch_dense_prep((int)T, (int)T, 1, act, na, perm, nullptr, 0, st)) != cudaSuccess)
+            return cuda_fail(h, e, "mul_mat tile table");
+        if ((e = tmoe::launch_dequant_f16(wt, (const uint8_t *)W, 0, (int)N, (int)K, act, na, 1, w16, st)) !=
+            cudaSuccess)
+            return cuda_fail(h, e, "mul_mat dequant");
+        if ((e = tmoe::launch_prefill_gemm(false, a16, (int)T, (int)K, w16, nullptr, 1, (int)N, act, na, 1, ts,
+                                           nullptr, out, h->err, h->sm_count, st)) != cudaSuccess)
+            return cuda_fail(h, e, "mul_mat gemm");
+        return TMOE_OK;
+    }
     const size_t nbw = (size_t)tmoe::q8_nbw(wt);
     const size_t o_q = lay((size_t)T * K), o_d = lay((size_t)T * (K / 256) * 4);
     const size_t o_bl = lay((size_t)T * (K / 256) * nbw * 4), o_bh = lay((size_t)T * (K / 256) * nbw * 4);
@@ -919,7 +965,7 @@ int tmoe_mul_mat(tmoe_handle *h, void *stream, int32_t type, const void *W, size
     if (!reuse) {
         if ((e = tmoe::launch_quantize_q8k(x, T, (int)K, nullptr, tmoe::Q8Rows{q, d, bl, bh, wt}, st)) != cudaSuccess)
             return cuda_fail(h, e, "quantize x");
-        h->dense_x = x, h->dense_wt = wt, h->dense_k = K, h->dense_t = T;
+        h->dense_x = x, h->dense_wt = wt, h->dense_k = K, h->dense_t = T, h->dense_a16 = false;
     }
     for (;;) {
         if ((e = tmoe::launch_dense_prep((int)T, kGroup, ks, act, na, perm, work, kCounters, st)) != cudaSuccess)
