@@ -345,6 +345,111 @@ float tmo_vec_dot_q6k_q8k(int64_t ncols, const void *w, const tmo_block_q8k *x) 
 }
 
 /* ------------------------------------------------------------------------ */
+/* SIMD forms of the two dots (AVX2), used by mul_mat_id / experts            */
+/* ------------------------------------------------------------------------ */
+/* ggml's CPU path computes the same integer sub-block sums with byte multiply-adds (maddubs:
+ * unsigned weight bytes times signed activation bytes, pairs summed to 16 bits, then to 32).  These
+ * restate that method on the same blocks: the integer sums are exact, and the float scaling is the
+ * scalar functions' statement for statement, so the results equal tmo_vec_dot_q4k_q8k /
+ * tmo_vec_dot_q6k_q8k bit for bit (tests/test_oracle.py checks it).  They make the timed CPU
+ * baseline a vectorised CPU path, as the reference's is. */
+#if defined(__AVX2__)
+#include <immintrin.h>
+
+/* Sum of the 8 int32 lanes, and of the 4 lanes of each 128-bit half. */
+static inline int32_t hsum8(__m256i v) {
+    __m128i s = _mm_add_epi32(_mm256_castsi256_si128(v), _mm256_extracti128_si256(v, 1));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0x4e));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0xb1));
+    return _mm_cvtsi128_si32(s);
+}
+static inline int32_t hsum4(__m128i s) {
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0x4e));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0xb1));
+    return _mm_cvtsi128_si32(s);
+}
+
+/* 32 unsigned bytes (at most 63) times 32 signed bytes -> 8 int32 partial sums (exact). */
+static inline __m256i dot32(__m256i u, __m256i s) {
+    return _mm256_madd_epi16(_mm256_maddubs_epi16(u, s), _mm256_set1_epi16(1));
+}
+
+float tmo_vec_dot_q4k_q8k_simd(int64_t ncols, const void *w, const tmo_block_q8k *x) {
+    const uint8_t *blk = (const uint8_t *)w;
+    const __m256i low = _mm256_set1_epi8(0x0f);
+    float acc = 0.f;
+    for (int64_t b = 0; b < ncols / TMO_QK_K; b++, blk += TMO_Q4K_BYTES) {
+        const int8_t *q8 = x[b].qs;
+        const uint8_t *qs = blk + 16;
+        int32_t isum = 0, msum = 0;
+        for (int j = 0; j < 4; j++) {
+            int sc0, m0, sc1, m1;
+            q4k_scale_min(blk + 4, 2 * j, &sc0, &m0);
+            q4k_scale_min(blk + 4, 2 * j + 1, &sc1, &m1);
+            const __m256i qv = _mm256_loadu_si256((const __m256i *)(qs + 32 * j));
+            const __m256i lo = _mm256_and_si256(qv, low), hi = _mm256_and_si256(_mm256_srli_epi16(qv, 4), low);
+            const int32_t s0 = hsum8(dot32(lo, _mm256_loadu_si256((const __m256i *)(q8 + 64 * j))));
+            const int32_t s1 = hsum8(dot32(hi, _mm256_loadu_si256((const __m256i *)(q8 + 64 * j + 32))));
+            isum += sc0 * s0 + sc1 * s1;
+            msum += m0 * (x[b].bsums[4 * j] + x[b].bsums[4 * j + 1]) +
+                    m1 * (x[b].bsums[4 * j + 2] + x[b].bsums[4 * j + 3]);
+        }
+        float d = tmo_f16_to_f32(rd16(blk)) * x[b].d;
+        float dmin = tmo_f16_to_f32(rd16(blk + 2)) * x[b].d;
+        acc += d * (float)isum;
+        acc -= dmin * (float)msum;
+    }
+    return acc;
+}
+
+/* Q6_K: per 128-element half h, element r of the half is the low nibble of ql[64h + r] (r < 64) or
+ * the high nibble of ql[64h + r - 64], with bits 4-5 from qh[32h + r % 32] >> 2 (r / 32); the 6-bit
+ * value goes in unsigned and the -32 is -32 times the activation's 16-element block sum. */
+float tmo_vec_dot_q6k_q8k_simd(int64_t ncols, const void *w, const tmo_block_q8k *x) {
+    const uint8_t *blk = (const uint8_t *)w;
+    const __m256i low = _mm256_set1_epi8(0x0f), two = _mm256_set1_epi8(0x03);
+    float acc = 0.f;
+    for (int64_t b = 0; b < ncols / TMO_QK_K; b++, blk += TMO_Q6K_BYTES) {
+        const uint8_t *ql = blk, *qh = blk + 128;
+        const int8_t *scp = (const int8_t *)(blk + 192);
+        const int8_t *q8 = x[b].qs;
+        int32_t isum = 0;
+        for (int h = 0; h < 2; h++) {
+            const __m256i l0 = _mm256_loadu_si256((const __m256i *)(ql + 64 * h));
+            const __m256i l1 = _mm256_loadu_si256((const __m256i *)(ql + 64 * h + 32));
+            const __m256i hb = _mm256_loadu_si256((const __m256i *)(qh + 32 * h));
+            __m256i q[4];
+            q[0] = _mm256_or_si256(_mm256_and_si256(l0, low), _mm256_slli_epi16(_mm256_and_si256(hb, two), 4));
+            q[1] = _mm256_or_si256(_mm256_and_si256(l1, low),
+                                   _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(hb, 2), two), 4));
+            q[2] = _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(l0, 4), low),
+                                   _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(hb, 4), two), 4));
+            q[3] = _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(l1, 4), low),
+                                   _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(hb, 6), two), 4));
+            for (int v = 0; v < 4; v++) {
+                const int base = 128 * h + 32 * v; /* elements base .. base+31: sub-blocks s, s+1 */
+                const __m256i p = dot32(q[v], _mm256_loadu_si256((const __m256i *)(q8 + base)));
+                const int s = base / 16;
+                const int32_t ss0 = hsum4(_mm256_castsi256_si128(p)) - 32 * x[b].bsums[s];
+                const int32_t ss1 = hsum4(_mm256_extracti128_si256(p, 1)) - 32 * x[b].bsums[s + 1];
+                isum += scp[s] * ss0 + scp[s + 1] * ss1;
+            }
+        }
+        float d = tmo_f16_to_f32(rd16(blk + 208)) * x[b].d;
+        acc += d * (float)isum;
+    }
+    return acc;
+}
+#else
+float tmo_vec_dot_q4k_q8k_simd(int64_t ncols, const void *w, const tmo_block_q8k *x) {
+    return tmo_vec_dot_q4k_q8k(ncols, w, x);
+}
+float tmo_vec_dot_q6k_q8k_simd(int64_t ncols, const void *w, const tmo_block_q8k *x) {
+    return tmo_vec_dot_q6k_q8k(ncols, w, x);
+}
+#endif
+
+/* ------------------------------------------------------------------------ */
 /* canonical router arithmetic                                               */
 /* ------------------------------------------------------------------------ */
 
@@ -530,8 +635,8 @@ static void prep_act(int type, const float *x, int64_t K, tmo_block_q8k *q, floa
 
 static float row_dot(int type, int mode, const uint8_t *wrow, int64_t K, const tmo_block_q8k *q,
                      const float *deq, float *scratch) {
-    if (mode == TMO_MODE_Q8K && type == TMO_TYPE_Q4_K) return tmo_vec_dot_q4k_q8k(K, wrow, q);
-    if (mode == TMO_MODE_Q8K && type == TMO_TYPE_Q6_K) return tmo_vec_dot_q6k_q8k(K, wrow, q);
+    if (mode == TMO_MODE_Q8K && type == TMO_TYPE_Q4_K) return tmo_vec_dot_q4k_q8k_simd(K, wrow, q);
+    if (mode == TMO_MODE_Q8K && type == TMO_TYPE_Q6_K) return tmo_vec_dot_q6k_q8k_simd(K, wrow, q);
     tmo_dequantize(type, wrow, scratch, K);
     double s = 0.0;
     for (int64_t i = 0; i < K; i++) s += (double)scratch[i] * (double)deq[i];

@@ -100,6 +100,9 @@ void tmo_dequantize_q8k(const tmo_block_q8k *y, float *x, int64_t n);
 /* One weight row (ncols) against one Q8_K activation row. */
 float tmo_vec_dot_q4k_q8k(int64_t ncols, const void *w, const tmo_block_q8k *x);
 float tmo_vec_dot_q6k_q8k(int64_t ncols, const void *w, const tmo_block_q8k *x);
+/* The same two dots with AVX2 byte multiply-adds (bit-identical results; mul_mat_id uses these). */
+float tmo_vec_dot_q4k_q8k_simd(int64_t ncols, const void *w, const tmo_block_q8k *x);
+float tmo_vec_dot_q6k_q8k_simd(int64_t ncols, const void *w, const tmo_block_q8k *x);
 
 /* --- canonical router arithmetic (bit-exact with the CUDA path) --------- */
 /* e^x for finite x <= 0 (Cody-Waite reduction by ln 2, degree-7 Taylor). */

@@ -86,6 +86,30 @@ def test_vec_dot_within_iqk_bound(qt, ncols):
         assert abs(got - ref) <= 1e-5 * float(np.sum(np.abs(wd * xd))) + 1e-6
 
 
+@pytest.mark.parametrize("qt", [O.TYPE_Q4_K, O.TYPE_Q6_K])
+def test_simd_dots_equal_the_scalar_restatement(qt):
+    """The AVX2 dots that mul_mat_id runs (byte multiply-adds, as ggml's CPU path) against the
+    scalar restatement, bit for bit: fitted rows, random valid blocks (every nibble, scale and high
+    bit pattern), and activations at the Q8_K extremes."""
+    from tests.common import random_kquant_bytes
+    rng = np.random.default_rng(qt)
+    ncols = 2048
+    rows = [O.quantize(qt, rng.uniform(-1, 1, (16, ncols)).astype(np.float32)),
+            random_kquant_bytes(rng, qt, 64, ncols, 1.0)]
+    xs = [rng.uniform(-1, 1, ncols), rng.standard_normal(ncols) * 30,
+          np.where(rng.random(ncols) < 0.5, -1.0, 1.0) * 127]
+    scalar = O.lib().tmo_vec_dot_q4k_q8k if qt == O.TYPE_Q4_K else O.lib().tmo_vec_dot_q6k_q8k
+    simd = O.lib().tmo_vec_dot_q4k_q8k_simd if qt == O.TYPE_Q4_K else O.lib().tmo_vec_dot_q6k_q8k_simd
+    for x in xs:
+        xq = O.quantize_q8k(np.asarray(x, np.float32))
+        for block in rows:
+            for r in range(block.shape[0]):
+                row = np.ascontiguousarray(block[r])
+                a = np.float32(scalar(ncols, row.ctypes.data, xq.ctypes.data))
+                b = np.float32(simd(ncols, row.ctypes.data, xq.ctypes.data))
+                assert a.view(np.uint32) == b.view(np.uint32), (r, float(a), float(b))
+
+
 TYPES = [O.TYPE_Q4_K, O.TYPE_Q6_K]
 
 
