@@ -183,6 +183,21 @@ extern "C" {
         ids_out: *mut i32,
         w_out: *mut f32,
     ) -> c_int;
+    pub fn tmoe_layer_bf16(
+        h: *mut tmoe_handle,
+        stream: *mut c_void,
+        x: *const uint16_t,
+        T: i64,
+        use_norm: i32,
+        norm_w: *const f32,
+        router_w: *const f32,
+        logits: *const f32,
+        id_map: *const i32,
+        wts: *const tmoe_expert_tensors,
+        out: *mut f32,
+        ids_out: *mut i32,
+        w_out: *mut f32,
+    ) -> c_int;
     pub fn tmoe_comm_unique_id(id_out: *mut c_void) -> c_int;
     pub fn tmoe_comm_init(
         id: *const c_void,

@@ -168,6 +168,14 @@ TMOE_API int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T,
                const float *norm_w, const float *router_w, const float *logits,
                const int32_t *id_map, const tmoe_expert_tensors *wts, float *out,
                int32_t *ids_out, float *w_out);
+/* tmoe_layer with bf16 activations x [T][H] (the x_dtype of the survey's boundary: a caller whose
+ * hidden state is bf16).  The rows are widened to f32, which is exact, into the handle's workspace,
+ * and then the layer runs as tmoe_layer on them, so the results equal tmoe_layer's on the f32
+ * values bit for bit.  `out` stays f32. */
+TMOE_API int tmoe_layer_bf16(tmoe_handle *h, void *stream, const uint16_t *x, int64_t T, int32_t use_norm,
+                             const float *norm_w, const float *router_w, const float *logits,
+                             const int32_t *id_map, const tmoe_expert_tensors *wts, float *out,
+                             int32_t *ids_out, float *w_out);
 
 /* --- expert parallelism (qwen3moe_shard.rs:1038-1056) ----------------------------------------
  * A communicator over the ranks of an expert-parallel group, one rank per GPU (NCCL).  Rank 0

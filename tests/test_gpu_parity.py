@@ -311,3 +311,32 @@ def test_misaligned_tensors_are_rejected():
     w = torch.ones(4, k, device="cuda")
     with pytest.raises(tb.TmoeError, match="aligned"):
         layer.weighted_experts(x, ids, w, tb.ExpertWeights(bad, good, down))
+
+
+def test_layer_bf16_input_equals_f32_of_the_same_values():
+    """tmoe_layer_bf16 (bf16 activations at the boundary): the rows are widened to f32 exactly, so
+    the layer's ids, weights and output equal tmoe_layer's on the f32 values bit for bit, and both
+    meet the oracle on them; with the router norm too."""
+    H, I, E, k, T = 2048, 768, 128, 8, 16
+    gate, up, down, rw, _ = _layer_case(H, I, E, k, T, O.TYPE_Q4_K, O.TYPE_Q6_K, 21, False)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(22)
+    xb = torch.randn((T, H), generator=g, device="cuda").to(torch.bfloat16)
+    nw = cuda((1 + 0.1 * np.random.default_rng(23).standard_normal(H)).astype(np.float32))
+    layer = tb.MoeLayer(H, I, E, k, max_tokens=T)
+    wts = tb.ExpertWeights(cuda(gate), cuda(up), cuda(down))
+    for use_norm in (False, True):
+        ids_b, ids_f = (torch.empty((T, k), dtype=torch.int32, device="cuda") for _ in range(2))
+        ob = layer.moe_ffn(xb, wts, router_w=cuda(rw), ffn_norm=nw, use_norm=use_norm, ids_out=ids_b)
+        of = layer.moe_ffn(xb.float(), wts, router_w=cuda(rw), ffn_norm=nw, use_norm=use_norm, ids_out=ids_f)
+        layer.check()
+        assert torch.equal(ids_b, ids_f) and torch.equal(ob, of), f"use_norm={use_norm}"
+    x = host(xb.float())
+    want_ids, want_w, _, _ = O.route(x, k, router_w=rw)
+    ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    out = layer.moe_ffn(xb, wts, router_w=cuda(rw), ids_out=ids)
+    layer.check()
+    assert np.array_equal(host(ids), want_ids)
+    assert_close(host(out), O.experts(x, want_ids, want_w, gate, up, down, H, I, E, O.TYPE_Q4_K, O.TYPE_Q4_K,
+                                      O.TYPE_Q6_K), what="bf16 input")
+    layer.close()

@@ -54,6 +54,7 @@ SIGNATURES = {
     "tmoe_route": ([P, P, P, I64, I32, P, P, P, P, P, P, P], C.c_int),
     "tmoe_experts": ([P, P, P, I64, P, P, C.POINTER(ExpertTensors), P], C.c_int),
     "tmoe_layer": ([P, P, P, I64, I32, P, P, P, P, C.POINTER(ExpertTensors), P, P, P], C.c_int),
+    "tmoe_layer_bf16": ([P, P, P, I64, I32, P, P, P, P, C.POINTER(ExpertTensors), P, P, P], C.c_int),
     "tmoe_map_ids": ([P, P, P, I64, P, I64, P], C.c_int),
     "tmoe_dispatch": ([P, P, P, I64, I32, P, P, P], C.c_int),
     "tmoe_quantize": ([I32, P, I64, I64, P, P], C.c_int),

@@ -55,6 +55,8 @@ cudaError_t launch_softmax_topk(const float *logits, int64_t T, int E, int k, in
 // Q8_K of rows of K f32; rows whose valid entry is negative are skipped (valid may be NULL).
 cudaError_t launch_quantize_q8k(const float *x, int64_t rows, int K, const int32_t *valid, const Q8Rows &out,
                                 cudaStream_t st);
+// bf16 [n] -> f32 [n] (exact; n % 8 == 0 and 16-byte aligned pointers use 16-byte accesses)
+cudaError_t launch_widen_bf16(const uint16_t *x, int64_t n, float *out, cudaStream_t st);
 
 // dispatch.cu
 size_t sort_pairs_smem(int n_slots);

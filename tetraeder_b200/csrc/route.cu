@@ -315,6 +315,18 @@ __global__ void quantize_q8k_kernel(const float *__restrict__ x, int64_t rows, i
     q8k_store_warp(out, row, K, b, q, dd, s16);
 }
 
+// bf16 -> f32: the bf16 bits are the top half of the f32's, so the widening is exact.
+__global__ void widen_bf16_kernel(const uint4 *__restrict__ x, int64_t n8, float4 *__restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n8) return;
+    const uint4 v = x[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    out[2 * i] = make_float4(__uint_as_float(w[0] << 16), __uint_as_float(w[0] & 0xffff0000u),
+                             __uint_as_float(w[1] << 16), __uint_as_float(w[1] & 0xffff0000u));
+    out[2 * i + 1] = make_float4(__uint_as_float(w[2] << 16), __uint_as_float(w[2] & 0xffff0000u),
+                                 __uint_as_float(w[3] << 16), __uint_as_float(w[3] & 0xffff0000u));
+}
+
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_rms_norm(const float *x, const float *norm_w, float eps, int64_t T, int H, float *out,
                             cudaStream_t st) {
@@ -426,6 +438,16 @@ cudaError_t launch_quantize_q8k(const float *x, int64_t rows, int K, const int32
     const int per_block = 8;
     quantize_q8k_kernel<<<(unsigned)((warps + per_block - 1) / per_block), per_block * 32, 0, st>>>(x, rows, K, valid,
                                                                                                     out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_widen_bf16(const uint16_t *x, int64_t n, float *out, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    if (n % 8 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+        return cudaErrorInvalidValue;
+    const int64_t n8 = n / 8;
+    widen_bf16_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, st>>>(reinterpret_cast<const uint4 *>(x), n8,
+                                                                   reinterpret_cast<float4 *>(out));
     return cudaGetLastError();
 }
 

@@ -55,6 +55,7 @@ struct tmoe_handle {
     int4 *active = nullptr;
     // activations: Q8_K of the layer input (read by gate/up) and of the SwiGLU output (read by down)
     float *xn = nullptr;
+    float *x32 = nullptr;  // bf16 layer inputs widened to f32 (tmoe_layer_bf16)
     int8_t *xq = nullptr;
     float *xd = nullptr;
     uint32_t *xbl = nullptr, *xbh = nullptr;
@@ -192,6 +193,7 @@ size_t carve(tmoe_handle *h, char *base) {
     h->perm = (int32_t *)take(P * 4 + 16);  // + the GEMV's bulk-copy round-up
     const size_t nbg = (size_t)tmoe::q8_nbw(wt_of(c.gate_type)), nbd = (size_t)tmoe::q8_nbw(wt_of(c.down_type));
     h->xn = (float *)take(T * H * 4);
+    h->x32 = (float *)take(T * H * 4);
     h->xq = (int8_t *)take(T * H);
     h->xd = (float *)take(T * (H / 256) * 4);
     h->xbl = (uint32_t *)take(T * (H / 256) * nbg * 4);
@@ -716,6 +718,22 @@ int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
         }
     }
     return run_experts(h, st, xn, T, used, w, wts, out, dispatched, x_quantized);
+}
+
+int tmoe_layer_bf16(tmoe_handle *h, void *stream, const uint16_t *x, int64_t T, int32_t use_norm, const float *norm_w,
+                    const float *router_w, const float *logits, const int32_t *id_map, const tmoe_expert_tensors *wts,
+                    float *out, int32_t *ids_out, float *w_out) {
+    if (!h) return TMOE_E_INVALID;
+    const tmoe_config &c = h->cfg;
+    if (T < 0 || T > c.max_tokens) return fail(h, TMOE_E_INVALID, "T=%lld outside [0, max_tokens]", (long long)T);
+    if (!x) return fail(h, TMOE_E_INVALID, "null tensor");
+    if (!aligned16(x)) return fail(h, TMOE_E_INVALID, "x must be 16-byte aligned");
+    if (T == 0) return tmoe_layer(h, stream, h->x32, 0, use_norm, norm_w, router_w, logits, id_map, wts, out, ids_out,
+                                  w_out);
+    DeviceGuard dg(c.device);
+    const cudaError_t e = tmoe::launch_widen_bf16(x, T * c.n_embd, h->x32, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(h, e, "widen bf16");
+    return tmoe_layer(h, stream, h->x32, T, use_norm, norm_w, router_w, logits, id_map, wts, out, ids_out, w_out);
 }
 
 int tmoe_ep_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float *x, int64_t T, int32_t use_norm,

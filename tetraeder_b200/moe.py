@@ -165,13 +165,15 @@ class MoeLayer:
                 logits: torch.Tensor | None = None, id_map: torch.Tensor | None = None,
                 ffn_norm: torch.Tensor | None = None, use_norm: bool = False, out=None, ids_out=None,
                 w_out=None, stream=None):
-        """router + (EP id map) + weighted_experts in one C call -> [T, H]."""
+        """router + (EP id map) + weighted_experts in one C call -> [T, H] f32.  x is f32 or bf16
+        (tmoe_layer_bf16: widened exactly, then the same layer)."""
         T = x.shape[0]
         out = torch.empty((T, self.cfg.n_embd), dtype=torch.float32, device=self.device) if out is None else out
         st = experts.c_struct()
-        _lib.check(self.lib.tmoe_layer(self.h, _stream(stream), _ptr(x), T, int(use_norm), _ptr(ffn_norm),
-                                       _ptr(router_w), _ptr(logits), _ptr(id_map), C.byref(st), _ptr(out),
-                                       _ptr(ids_out), _ptr(w_out)), self.h)
+        fn = self.lib.tmoe_layer_bf16 if x.dtype == torch.bfloat16 else self.lib.tmoe_layer
+        _lib.check(fn(self.h, _stream(stream), _ptr(x), T, int(use_norm), _ptr(ffn_norm),
+                      _ptr(router_w), _ptr(logits), _ptr(id_map), C.byref(st), _ptr(out),
+                      _ptr(ids_out), _ptr(w_out)), self.h)
         return out
 
     def moe_ffn_streamed(self, x: torch.Tensor, cache: "SlotCache", router_w: torch.Tensor | None = None,
