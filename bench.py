@@ -435,20 +435,27 @@ def run_ours(args, rank, world, local_rank):
 
 def c4_line(args, rank, world, local_rank):
     """Config 4 beside the C2 line: the Qwen3-235B-A22B-shaped layer (H 4096, I 1536, 128 experts
-    top-8, all Q4_K) at decode T = --tokens per rank, 16 distinct layers (21.7 GB of experts over the
-    ranks, above L2), the experts split contiguously over the ranks and the tokens dispatched
-    all-to-all at N > 1 (the same EP mode as the C2 line)."""
+    top-8, all Q4_K), the experts split contiguously over the ranks and the tokens dispatched
+    all-to-all at N > 1 (the same EP mode as the C2 line):
+      decode: T = --tokens per rank, 16 distinct layers (21.7 GB of experts over the ranks, above L2);
+      prefill (key "prefill"): T = 4096 per rank, 2 distinct layers, 5 timed steps (the grouped
+      tcgen05 GEMMs; tensor roofline)."""
     import copy
-    a = copy.copy(args)
-    a.shape, a.layers, a.sweep = "235b", 16, False
-    set_shape("235b")
-    try:
-        r = run_ours(a, rank, world, local_rank)
-    finally:
-        set_shape("c2")
     keep = ("metric", "value", "unit", "n_gpus", "steps", "ms_per_step", "scaling", "config", "roofline",
             "layer_roofline", "e2e", "gpu_launches", "clocks")
-    return {k: r[k] for k in keep if k in r}
+    set_shape("235b")
+    try:
+        a = copy.copy(args)
+        a.shape, a.layers, a.sweep = "235b", 16, False
+        r = run_ours(a, rank, world, local_rank)
+        line = {k: r[k] for k in keep if k in r}
+        p = copy.copy(args)
+        p.shape, p.mode, p.tokens, p.layers, p.sweep, p.steps, p.warmup = "235b", "prefill", 4096, 2, False, 5, 3
+        rp = run_ours(p, rank, world, local_rank)
+        line["prefill"] = {k: rp[k] for k in keep if k in rp}
+    finally:
+        set_shape("c2")
+    return line
 
 
 def zipf_bias(torch, E_, seed, s_=1.2):
