@@ -810,9 +810,22 @@ int tmoe_ep_a2a_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float
     // route this rank's tokens and pack the messages; on a failure the rank still takes both
     // exchange steps, with messages that carry no rows
     cudaError_t e = cudaSuccess;
-    rc = T ? tmoe_route(h, stream, x, T, use_norm, norm_w, router_w, logits, ids, w, use_norm ? h->xn : nullptr,
-                        nullptr)
-           : TMOE_OK;
+    if (T && router_w && tmoe::route_fused_fits(T, k, E, H, E)) {
+        // decode batches: the fused routing kernel (logits, top-k and a dispatch the exchange does not
+        // use, in one launch), the same ids and weights as tmoe_route's two kernels
+        if (use_norm) e = tmoe::launch_rms_norm(x, norm_w, c.rms_eps, T, H, h->xn, st);
+        if (e == cudaSuccess) {
+            PhaseMark pm(h, st, TMOE_PHASE_ROUTER_LOGITS);
+            e = tmoe::launch_route_fused(use_norm ? h->xn : x, router_w, (int)T, H, E, k, nullptr, h->logits, nullptr,
+                                         E, ids, w, h->mapped, E, h->counts, h->offsets, h->perm, h->active,
+                                         h->n_active, h->counters, kCounters, h->route_done, h->err, st);
+        }
+        rc = e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "fused routing");
+    } else {
+        rc = T ? tmoe_route(h, stream, x, T, use_norm, norm_w, router_w, logits, ids, w, use_norm ? h->xn : nullptr,
+                            nullptr)
+               : TMOE_OK;
+    }
     const float *xn = use_norm ? h->xn : x;
     if (rc == TMOE_OK && T) {
         PhaseMark pm(h, st, TMOE_PHASE_MAP_IDS);
