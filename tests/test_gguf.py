@@ -184,3 +184,42 @@ def test_corrupt_files(tmp_path, moe_file):
     lib = _lib.load()
     assert lib.tmoe_gguf_n_tensors(None) == -1
     assert lib.tmoe_gguf_open(None, None) == -1
+
+
+def _reference_fixture():
+    """The reference's own fixture model (tests/fixtures/tiny-qwen3moe-f16.gguf of the tetraeder tree,
+    written by its xtask/tiny_moe.py), found through TETRAEDER_REFERENCE = the root of that tree."""
+    root = os.environ.get("TETRAEDER_REFERENCE")
+    p = os.path.join(root, "tests", "fixtures", "tiny-qwen3moe-f16.gguf") if root else None
+    if not p or not os.path.exists(p):
+        pytest.skip("TETRAEDER_REFERENCE does not point at a tetraeder tree with its fixture model")
+    return p
+
+
+def test_reference_fixture_matches_golden():
+    """This reader on the reference's fixture model agrees with gguf-py's reading of it, as recorded
+    in tests/golden/tiny_qwen3moe_f16.json by tests/golden/make_gguf_golden.py: every metadata value,
+    the tensor index (type, shape, absolute offset, size) and the sha256 of every tensor's bytes; and
+    the hparams are those the reference's desc test asserts (crates/model/tests/desc.rs:16-27)."""
+    import hashlib
+    import json
+    path = _reference_fixture()
+    here = os.path.dirname(os.path.abspath(__file__))
+    with open(os.path.join(here, "golden", "tiny_qwen3moe_f16.json")) as f:
+        gold = json.load(f)
+    assert os.path.getsize(path) == gold["bytes"]
+    with GgufFile(path) as g:
+        assert sorted(g.keys()) == sorted(gold["kv"])
+        for k, v in gold["kv"].items():
+            got = g.get(k)
+            assert got == (ArrayValue(v["array_len"]) if isinstance(v, dict) else v), k
+        assert [t.name for t in g.tensors] == [t["name"] for t in gold["tensors"]]
+        for t, gt in zip(g.tensors, gold["tensors"]):
+            assert t.type == gt["type"], t.name
+            assert t.ne == tuple(gt["shape"]) + (1,) * (4 - len(gt["shape"])), t.name
+            assert (t.offset, t.nbytes) == (gt["offset"], gt["nbytes"]), t.name
+            assert hashlib.sha256(g.read(t.name).tobytes()).hexdigest() == gt["sha256"], t.name
+        h = g.hparams
+        assert (h.n_layer, h.n_embd, h.n_head, h.n_head_kv, h.head_dim) == (2, 64, 4, 2, 16)
+        assert (h.n_expert, h.n_expert_used, h.n_ff_exp, h.n_vocab) == (8, 2, 32, 260)
+        assert sum(s.len for s in g.expert_slabs(1, 3)) == 3 * 32 * 64 * 2
