@@ -22,14 +22,14 @@ constexpr int SORT_WARPS = 32;
 // ids outside [0, n_slots) are not dispatched; ids >= n_slots also latch TMOE_DEV_ERR_BADID.
 // Also writes the increasing list of experts with pairs (n_active[0] of them) with their pair
 // ranges: active[i] = {e, offsets[e], offsets[e + 1], 0}.
-// NW: the warps of the CTA.  sh: NW * n_slots + n_slots + 1 ints of shared memory.
+// NW: the warps of the CTA.  sh: NW * n_slots + n_slots + 65 ints of shared memory; n_slots <= 1024.
 template <int NW>
 __device__ void sort_pairs_cta(const int32_t *ids, int n_pairs, int n_slots, int32_t *__restrict__ counts,
                                int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
                                int4 *__restrict__ active, int32_t *__restrict__ n_active, int *counters,
                                int n_counters, int *err, int32_t *sh) {
     int32_t *hist = sh;                         // [NW][n_slots]
-    int32_t *offs = sh + NW * n_slots;  // [n_slots + 1]
+    int32_t *offs = sh + NW * n_slots;  // [n_slots + 1], then the chunk totals
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (counters && (int)threadIdx.x < n_counters) counters[threadIdx.x] = 0;  // work counters of the GEMVs
     for (int i = threadIdx.x; i < NW * n_slots; i += blockDim.x) hist[i] = 0;
@@ -56,39 +56,56 @@ __device__ void sort_pairs_cta(const int32_t *ids, int n_pairs, int n_slots, int
         offs[e] = run;
     }
     __syncthreads();
-    if (warp == 0) {  // exclusive scan of the counts, 32 experts per step
-        int carry = 0;
-        for (int base = 0; base < n_slots; base += 32) {
-            const int e = base + lane;
-            const int c = e < n_slots ? offs[e] : 0;
-            int inc = c;
+    // Exclusive scan of the counts and the active list, 32 experts per warp step: each chunk's
+    // inclusive scan and its pair and active totals first, then every chunk adds the totals of the
+    // chunks before it (n_slots <= 32 * 32).
+    int32_t *ctot = offs + n_slots + 1;  // [32] pair totals, then [32] active-expert totals
+    const int nch = (n_slots + 31) >> 5;
+    const unsigned lt = (1u << lane) - 1u;
+    for (int c = warp; c < nch; c += NW) {
+        const int e = 32 * c + lane;
+        const int v = e < n_slots ? offs[e] : 0;
+        int inc = v;
 #pragma unroll
-            for (int off = 1; off < 32; off <<= 1) {
-                const int o = __shfl_up_sync(0xffffffffu, inc, off);
-                if (lane >= off) inc += o;
-            }
-            if (e < n_slots) offs[e] = carry + inc - c;
-            carry += __shfl_sync(0xffffffffu, inc, 31);
+        for (int off = 1; off < 32; off <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, inc, off);
+            if (lane >= off) inc += o;
         }
-        if (lane == 0) offs[n_slots] = carry;
+        const unsigned m = __ballot_sync(0xffffffffu, v > 0);
+        if (e < n_slots) offs[e] = inc;
+        if (lane == 31) {
+            ctot[c] = inc;
+            ctot[32 + c] = __popc(m);
+        }
     }
     __syncthreads();
-    for (int e = threadIdx.x; e <= n_slots; e += blockDim.x) offsets[e] = offs[e];
-    if (warp == 0) {
-        int na = 0;
-        for (int base = 0; base < n_slots; base += 32) {
-            const int e = base + lane;
-            const bool has = e < n_slots && (offs[e + 1] - offs[e]) > 0;
-            const unsigned m = __ballot_sync(0xffffffffu, has);
-            if (has) active[na + __popc(m & ((1u << lane) - 1u))] = make_int4(e, offs[e], offs[e + 1], 0);
-            na += __popc(m);
+    for (int c = warp; c < nch; c += NW) {
+        int base = 0, abase = 0;
+        for (int j = 0; j < c; j++) {
+            base += ctot[j];
+            abase += ctot[32 + j];
         }
-        if (lane == 0) n_active[0] = na;
+        const int e = 32 * c + lane;
+        const int inc = e < n_slots ? offs[e] : 0;
+        const int prev = __shfl_up_sync(0xffffffffu, inc, 1);
+        const int v = e < n_slots ? inc - (lane ? prev : 0) : 0;
+        const unsigned m = __ballot_sync(0xffffffffu, v > 0);
+        const int start = base + inc - v;
+        if (e < n_slots) {
+            offs[e] = start;
+            offsets[e] = start;
+            if (v > 0) active[abase + __popc(m & lt)] = make_int4(e, start, start + v, 0);
+        }
+        if (c == nch - 1 && lane == 0) {
+            offs[n_slots] = base + ctot[c];
+            offsets[n_slots] = base + ctot[c];
+            n_active[0] = abase + ctot[32 + c];
+        }
     }
+    __syncthreads();
     for (int e = threadIdx.x; e < n_slots; e += blockDim.x)
         for (int w = 0; w < NW; w++) hist[w * n_slots + e] += offs[e];
     __syncthreads();
-    const unsigned lt = (1u << lane) - 1u;
     for (int base = p0; base < p1; base += 32) {
         const int p = base + lane;
         const int e = p < p1 ? ids[p] : -1;
@@ -263,13 +280,23 @@ __global__ void __launch_bounds__(1024) route_dispatch_kernel(const float *__res
 // The decode regime's whole routing in one launch: router logits, Q8_K of x, softmax/top-k, the
 // optional EP map and the dispatch.  CTA (i, j) of a (ceil(E/8), ceil(T/TT)) grid:
 //  1. stages TT token rows of x and 8 expert rows of the router matrix into shared memory with
-//     bulk copies, and computes those logits in the canonical dot order (the same arithmetic as
-//     router_logits_kernel: bit-identical logits); the tile's CTAs also write the Q8_K rows of x;
-//  2. the last CTA of token tile j (a counter per tile, threadfence-ordered; no CTA waits on
-//     another) reads the tile's logits back and runs top-k for its tokens, one warp per token;
-//  3. the last token tile to finish runs the dispatch of all T * k pairs and resets the counters.
+//     bulk copies.  Warps 0-3 compute those logits in the canonical dot order (the same arithmetic
+//     as router_logits_kernel: bit-identical logits), warp w the 4 experts 4 (w & 1) .. and the
+//     token half w >> 1, each thread holding 4 x TT/2 sums, so that a staged word feeds several
+//     products; warps 4-7 write the Q8_K rows of x, spread over the tile's CTAs;
+//  2. the last CTA of token tile j (a counter per tile, taken with an acquire-release atomic; no
+//     CTA waits on another) reads the tile's logits back and runs top-k, one warp per token;
+//  3. with one token tile that CTA goes on to dispatch the pairs, whose ids it holds; with several,
+//     the last tile to finish (a second counter) reads all the ids back and dispatches them.
 // done: gridDim.y + 1 ints, zero before the first launch (the kernel leaves them zero).
-constexpr int FR_WARPS = 8;  // experts per CTA, one warp each
+constexpr int FR_WARPS = 8;      // warps per CTA, and experts per CTA
+constexpr int FR_DOT_WARPS = 4;  // the warps that compute logits (2 expert halves x 2 token halves)
+
+__device__ __forceinline__ int atomic_add_acq_rel(int *p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
 
 template <int TT, int MAXPER>
 __global__ void __launch_bounds__(FR_WARPS * 32) route_fused_kernel(
@@ -306,51 +333,65 @@ __global__ void __launch_bounds__(FR_WARPS * 32) route_fused_kernel(
         if (threadIdx.x == 0) mbar_wait_bounded(bar, 0);
     }
     const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
-    if (q8.qs) {  // Q8_K of the staged rows: one warp per (token, 256-block), spread over the tile's CTAs
-        const int nb = H / TMOE_QK;
-        for (int u = blockIdx.x * FR_WARPS + warp; u < nt * nb; u += gridDim.x * FR_WARPS) {
-            const int j = u / nb, b = u % nb;
-            const float4 a0 = xs4[j * H4 + b * 64 + 2 * lane], a1 = xs4[j * H4 + b * 64 + 2 * lane + 1];
-            const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-            uint2 q;
-            float d;
-            int s16;
-            q8k_block_warp(v, q, d, s16);
-            q8k_store_warp(q8, t0 + j, H, b, q, d, s16);
-        }
-    }
-    if (warp < ne) {  // canonical dot: lane l takes elements 128m + 4l .. 4l+3 in m order, then a butterfly
-        const float4 *w4 = reinterpret_cast<const float4 *>(ws + warp * H);
-        float acc[TT];
-#pragma unroll
-        for (int j = 0; j < TT; j++) acc[j] = 0.0f;
-        for (int m = 0; m < H / 128; m++) {
-            const float4 w = w4[32 * m + lane];
-#pragma unroll
-            for (int j = 0; j < TT; j++) {
-                const float4 xv = xs4[j * H4 + 32 * m + lane];
-                acc[j] = __fmaf_rn(w.x, xv.x, acc[j]);
-                acc[j] = __fmaf_rn(w.y, xv.y, acc[j]);
-                acc[j] = __fmaf_rn(w.z, xv.z, acc[j]);
-                acc[j] = __fmaf_rn(w.w, xv.w, acc[j]);
+    if (warp >= FR_DOT_WARPS) {
+        if (q8.qs) {  // Q8_K of the staged rows: one warp per (token, 256-block)
+            constexpr int QW = FR_WARPS - FR_DOT_WARPS;
+            const int nb = H / TMOE_QK;
+            for (int u = blockIdx.x * QW + warp - FR_DOT_WARPS; u < nt * nb; u += gridDim.x * QW) {
+                const int j = u / nb, b = u % nb;
+                const float4 a0 = xs4[j * H4 + b * 64 + 2 * lane], a1 = xs4[j * H4 + b * 64 + 2 * lane + 1];
+                const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                uint2 q;
+                float d;
+                int s16;
+                q8k_block_warp(v, q, d, s16);
+                q8k_store_warp(q8, t0 + j, H, b, q, d, s16);
             }
         }
+    } else {
+        // canonical dot: lane l takes elements 128m + 4l .. 4l+3 in m order, then a butterfly
+        constexpr int TK = TT >= 2 ? TT / 2 : 1;
+        const int eg = 4 * (warp & 1), tg = TK * (warp >> 1);
+        if (tg < nt) {
+            const float4 *w4 = reinterpret_cast<const float4 *>(ws + eg * H);
+            float acc[4][TK];
 #pragma unroll
-        for (int j = 0; j < TT; j++) {
-            const float sv = butterfly_f32(acc[j]);
-            if (lane == 0 && j < nt) logits[(int64_t)(t0 + j) * E + e0 + warp] = sv;
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < TK; j++) acc[i][j] = 0.0f;
+            for (int m = 0; m < H / 128; m++) {
+                float4 w[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) w[i] = w4[i * H4 + 32 * m + lane];
+#pragma unroll
+                for (int j = 0; j < TK; j++) {
+                    const float4 xv = xs4[(tg + j) * H4 + 32 * m + lane];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        acc[i][j] = __fmaf_rn(w[i].x, xv.x, acc[i][j]);
+                        acc[i][j] = __fmaf_rn(w[i].y, xv.y, acc[i][j]);
+                        acc[i][j] = __fmaf_rn(w[i].z, xv.z, acc[i][j]);
+                        acc[i][j] = __fmaf_rn(w[i].w, xv.w, acc[i][j]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < TK; j++) {
+                    const float sv = butterfly_f32(acc[i][j]);
+                    if (lane == 0 && eg + i < ne && tg + j < nt) logits[(int64_t)(t0 + tg + j) * E + e0 + eg + i] = sv;
+                }
         }
     }
     // 2. the last CTA of this token tile: top-k of its tokens
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        *flag = atomicAdd(&done[blockIdx.y], 1) == (int)gridDim.x - 1;
-    }
+    if (threadIdx.x == 0) *flag = atomic_add_acq_rel(&done[blockIdx.y], 1) == (int)gridDim.x - 1;
     __syncthreads();
     if (!*flag) return;
-    __threadfence();
     float *lgs = xs;  // [TT][E], the staged rows are no longer needed
+    const int n_pairs = T * k;
+    int32_t *sid = reinterpret_cast<int32_t *>(lgs + TT * E);  // [n_pairs], then the sort's scratch
     for (int i = threadIdx.x; i < nt * E; i += blockDim.x) lgs[i] = __ldcg(logits + (int64_t)t0 * E + i);
     __syncthreads();
     if (warp < nt) {
@@ -363,25 +404,22 @@ __global__ void __launch_bounds__(FR_WARPS * 32) route_fused_kernel(
             ids_out[t * k + lane] = id;
             w_out[t * k + lane] = wt;
             mapped[t * k + lane] = m;
+            sid[t * k + lane] = m;
         }
     }
-    // 3. the last token tile: the dispatch of all pairs
     __syncthreads();
-    if (threadIdx.x == 0) {
-        done[blockIdx.y] = 0;  // every CTA of this tile has counted
-        __threadfence();
-        *flag = atomicAdd(&done[gridDim.y], 1) == (int)gridDim.y - 1;
+    if (threadIdx.x == 0) done[blockIdx.y] = 0;  // every CTA of this tile has counted
+    // 3. the dispatch of all pairs: here with one token tile, else by the last tile to finish
+    if (gridDim.y > 1) {
+        if (threadIdx.x == 0) *flag = atomic_add_acq_rel(&done[gridDim.y], 1) == (int)gridDim.y - 1;
+        __syncthreads();
+        if (!*flag) return;
+        for (int i = threadIdx.x; i < n_pairs; i += blockDim.x) sid[i] = __ldcg(mapped + i);
+        __syncthreads();
     }
-    __syncthreads();
-    if (!*flag) return;
-    __threadfence();
-    const int n_pairs = T * k;
-    int32_t *sid = reinterpret_cast<int32_t *>(sm);  // [n_pairs], then the sort's scratch
-    for (int i = threadIdx.x; i < n_pairs; i += blockDim.x) sid[i] = __ldcg(mapped + i);
-    __syncthreads();
     sort_pairs_cta<FR_WARPS>(sid, n_pairs, n_slots, counts, offsets, perm, active, n_active, counters, n_counters,
                              err, sid + ((n_pairs + 3) & ~3));
-    if (threadIdx.x == 0) done[gridDim.y] = 0;
+    if (threadIdx.x == 0 && gridDim.y > 1) done[gridDim.y] = 0;
 }
 
 __global__ void map_ids_kernel(const int32_t *__restrict__ ids, int64_t n, const int32_t *__restrict__ table,
@@ -443,7 +481,7 @@ __global__ void combine_kernel(const float *__restrict__ dout, const int32_t *__
 }
 
 // ------------------------------------------------------------------ launchers
-size_t sort_pairs_smem(int n_slots) { return sizeof(int32_t) * ((size_t)SORT_WARPS * n_slots + n_slots + 1); }
+size_t sort_pairs_smem(int n_slots) { return sizeof(int32_t) * ((size_t)SORT_WARPS * n_slots + n_slots + 65); }
 
 template <typename KernT>
 static cudaError_t set_smem_once(KernT kern, size_t smem, int *cache) {
@@ -514,29 +552,30 @@ cudaError_t launch_route_dispatch(const float *logits, int T, int E, int k, cons
     return cudaGetLastError();
 }
 
-static size_t route_fused_smem(int tt, int H, int T, int k, int n_slots) {
+static size_t route_fused_smem(int tt, int H, int E, int T, int k, int n_slots) {
     const size_t staged = (size_t)(tt + FR_WARPS) * H * 4;
-    const size_t sorting = 4 * ((size_t)((T * k + 3) & ~3) + (size_t)FR_WARPS * n_slots + n_slots + 1);
+    const size_t sorting =
+        4 * ((size_t)tt * E + (size_t)((T * k + 3) & ~3) + (size_t)FR_WARPS * n_slots + n_slots + 65);
     return staged > sorting ? staged : sorting;
 }
 
 // Tokens per CTA: the batch itself below 8 tokens (rounded up to a power of two, so that a CTA
 // computes no dot products of empty token rows: at T = 1 a tile of 8 did eight times the work),
 // else 8, or 4 when 8 staged rows do not fit.
-static int route_fused_tt(int H, int T, int k, int n_slots) {
+static int route_fused_tt(int H, int E, int T, int k, int n_slots) {
     int want = 8;
     while (want > 1 && want / 2 >= T) want /= 2;
     for (int tt = want; tt >= (want < 4 ? want : 4); tt >>= 1)
-        if (route_fused_smem(tt, H, T, k, n_slots) <= 200 * 1024) return tt;
+        if (route_fused_smem(tt, H, E, T, k, n_slots) <= 200 * 1024) return tt;
     return 0;
 }
 
 bool route_fused_fits(int64_t T, int k, int E, int H, int n_slots) {
-    return route_dispatch_fits(T, k, E, n_slots) && H % 128 == 0 && route_fused_tt(H, (int)T, k, n_slots) > 0;
+    return route_dispatch_fits(T, k, E, n_slots) && H % 128 == 0 && route_fused_tt(H, E, (int)T, k, n_slots) > 0;
 }
 
 int route_fused_tiles(int64_t T, int k, int E, int H, int n_slots) {
-    const int tt = route_fused_tt(H, (int)T, k, n_slots);
+    const int tt = route_fused_tt(H, E, (int)T, k, n_slots);
     return tt ? (int)((T + tt - 1) / tt) : 0;
 }
 
@@ -545,9 +584,9 @@ cudaError_t launch_route_fused(const float *x, const float *rw, int T, int H, in
                                int32_t *mapped, int n_slots, int32_t *counts, int32_t *offsets, int32_t *perm,
                                int4 *active, int32_t *n_active, int *counters, int n_counters, int *done, int *err,
                                cudaStream_t st) {
-    const int tt = route_fused_tt(H, T, k, n_slots);
+    const int tt = route_fused_tt(H, E, T, k, n_slots);
     if (!tt || !route_dispatch_fits(T, k, E, n_slots)) return cudaErrorInvalidValue;
-    const size_t smem = route_fused_smem(tt, H, T, k, n_slots);
+    const size_t smem = route_fused_smem(tt, H, E, T, k, n_slots);
     const dim3 grid((E + FR_WARPS - 1) / FR_WARPS, (T + tt - 1) / tt);
     const Q8Rows none{nullptr, nullptr, nullptr, nullptr, 0};
     const Q8Rows qq = q8 ? *q8 : none;

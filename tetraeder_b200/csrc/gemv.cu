@@ -442,6 +442,8 @@ struct Feed {
     int gi;             // the CTA group index of the next draw
     int n_item, n_a;    // the next item and its active index (n_item < 0: none)
     int4 n_info;        // its record, loading
+    bool n_ready;       // n_item is drawn (else the next fill draws it, after issuing its copies)
+    bool ended;         // a draw found no more groups
     int item, tile, beg, end, e, pass, npass, chunk;  // the next fill (item < 0: none left)
 };
 
@@ -465,24 +467,29 @@ __device__ __forceinline__ int grab_item(const GemvArgs &a, Feed &f, const Group
 }
 
 __device__ __forceinline__ void fetch_next(const GemvArgs &a, Feed &f, const GroupQueue &q, int n_items) {
-    f.n_item = f.n_item < 0 && f.gi > 0 ? -1 : grab_item(a, f, q, n_items);
+    f.n_item = f.ended ? -1 : grab_item(a, f, q, n_items);
+    f.ended = f.n_item < 0;
+    f.n_ready = true;
     if (f.n_item >= 0) {
         f.n_a = fast_div(f.n_item, a.tiles_m);
         f.n_info = __ldg(a.active + f.n_a);
     }
 }
 
+// Takes the drawn item as the next fill's (drawing it first if need be); the one after it is drawn
+// by a later fill, after that fill's copies are on their way.
 template <int NG>
 __device__ __forceinline__ void next_item(const GemvArgs &a, Feed &f, const GroupQueue &q, int n_items) {
     const int lane = threadIdx.x & 31;
     for (;;) {
+        if (!f.n_ready) fetch_next(a, f, q, n_items);
         const int item = f.n_item, ai = f.n_a;
         if (item < 0) {
             f.item = -1;
             return;
         }
         const int4 info = f.n_info;
-        fetch_next(a, f, q, n_items);
+        f.n_ready = false;
         const int e = info.x, beg = info.y, end = info.z;
         if (e < 0 || e >= a.n_slots || beg < 0 || end > a.n_pairs || end < beg) {
             if (lane == 0) latch_error(a.err, TMOE_DEV_ERR_BADID);
@@ -553,6 +560,9 @@ __device__ __forceinline__ void fill(const GemvArgs &a, const GemvMaps &tm, Feed
         f.chunk = 0;
         if (++f.pass == f.npass) next_item<NG>(a, f, q, n_items);
     }
+    // the item after this one is drawn once the fill about to be issued is this item's last
+    if (!f.n_ready && f.item >= 0 && f.chunk == a.n_chunks - 1 && f.pass == f.npass - 1)
+        fetch_next(a, f, q, n_items);
 }
 
 // ------------------------------------------------------------------ kernel
@@ -569,11 +579,21 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
     SlotRec *recs = reinterpret_cast<SlotRec *>(smem + GEMV_NW * GEMV_MAXD * 8) + warp * GEMV_MAXD;
     uint8_t *slots = smem + GEMV_HDR + (size_t)warp * D * a.slot_bytes;
     if (lane == 0) {
+        if constexpr (WT == TMOE_WT_Q4K) {  // the tensor maps' descriptors, fetched while the prologue runs
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm.m[0])) : "memory");
+            if constexpr (GATEUP)
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm.m[1])) : "memory");
+        }
         for (int s = 0; s < D; s++) mbar_init(&bars[s], 1);
         fence_barrier_init();
     }
     __syncwarp();
 
+    // The warp's first item is in the CTA's first (static) group: its record is loaded alongside
+    // the active count, not after it (an index past the count reads a stale record, never used).
+    const int item0 = (int)blockIdx.x * GEMV_NW + warp;
+    const int a0 = fast_div(item0, a.tiles_m);
+    const int4 info0 = __ldg(a.active + min(a0, a.max_active - 1));
     // Dispatch data are checked before they become addresses: an active count above the grid's
     // sizing latches TMOE_DEV_ERR_BADID and is clamped; bad experts or offsets are skipped.
     int na = a.n_active[0];
@@ -585,14 +605,22 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
     GroupQueue q;
     q.ring = reinterpret_cast<unsigned long long *>(smem + GEMV_NW * GEMV_MAXD * (8 + (int)sizeof(SlotRec)));
     q.prog = reinterpret_cast<int *>(q.ring + GQ_RING);
-    q.n_static = (((n_items + GEMV_NW - 1) / GEMV_NW) * 4 / 5) / (int)gridDim.x;
+    q.n_static = max(1, (((n_items + GEMV_NW - 1) / GEMV_NW) * 4 / 5) / (int)gridDim.x);
     if (threadIdx.x < GQ_RING) q.ring[threadIdx.x] = (uint32_t)((int)threadIdx.x - GQ_RING);  // "index d - ring read"
     if (threadIdx.x < GEMV_NW) q.prog[threadIdx.x] = -1;
     __syncthreads();
     Feed f;
-    f.gi = 0;
-    f.n_item = -1;
-    fetch_next(a, f, q, n_items);
+    f.ended = false;
+    if (item0 < n_items) {  // static group 0 = this CTA's index
+        f.gi = 1;
+        f.n_item = item0;
+        f.n_a = a0;
+        f.n_info = info0;
+        f.n_ready = true;
+    } else {
+        f.gi = 0;
+        f.n_ready = false;
+    }
     next_item<NG>(a, f, q, n_items);
     for (int s = 0; s < D; s++)
         fill<WT, GATEUP, NG>(a, tm, f, &bars[s], &recs[s], slots + (size_t)s * a.slot_bytes, q, n_items);

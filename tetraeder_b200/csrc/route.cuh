@@ -15,10 +15,11 @@
 namespace tmoe {
 
 __device__ __forceinline__ float exp_canon(float x) {
-    if (x != x) return x;
-    if (x < -87.0f) return 0.0f;
-    if (x > 88.0f) return __int_as_float(0x7f800000);
-    float kf = rintf(__fmul_rn(x, 1.44269504088896341f));
+    // k = rint(x log2 e) through the 1.5 * 2^23 shift (exact rounding to an integer, ties to even,
+    // for |x log2 e| < 2^22), and no branches, so that a thread's several exps overlap
+    const float y = __fmul_rn(x, 1.44269504088896341f);
+    const float sh = __fadd_rn(y, 12582912.0f);
+    const float kf = __fsub_rn(sh, 12582912.0f);
     float r = __fmaf_rn(kf, -0.693145751953125f, x);
     r = __fmaf_rn(kf, -1.42860682030941723212e-6f, r);
     float p = 1.98412698412698412698e-4f;
@@ -29,8 +30,9 @@ __device__ __forceinline__ float exp_canon(float x) {
     p = __fmaf_rn(p, r, 0.5f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    int ki = static_cast<int>(kf);
-    return __fmul_rn(p, __int_as_float((ki + 127) << 23));
+    const unsigned ki = (unsigned)__float_as_int(sh) - 0x4B400000u;
+    const float v = __fmul_rn(p, __uint_as_float((ki + 127u) << 23));
+    return x != x ? x : (x < -87.0f ? 0.0f : (x > 88.0f ? __int_as_float(0x7f800000) : v));
 }
 
 __device__ __forceinline__ float butterfly_f32(float v) {
