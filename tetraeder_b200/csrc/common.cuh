@@ -100,6 +100,16 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization (launch_k under a PdlScope) may start
+// while the kernel before it in the stream is still running.  pdl_wait() returns once that kernel
+// has completed and its writes are visible (for a plain launch it returns at once); pdl_trigger()
+// lets the next such kernel start.  Every kernel here triggers only after its own wait, so when a
+// kernel starts, the kernel two launches back has completed: code before the wait may read what
+// that one and earlier kernels wrote (through L2), and nothing of its direct predecessor.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- warp helpers
 __device__ __forceinline__ float warp_sum_xor(float v, int width) {
     for (int off = width / 2; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);

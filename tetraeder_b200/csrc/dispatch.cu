@@ -10,6 +10,11 @@
 
 namespace tmoe {
 
+static thread_local bool g_pdl = false;
+PdlScope::PdlScope(bool on) : prev(g_pdl) { g_pdl = on; }
+PdlScope::~PdlScope() { g_pdl = prev; }
+bool pdl_on() { return g_pdl; }
+
 constexpr int SORT_WARPS = 32;
 
 // The dispatch of n_pairs ids (ids may live in shared memory) by one CTA of 1024 threads.  Warp w
@@ -321,12 +326,15 @@ __global__ void __launch_bounds__(FR_WARPS * 32) route_fused_kernel(
         fence_barrier_init();
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        const uint32_t row = (uint32_t)H * 4u;
+    const uint32_t row = (uint32_t)H * 4u;
+    if (threadIdx.x == 0) {  // the router rows are not written by the kernel before: staged before the wait
         mbar_arrive_expect_tx(bar, (uint32_t)(nt + ne) * row);
-        for (int j = 0; j < nt; j++) bulk_g2s(xs + j * H, x + (int64_t)(t0 + j) * H, row, bar);
         for (int j = 0; j < ne; j++) bulk_g2s(ws + j * H, rw + (int64_t)(e0 + j) * H, row, bar);
     }
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x == 0)
+        for (int j = 0; j < nt; j++) bulk_g2s(xs + j * H, x + (int64_t)(t0 + j) * H, row, bar);
     if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar, 0))) {
         // nothing else may run on this tile: the copies may still be in flight
         if (lane == 0) latch_error(err, TMOE_DEV_ERR_TIMEOUT);
@@ -448,6 +456,8 @@ template <int KMAX>
 __global__ void combine_kernel(const float *__restrict__ dout, const int32_t *__restrict__ ids,
                                const float *__restrict__ w, int64_t T, int k, int H, int n_slots,
                                float *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (i >= T * H) return;
     const int64_t t = i / H;
@@ -595,9 +605,10 @@ cudaError_t launch_route_fused(const float *x, const float *rw, int T, int H, in
     do {                                                                                                       \
         cudaError_t e = set_smem_once(route_fused_kernel<TTV, MP>, smem, cache[CI]);                           \
         if (e != cudaSuccess) return e;                                                                        \
-        route_fused_kernel<TTV, MP><<<grid, FR_WARPS * 32, smem, st>>>(                                         \
+        e = launch_k(route_fused_kernel<TTV, MP>, grid, FR_WARPS * 32, smem, st,                                \
             x, rw, T, H, E, k, qq, logits, table, n_table, ids_out, w_out, mapped, n_slots, counts, offsets,    \
             perm, active, n_active, counters, n_counters, done, err);                                           \
+        if (e != cudaSuccess) return e;                                                                        \
     } while (0)
     const int mp = E <= 32 ? 1 : E <= 64 ? 2 : E <= 128 ? 4 : 8;
 #define TMOE_RF_TT(TTV, C0)                      \
@@ -658,13 +669,14 @@ cudaError_t launch_combine(const float *dout, const int32_t *ids, const float *w
     if (T <= 0) return cudaSuccess;
     const int64_t n4 = T * H / 4;
     const unsigned grid = (unsigned)((n4 + 127) / 128);
+    cudaError_t e;
     if (k <= 8)
-        combine_kernel<8><<<grid, 128, 0, st>>>(dout, ids, w, T, k, H, n_slots, out);
+        e = launch_k(combine_kernel<8>, grid, 128, 0, st, dout, ids, w, T, k, H, n_slots, out);
     else if (k <= 16)
-        combine_kernel<16><<<grid, 128, 0, st>>>(dout, ids, w, T, k, H, n_slots, out);
+        e = launch_k(combine_kernel<16>, grid, 128, 0, st, dout, ids, w, T, k, H, n_slots, out);
     else
-        combine_kernel<32><<<grid, 128, 0, st>>>(dout, ids, w, T, k, H, n_slots, out);
-    return cudaGetLastError();
+        e = launch_k(combine_kernel<32>, grid, 128, 0, st, dout, ids, w, T, k, H, n_slots, out);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace tmoe

@@ -472,7 +472,7 @@ __device__ __forceinline__ void fetch_next(const GemvArgs &a, Feed &f, const Gro
     f.n_ready = true;
     if (f.n_item >= 0) {
         f.n_a = fast_div(f.n_item, a.tiles_m);
-        f.n_info = __ldg(a.active + f.n_a);
+        f.n_info = __ldcg(a.active + f.n_a);
     }
 }
 
@@ -588,15 +588,22 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
         fence_barrier_init();
     }
     __syncwarp();
+    // Programmatic launch: gate/up reads what the routing kernel (its predecessor) wrote, so it
+    // waits here.  Down's predecessor only writes its activations: the dispatch data and the
+    // weights are two and more launches back, so down issues its first fills before it waits.
+    if constexpr (GATEUP) {
+        pdl_wait();
+        pdl_trigger();
+    }
 
     // The warp's first item is in the CTA's first (static) group: its record is loaded alongside
     // the active count, not after it (an index past the count reads a stale record, never used).
     const int item0 = (int)blockIdx.x * GEMV_NW + warp;
     const int a0 = fast_div(item0, a.tiles_m);
-    const int4 info0 = __ldg(a.active + min(a0, a.max_active - 1));
+    const int4 info0 = __ldcg(a.active + min(a0, a.max_active - 1));
     // Dispatch data are checked before they become addresses: an active count above the grid's
     // sizing latches TMOE_DEV_ERR_BADID and is clamped; bad experts or offsets are skipped.
-    int na = a.n_active[0];
+    int na = __ldcg(a.n_active);
     if (na > a.max_active || na < 0) {
         if (threadIdx.x == 0 && blockIdx.x == 0) latch_error(a.err, TMOE_DEV_ERR_BADID);
         na = na < 0 ? 0 : a.max_active;
@@ -624,6 +631,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
     next_item<NG>(a, f, q, n_items);
     for (int s = 0; s < D; s++)
         fill<WT, GATEUP, NG>(a, tm, f, &bars[s], &recs[s], slots + (size_t)s * a.slot_bytes, q, n_items);
+    if constexpr (!GATEUP) {
+        pdl_wait();
+        pdl_trigger();
+    }
 
     TokCols tc[NG];
     XBase xb0;  // NG == 1: the group's bases, kept for the pass (two-group passes address from tc)
@@ -912,7 +923,8 @@ static cudaError_t launch_t(const GemvArgs &args_in, int max_items, int sm_count
 #define TMOE_GEMV_LAUNCH(MINB, NG, CI)                                                                      \
     do {                                                                                                 \
         if ((e = set_smem_once(gemv_kernel<WT, GATEUP, MINB, NG>, smem, cache[CI])) != cudaSuccess) return e; \
-        gemv_kernel<WT, GATEUP, MINB, NG><<<grid, GEMV_THREADS, smem, st>>>(a, tm);                       \
+        if ((e = launch_k(gemv_kernel<WT, GATEUP, MINB, NG>, grid, GEMV_THREADS, smem, st, a, tm)) != cudaSuccess) \
+            return e;                                                                                    \
     } while (0)
     if (pl.ctas_per_sm == 2) {
         if (one) TMOE_GEMV_LAUNCH(2, 1, 0);

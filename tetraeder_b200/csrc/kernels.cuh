@@ -13,6 +13,32 @@ struct tmoe_comm;
 
 namespace tmoe {
 
+// While a PdlScope(true) lives on this thread, launch_k launches with programmatic stream
+// serialization: the kernel may start during its predecessor's tail (see pdl_wait in common.cuh).
+struct PdlScope {
+    bool prev;
+    explicit PdlScope(bool on);
+    ~PdlScope();
+};
+bool pdl_on();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    if (pdl_on()) {
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // ep.cu: in-place sum of n floats over the communicator's ranks (stream-ordered); TMOE_OK or
 // TMOE_E_COMM with a message.
 int ep_allreduce_sum(tmoe_comm *c, float *buf, size_t n, cudaStream_t st, char *msg, size_t msg_len);

@@ -298,6 +298,8 @@ __global__ void softmax_topk_kernel(const float *__restrict__ logits, int64_t T,
 // weight type.  Rows whose `valid` entry is negative are skipped.
 __global__ void quantize_q8k_kernel(const float *__restrict__ x, int64_t rows, int K, const int32_t *__restrict__ valid,
                                     Q8Rows out) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int nb = K / TMOE_QK;
@@ -436,9 +438,9 @@ cudaError_t launch_quantize_q8k(const float *x, int64_t rows, int K, const int32
     if (rows <= 0) return cudaSuccess;
     const int64_t warps = rows * (K / TMOE_QK);
     const int per_block = 8;
-    quantize_q8k_kernel<<<(unsigned)((warps + per_block - 1) / per_block), per_block * 32, 0, st>>>(x, rows, K, valid,
-                                                                                                    out);
-    return cudaGetLastError();
+    const cudaError_t e = launch_k(quantize_q8k_kernel, (unsigned)((warps + per_block - 1) / per_block),
+                                   per_block * 32, 0, st, x, rows, K, valid, out);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_widen_bf16(const uint16_t *x, int64_t n, float *out, cudaStream_t st) {

@@ -666,7 +666,10 @@ int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
     bool x_quantized = false;
     const float *lg = logits;
     if (router_w && tmoe::route_fused_fits(T, k, c.n_expert, c.n_embd, wts->n_slots)) {
-        // decode regime: logits + Q8_K of xn + top-k + id map + dispatch in one launch
+        // decode regime: logits + Q8_K of xn + top-k + id map + dispatch in one launch.  Its kernels
+        // start during their predecessors' tails (programmatic dependent launch), except while the
+        // per-kernel events of profile() sit between them.
+        tmoe::PdlScope pdl(!h->prof.on);
         const tmoe::Q8Rows q8{h->xq, h->xd, h->xbl, h->xbh, wt_of(c.gate_type)};
         {
             PhaseMark pm(h, st, TMOE_PHASE_ROUTER_LOGITS);
