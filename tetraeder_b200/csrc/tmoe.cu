@@ -277,6 +277,9 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
     const int64_t P = T * k;
     const int wg = wt_of(c.gate_type), wd = wt_of(c.down_type);
     cudaError_t e;
+    // the expert kernels overlap their predecessors' tails (programmatic dependent launch) unless
+    // profile()'s per-kernel events sit between them
+    tmoe::PdlScope pdl(!h->prof.on);
     if (!dispatched) {
         {
             PhaseMark pm(h, st, TMOE_PHASE_DISPATCH);
