@@ -224,6 +224,10 @@ LAYER_CASES = [
     ("C2 30B T=16", 2048, 768, 128, 8, 16, O.TYPE_Q4_K, O.TYPE_Q6_K, False),
     ("C2 30B T=64", 2048, 768, 128, 8, 64, O.TYPE_Q4_K, O.TYPE_Q6_K, False),
     ("235B shape T=64", 4096, 1536, 32, 8, 64, O.TYPE_Q4_K, O.TYPE_Q4_K, False),
+    # more tokens per expert (12, 32 and 64 pairs an expert): the GEMVs' two-group passes, and more passes
+    ("C2 30B T=192", 2048, 768, 128, 8, 192, O.TYPE_Q4_K, O.TYPE_Q6_K, False),
+    ("C2 30B T=512", 2048, 768, 128, 8, 512, O.TYPE_Q4_K, O.TYPE_Q6_K, False),
+    ("tiny Q6_K gate/up T=256", 512, 256, 16, 4, 256, O.TYPE_Q6_K, O.TYPE_Q6_K, True),
 ]
 
 

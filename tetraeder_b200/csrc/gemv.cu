@@ -49,7 +49,10 @@ struct SlotRec {
     int item, tile, pass, chunk, beg, end, poff, r0;
 };
 static_assert(GEMV_NW * GEMV_MAXD * (8 + (int)sizeof(SlotRec)) + 8 * 8 + 4 * GEMV_NW <= GEMV_HDR, "header");
-constexpr int PERM_STAGE = 128;  // bytes after a slot's weights for the pass's pair indices
+// Bytes after a slot's weights for the pass's pair indices.  Q4_K slots stay multiples of 128
+// bytes: a tensor-map copy (the Q4_K fills) must land on a 128-byte boundary of shared memory.
+constexpr int PERM_STAGE = 128;
+static_assert(ITEM_ROWS * TMOE_Q4K_BYTES % 128 == 0 && PERM_STAGE % 128 == 0, "Q4_K slots on 128-byte boundaries");
 
 // Tensor maps of the Q4_K matrices (unused for Q6_K).
 struct GemvMaps {
@@ -895,6 +898,7 @@ static cudaError_t launch_t(const GemvArgs &args_in, int max_items, int sm_count
     a.row_stride = (WT == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES) * pl.cb;
     a.wbytes = WT == TMOE_WT_Q4K ? ITEM_ROWS * a.row_stride : ITEM_ROWS * a.row_stride + 16;
     a.slot_bytes = a.wbytes + PERM_STAGE;
+    if (WT == TMOE_WT_Q4K && a.slot_bytes % 128 != 0) return cudaErrorInvalidValue;
     a.d_slots = pl.d;
     a.tiles = a.N / (GATEUP ? ITEM_ROWS / 2 : ITEM_ROWS);
     const uint64_t two40 = 1ull << 40;
