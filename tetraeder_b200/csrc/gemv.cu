@@ -450,8 +450,25 @@ struct Feed {
     int item, tile, beg, end, e, pass, npass, chunk;  // the next fill (item < 0: none left)
 };
 
+// Spread dealing (a.spread: at most one item per warp of the full grid): draw 0 of warp w in CTA c
+// is item 2 * ((w / 2) * gridDim.x + c) + w % 2, so pairs of neighbouring row tiles go to
+// consecutive CTAs and every SM gets about the same number of items; later draws (none while the
+// items fit the warps) come from the work counter, one item at a time.
+__device__ __forceinline__ int spread_item0(int warp) {
+    return 2 * ((warp >> 1) * (int)gridDim.x + (int)blockIdx.x) + (warp & 1);
+}
+
 __device__ __forceinline__ int grab_item(const GemvArgs &a, Feed &f, const GroupQueue &q, int n_items) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (a.spread) {
+        int item = 0;
+        const int dealt = GEMV_NW * (int)gridDim.x;  // items of draw 0
+        if (lane == 0)
+            item = f.gi == 0 ? spread_item0(warp) : dealt < n_items ? dealt + atomicAdd(a.work, 1) : n_items;
+        item = __shfl_sync(FULL, item, 0);
+        f.gi++;
+        return item < n_items ? item : -1;
+    }
     const int n_groups = (n_items + GEMV_NW - 1) / GEMV_NW;
     for (;;) {
         int gid = 0;
@@ -601,7 +618,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
 
     // The warp's first item is in the CTA's first (static) group: its record is loaded alongside
     // the active count, not after it (an index past the count reads a stale record, never used).
-    const int item0 = (int)blockIdx.x * GEMV_NW + warp;
+    const int item0 = a.spread ? spread_item0(warp) : (int)blockIdx.x * GEMV_NW + warp;
     const int a0 = fast_div(item0, a.tiles_m);
     const int4 info0 = __ldcg(a.active + min(a0, a.max_active - 1));
     // Dispatch data are checked before they become addresses: an active count above the grid's
@@ -919,6 +936,10 @@ static cudaError_t launch_t(const GemvArgs &args_in, int max_items, int sm_count
     const int slots = sm_count * pl.ctas_per_sm;
     if (grid > slots) grid = slots;
     if (grid < 1) return cudaSuccess;
+    // Few items (at most one per warp of the full grid): the whole grid, items dealt out spread, so
+    // that every SM gets about as many (groups of 8 on fewer CTAs put 16 items on some SMs, 8 on others)
+    a.spread = items <= GEMV_NW * slots ? 1 : 0;
+    if (a.spread) grid = slots;
     // One token group per pass when the batch averages at most 4 pairs per active expert (decode):
     // an expert with more tokens then takes more passes over rows that L2 still holds.
     const bool one = (int64_t)a.n_pairs <= 4 * (int64_t)max_items;

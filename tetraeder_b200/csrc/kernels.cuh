@@ -173,6 +173,7 @@ struct GemvArgs {
     int slot_bytes;    // shared-memory bytes per slot (16 rows, then the pass's pair indices)
     int wbytes;        // weight bytes of a slot
     int d_slots;       // slots per warp
+    int spread;        // items dealt one per warp over the whole grid (few items)
     uint64_t tiles_m, xdiv_m;  // ceil(2^40 / tiles), ceil(2^40 / x_div): exact division of n < 2^24
 };
 // prefill.cu: the grouped tcgen05 GEMMs of the large-batch regime (see prefill.cu)
