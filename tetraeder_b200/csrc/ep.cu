@@ -73,12 +73,13 @@ int ep_comm_ranks(const tmoe_comm *c, int *rank) {
 // All-to-all of fixed-size blocks: block p of every buffer's `send` goes to rank p, whose block
 // `rank` of `recv` receives it.  The local block is a device copy; the others are one NCCL group
 // of sends and receives, so the exchange is one collective step for the ranks.
-int ep_alltoall(tmoe_comm *c, const EpBuf *bufs, int nbufs, cudaStream_t st, char *msg, size_t msg_len) {
+int ep_alltoall(tmoe_comm *c, const EpBuf *bufs, int nbufs, cudaStream_t st, char *msg, size_t msg_len,
+                bool copy_self) {
     if (!c->comm) {
         snprintf(msg, msg_len, "the communicator was aborted");
         return TMOE_E_COMM;
     }
-    for (int b = 0; b < nbufs; b++) {
+    for (int b = 0; b < nbufs && copy_self; b++) {
         const size_t n = bufs[b].bytes_per_peer;
         const cudaError_t e = cudaMemcpyAsync((char *)bufs[b].recv + (size_t)c->rank * n,
                                               (const char *)bufs[b].send + (size_t)c->rank * n, n,

@@ -49,13 +49,15 @@ struct EpBuf {
     void *recv;        // [nranks][bytes_per_peer]
     size_t bytes_per_peer;
 };
-int ep_alltoall(tmoe_comm *c, const EpBuf *bufs, int nbufs, cudaStream_t st, char *msg, size_t msg_len);
+// copy_self: also copy this rank's own block send -> recv (false when the producer wrote it in place)
+int ep_alltoall(tmoe_comm *c, const EpBuf *bufs, int nbufs, cudaStream_t st, char *msg, size_t msg_len,
+                bool copy_self = true);
 // ep_a2a.cu: the token dispatch and combine of the all-to-all mode (see ep_a2a.cu)
 cudaError_t launch_ep_pack(const int32_t *ids, const float *w, const float *x, int T, int k, int H, int per, int g,
-                           int cap, int32_t *row_of, int32_t *s_ids, float *s_w, int32_t *s_tok, int32_t *counts,
-                           float *s_x, cudaStream_t st);
-cudaError_t launch_ep_combine(const float *ret, const int32_t *row_of, int T, int H, int g, int cap, float *out,
-                              cudaStream_t st);
+                           int cap, int self, int32_t *row_of, int32_t *s_ids, float *s_w, int32_t *r_ids,
+                           float *r_w, int32_t *s_tok, int32_t *counts, float *s_x, float *r_x, cudaStream_t st);
+cudaError_t launch_ep_combine(const float *ret, const float *part, int self, const int32_t *row_of, int T, int H,
+                              int g, int cap, float *out, cudaStream_t st);
 
 // Q8_K rows as the expert GEMV reads them: qs int8 [rows][K], d f32 [rows][K/256], and per
 // super-block the activation sums over the weight type's sub-blocks (32 elements for Q4_K, 16 for

@@ -835,28 +835,32 @@ int tmoe_ep_a2a_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float
     const float *xn = use_norm ? h->xn : x;
     if (rc == TMOE_OK && T) {
         PhaseMark pm(h, st, TMOE_PHASE_MAP_IDS);
-        e = tmoe::launch_ep_pack(ids, w, xn, (int)T, k, H, E / g, g, cap, A.row_of, A.s_ids, A.s_w, A.s_tok, A.counts,
-                                 A.s_x, st);
+        e = tmoe::launch_ep_pack(ids, w, xn, (int)T, k, H, E / g, g, cap, rank, A.row_of, A.s_ids, A.s_w, A.r_ids,
+                                 A.r_w, A.s_tok, A.counts, A.s_x, A.r_x, st);
         if (e != cudaSuccess) rc = cuda_fail(h, e, "all-to-all pack");
     }
-    if (rc != TMOE_OK || T == 0) cudaMemsetAsync(A.s_ids, 0xff, (size_t)g * cap * k * 4, st);
+    if (rc != TMOE_OK || T == 0) {  // no rows: -1 ids in every message, this rank's own one included
+        cudaMemsetAsync(A.s_ids, 0xff, (size_t)g * cap * k * 4, st);
+        cudaMemsetAsync(A.r_ids + (size_t)rank * cap * k, 0xff, (size_t)cap * k * 4, st);
+    }
     char msg[256];
     const size_t nk = (size_t)cap * k * 4;
     const tmoe::EpBuf out_bufs[3] = {{A.s_ids, A.r_ids, nk}, {A.s_w, A.r_w, nk}, {A.s_x, A.r_x, (size_t)cap * H * 4}};
-    int rc2 = tmoe::ep_alltoall(comm, out_bufs, 3, st, msg, sizeof msg);
+    // the pack wrote this rank's own message into the receive buffers already
+    int rc2 = tmoe::ep_alltoall(comm, out_bufs, 3, st, msg, sizeof msg, false);
     if (rc2) return fail(h, rc2, "%s", msg);
     // this rank's experts over every received row (rows of other ranks' tokens), combined per row
     // in choice order: the partial sums of the reference's EP mode
     const int rc3 = run_experts(h, st, A.r_x, (int64_t)g * cap, A.r_ids, A.r_w, wts, A.part, false, false);
     if (rc3 != TMOE_OK) cudaMemsetAsync(A.part, 0, (size_t)g * cap * H * 4, st);
     const tmoe::EpBuf back = {A.part, A.ret, (size_t)cap * H * 4};
-    rc2 = tmoe::ep_alltoall(comm, &back, 1, st, msg, sizeof msg);
+    rc2 = tmoe::ep_alltoall(comm, &back, 1, st, msg, sizeof msg, false);  // own partials: read from A.part
     if (rc2) return fail(h, rc2, "%s", msg);
     if (rc) return rc;
     if (rc3) return rc3;
     if (T) {
         PhaseMark pm(h, st, TMOE_PHASE_COMBINE);
-        e = tmoe::launch_ep_combine(A.ret, A.row_of, (int)T, H, g, cap, out, st);
+        e = tmoe::launch_ep_combine(A.ret, A.part, rank, A.row_of, (int)T, H, g, cap, out, st);
     }
     return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "all-to-all combine");
 }
