@@ -420,7 +420,9 @@ def run_ours(args, rank, world, local_rank):
     }
     if a2a:
         result["config"]["parallelism"] = (f"ep{world} all-to-all (experts split contiguously, {T} tokens per rank "
-                                           "dispatched to the experts' ranks and combined back over NCCL)")
+                                           "dispatched to the experts' ranks and combined back; the messages are "
+                                           "written into the peers' buffers over NVLink, NCCL if those cannot be "
+                                           "mapped)")
     elif ep:
         result["config"]["parallelism"] = f"ep{world} (experts split contiguously, tokens replicated, NCCL all-reduce)"
         result["scaling"] = "strong"

@@ -70,6 +70,23 @@ int ep_comm_ranks(const tmoe_comm *c, int *rank) {
     return c->nranks;
 }
 
+// recv[p * bytes ...] = rank p's `send` bytes (device buffers), for every rank p: the one-time
+// exchange of the all-to-all mode's buffer handles.
+int ep_allgather_bytes(tmoe_comm *c, const void *send, void *recv, size_t bytes, cudaStream_t st, char *msg,
+                       size_t msg_len) {
+    if (!c->comm) {
+        snprintf(msg, msg_len, "the communicator was aborted");
+        return TMOE_E_COMM;
+    }
+    ncclResult_t r = ncclAllGather(send, recv, bytes, ncclUint8, c->comm, st);
+    if (r == ncclInProgress) r = nccl_wait(c);
+    if (r != ncclSuccess) {
+        snprintf(msg, msg_len, "ncclAllGather: %s", ncclGetErrorString(r));
+        return TMOE_E_COMM;
+    }
+    return TMOE_OK;
+}
+
 // All-to-all of fixed-size blocks: block p of every buffer's `send` goes to rank p, whose block
 // `rank` of `recv` receives it.  The local block is a device copy; the others are one NCCL group
 // of sends and receives, so the exchange is one collective step for the ranks.

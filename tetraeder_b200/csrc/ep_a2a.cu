@@ -115,6 +115,181 @@ __global__ void ep_combine_kernel(const float *__restrict__ ret, const float *__
     reinterpret_cast<float4 *>(out)[i] = acc;
 }
 
+// ------------------------------------------------------------------ the exchange over peer memory
+// The same messages as the NCCL exchange, but written by the sending rank straight into the
+// receiving rank's buffers through NVLink: block `self` of rank d's r_ids / r_w / r_x for the
+// dispatch, block `self` of rank d's ret for the return.  The buffers of every rank are mapped
+// into this process once (CUDA IPC).  After the last CTA of a writing kernel has seen every CTA's
+// writes fenced at system scope, it bumps this rank's count of messages sent in that direction
+// and stores the count (release, system scope) into each peer's counter for this rank; a
+// receiver waits (bounded) for every peer's counter to pass its own count of messages consumed.
+// Counts only grow, so a captured graph replays the same kernels without any reset.  A rank
+// writes a peer's buffers only after that peer has consumed the previous message there: the
+// dispatch of call n + 1 follows this rank's combine of call n, which waited for the peers'
+// returns of call n, which each peer sends after its expert products of call n.
+__device__ __forceinline__ void st_release_sys(int *p, int v) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int *p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Called by every thread of every CTA once its writes are issued: the last CTA signals the peers.
+__device__ void ep_signal_last(int dir, int g, int self, const EpPeers &P, int *ctl) {
+    __shared__ int last, count;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        last = atomicAdd(&ctl[2 + dir], 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        count = ctl[dir] + 1;
+        ctl[dir] = count;
+        ctl[2 + dir] = 0;  // the tally of the next call
+    }
+    __syncthreads();
+    const int p = threadIdx.x;
+    if (p < g && p != self) st_release_sys(P.flags[p] + dir * g + self, count);
+}
+
+// ep_pack_kernel with each destination's block in that rank's receive buffers.
+__global__ void __launch_bounds__(1024) ep_pack_p2p_kernel(const int32_t *__restrict__ ids,
+                                                           const float *__restrict__ w, int T, int k, int per,
+                                                           int g, int cap, int self, const EpPeers P,
+                                                           int32_t *__restrict__ row_of, int32_t *__restrict__ s_tok,
+                                                           int32_t *__restrict__ counts) {
+    __shared__ int warp_sum[32];
+    __shared__ int base;
+    const int d = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int32_t *d_ids = P.r_ids[d] + (int64_t)self * cap * k;
+    float *d_w = P.r_w[d] + (int64_t)self * cap * k;
+    const int lo = d * per, hi = lo + per;
+    if (tid == 0) base = 0;
+    __syncthreads();
+    for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+        const int t = t0 + tid;
+        bool has = false;
+        if (t < T)
+            for (int j = 0; j < k; j++) {
+                const int e = ids[(int64_t)t * k + j];
+                has |= e >= lo && e < hi;
+            }
+        const unsigned b = __ballot_sync(0xffffffffu, has);
+        if (lane == 0) warp_sum[warp] = __popc(b);
+        __syncthreads();
+        int before = 0, total = 0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) {
+            before += i < warp ? warp_sum[i] : 0;
+            total += warp_sum[i];
+        }
+        const int row = base + before + __popc(b & ((1u << lane) - 1));
+        if (t < T) {
+            row_of[(int64_t)t * g + d] = has ? row : -1;
+            if (has && row < cap) {
+                for (int j = 0; j < k; j++) {
+                    const int e = ids[(int64_t)t * k + j];
+                    d_ids[(int64_t)row * k + j] = e >= lo && e < hi ? e - lo : -1;
+                    d_w[(int64_t)row * k + j] = w[(int64_t)t * k + j];
+                }
+                s_tok[(int64_t)d * cap + row] = t;
+            }
+        }
+        __syncthreads();
+        if (tid == 0) base += total;
+        __syncthreads();
+    }
+    const int n = min(base, cap);
+    if (tid == 0) counts[d] = n;
+    for (int i = n * k + tid; i < cap * k; i += blockDim.x) d_ids[i] = -1;
+    __threadfence_system();
+}
+
+// The message rows into each destination's r_x, one warp per row; then the dispatch signal.
+__global__ void ep_gather_p2p_kernel(const float *__restrict__ x, int H, int g, int cap, int self, const EpPeers P,
+                                     const int32_t *__restrict__ s_tok, const int32_t *__restrict__ counts,
+                                     int *ctl) {
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw < (int64_t)g * cap) {
+        const int d = (int)(gw / cap), row = (int)(gw % cap);
+        if (row < counts[d]) {
+            const float4 *src = reinterpret_cast<const float4 *>(x + (int64_t)s_tok[gw] * H);
+            float4 *dst = reinterpret_cast<float4 *>(P.r_x[d] + ((int64_t)self * cap + row) * H);
+            for (int i = lane; i < H / 4; i += 32) dst[i] = src[i];
+        }
+    }
+    ep_signal_last(0, g, self, P, ctl);
+}
+
+// The partial rows back to their tokens' ranks: row r of block d (received from rank d) goes to
+// row r of block `self` of rank d's ret, when the row has an expert here (one warp per row).
+__global__ void ep_return_p2p_kernel(const float *__restrict__ part, const int32_t *__restrict__ r_ids, int k, int H,
+                                     int g, int cap, int self, const EpPeers P, int *ctl) {
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw < (int64_t)g * cap) {
+        const int d = (int)(gw / cap), row = (int)(gw % cap);
+        const bool has = __any_sync(0xffffffffu, lane < k && __ldg(r_ids + gw * k + lane) >= 0);
+        if (d != self && has) {
+            const float4 *src = reinterpret_cast<const float4 *>(part + gw * H);
+            float4 *dst = reinterpret_cast<float4 *>(P.ret[d] + ((int64_t)self * cap + row) * H);
+            for (int i = lane; i < H / 4; i += 32) dst[i] = src[i];
+        }
+    }
+    ep_signal_last(1, g, self, P, ctl);
+}
+
+__global__ void ep_wait_kernel(int dir, int g, int self, const int *flags, int *ctl, int *err) {
+    const int p = threadIdx.x;
+    if (p >= g || p == self) return;
+    int *seen = ctl + 4 + dir * g + p;
+    const int want = *seen + 1;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t nap = 32;
+    while (ld_acquire_sys(flags + dir * g + p) - want < 0) {
+        if (globaltimer_ns() - t0 > TMOE_WAIT_LIMIT_NS) {
+            latch_error(err, TMOE_DEV_ERR_TIMEOUT);
+            break;
+        }
+        __nanosleep(nap);
+        if (nap < 1024) nap *= 2;
+    }
+    *seen = want;
+    __threadfence_system();
+}
+
+cudaError_t launch_ep_dispatch_p2p(const int32_t *ids, const float *w, const float *x, int T, int k, int H, int per,
+                                   int g, int cap, int self, const EpPeers &P, int32_t *row_of, int32_t *s_tok,
+                                   int32_t *counts, int *ctl, cudaStream_t st) {
+    if (g <= 0 || g > EP_MAX_PEERS || cap <= 0 || self < 0 || self >= g || k > 32 || H % 4) return cudaErrorInvalidValue;
+    ep_pack_p2p_kernel<<<g, 1024, 0, st>>>(ids, w, T, k, per, g, cap, self, P, row_of, s_tok, counts);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const int64_t warps = (int64_t)g * cap;
+    ep_gather_p2p_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(x, H, g, cap, self, P, s_tok, counts, ctl);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_return_p2p(const float *part, const int32_t *r_ids, int k, int H, int g, int cap, int self,
+                                 const EpPeers &P, int *ctl, cudaStream_t st) {
+    if (g <= 0 || g > EP_MAX_PEERS || cap <= 0 || self < 0 || self >= g || k > 32 || H % 4) return cudaErrorInvalidValue;
+    const int64_t warps = (int64_t)g * cap;
+    ep_return_p2p_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(part, r_ids, k, H, g, cap, self, P, ctl);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_wait(int dir, int g, int self, const int *flags, int *ctl, int *err, cudaStream_t st) {
+    if (g <= 0 || g > 32 || self < 0 || self >= g) return cudaErrorInvalidValue;
+    ep_wait_kernel<<<1, 32, 0, st>>>(dir, g, self, flags, ctl, err);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_ep_pack(const int32_t *ids, const float *w, const float *x, int T, int k, int H, int per, int g,
                            int cap, int self, int32_t *row_of, int32_t *s_ids, float *s_w, int32_t *r_ids,
                            float *r_w, int32_t *s_tok, int32_t *counts, float *s_x, float *r_x, cudaStream_t st) {

@@ -49,6 +49,8 @@ struct EpBuf {
     void *recv;        // [nranks][bytes_per_peer]
     size_t bytes_per_peer;
 };
+int ep_allgather_bytes(tmoe_comm *c, const void *send, void *recv, size_t bytes, cudaStream_t st, char *msg,
+                       size_t msg_len);
 // copy_self: also copy this rank's own block send -> recv (false when the producer wrote it in place)
 int ep_alltoall(tmoe_comm *c, const EpBuf *bufs, int nbufs, cudaStream_t st, char *msg, size_t msg_len,
                 bool copy_self = true);
@@ -58,6 +60,27 @@ cudaError_t launch_ep_pack(const int32_t *ids, const float *w, const float *x, i
                            float *r_w, int32_t *s_tok, int32_t *counts, float *s_x, float *r_x, cudaStream_t st);
 cudaError_t launch_ep_combine(const float *ret, const float *part, int self, const int32_t *row_of, int T, int H,
                               int g, int cap, float *out, cudaStream_t st);
+// The exchange over peer memory (ep_a2a.cu): every rank's receive buffers, mapped into this
+// process (this rank's own included), and its arrival counters flags[2][g]: [0][p] counts the
+// dispatch messages rank p has finished writing here, [1][p] its returns.
+constexpr int EP_MAX_PEERS = 8;
+struct EpPeers {
+    int32_t *r_ids[EP_MAX_PEERS];
+    float *r_w[EP_MAX_PEERS];
+    float *r_x[EP_MAX_PEERS];
+    float *ret[EP_MAX_PEERS];
+    int *flags[EP_MAX_PEERS];
+};
+// ctl: this rank's counters: [0..1] messages sent per direction, [2..3] CTA tallies of the
+// writing kernels (zero between calls), [4..] seen[2][g] (messages consumed per direction, peer).
+cudaError_t launch_ep_dispatch_p2p(const int32_t *ids, const float *w, const float *x, int T, int k, int H, int per,
+                                   int g, int cap, int self, const EpPeers &P, int32_t *row_of, int32_t *s_tok,
+                                   int32_t *counts, int *ctl, cudaStream_t st);
+cudaError_t launch_ep_return_p2p(const float *part, const int32_t *r_ids, int k, int H, int g, int cap, int self,
+                                 const EpPeers &P, int *ctl, cudaStream_t st);
+// Waits (bounded) until every peer's next message of direction `dir` has arrived; on a timeout
+// latches TMOE_DEV_ERR_TIMEOUT in err and returns.
+cudaError_t launch_ep_wait(int dir, int g, int self, const int *flags, int *ctl, int *err, cudaStream_t st);
 
 // Q8_K rows as the expert GEMV reads them: qs int8 [rows][K], d f32 [rows][K/256], and per
 // super-block the activation sums over the weight type's sub-blocks (32 elements for Q4_K, 16 for

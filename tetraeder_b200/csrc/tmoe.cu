@@ -76,9 +76,17 @@ struct tmoe_handle {
     // exchange buffers of the all-to-all EP mode (allocated on its first call; see tmoe_ep_a2a_layer)
     struct A2A {
         void *mem = nullptr;
+        size_t bytes = 0;
         int g = 0, cap = 0;
         int32_t *row_of = nullptr, *s_ids = nullptr, *r_ids = nullptr, *s_tok = nullptr, *counts = nullptr;
         float *s_w = nullptr, *r_w = nullptr, *s_x = nullptr, *r_x = nullptr, *part = nullptr, *ret = nullptr;
+        // the exchange over peer memory: arrival counters (written by the peers), this rank's
+        // counters, every rank's buffers mapped here (peer_base: the IPC mappings to close)
+        int *flags = nullptr, *ctl = nullptr;
+        const tmoe_comm *comm = nullptr;
+        bool p2p = false;
+        void *peer_base[tmoe::EP_MAX_PEERS] = {};
+        tmoe::EpPeers peers{};
     } a2a;
     // scratch of tmoe_mul_mat_id, sized at create for max_tokens * n_expert_used rows of
     // K = max(n_embd, n_ff) in the larger (Q6_K) Q8_K layout
@@ -454,6 +462,109 @@ int run_mmid(tmoe_handle *h, cudaStream_t st, int wt, const void *W, size_t nb1,
     return TMOE_OK;
 }
 
+// Unmaps the peers' all-to-all buffers.
+void close_peers(tmoe_handle::A2A &A) {
+    for (auto &b : A.peer_base)
+        if (b) cudaIpcCloseMemHandle(b), b = nullptr;
+    A.p2p = false;
+    A.comm = nullptr;
+}
+
+// Maps every rank's all-to-all buffers into this process for the exchange over peer memory (one
+// collective step of all the communicator's ranks, on the first call with this communicator and
+// buffer size): the ranks exchange their CUDA IPC handles and layouts with an all-gather, open
+// the peers' handles, and take the path only if every rank mapped every peer and all layouts are
+// the same; otherwise they keep the NCCL exchange.  Host-synchronous; returns TMOE_OK either way,
+// or an error of the all-gather.
+struct PeerInfo {
+    cudaIpcMemHandle_t handle;
+    uint64_t bytes;
+    int32_t g, cap, k, H, ok;
+    char pad[128 - sizeof(cudaIpcMemHandle_t) - 8 - 20];
+};
+static_assert(sizeof(PeerInfo) == 128, "peer info");
+
+int setup_peers(tmoe_handle *h, tmoe_comm *comm, int g, int rank, cudaStream_t st) {
+    auto &A = h->a2a;
+    const tmoe_config &c = h->cfg;
+    close_peers(A);
+    A.comm = comm;
+    // the counters start from zero on every rank before any rank can write to another
+    if (cudaMemset(A.flags, 0, (size_t)((char *)A.ctl - (char *)A.flags) + (size_t)(4 + 2 * g) * 4) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(h, TMOE_E_CUDA, "all-to-all counters");
+    }
+    PeerInfo mine{};
+    mine.ok = g <= tmoe::EP_MAX_PEERS && cudaIpcGetMemHandle(&mine.handle, A.mem) == cudaSuccess;
+    cudaGetLastError();
+    mine.bytes = A.bytes, mine.g = g, mine.cap = A.cap, mine.k = c.n_expert_used, mine.H = c.n_embd;
+    void *dev = nullptr;
+    if (cudaMalloc(&dev, sizeof(PeerInfo) * (g + 1) + 8 * (g + 1)) != cudaSuccess)
+        return fail(h, TMOE_E_NOMEM, "peer exchange scratch");
+    std::vector<PeerInfo> all(g);
+    char msg[256];
+    int rc = TMOE_OK;
+    int ok = 0;
+    if (cudaMemcpy(dev, &mine, sizeof mine, cudaMemcpyHostToDevice) != cudaSuccess)
+        rc = fail(h, TMOE_E_CUDA, "peer exchange copy");
+    if (rc == TMOE_OK) {
+        rc = tmoe::ep_allgather_bytes(comm, dev, (char *)dev + sizeof(PeerInfo), sizeof(PeerInfo), st, msg, sizeof msg);
+        if (rc) rc = fail(h, rc, "%s", msg);
+    }
+    if (rc == TMOE_OK && (cudaStreamSynchronize(st) != cudaSuccess ||
+                          cudaMemcpy(all.data(), (char *)dev + sizeof(PeerInfo), sizeof(PeerInfo) * g,
+                                     cudaMemcpyDeviceToHost) != cudaSuccess))
+        rc = fail(h, TMOE_E_CUDA, "peer exchange read-back");
+    if (rc == TMOE_OK) {
+        ok = 1;
+        for (int p = 0; p < g; p++)
+            if (!all[p].ok || all[p].bytes != mine.bytes || all[p].g != g || all[p].cap != mine.cap ||
+                all[p].k != mine.k || all[p].H != mine.H)
+                ok = 0;
+        for (int p = 0; p < g && ok; p++) {
+            if (p == rank) continue;
+            if (cudaIpcOpenMemHandle(&A.peer_base[p], all[p].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                A.peer_base[p] = nullptr;
+                ok = 0;
+            }
+        }
+        // every rank must take the same path: the minimum of the ranks' results
+        int *oks = (int *)((char *)dev + sizeof(PeerInfo) * (g + 1));
+        if (cudaMemcpy(oks, &ok, 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = fail(h, TMOE_E_CUDA, "peer status");
+        if (rc == TMOE_OK) {
+            rc = tmoe::ep_allgather_bytes(comm, oks, oks + 1, 4, st, msg, sizeof msg);
+            if (rc) rc = fail(h, rc, "%s", msg);
+        }
+        std::vector<int> all_ok(g, 0);
+        if (rc == TMOE_OK && (cudaStreamSynchronize(st) != cudaSuccess ||
+                              cudaMemcpy(all_ok.data(), oks + 1, 4 * g, cudaMemcpyDeviceToHost) != cudaSuccess))
+            rc = fail(h, TMOE_E_CUDA, "peer status read-back");
+        for (int p = 0; p < g; p++)
+            if (!all_ok[p]) ok = 0;
+    }
+    cudaFree(dev);
+    if (rc != TMOE_OK || !ok) {
+        for (auto &b : A.peer_base)
+            if (b) cudaIpcCloseMemHandle(b), b = nullptr;
+        A.p2p = false;
+        return rc;
+    }
+    auto at = [&](int p, const void *local) -> char * {
+        const size_t off = (size_t)((const char *)local - (const char *)A.mem);
+        return (char *)(p == rank ? A.mem : A.peer_base[p]) + off;
+    };
+    for (int p = 0; p < g; p++) {
+        A.peers.r_ids[p] = (int32_t *)at(p, A.r_ids);
+        A.peers.r_w[p] = (float *)at(p, A.r_w);
+        A.peers.r_x[p] = (float *)at(p, A.r_x);
+        A.peers.ret[p] = (float *)at(p, A.ret);
+        A.peers.flags[p] = (int *)at(p, A.flags);
+    }
+    A.p2p = true;
+    return TMOE_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -524,6 +635,7 @@ void tmoe_destroy(tmoe_handle *h) {
     if (h->ws) cudaFree(h->ws);
     if (h->op_ws) cudaFree(h->op_ws);
     if (h->dense_ws) cudaFree(h->dense_ws);
+    close_peers(h->a2a);
     if (h->a2a.mem) cudaFree(h->a2a.mem);
     for (auto &ev : h->prof.ev)
         if (ev) cudaEventDestroy(ev);
@@ -789,10 +901,12 @@ int tmoe_ep_a2a_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float
     cudaStream_t st = (cudaStream_t)stream;
     auto &A = h->a2a;
     if (A.g != g || A.cap != cap) {  // the exchange buffers of this rank count
+        close_peers(A);
         if (A.mem) cudaFree(A.mem), A.mem = nullptr;
         const size_t ni = (size_t)g * cap, rows_x = ni * H * 4;
         const size_t bytes = align_up(ni * 4, 256) * 2 /* row_of, s_tok */ + align_up((size_t)g * 4, 256) +
-                             align_up(ni * k * 4, 256) * 4 /* ids, w both ways */ + align_up(rows_x, 256) * 4;
+                             align_up(ni * k * 4, 256) * 4 /* ids, w both ways */ + align_up(rows_x, 256) * 4 +
+                             align_up((size_t)2 * g * 4, 256) + align_up((size_t)(4 + 2 * g) * 4, 256);
         if (cudaMalloc(&A.mem, bytes) != cudaSuccess) {
             cudaGetLastError();
             A.g = A.cap = 0;
@@ -809,7 +923,17 @@ int tmoe_ep_a2a_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float
         A.s_w = (float *)take(ni * k * 4), A.r_w = (float *)take(ni * k * 4);
         A.s_x = (float *)take(rows_x), A.r_x = (float *)take(rows_x);
         A.part = (float *)take(rows_x), A.ret = (float *)take(rows_x);
+        A.flags = (int *)take((size_t)2 * g * 4), A.ctl = (int *)take((size_t)(4 + 2 * g) * 4);
+        if (cudaMemset(A.flags, 0, (size_t)((char *)p - (char *)A.flags)) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(h, TMOE_E_CUDA, "all-to-all counters");
+        }
+        A.bytes = bytes;
         A.g = g, A.cap = cap;
+    }
+    if (A.comm != comm) {  // map the peers' buffers (every rank of the communicator takes this step)
+        const int r = setup_peers(h, comm, g, rank, st);
+        if (r != TMOE_OK) return r;
     }
     int32_t *ids = ids_out ? ids_out : h->ids;
     float *w = w_out ? w_out : h->w;
@@ -833,6 +957,29 @@ int tmoe_ep_a2a_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float
                : TMOE_OK;
     }
     const float *xn = use_norm ? h->xn : x;
+    if (A.p2p) {
+        // the exchange over peer memory: the messages written into the peers' buffers, a bounded
+        // wait for theirs, the experts, the partial rows written back, a bounded wait, the combine
+        {
+            PhaseMark pm(h, st, TMOE_PHASE_MAP_IDS);
+            e = tmoe::launch_ep_dispatch_p2p(ids, w, xn, rc == TMOE_OK ? (int)T : 0, k, H, E / g, g, cap, rank,
+                                             A.peers, A.row_of, A.s_tok, A.counts, A.ctl, st);
+        }
+        if (e == cudaSuccess) e = tmoe::launch_ep_wait(0, g, rank, A.flags, A.ctl, h->err, st);
+        if (e != cudaSuccess) return cuda_fail(h, e, "all-to-all dispatch over peer memory");
+        const int rc3 = run_experts(h, st, A.r_x, (int64_t)g * cap, A.r_ids, A.r_w, wts, A.part, false, false);
+        if (rc3 != TMOE_OK) cudaMemsetAsync(A.part, 0, (size_t)g * cap * H * 4, st);
+        e = tmoe::launch_ep_return_p2p(A.part, A.r_ids, k, H, g, cap, rank, A.peers, A.ctl, st);
+        if (e == cudaSuccess) e = tmoe::launch_ep_wait(1, g, rank, A.flags, A.ctl, h->err, st);
+        if (e != cudaSuccess) return cuda_fail(h, e, "all-to-all return over peer memory");
+        if (rc) return rc;
+        if (rc3) return rc3;
+        if (T) {
+            PhaseMark pm(h, st, TMOE_PHASE_COMBINE);
+            e = tmoe::launch_ep_combine(A.ret, A.part, rank, A.row_of, (int)T, H, g, cap, out, st);
+        }
+        return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "all-to-all combine");
+    }
     if (rc == TMOE_OK && T) {
         PhaseMark pm(h, st, TMOE_PHASE_MAP_IDS);
         e = tmoe::launch_ep_pack(ids, w, xn, (int)T, k, H, E / g, g, cap, rank, A.row_of, A.s_ids, A.s_w, A.r_ids,
