@@ -256,7 +256,13 @@ TMOE_API int tmoe_streamed_layer(tmoe_handle *h, void *stream, tmoe_slots *s, co
  * them in choice order (the reference's per-rank partial, qwen3moe_shard.rs:1043-1056), sends the
  * partial row back, and the token's rank adds the partials in rank order.  Messages have a fixed
  * capacity of max_tokens / g rows per peer (no host readback).  Every rank must make the same
- * calls in the same order; a rank whose routing fails still takes both exchange steps. */
+ * calls in the same order; a rank whose routing fails still takes both exchange steps.
+ * Exchange: the first call with a communicator maps every rank's exchange buffers into every
+ * rank (CUDA IPC; host-synchronous, so not under stream capture), and from then on the messages
+ * are written straight into the peers' buffers over NVLink with counted arrivals (a wait that runs
+ * out after 1 s latches TMOE_DEV_ERR_TIMEOUT, reported by tmoe_check).  With g > 8, or if any rank
+ * cannot map a peer, the ranks exchange through NCCL instead.  A rank must not destroy its handle
+ * while another rank is still inside a call with it. */
 TMOE_API int tmoe_ep_a2a_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float *x, int64_t T,
                                int32_t use_norm, const float *norm_w, const float *router_w, const float *logits,
                                const tmoe_expert_tensors *wts, float *out, int32_t *ids_out, float *w_out);
