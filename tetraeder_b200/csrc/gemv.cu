@@ -609,9 +609,11 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
     }
     __syncwarp();
     // Programmatic launch: gate/up reads what the routing kernel (its predecessor) wrote, so it
-    // waits here.  Down's predecessor only writes its activations: the dispatch data and the
-    // weights are two and more launches back, so down issues its first fills before it waits.
-    if constexpr (GATEUP) {
+    // waits here.  The layer's down GEMV (a.early) has a predecessor that only writes its
+    // activations: the dispatch data and the weights are two and more launches back, so it issues
+    // its first fills before it waits.  Any other launch waits here.
+    const bool early = !GATEUP && a.early;
+    if (!early) {
         pdl_wait();
         pdl_trigger();
     }
@@ -651,7 +653,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
     next_item<NG>(a, f, q, n_items);
     for (int s = 0; s < D; s++)
         fill<WT, GATEUP, NG>(a, tm, f, &bars[s], &recs[s], slots + (size_t)s * a.slot_bytes, q, n_items);
-    if constexpr (!GATEUP) {
+    if (early) {
         pdl_wait();
         pdl_trigger();
     }

@@ -190,6 +190,10 @@ struct GemvArgs {
     int *work;       // work counter, zero at launch (the dispatch kernels zero it)
     float *out;      // [pairs][N]
     int *err;
+    // the dispatch data (n_active, active, perm, work) were written two or more launches back, so
+    // that under programmatic launch the kernel may read them and issue its first weight fills
+    // before it waits for its predecessor (non-gate/up only)
+    int early;
     // filled by the launcher
     int tiles;         // items per active expert
     int chunk_blocks;  // super-blocks per fill

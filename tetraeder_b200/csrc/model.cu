@@ -22,6 +22,8 @@ namespace tmoe {
 // x [n_tok][n_head][head_dim] in place, token t at position pos[t].
 __global__ void rope_neox_kernel(float *__restrict__ x, const int32_t *__restrict__ pos, int64_t n_tok, int n_head,
                                  int head_dim, int n_rot, float freq_base) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x;  // token * n_head + head
     const int64_t t = row / n_head;
     if (t >= n_tok) return;
@@ -44,6 +46,8 @@ __global__ void rope_neox_kernel(float *__restrict__ x, const int32_t *__restric
 __global__ void qk_norm_rope_kernel(float *__restrict__ q, float *__restrict__ k, const float *__restrict__ qw,
                                     const float *__restrict__ kw, const int32_t *__restrict__ pos, int n_head,
                                     int n_kv, int d, int n_rot, float freq_base, float eps) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float row[128];
     __shared__ double part[4];
     const int r = blockIdx.x, per_tok = n_head + n_kv;
@@ -80,6 +84,8 @@ __global__ void qk_norm_rope_kernel(float *__restrict__ q, float *__restrict__ k
 __global__ void kv_store_kernel(const float *__restrict__ k, const float *__restrict__ v, __half *__restrict__ kc,
                                 __half *__restrict__ vc, const int32_t *__restrict__ pos, int n_ctx, int width,
                                 int *err) {
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.x;
     const int p = pos[b];
     if (p < 0 || p >= n_ctx) {
@@ -155,6 +161,8 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const float *__
                                                                  const int32_t *__restrict__ pos, int n_head,
                                                                  int n_kv, int n_ctx, float scale,
                                                                  float *__restrict__ part) {
+    pdl_wait();
+    pdl_trigger();
     using SM = AttnSmem<HD>;
     constexpr int KB = HD / 16;  // dim blocks of the QK^T product
     constexpr int NB = HD / 8;   // dim blocks of the output
@@ -305,6 +313,8 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const float *__
 
 // out[b][head][:] from the S partials of (b, head): one CTA per (b, head).
 __global__ void attn_merge_kernel(const float *__restrict__ part, int S, int HD, float *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const size_t bh = blockIdx.x;
     const float *pp = part + bh * S * ((size_t)HD + 2);
     float M = -INFINITY;
@@ -518,6 +528,8 @@ __global__ void __launch_bounds__(AP_THREADS) attn_prefill_kernel(const float *_
 
 __global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ out,
                            int64_t n) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) out[i] = a[i] + b[i];
 }
@@ -525,6 +537,8 @@ __global__ void add_kernel(const float *__restrict__ a, const float *__restrict_
 // out[r] = the first index of the largest value of row r.  One CTA per row.
 __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ x, int64_t n, bool vec4,
                                                       int32_t *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const float *row = x + (int64_t)blockIdx.x * n;
     float best = -INFINITY;
     int64_t bi = 0x7fffffff;
@@ -579,6 +593,8 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
 // outputs as [T][ks][N].  Entry j = s * ng + g holds slice s of group g; perm[s*T + t] = t*ks + s.
 __global__ void dense_prep_kernel(int T, int group, int ks, int4 *__restrict__ active, int32_t *__restrict__ n_active,
                                   int32_t *__restrict__ perm, int *__restrict__ counters, int n_counters) {
+    pdl_wait();
+    pdl_trigger();
     const int ng = (T + group - 1) / group;
     for (int i = threadIdx.x; i < T * ks; i += blockDim.x) perm[i] = (i % T) * ks + i / T;
     for (int j = threadIdx.x; j < ng * ks; j += blockDim.x) {
@@ -591,6 +607,8 @@ __global__ void dense_prep_kernel(int T, int group, int ks, int4 *__restrict__ a
 
 // out[t][n] = sum over s of part[t][s][n], the slices added in order (the same sums every call).
 __global__ void splitk_sum_kernel(const float *__restrict__ part, int64_t T, int N, int ks, float *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // a group of 4 outputs
     const int64_t n4 = (int64_t)N / 4;
     if (i >= T * n4) return;
@@ -608,7 +626,7 @@ __global__ void splitk_sum_kernel(const float *__restrict__ part, int64_t T, int
 cudaError_t launch_dense_prep(int T, int group, int ks, int4 *active, int32_t *n_active, int32_t *perm, int *counters,
                               int n_counters, cudaStream_t st) {
     if (n_counters > 256 || group < 1 || ks < 1 || (int64_t)T * ks >= (1 << 24)) return cudaErrorInvalidValue;
-    dense_prep_kernel<<<1, 256, 0, st>>>(T, group, ks, active, n_active, perm, counters, n_counters);
+    launch_k(dense_prep_kernel, 1, 256, 0, st, T, group, ks, active, n_active, perm, counters, n_counters);
     return cudaGetLastError();
 }
 
@@ -616,7 +634,7 @@ cudaError_t launch_splitk_sum(const float *part, int64_t T, int N, int ks, float
     if (T <= 0) return cudaSuccess;
     if (N % 4 || ks < 1 || ((uintptr_t)part & 15) || ((uintptr_t)out & 15)) return cudaErrorInvalidValue;
     const int64_t n = T * (N / 4);
-    splitk_sum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, T, N, ks, out);
+    launch_k(splitk_sum_kernel, (unsigned)((n + 255) / 256), 256, 0, st, part, T, N, ks, out);
     return cudaGetLastError();
 }
 
@@ -625,8 +643,8 @@ cudaError_t launch_qk_norm_rope(float *q, float *k, const float *qw, const float
     if (T <= 0) return cudaSuccess;
     if (d <= 0 || d > 128 || d % 32 || n_rot <= 0 || n_rot > d || n_rot % 2 || T * (n_head + n_kv) > 0x7fffffff)
         return cudaErrorInvalidValue;
-    qk_norm_rope_kernel<<<(unsigned)(T * (n_head + n_kv)), d, 0, st>>>(q, k, qw, kw, pos, n_head, n_kv, d, n_rot,
-                                                                       freq_base, eps);
+    launch_k(qk_norm_rope_kernel, (unsigned)(T * (n_head + n_kv)), d, 0, st, q, k, qw, kw, pos, n_head, n_kv, d, n_rot,
+             freq_base, eps);
     return cudaGetLastError();
 }
 
@@ -634,7 +652,7 @@ cudaError_t launch_rope_neox(float *x, const int32_t *pos, int64_t n_tok, int n_
                              float freq_base, cudaStream_t st) {
     if (n_tok <= 0) return cudaSuccess;
     if (n_rot <= 0 || n_rot > head_dim || n_rot % 2 || n_tok * n_head > 0x7fffffff) return cudaErrorInvalidValue;
-    rope_neox_kernel<<<(unsigned)(n_tok * n_head), 64, 0, st>>>(x, pos, n_tok, n_head, head_dim, n_rot, freq_base);
+    launch_k(rope_neox_kernel, (unsigned)(n_tok * n_head), 64, 0, st, x, pos, n_tok, n_head, head_dim, n_rot, freq_base);
     return cudaGetLastError();
 }
 
@@ -656,7 +674,7 @@ cudaError_t launch_attn_decode(const float *q, const float *k, const float *v, _
         n_ctx <= 0 || B > 65535 || n_kv > 65535)
         return cudaErrorInvalidValue;
     const int width = n_kv * head_dim;
-    kv_store_kernel<<<B, 128, 0, st>>>(k, v, kc, vc, pos, n_ctx, width, err);
+    launch_k(kv_store_kernel, B, 128, 0, st, k, v, kc, vc, pos, n_ctx, width, err);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const int S = attn_splits(B, n_kv, n_ctx, sm_count);
@@ -672,7 +690,7 @@ cudaError_t launch_attn_decode(const float *q, const float *k, const float *v, _
                                       (int)smem)) != cudaSuccess)
             return e;
         set128[dev] = 1;
-        attn_decode_kernel<128><<<grid, AT_THREADS, smem, st>>>(q, kc, vc, pos, n_head, n_kv, n_ctx, scale, part);
+        launch_k(attn_decode_kernel<128>, grid, AT_THREADS, smem, st, q, kc, vc, pos, n_head, n_kv, n_ctx, scale, part);
     } else {
         constexpr size_t smem = AttnSmem<64>::BYTES;
         if (!set64[dev] &&
@@ -680,10 +698,10 @@ cudaError_t launch_attn_decode(const float *q, const float *k, const float *v, _
                                       (int)smem)) != cudaSuccess)
             return e;
         set64[dev] = 1;
-        attn_decode_kernel<64><<<grid, AT_THREADS, smem, st>>>(q, kc, vc, pos, n_head, n_kv, n_ctx, scale, part);
+        launch_k(attn_decode_kernel<64>, grid, AT_THREADS, smem, st, q, kc, vc, pos, n_head, n_kv, n_ctx, scale, part);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    attn_merge_kernel<<<B * n_head, 128, 0, st>>>(part, S, head_dim, out);
+    launch_k(attn_merge_kernel, B * n_head, 128, 0, st, part, S, head_dim, out);
     return cudaGetLastError();
 }
 
@@ -727,7 +745,7 @@ cudaError_t launch_attn_prefill(const float *q, const float *k, const float *v, 
 
 cudaError_t launch_add(const float *a, const float *b, float *out, int64_t n, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    add_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a, b, out, n);
+    launch_k(add_kernel, (unsigned)((n + 255) / 256), 256, 0, st, a, b, out, n);
     return cudaGetLastError();
 }
 
@@ -735,7 +753,7 @@ cudaError_t launch_argmax(const float *x, int64_t rows, int64_t n, int32_t *out,
     if (rows <= 0) return cudaSuccess;
     if (rows > 0x7fffffff || n <= 0) return cudaErrorInvalidValue;
     const bool vec4 = n % 4 == 0 && ((uintptr_t)x & 15) == 0;
-    argmax_kernel<<<(unsigned)rows, 1024, 0, st>>>(x, n, vec4, out);
+    launch_k(argmax_kernel, (unsigned)rows, 1024, 0, st, x, n, vec4, out);
     return cudaGetLastError();
 }
 

@@ -158,6 +158,8 @@ __global__ void dequantize_kernel(int wt, const uint8_t *__restrict__ in, int64_
 // apart).  One CTA per output row.
 __global__ void get_rows_kernel(int32_t type, const uint8_t *__restrict__ W, size_t nb1, int K, int64_t n_rows_w,
                                 const int32_t *__restrict__ rows, float *__restrict__ out, int *err) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = blockIdx.x;
     const int32_t r = rows[i];
     float *o = out + i * K;
@@ -192,7 +194,7 @@ cudaError_t launch_get_rows(int32_t type, const uint8_t *W, size_t nb1, int K, i
                             int64_t n, float *out, int *err, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
     if (n > 0x7fffffff) return cudaErrorInvalidValue;
-    get_rows_kernel<<<(unsigned)n, 128, 0, st>>>(type, W, nb1, K, n_rows_w, rows, out, err);
+    launch_k(get_rows_kernel, (unsigned)n, 128, 0, st, type, W, nb1, K, n_rows_w, rows, out, err);
     return cudaGetLastError();
 }
 

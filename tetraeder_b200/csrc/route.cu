@@ -20,6 +20,8 @@ namespace tmoe {
 // One warp per token: ggml rms_norm (f64 sum of f32 squares) times the optional norm weight.
 __global__ void rms_norm_kernel(const float *__restrict__ x, const float *__restrict__ norm_w, float eps, int64_t T,
                                 int H, float *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= T) return;
@@ -45,6 +47,8 @@ __global__ void rms_norm_kernel(const float *__restrict__ x, const float *__rest
 // warps' sums added in order; the same f32 mean, scale and products as rms_norm_kernel.
 __global__ void __launch_bounds__(256) rms_norm_row_kernel(const float *__restrict__ x, const float *__restrict__ norm_w,
                                                           float eps, int H, float *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ double part[8];
     const int64_t row = blockIdx.x;
     const float *xr = x + row * H;
@@ -334,11 +338,11 @@ cudaError_t launch_rms_norm(const float *x, const float *norm_w, float eps, int6
                             cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (T <= 2048 && H >= 1024) {  // few long rows: a CTA per row
-        rms_norm_row_kernel<<<(unsigned)T, 256, 0, st>>>(x, norm_w, eps, H, out);
+        launch_k(rms_norm_row_kernel, (unsigned)T, 256, 0, st, x, norm_w, eps, H, out);
         return cudaGetLastError();
     }
     const int warps = 8;
-    rms_norm_kernel<<<(unsigned)((T + warps - 1) / warps), warps * 32, 0, st>>>(x, norm_w, eps, T, H, out);
+    launch_k(rms_norm_kernel, (unsigned)((T + warps - 1) / warps), warps * 32, 0, st, x, norm_w, eps, T, H, out);
     return cudaGetLastError();
 }
 

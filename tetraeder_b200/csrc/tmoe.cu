@@ -374,7 +374,7 @@ int run_experts(tmoe_handle *h, cudaStream_t st, const float *xn, int64_t T, con
     d.xq = h->aq, d.xd = h->ad, d.xbl = h->abl, d.xbh = h->abh, d.x_div = 1;
     d.perm = h->perm, d.active = h->active, d.n_active = h->n_active;
     d.n_slots = t->n_slots, d.max_active = max_active, d.n_pairs = (int)P, d.work = h->counters + 1;
-    d.out = h->dout, d.err = h->err;
+    d.out = h->dout, d.err = h->err, d.early = 1;  // the dispatch is three launches back
     {
         PhaseMark pm(h, st, TMOE_PHASE_DOWN);
         e = tmoe::launch_gemv(wd, false, d, max_active, h->sm_count, st);
@@ -763,6 +763,7 @@ int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
     if (rc) return rc;
     if (T == 0) return TMOE_OK;
     DeviceGuard dg(c.device);
+    tmoe::PdlScope pdl(!h->prof.on);  // its kernels overlap their predecessors' tails (programmatic launch)
     cudaStream_t st = (cudaStream_t)stream;
     const int k = c.n_expert_used;
     int32_t *ids = ids_out ? ids_out : h->ids;
@@ -781,10 +782,7 @@ int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t 
     bool x_quantized = false;
     const float *lg = logits;
     if (router_w && tmoe::route_fused_fits(T, k, c.n_expert, c.n_embd, wts->n_slots)) {
-        // decode regime: logits + Q8_K of xn + top-k + id map + dispatch in one launch.  Its kernels
-        // start during their predecessors' tails (programmatic dependent launch), except while the
-        // per-kernel events of profile() sit between them.
-        tmoe::PdlScope pdl(!h->prof.on);
+        // decode regime: logits + Q8_K of xn + top-k + id map + dispatch in one launch
         const tmoe::Q8Rows q8{h->xq, h->xd, h->xbl, h->xbh, wt_of(c.gate_type)};
         {
             PhaseMark pm(h, st, TMOE_PHASE_ROUTER_LOGITS);
@@ -1059,6 +1057,7 @@ int tmoe_mul_mat(tmoe_handle *h, void *stream, int32_t type, const void *W, size
     if (reuse && (h->dense_x != x || h->dense_wt != wt || h->dense_k != K || h->dense_t != T))
         return fail(h, TMOE_E_INVALID, "reuse_x: the last quantised activations are not these (x, K, T, weight family)");
     DeviceGuard dg(h->cfg.device);
+    tmoe::PdlScope pdl(!h->prof.on);  // overlap with the kernel before (programmatic launch)
     cudaStream_t st = (cudaStream_t)stream;
     size_t need = 0;
     auto lay = [&](size_t bytes) {
@@ -1284,6 +1283,7 @@ int tmoe_get_rows(tmoe_handle *h, void *stream, int32_t type, const void *W, siz
     if (n == 0) return TMOE_OK;
     if (!W || !rows || !out) return fail(h, TMOE_E_INVALID, "null tensor");
     DeviceGuard dg(h->cfg.device);
+    tmoe::PdlScope pdl(!h->prof.on);  // overlap with the kernel before (programmatic launch)
     cudaError_t e = tmoe::launch_get_rows(type, (const uint8_t *)W, nb1, (int)K, n_rows_w, rows, n, out, h->err,
                                           (cudaStream_t)stream);
     return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "get_rows");
@@ -1296,6 +1296,7 @@ int tmoe_rms_norm(tmoe_handle *h, void *stream, const float *x, const float *w, 
     if (rows == 0) return TMOE_OK;
     if (!x || !out) return fail(h, TMOE_E_INVALID, "null tensor");
     DeviceGuard dg(h->cfg.device);
+    tmoe::PdlScope pdl(!h->prof.on);  // overlap with the kernel before (programmatic launch)
     cudaError_t e = tmoe::launch_rms_norm(x, w, eps, rows, (int)n, out, (cudaStream_t)stream);
     return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "rms_norm");
 }
@@ -1308,6 +1309,7 @@ int tmoe_rope_neox(tmoe_handle *h, void *stream, float *x, const int32_t *pos, i
     if (n_tok == 0) return TMOE_OK;
     if (!x || !pos) return fail(h, TMOE_E_INVALID, "null tensor");
     DeviceGuard dg(h->cfg.device);
+    tmoe::PdlScope pdl(!h->prof.on);  // overlap with the kernel before (programmatic launch)
     cudaError_t e = tmoe::launch_rope_neox(x, pos, n_tok, n_head, head_dim, n_rot, freq_base, (cudaStream_t)stream);
     return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "rope");
 }
@@ -1322,6 +1324,7 @@ int tmoe_qk_norm_rope(tmoe_handle *h, void *stream, float *q, float *k, const fl
     if (T == 0) return TMOE_OK;
     if (!q || !k || !q_norm || !k_norm || !pos) return fail(h, TMOE_E_INVALID, "null tensor");
     DeviceGuard dg(h->cfg.device);
+    tmoe::PdlScope pdl(!h->prof.on);  // overlap with the kernel before (programmatic launch)
     cudaError_t e = tmoe::launch_qk_norm_rope(q, k, q_norm, k_norm, pos, T, n_head, n_kv, head_dim, n_rot, freq_base,
                                               eps, (cudaStream_t)stream);
     return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "qk_norm_rope");
@@ -1344,6 +1347,7 @@ int tmoe_attn_decode(tmoe_handle *h, void *stream, const float *q, const float *
     if (!q || !k || !v || !k_cache || !v_cache || !pos || !scratch || !out) return fail(h, TMOE_E_INVALID, "null tensor");
     if (((uintptr_t)k_cache | (uintptr_t)v_cache) & 15u) return fail(h, TMOE_E_INVALID, "caches must be 16-byte aligned");
     DeviceGuard dg(h->cfg.device);
+    tmoe::PdlScope pdl(!h->prof.on);  // overlap with the kernel before (programmatic launch)
     cudaError_t e = tmoe::launch_attn_decode(q, k, v, (__half *)k_cache, (__half *)v_cache, pos, B, n_head, n_kv,
                                              head_dim, n_ctx, scale, (float *)scratch, out, h->sm_count, h->err,
                                              (cudaStream_t)stream);
@@ -1376,6 +1380,7 @@ int tmoe_add(tmoe_handle *h, void *stream, const float *a, const float *b, float
     if (n == 0) return TMOE_OK;
     if (!a || !b || !out) return fail(h, TMOE_E_INVALID, "null tensor");
     DeviceGuard dg(h->cfg.device);
+    tmoe::PdlScope pdl(!h->prof.on);  // overlap with the kernel before (programmatic launch)
     cudaError_t e = tmoe::launch_add(a, b, out, n, (cudaStream_t)stream);
     return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "add");
 }
@@ -1386,6 +1391,7 @@ int tmoe_argmax(tmoe_handle *h, void *stream, const float *x, int64_t rows, int6
     if (rows == 0) return TMOE_OK;
     if (!x || !out) return fail(h, TMOE_E_INVALID, "null tensor");
     DeviceGuard dg(h->cfg.device);
+    tmoe::PdlScope pdl(!h->prof.on);  // overlap with the kernel before (programmatic launch)
     cudaError_t e = tmoe::launch_argmax(x, rows, n, out, (cudaStream_t)stream);
     return e == cudaSuccess ? TMOE_OK : cuda_fail(h, e, "argmax");
 }
