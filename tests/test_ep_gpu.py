@@ -133,3 +133,80 @@ def test_ep_a2a_two_ranks_equal_the_one_rank_layer(shape):
         n, m = nrms(out, want[rows]), maxabs_over_rms(out, want[rows])
         bound = (1e-3, 2.5e-2) if T * world * k >= 4096 else (1e-3, 1e-2)
         assert n <= bound[0] and m <= bound[1], f"rank {rank}: nrms={n:.2e} maxabs/rms={m:.2e}"
+
+
+def _rank_a2a_silent_peer(rank, world, uid, done, q):
+    """Both ranks make one all-to-all call; then rank 0 calls again and rank 1 does not.  Rank 1
+    keeps its handle (rank 0 writes into its buffers) until rank 0 has finished."""
+    import os
+    import time
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import tetraeder_b200 as tb
+    from tetraeder_b200 import moe
+    H, I, E, k, T, seed = 512, 256, 16, 4, 32, 11
+    torch.cuda.set_device(rank)
+    gate, up, down, rw, x = _case(H, I, E, world * T, seed)
+    per = E // world
+    sl = slice(rank * per, (rank + 1) * per)
+    cu = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    layer = tb.MoeLayer(H, I, E, k, gate_type=O.TYPE_Q4_K, up_type=O.TYPE_Q4_K, down_type=O.TYPE_Q6_K,
+                        max_tokens=world * T, device=rank)
+    comm = moe.EPComm(uid, world, rank, device=rank, timeout_s=60.0)
+    try:
+        wts = moe.ExpertWeights(cu(gate[sl]), cu(up[sl]), cu(down[sl]))
+        xs = cu(x[rank * T:(rank + 1) * T])
+        out = moe.ep_a2a_moe_ffn(layer, comm, xs, wts, router_w=cu(rw))
+        torch.cuda.synchronize()
+        layer.check()
+        if rank == 0:
+            t0 = time.monotonic()
+            err = None
+            try:
+                moe.ep_a2a_moe_ffn(layer, comm, xs, wts, router_w=cu(rw), out=out)  # rank 1 never answers
+                layer.check()
+            except tb.TmoeError as e:
+                err = str(e)
+            dt = time.monotonic() - t0
+            if err and "TMOE_E_COMM" in err:  # the NCCL exchange (buffers not mapped): its own deadline
+                err = None
+            # the context is still usable: a plain one-rank layer call on the same handle
+            solo = tb.MoeLayer(H, I, E, k, gate_type=O.TYPE_Q4_K, up_type=O.TYPE_Q4_K, down_type=O.TYPE_Q6_K,
+                               max_tokens=T, device=rank)
+            full = moe.ExpertWeights(cu(gate), cu(up), cu(down))
+            solo.moe_ffn(xs, full, router_w=cu(rw))
+            solo.check()
+            solo.close()
+            q.put((rank, err, dt))
+            done.set()
+        else:
+            done.wait(timeout=120)
+            q.put((rank, None, 0.0))
+    finally:
+        comm.close()
+        layer.close()
+
+
+@needs_two
+def test_ep_a2a_silent_peer_ends_in_a_bounded_wait():
+    """The exchange over peer memory waits for each peer's messages with a bounded device wait: a
+    peer that never answers makes the wait run out (about 1 s per direction), the error is latched
+    and reported by check(), and the GPU context stays usable.  No kernel faults or hangs; the
+    failure is a rank that does not make the call (NVLS is off)."""
+    from tetraeder_b200 import moe
+    world = 2
+    uid = moe.EPComm.unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    done = ctx.Event()
+    procs = [ctx.Process(target=_rank_a2a_silent_peer, args=(r, world, uid, done, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict((r, (e, dt)) for r, e, dt in (q.get(timeout=300) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    err, dt = res[0]
+    if err is None:
+        pytest.skip("the ranks exchanged through NCCL (the peers' buffers could not be mapped)")
+    assert "TMOE_E_DEVICE" in err or "timeout" in err.lower(), err
+    assert 1.5 < dt < 30.0, dt
