@@ -163,7 +163,13 @@ TMOE_API int tmoe_experts(tmoe_handle *h, void *stream, const float *xn, int64_t
                  const float *w, const tmoe_expert_tensors *wts, float *out);
 
 /* route + (optional id map) + experts in one call.  id_map int32 [E] (device) maps global
- * expert ids to slots of `wts` or -1 (NULL: identity).  ids_out / w_out may be NULL. */
+ * expert ids to slots of `wts` or -1 (NULL: identity).  ids_out / w_out may be NULL.
+ * The layer's kernels are launched with programmatic stream serialization: each may start while
+ * the kernel before it runs, and waits for it before reading its outputs.  Two reads happen
+ * before that wait: the routing kernel stages router_w, and the down products start loading
+ * `wts->down`.  So a kernel that writes router_w or the expert tensors must not be the one
+ * launched on the stream right before this call (a copy, an event or any other kernel in between
+ * is enough).  While profile() is on, the kernels launch one after another. */
 TMOE_API int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T, int32_t use_norm,
                const float *norm_w, const float *router_w, const float *logits,
                const int32_t *id_map, const tmoe_expert_tensors *wts, float *out,
