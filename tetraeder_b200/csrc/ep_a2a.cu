@@ -92,6 +92,8 @@ __global__ void ep_gather_rows_kernel(const float *__restrict__ x, int H, int g,
 __global__ void ep_combine_kernel(const float *__restrict__ ret, const float *__restrict__ part, int self,
                                   const int32_t *__restrict__ row_of, int T, int H, int g, int cap,
                                   float *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // float4 of out
     const int H4 = H / 4;
     if (i >= (int64_t)T * H4) return;
@@ -164,6 +166,8 @@ __global__ void __launch_bounds__(1024) ep_pack_p2p_kernel(const int32_t *__rest
                                                            int g, int cap, int self, const EpPeers P,
                                                            int32_t *__restrict__ row_of, int32_t *__restrict__ s_tok,
                                                            int32_t *__restrict__ counts) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int warp_sum[32];
     __shared__ int base;
     const int d = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -214,6 +218,8 @@ __global__ void __launch_bounds__(1024) ep_pack_p2p_kernel(const int32_t *__rest
 __global__ void ep_gather_p2p_kernel(const float *__restrict__ x, int H, int g, int cap, int self, const EpPeers P,
                                      const int32_t *__restrict__ s_tok, const int32_t *__restrict__ counts,
                                      int *ctl) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (gw < (int64_t)g * cap) {
@@ -231,6 +237,8 @@ __global__ void ep_gather_p2p_kernel(const float *__restrict__ x, int H, int g, 
 // row r of block `self` of rank d's ret, when the row has an expert here (one warp per row).
 __global__ void ep_return_p2p_kernel(const float *__restrict__ part, const int32_t *__restrict__ r_ids, int k, int H,
                                      int g, int cap, int self, const EpPeers P, int *ctl) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (gw < (int64_t)g * cap) {
@@ -246,6 +254,8 @@ __global__ void ep_return_p2p_kernel(const float *__restrict__ part, const int32
 }
 
 __global__ void ep_wait_kernel(int dir, int g, int self, const int *flags, int *ctl, int *err) {
+    pdl_wait();
+    pdl_trigger();
     const int p = threadIdx.x;
     if (p >= g || p == self) return;
     int *seen = ctl + 4 + dir * g + p;
@@ -268,26 +278,28 @@ cudaError_t launch_ep_dispatch_p2p(const int32_t *ids, const float *w, const flo
                                    int g, int cap, int self, const EpPeers &P, int32_t *row_of, int32_t *s_tok,
                                    int32_t *counts, int *ctl, cudaStream_t st) {
     if (g <= 0 || g > EP_MAX_PEERS || cap <= 0 || self < 0 || self >= g || k > 32 || H % 4) return cudaErrorInvalidValue;
-    ep_pack_p2p_kernel<<<g, 1024, 0, st>>>(ids, w, T, k, per, g, cap, self, P, row_of, s_tok, counts);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_k(ep_pack_p2p_kernel, g, 1024, 0, st, ids, w, T, k, per, g, cap, self, P, row_of, s_tok,
+                             counts);
     if (e != cudaSuccess) return e;
     const int64_t warps = (int64_t)g * cap;
-    ep_gather_p2p_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(x, H, g, cap, self, P, s_tok, counts, ctl);
-    return cudaGetLastError();
+    e = launch_k(ep_gather_p2p_kernel, (unsigned)((warps + 7) / 8), 256, 0, st, x, H, g, cap, self, P, s_tok, counts,
+                 ctl);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_ep_return_p2p(const float *part, const int32_t *r_ids, int k, int H, int g, int cap, int self,
                                  const EpPeers &P, int *ctl, cudaStream_t st) {
     if (g <= 0 || g > EP_MAX_PEERS || cap <= 0 || self < 0 || self >= g || k > 32 || H % 4) return cudaErrorInvalidValue;
     const int64_t warps = (int64_t)g * cap;
-    ep_return_p2p_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(part, r_ids, k, H, g, cap, self, P, ctl);
-    return cudaGetLastError();
+    const cudaError_t e = launch_k(ep_return_p2p_kernel, (unsigned)((warps + 7) / 8), 256, 0, st, part, r_ids, k, H,
+                                   g, cap, self, P, ctl);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_ep_wait(int dir, int g, int self, const int *flags, int *ctl, int *err, cudaStream_t st) {
     if (g <= 0 || g > 32 || self < 0 || self >= g) return cudaErrorInvalidValue;
-    ep_wait_kernel<<<1, 32, 0, st>>>(dir, g, self, flags, ctl, err);
-    return cudaGetLastError();
+    const cudaError_t e = launch_k(ep_wait_kernel, 1, 32, 0, st, dir, g, self, flags, ctl, err);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_ep_pack(const int32_t *ids, const float *w, const float *x, int T, int k, int H, int per, int g,
@@ -307,8 +319,9 @@ cudaError_t launch_ep_combine(const float *ret, const float *part, int self, con
     if (T <= 0) return cudaSuccess;
     if (H % 4 || self < 0 || self >= g) return cudaErrorInvalidValue;
     const int64_t n4 = (int64_t)T * H / 4;
-    ep_combine_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(ret, part, self, row_of, T, H, g, cap, out);
-    return cudaGetLastError();
+    const cudaError_t e = launch_k(ep_combine_kernel, (unsigned)((n4 + 255) / 256), 256, 0, st, ret, part, self, row_of,
+                                   T, H, g, cap, out);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace tmoe

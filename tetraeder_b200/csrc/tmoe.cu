@@ -957,7 +957,9 @@ int tmoe_ep_a2a_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float
     const float *xn = use_norm ? h->xn : x;
     if (A.p2p) {
         // the exchange over peer memory: the messages written into the peers' buffers, a bounded
-        // wait for theirs, the experts, the partial rows written back, a bounded wait, the combine
+        // wait for theirs, the experts, the partial rows written back, a bounded wait, the combine;
+        // the kernels overlap their predecessors' tails (programmatic launch)
+        tmoe::PdlScope pdl(!h->prof.on);
         {
             PhaseMark pm(h, st, TMOE_PHASE_MAP_IDS);
             e = tmoe::launch_ep_dispatch_p2p(ids, w, xn, rc == TMOE_OK ? (int)T : 0, k, H, E / g, g, cap, rank,
