@@ -92,8 +92,11 @@ def test_dispatch_matches_group_pairs_routing():
     assert np.array_equal(host(perm)[: o[-1]], p)
 
 
-@pytest.mark.parametrize("T,E,k,neg", [(1, 128, 8, 0), (64, 128, 8, 30), (8192, 128, 8, 10), (4096, 64, 6, 50)])
+@pytest.mark.parametrize("T,E,k,neg", [(1, 128, 8, 0), (5, 16, 4, 20), (8, 128, 8, 30), (16, 64, 4, 10),
+                                       (64, 128, 8, 30), (8192, 128, 8, 10), (4096, 64, 6, 50)])
 def test_dispatch_bit_exact(T, E, k, neg):
+    """The dispatch against the oracle's stable sort: the ranking sort of up to 64 pairs (the first four
+    cases, 64 pairs exactly in the fourth), the one-CTA and the many-CTA sorts."""
     rng = np.random.default_rng(T + E)
     ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
     ids[rng.random(ids.shape) < neg / 100] = -1

@@ -123,12 +123,71 @@ __device__ void sort_pairs_cta(const int32_t *ids, int n_pairs, int n_slots, int
     }
 }
 
+// The same dispatch for a few pairs (n_pairs and n_slots at most NT, the CTA's threads), by
+// ranking instead of histograms: thread e counts expert e's pairs and the valid pairs of the
+// experts below it (its offset), and thread p puts pair p after them and after the earlier pairs
+// of its own expert -- the stable order of sort_pairs_cta.  sids: the ids in shared memory.
+// sh: n_slots + NT / 32 ints.
+constexpr int SMALL_SORT_PAIRS = 64;  // the batches of one token tile at top-8
+
+template <int NT>
+__device__ void sort_pairs_small(const int32_t *sids, int n_pairs, int n_slots, int32_t *__restrict__ counts,
+                                 int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
+                                 int4 *__restrict__ active, int32_t *__restrict__ n_active, int *counters,
+                                 int n_counters, int *err, int32_t *sh) {
+    int32_t *offs = sh;            // [n_slots]
+    int32_t *wtot = sh + n_slots;  // [NT / 32] experts with pairs, per warp
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (counters && tid < n_counters) counters[tid] = 0;  // work counters of the GEMVs
+    const int e = tid;
+    int c = 0, below = 0;
+    if (e < n_slots) {
+        for (int q = 0; q < n_pairs; q++) {
+            const int f = sids[q];
+            c += f == e;
+            below += f >= 0 && f < e;
+        }
+        counts[e] = c;
+        offsets[e] = below;
+        offs[e] = below;
+        if (e == n_slots - 1) offsets[n_slots] = below + c;
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, e < n_slots && c > 0);
+    if (lane == 0) wtot[warp] = __popc(m);
+    const bool bad = tid < n_pairs && sids[tid] >= n_slots;
+    if (__any_sync(0xffffffffu, bad) && lane == 0) latch_error(err, TMOE_DEV_ERR_BADID);
+    __syncthreads();
+    int base = 0, total = 0;
+    for (int w = 0; w < NT / 32; w++) {
+        base += w < warp ? wtot[w] : 0;
+        total += wtot[w];
+    }
+    if (e < n_slots && c > 0) active[base + __popc(m & ((1u << lane) - 1u))] = make_int4(e, below, below + c, 0);
+    if (tid == 0) n_active[0] = total;
+    if (tid < n_pairs) {
+        const int f = sids[tid];
+        if (f >= 0 && f < n_slots) {
+            int r = 0;
+            for (int q = 0; q < tid; q++) r += sids[q] == f;
+            perm[offs[f] + r] = tid;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(1024) sort_pairs_kernel(const int32_t *__restrict__ ids, int n_pairs, int n_slots,
                                                           int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
                                                           int32_t *__restrict__ perm, int4 *__restrict__ active,
                                                           int32_t *__restrict__ n_active, int *counters, int n_counters,
                                                           int *err) {
     extern __shared__ int32_t sh[];
+    if (n_pairs <= SMALL_SORT_PAIRS && n_slots <= SORT_WARPS * 32) {
+        int32_t *sid = sh;  // [n_pairs], then the ranking's scratch
+        if ((int)threadIdx.x < n_pairs) sid[threadIdx.x] = ids[threadIdx.x];
+        __syncthreads();
+        sort_pairs_small<SORT_WARPS * 32>(sid, n_pairs, n_slots, counts, offsets, perm, active, n_active, counters,
+                                          n_counters, err, sh + SMALL_SORT_PAIRS);
+        return;
+    }
     sort_pairs_cta<SORT_WARPS>(ids, n_pairs, n_slots, counts, offsets, perm, active, n_active, counters, n_counters,
                                err, sh);
 }
@@ -425,8 +484,12 @@ __global__ void __launch_bounds__(FR_WARPS * 32) route_fused_kernel(
         for (int i = threadIdx.x; i < n_pairs; i += blockDim.x) sid[i] = __ldcg(mapped + i);
         __syncthreads();
     }
-    sort_pairs_cta<FR_WARPS>(sid, n_pairs, n_slots, counts, offsets, perm, active, n_active, counters, n_counters,
-                             err, sid + ((n_pairs + 3) & ~3));
+    if (n_pairs <= SMALL_SORT_PAIRS && n_slots <= FR_WARPS * 32)
+        sort_pairs_small<FR_WARPS * 32>(sid, n_pairs, n_slots, counts, offsets, perm, active, n_active, counters,
+                                        n_counters, err, sid + ((n_pairs + 3) & ~3));
+    else
+        sort_pairs_cta<FR_WARPS>(sid, n_pairs, n_slots, counts, offsets, perm, active, n_active, counters,
+                                 n_counters, err, sid + ((n_pairs + 3) & ~3));
     if (threadIdx.x == 0 && gridDim.y > 1) done[gridDim.y] = 0;
 }
 

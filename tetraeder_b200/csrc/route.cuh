@@ -87,6 +87,13 @@ __device__ __forceinline__ void topk_token(const float *__restrict__ lg, int E, 
     // [0, 1], so their bit patterns order like the values; key = bits + 1 for a candidate, 0 for
     // a removed (or absent, or NaN) one.  Two warp reductions per round: the largest key, then
     // the smallest index holding it.
+    // The keys are computed once; taking a candidate sets its key to 0.
+    uint32_t key[MAXPER];
+#pragma unroll
+    for (int i = 0; i < MAXPER; i++) {
+        const int e = lane + 32 * i;
+        key[i] = (e < E && v[i] >= 0.0f) ? __float_as_uint(v[i]) + 1u : 0u;
+    }
     float sel_mine = 0.0f;
     int id_mine = -1;
     for (int j = 0; j < k; j++) {
@@ -94,11 +101,9 @@ __device__ __forceinline__ void topk_token(const float *__restrict__ lg, int E, 
         int bi = 0x7fffffff;
 #pragma unroll
         for (int i = 0; i < MAXPER; i++) {
-            const int e = lane + 32 * i;
-            const uint32_t key = (e < E && v[i] >= 0.0f) ? __float_as_uint(v[i]) + 1u : 0u;
-            if (key > bk) {  // e increases with i: an equal key keeps the lower index
-                bk = key;
-                bi = e;
+            if (key[i] > bk) {  // e increases with i: an equal key keeps the lower index
+                bk = key[i];
+                bi = lane + 32 * i;
             }
         }
         const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
@@ -106,7 +111,7 @@ __device__ __forceinline__ void topk_token(const float *__restrict__ lg, int E, 
         if ((mi & 31) == lane) {
 #pragma unroll
             for (int i = 0; i < MAXPER; i++)
-                if (lane + 32 * i == mi) v[i] = -1.0f;
+                if (lane + 32 * i == mi) key[i] = 0u;
         }
         if (lane == j) {
             sel_mine = __uint_as_float(mk - 1u);
