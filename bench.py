@@ -46,6 +46,12 @@ def log(msg):
 H, I, E, K_USED = 2048, 768, 128, 8
 Q4K, Q6K = 12, 14
 DOWN_T = Q6K                                                      # Q4_K_M promotes ffn_down to Q6_K
+PREPACK = True  # Q6_K down tensors repacked once at load by tmoe_prepack (TYPE_Q6_K_R8); --no-prepack
+
+
+def down_type_gpu():
+    """The down type the GPU arm's layers are created with (the packed type when --prepack)."""
+    return 270 if PREPACK and DOWN_T == Q6K else DOWN_T
 EXPERT_BYTES = 2 * I * (H // 256) * 144 + H * (I // 256) * 210  # 3,059,712
 GATE_UP_BYTES = 2 * I * (H // 256) * 144                          # 1,769,472
 DOWN_BYTES = H * (I // 256) * 210                                 # 1,290,240
@@ -94,6 +100,10 @@ def parse():
                    help="streamed mode: also write the routing of --steps steps as a tetraeder-routing v1 trace")
     p.add_argument("--shape", choices=["c2", "235b"], default="c2",
                    help="c2: the Qwen3-30B-A3B layer (the metric's config); 235b: config 4's layer shape")
+    p.add_argument("--no-prepack", dest="prepack", action="store_false",
+                   help="keep the Q6_K down tensors in ggml's layout (default: repacked once at load with "
+                        "tmoe_prepack, the optional explicit repack of the boundary; the products are bit for bit "
+                        "those of the ggml layout, and a one-GPU decode line also times the ggml layout)")
     p.add_argument("--no-c4", action="store_true",
                    help="decode mode: skip the config-4 line (the 235B-shaped layer, expert-parallel over the ranks "
                         "at N > 1) added to the C2 line")
@@ -101,6 +111,8 @@ def parse():
                    help="N > 1: a2a = each rank its own --tokens, dispatched to the experts' ranks (all-to-all); "
                         "allreduce = the reference's EP mode, the same tokens on every rank, outputs summed")
     a = p.parse_args()
+    global PREPACK
+    PREPACK = a.prepack and a.mode == "decode"  # the large-batch modes keep ggml's layout
     set_shape(a.shape)
     if a.mode in ("prefill", "streamed") and a.tokens == 64:
         a.tokens = 8192
@@ -122,9 +134,13 @@ def workload(args, n_gpus):
     name = {"decode": "C2 Qwen3-30B-A3B MoE layer, decode",
             "prefill": "C2-shaped Qwen3-30B-A3B MoE layer, prefill (north-star tensor target)",
             "streamed": "C5 skewed large-batch stress, 64 of 128 experts in device slots"}[args.mode]
+    types = "gate/up Q4_K, down Q6_K (this repo's quantiser)"
+    if down_type_gpu() != DOWN_T:
+        types += ("; down repacked once at load by tmoe_prepack (Q6_K_R8, 8-row fragment order, outside the timed "
+                  "region)")
     return {"workload": name, "tokens_per_layer_call": args.tokens,
             "n_embd": H, "n_ff": I, "n_expert": E, "n_expert_used": K_USED,
-            "types": "gate/up Q4_K, down Q6_K (this repo's quantiser)", "layers_per_step": args.layers,
+            "types": types, "layers_per_step": args.layers,
             "l2": f"inputs larger than L2: {args.layers} distinct resident layers rotated each step",
             "parallelism": f"replicas x{n_gpus}" if n_gpus > 1 else "single GPU", "seed": args.seed}
 
@@ -182,9 +198,10 @@ class Clocks:
 
 
 # ---------------------------------------------------------------------------------------- ours
-def make_layers(torch, moe, n_layers, seed, device, world=1, rank=0):
+def make_layers(torch, moe, n_layers, seed, device, world=1, rank=0, ggml_down=None):
     """n_layers C2 layers.  With world > 1 (expert parallelism) every rank draws the same router
-    (the routing is replicated) and holds only its contiguous share of each layer's experts."""
+    (the routing is replicated) and holds only its contiguous share of each layer's experts.  When
+    the down tensors are repacked, ggml_down (a list) receives the ggml-layout originals."""
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     ge = torch.Generator(device=device)
@@ -196,6 +213,10 @@ def make_layers(torch, moe, n_layers, seed, device, world=1, rank=0):
         gate = moe.quantize(Q4K, torch.randn((per, I, H), generator=ge, device=device) * 0.02)
         up = moe.quantize(Q4K, torch.randn((per, I, H), generator=ge, device=device) * 0.02)
         down = moe.quantize(DOWN_T, torch.randn((per, H, I), generator=ge, device=device) * 0.02)
+        if down_type_gpu() != DOWN_T:
+            if ggml_down is not None:
+                ggml_down.append(down)
+            down = moe.prepack(down)
         layers.append((rw, moe.ExpertWeights(gate, up, down)))
     torch.cuda.synchronize()
     return layers
@@ -215,7 +236,9 @@ def run_ours(args, rank, world, local_rank):
     a2a = ep and args.ep == "a2a"
     # N = 1: the layer on one GPU.  N > 1: the reference's EP mode, experts split contiguously over
     # the ranks, the same tokens on every rank, partial outputs summed with NCCL (strong scaling)
-    layers = make_layers(torch, moe, L, args.seed, dev, world, rank)
+    # one GPU, decode, repacked down tensors: the ggml layout is timed too (key "ggml_layout")
+    ggml_down = [] if world == 1 and args.mode == "decode" and down_type_gpu() != DOWN_T else None
+    layers = make_layers(torch, moe, L, args.seed, dev, world, rank, ggml_down)
     log(f"{L} layers generated ({E // world} experts each on this rank)")
     gen = torch.Generator(device=dev)
     gen.manual_seed(args.seed + 1 + (rank if a2a else 0))  # a2a: every rank has tokens of its own
@@ -224,7 +247,7 @@ def run_ours(args, rank, world, local_rank):
     x_host = torch.randn((L, T, H), generator=torch.Generator().manual_seed(args.seed + 2)).pin_memory()
     out_host = torch.empty((L, T, H), dtype=torch.float32).pin_memory()
     x_call = [torch.empty((T, H), device=dev) for _ in range(L)]
-    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=DOWN_T,
+    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=down_type_gpu(),
                         max_tokens=world * T if a2a else T, device=local_rank)
     outs = [torch.empty((T, H), device=dev) for _ in range(L)]
     ids = [torch.empty((T, K_USED), dtype=torch.int32, device=dev) for _ in range(L)]
@@ -331,6 +354,41 @@ def run_ours(args, rank, world, local_rank):
 
     e2e_ms = timed(e2e_step, args.steps, max(args.warmup, 3))
     e2e_value = units / (e2e_ms / 1e3)
+
+    ggml_line = None
+    if ggml_down:
+        # the same step over the down tensors in ggml's Q6_K layout (no repack): its own handle and
+        # graph; the outputs of the two layouts are compared bit for bit
+        graph.replay()
+        torch.cuda.synchronize()
+        want = [o.clone() for o in outs]
+        layer_g = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=DOWN_T, max_tokens=T,
+                              device=local_rank)
+        layers_g = [(rw, moe.ExpertWeights(w.gate, w.up, d)) for (rw, w), d in zip(layers, ggml_down)]
+
+        def step_g():
+            for li in range(L):
+                rw, wts = layers_g[li]
+                layer_g.moe_ffn(x_dev, wts, router_w=rw, out=outs[li], ids_out=ids[li], w_out=ws[li])
+
+        step_g()
+        layer_g.check()
+        same = all(torch.equal(a.view(torch.int32), b.view(torch.int32)) for a, b in zip(outs, want))
+        graph_g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            step_g()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph_g, stream=s):
+                step_g()
+        torch.cuda.synchronize()
+        ms_g = timed(graph_g.replay, args.steps, max(args.warmup, 3))
+        layer_g.check()
+        ggml_line = {"value": round(units / (ms_g / 1e3), 1), "unit": "tokens/s",
+                     "ms_per_step": round(ms_g / args.steps, 4), "outputs_bitwise_equal": same,
+                     "note": "the same step with the down tensors in ggml's Q6_K layout (no tmoe_prepack)"}
+        log(f"ggml layout: {ms_g / args.steps:.3f} ms/step, outputs equal: {same}")
+        del graph_g, layers_g, want
+        layer_g.close()
     log(f"e2e timed: {e2e_ms / args.steps:.3f} ms/step")
 
     # distinct experts per layer (the D of the roofline bytes); a2a: over every rank's tokens
@@ -418,6 +476,8 @@ def run_ours(args, rank, world, local_rank):
                         "and D2H output, copies pipelined with the calls on two copy streams"},
         "gpu_launches": int(launches_per_call * L * args.steps), "clocks": clocks,
     }
+    if ggml_line:
+        result["ggml_layout"] = ggml_line
     if a2a:
         result["config"]["parallelism"] = (f"ep{world} all-to-all (experts split contiguously, {T} tokens per rank "
                                            "dispatched to the experts' ranks and combined back; the messages are "
@@ -509,7 +569,7 @@ def run_streamed(args, local_rank):
         replay = [torch.from_numpy(r.logits(E)).to(dev) for r in steps]
     x = torch.randn((T, H), generator=gen, device=dev)
     lg = replay[0] if replay else torch.randn((T, E), generator=gen, device=dev) + bias.to(dev)
-    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=DOWN_T,
+    layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=down_type_gpu(),
                         max_tokens=T, device=local_rank)
     cache = tb.SlotCache(layer, slots, store)
     cache.make_resident([int(e) for e in perm[:NS]])
@@ -830,7 +890,7 @@ def sweep_tokens(torch, tb, layers, dev):
     res = {}
     for T in (1, 4, 16, 64):
         log(f"sweep T={T}")
-        layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=DOWN_T, max_tokens=T,
+        layer = tb.MoeLayer(H, I, E, K_USED, gate_type=Q4K, up_type=Q4K, down_type=down_type_gpu(), max_tokens=T,
                             device=dev.index)
         x = torch.randn((T, H), device=dev)
         out = torch.empty((T, H), device=dev)

@@ -21,7 +21,7 @@ use std::ffi::{c_void, CStr, CString};
 use std::marker::PhantomData;
 use std::ptr;
 
-pub use raw::{tmoe_config, tmoe_expert_tensors, TMOE_TYPE_Q4_K, TMOE_TYPE_Q6_K};
+pub use raw::{tmoe_config, tmoe_expert_tensors, TMOE_TYPE_Q4_K, TMOE_TYPE_Q6_K, TMOE_TYPE_Q6_K_R8};
 
 /// A failed call: the negative `TMOE_E_*` code and the library's message.
 #[derive(Debug, thiserror::Error)]
@@ -46,6 +46,20 @@ fn check(h: *const raw::tmoe_handle, rc: i32) -> Result<(), TmoeError> {
         return Ok(());
     }
     Err(TmoeError { code: rc, msg: message(unsafe { raw::tmoe_last_error(h) }) })
+}
+
+/// The optional, explicit repack of Q6_K expert matrices into `TMOE_TYPE_Q6_K_R8` (the upload
+/// path calls it once per tensor when it opts in; nothing repacks implicitly, as in ADR 0039).
+/// `n_mats` matrices of `n_rows` x `k`, rows `nb1` and matrices `nb2` bytes apart, into `dst`.
+///
+/// # Safety
+/// `src` and `dst` are device pointers of the sizes the header states, not overlapping, valid until
+/// the stream has passed the call.
+#[allow(clippy::too_many_arguments)]
+pub unsafe fn prepack_q6k(src: *const u8, nb1: usize, nb2: usize, n_rows: i64, k: i64, n_mats: i64, dst: *mut u8,
+                          stream: Stream) -> Result<(), TmoeError> {
+    check(ptr::null(), raw::tmoe_prepack(raw::TMOE_TYPE_Q6_K, src.cast(), nb1, nb2, n_rows, k, n_mats, dst.cast(),
+                                         stream))
 }
 
 /// One handle: the layer's shape and types and a workspace for `max_tokens`, on one device.

@@ -15,6 +15,7 @@ pub const TMOE_E_COMM: c_int = -6;
 pub const TMOE_E_NOTFOUND: c_int = -7;
 pub const TMOE_TYPE_Q4_K: c_int = 12;
 pub const TMOE_TYPE_Q6_K: c_int = 14;
+pub const TMOE_TYPE_Q6_K_R8: c_int = 270;
 pub const TMOE_COMM_ID_BYTES: c_int = 128;
 pub const TMOE_GGUF_U64: c_int = 0;
 pub const TMOE_GGUF_I64: c_int = 1;
@@ -313,6 +314,17 @@ extern "C" {
         stream: *mut c_void,
     ) -> c_int;
     pub fn tmoe_dequantize(ty: i32, r#in: *const c_void, n: i64, out: *mut f32, stream: *mut c_void) -> c_int;
+    pub fn tmoe_prepack(
+        ty: i32,
+        src: *const c_void,
+        nb1: usize,
+        nb2: usize,
+        n_rows: i64,
+        K: i64,
+        n_mats: i64,
+        dst: *mut c_void,
+        stream: *mut c_void,
+    ) -> c_int;
     pub fn tmoe_mul_mat(
         h: *mut tmoe_handle,
         stream: *mut c_void,

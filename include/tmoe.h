@@ -70,6 +70,10 @@ extern "C" {
 
 #define TMOE_TYPE_Q4_K 12
 #define TMOE_TYPE_Q6_K 14
+/* Q6_K in this library's 8-row fragment order, made from Q6_K matrices by tmoe_prepack (not a
+ * ggml type; the value is outside ggml's range).  Accepted for the expert tensors (tmoe_config's
+ * types, tmoe_mul_mat_id); its row size, nb1 and nb2 are those of the ggml matrix it was made from. */
+#define TMOE_TYPE_Q6_K_R8 270
 
 typedef struct tmoe_handle tmoe_handle;
 
@@ -120,7 +124,7 @@ TMOE_API int tmoe_check(tmoe_handle *h, void *stream);
 TMOE_API int tmoe_wait_flag(tmoe_handle *h, void *stream, const int32_t *flag, int32_t value, int64_t limit_ns);
 
 /* ggml mul_mat_id: out[t][j][:] = W[ids[t][j]] . b[t][b1 == 1 ? 0 : j][:]  (f32 [T][n_used][N]).
- * W: [K, N, n_w] of `type` (Q4_K or Q6_K, K % 256 == 0) with strides nb1/nb2;
+ * W: [K, N, n_w] of `type` (Q4_K, Q6_K or Q6_K_R8, K % 256 == 0) with strides nb1/nb2;
  * b: f32 [T][b1][K], b1 == 1 or n_used; activations go through Q8_K as on ggml's CPU path.
  * Its scratch is the handle's, allocated by tmoe_create for T * b1 and T * n_used up to
  * max_tokens * n_expert_used and K up to max(n_embd, n_ff); a call beyond that returns
@@ -292,6 +296,17 @@ TMOE_API int tmoe_quantize(int32_t type, const float *x, int64_t nrows, int64_t 
                            void *stream);
 /* quant::to_f32 (crates/ggml-sys/src/quant.rs:19) for Q4_K / Q6_K: n values (n % 256 == 0). */
 TMOE_API int tmoe_dequantize(int32_t type, const void *in, int64_t n, float *out, void *stream);
+
+/* The optional, explicit repack that the boundary allows (weights are never repacked implicitly;
+ * the reference keeps expert weights unrepacked, docs/adr/0039): n_mats Q6_K matrices of n_rows
+ * rows (n_rows % 8 == 0) and K columns (K % 256 == 0), rows nb1 bytes apart and matrices nb2 apart,
+ * are written to dst (16-byte aligned, n_mats * n_rows * row size bytes, not overlapping src) as
+ * TMOE_TYPE_Q6_K_R8: per matrix, n_rows / 8 row groups of K / 256 units of 1680 bytes, the same
+ * bytes rearranged so that the expert GEMV reads them with aligned, conflict-free vector loads and
+ * fills one super-block at a time.  The results of every product are bit for bit those of the Q6_K
+ * matrix it came from.  type must be TMOE_TYPE_Q6_K.  Stream-ordered; errors: tmoe_last_error(NULL). */
+TMOE_API int tmoe_prepack(int32_t type, const void *src, size_t nb1, size_t nb2, int64_t n_rows, int64_t K,
+                          int64_t n_mats, void *dst, void *stream);
 
 /* The decode step around the MoE layer (config 3: the full Qwen3-MoE model, attention() of
  * crates/model/src/attn.rs:246-405 and build_step of qwen3moe.rs:2777-2870), as stream-ordered

@@ -116,3 +116,24 @@ def maxabs_over_rms(got: np.ndarray, want: np.ndarray) -> float:
 
 # The north-star output tolerance: normalised RMS error <= 1e-2 and max-abs <= 5e-2 x output RMS.
 NORTH_NRMS, NORTH_MAXABS = 1e-2, 5e-2
+
+
+def q6r_pack(W: np.ndarray) -> np.ndarray:
+    """Q6_K matrices uint8 [n, rows, nb * 210] in the 8-row fragment order of tmoe_prepack, restated
+    from the layout's description with numpy reshapes: per 8-row group and super-block a unit of 1680
+    bytes; half h of the block holds the ql bytes 64h + 16i + 4t4 + j of row g at 768h + 16(4g + t4)
+    + 4i + j and the qh bytes 128 + 32h + 16i + 4t4 + j at 768h + 512 + 8(4g + t4) + 4i + j; then the
+    rows' 16 scale bytes (1536 + 16g) and their d (1664 + 2g)."""
+    n, rows, rb = W.shape
+    nb = rb // 210
+    blk = W.reshape(n, rows // 8, 8, nb, 210).transpose(0, 1, 3, 2, 4)  # [n, group, block, g, 210]
+    lead = blk.shape[:3]
+    unit = np.empty(lead + (1680,), np.uint8)
+    for h in range(2):
+        ql = blk[..., 64 * h:64 * h + 64].reshape(lead + (8, 4, 4, 4))  # g, i, t4, j
+        unit[..., 768 * h:768 * h + 512] = ql.transpose(0, 1, 2, 3, 5, 4, 6).reshape(lead + (512,))
+        qh = blk[..., 128 + 32 * h:160 + 32 * h].reshape(lead + (8, 2, 4, 4))  # g, i, t4, j
+        unit[..., 768 * h + 512:768 * h + 768] = qh.transpose(0, 1, 2, 3, 5, 4, 6).reshape(lead + (256,))
+    unit[..., 1536:1664] = blk[..., 192:208].reshape(lead + (128,))
+    unit[..., 1664:1680] = blk[..., 208:210].reshape(lead + (16,))
+    return np.ascontiguousarray(unit).reshape(n, rows, rb)

@@ -15,6 +15,7 @@ ERRORS = {-1: "TMOE_E_INVALID", -2: "TMOE_E_CUDA", -3: "TMOE_E_NOMEM", -4: "TMOE
           -5: "TMOE_E_DEVICE", -6: "TMOE_E_COMM", -7: "TMOE_E_NOTFOUND"}
 TMOE_E_INVALID, TMOE_E_UNSUPPORTED, TMOE_E_NOTFOUND = -1, -4, -7
 TYPE_Q4_K, TYPE_Q6_K = 12, 14
+TYPE_Q6_K_R8 = 270  # Q6_K in 8-row fragment order (tmoe_prepack)
 
 
 class TmoeError(RuntimeError):
@@ -59,6 +60,7 @@ SIGNATURES = {
     "tmoe_dispatch": ([P, P, P, I64, I32, P, P, P], C.c_int),
     "tmoe_quantize": ([I32, P, I64, I64, P, P], C.c_int),
     "tmoe_dequantize": ([I32, P, I64, P, P], C.c_int),
+    "tmoe_prepack": ([I32, P, C.c_size_t, C.c_size_t, I64, I64, I64, P, P], C.c_int),
     "tmoe_profile_enable": ([P, I32], C.c_int),
     "tmoe_profile_collect": ([P, P, P], C.c_int),
     "tmoe_comm_unique_id": ([P], C.c_int),

@@ -8,6 +8,29 @@
 #define TMOE_Q4K_BYTES 144
 #define TMOE_Q6K_BYTES 210
 
+// Q6_K in 8-row fragment order (made by tmoe_prepack): a matrix of N rows is N/8 row groups, each
+// K/256 units of 1680 bytes, one per super-block, holding the same 8 x 210 bytes as ggml's rows
+// rearranged for a warp's m16n8k16 fragments.  Row g (0..7) of the group, half h (0, 1) of the
+// super-block, lane L = 4 g + t4:
+//   768 h + 16 L        ql bytes 64 h + 16 i + 4 t4 .. +3 for i = 0..3 (16 bytes: one 128-bit load)
+//   768 h + 512 + 8 L   qh bytes 128 + 32 h + 16 i + 4 t4 .. +3 for i = 0, 1 (8 bytes)
+//   1536 + 16 g         the row's 16 scale bytes (ggml bytes 192..207)
+//   1664 + 2 g          the row's d (ggml bytes 208, 209)
+#define TMOE_Q6R_UNIT 1680
+
+namespace tmoe {
+// Where byte `off` (0..209) of row g's ggml super-block lands in its 8-row unit.
+__host__ __device__ __forceinline__ int q6r_offset(int g, int off) {
+    if (off < 128) return 768 * (off >> 6) + 16 * (4 * g + ((off >> 2) & 3)) + 4 * ((off >> 4) & 3) + (off & 3);
+    if (off < 192) {
+        const int o = off - 128;
+        return 768 * (o >> 5) + 512 + 8 * (4 * g + ((o >> 2) & 3)) + 4 * ((o >> 4) & 1) + (o & 3);
+    }
+    if (off < 208) return 1536 + 16 * g + (off - 192);
+    return 1664 + 2 * g + (off - 208);
+}
+}  // namespace tmoe
+
 // Device error codes latched in tmoe_handle's flag word (first error wins).
 #define TMOE_DEV_ERR_TIMEOUT 1
 #define TMOE_DEV_ERR_BADID 2

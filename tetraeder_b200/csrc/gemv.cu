@@ -19,7 +19,9 @@
 //  - Q4_K: a chunk of super-blocks, one 3D tiled TMA copy per matrix (tensor map over
 //    [expert][row][row bytes as u32]);
 //  - Q6_K: all of K, one 1D bulk copy per matrix (16 consecutive rows are contiguous and a
-//    multiple of 16 bytes; a chunk of one row is not even 4-byte aligned).
+//    multiple of 16 bytes; a chunk of one row is not even 4-byte aligned);
+//  - Q6_K in 8-row fragment order (tmoe_prepack): all of K, one 1D bulk copy per 8-row group, read
+//    with aligned vector loads free of bank conflicts (C2 T = 64: down 50.4 us against 54.3).
 // gate/up items take rows r..r+7 of gate as MMA rows 0-7 and the same rows of up as MMA rows
 // 8-15, so silu(g) * u (swiglu_split) is formed in the thread that holds both.
 // Tokens: up to 16 per pass (two 8-token MMA groups); an expert with more tokens runs more
@@ -96,7 +98,7 @@ __device__ __forceinline__ int sbyte(uint32_t w, int i) {
 __device__ __forceinline__ int fast_div(int n, uint64_t m) { return (int)(((uint64_t)(uint32_t)n * m) >> 40); }
 
 __device__ __forceinline__ uint2 ldg64(const void *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
-__device__ __forceinline__ uint32_t ldg32(const void *p) { return __ldg(reinterpret_cast<const uint32_t *>(p)); }
+__device__ __forceinline__ uint4 ldg128(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
 
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *m, int x, int y, int z, uint64_t *bar) {
     asm volatile(
@@ -116,7 +118,8 @@ struct TokCols {
 
 // The same group's activation data as this thread's base pointers, set once per pass (super-block
 // kb then sits at a fixed stride from each): the B-operand row of column g at the thread's k
-// offset, that row's sub-block sum words (2 per super-block for Q4_K, 4 for Q6_K, the thread's
+// offset (Q6_K rows are stored in fragment order, q8_frag_pos: the thread's 64 bytes of each
+// block), that row's sub-block sum words (2 per super-block for Q4_K, 4 for Q6_K, the thread's
 // one), and the super-block scales of columns 2*t4 and 2*t4+1.
 struct XBase {
     const int8_t *q;
@@ -130,7 +133,7 @@ __device__ __forceinline__ XBase x_base(const GemvArgs &a, const TokCols &c, int
     constexpr int NBW = WT == TMOE_WT_Q4K ? 2 : 4;
     const int64_t sw = (int64_t)c.xg * nb * NBW + (WT == TMOE_WT_Q4K ? (t4 & 1) : t4);
     XBase p;
-    p.q = a.xq + (int64_t)c.xg * a.K + (WT == TMOE_WT_Q4K ? 8 : 4) * t4;
+    p.q = a.xq + (int64_t)c.xg * a.K + (WT == TMOE_WT_Q4K ? 8 : 64) * t4;
     p.bl = a.xbl + sw;
     p.bh = a.xbh + sw;
     p.d0 = a.xd + (int64_t)c.x0 * nb;
@@ -141,8 +144,8 @@ __device__ __forceinline__ XBase x_base(const GemvArgs &a, const TokCols &c, int
 // ------------------------------------------------------------------ Q4_K
 // Per super-block and 8-token group: a thread's B operands.  Inside a sub-block the k order is
 // permuted identically for both operands (thread t4 holds elements 8*t4 .. 8*t4+7 of the 32),
-// so each operand is one 8-byte load, and one load of the nibble bytes serves sub-blocks 2j
-// (low nibbles) and 2j+1 (high nibbles).
+// so each weight operand is one 8-byte load, and one load of the nibble bytes serves sub-blocks
+// 2j (low nibbles) and 2j+1 (high nibbles).
 struct XQ4 {
     uint2 l[4], h[4];
     uint32_t bl, bh;
@@ -293,9 +296,12 @@ struct XQ6 {
 
 __device__ __forceinline__ void load_xq6(const GemvArgs &a, const TokCols &c, int kb, int nb, XQ6 &o) {
     const int t4 = threadIdx.x & 3;
-    const int8_t *q = a.xq + (int64_t)c.xg * a.K + TMOE_QK * kb + 4 * t4;
+    const int8_t *q = a.xq + (int64_t)c.xg * a.K + TMOE_QK * kb + 64 * t4;
 #pragma unroll
-    for (int s = 0; s < 16; s++) o.w[s] = ldg32(q + 16 * s);
+    for (int i = 0; i < 4; i++) {
+        const uint4 v = ldg128(q + 16 * i);
+        o.w[4 * i] = v.x, o.w[4 * i + 1] = v.y, o.w[4 * i + 2] = v.z, o.w[4 * i + 3] = v.w;
+    }
     const int64_t w = ((int64_t)c.xg * nb + kb) * 4 + t4;
     o.bl = __ldg(a.xbl + w);
     o.bh = __ldg(a.xbh + w);
@@ -306,7 +312,10 @@ __device__ __forceinline__ void load_xq6(const GemvArgs &a, const TokCols &c, in
 __device__ __forceinline__ void load_xq6(const XBase &p, int kb, XQ6 &o) {
     const int8_t *q = p.q + TMOE_QK * kb;
 #pragma unroll
-    for (int s = 0; s < 16; s++) o.w[s] = ldg32(q + 16 * s);
+    for (int i = 0; i < 4; i++) {
+        const uint4 v = ldg128(q + 16 * i);
+        o.w[4 * i] = v.x, o.w[4 * i + 1] = v.y, o.w[4 * i + 2] = v.z, o.w[4 * i + 3] = v.w;
+    }
     o.bl = __ldg(p.bl + 4 * kb);
     o.bh = __ldg(p.bh + 4 * kb);
     o.d0 = __ldg(p.d0 + kb);
@@ -382,6 +391,64 @@ __device__ __forceinline__ void q6_block(const uint8_t *ba, const uint8_t *bb, c
     const uint32_t wa = ld32<MA>(ba + 192 + 4 * t4), wb = ld32<MB>(bb + 192 + 4 * t4);
     const float fa = h2f(*reinterpret_cast<const uint16_t *>(ba + 208));
     const float fb = h2f(*reinterpret_cast<const uint16_t *>(bb + 208));
+#pragma unroll
+    for (int G = 0; G < NGR; G++) {
+        int cl[4], ch[4];
+        mma_k16_s8u8(cl, wa, wb, x[G].bl);
+        mma_k16_s8s8(ch, wa, wb, x[G].bh);
+        const float dd[4] = {fa * x[G].d0, fa * x[G].d1, fb * x[G].d0, fb * x[G].d1};
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[G][i] += __fmul_rn(dd[i], (float)(isum[G][i] - 32 * (cl[i] + 64 * ch[i])));
+    }
+}
+
+// The same super-block product from two 8-row units of the fragment-ordered layout (TMOE_Q6R_UNIT):
+// MMA rows g from unit ua, g+8 from unit ub.  Every word is aligned and each load is one vector
+// access over consecutive lanes (no bank conflicts): per half and unit a 128-bit ql load, a 64-bit
+// qh load and a 64-bit load of the half's 8 scales (the same address across a quad).
+__device__ __forceinline__ void q6r_load_half(const uint8_t *u, int h, int lane, Q6Half &q) {
+    const uint4 l = *reinterpret_cast<const uint4 *>(u + 768 * h + 16 * lane);
+    const uint2 hb = *reinterpret_cast<const uint2 *>(u + 768 * h + 512 + 8 * lane);
+    const uint2 sc = *reinterpret_cast<const uint2 *>(u + 1536 + 16 * (lane >> 2) + 8 * h);
+    q.ql[0] = l.x, q.ql[1] = l.y, q.ql[2] = l.z, q.ql[3] = l.w;
+    q.qh[0] = hb.x, q.qh[1] = hb.y;
+    q.sc[0] = sc.x, q.sc[1] = sc.y;
+}
+
+template <int NGR>
+__device__ __forceinline__ void q6r_block(const uint8_t *ua, const uint8_t *ub, const XQ6 (&x)[NGR],
+                                          float (*acc)[4]) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+    int isum[NGR][4];
+#pragma unroll
+    for (int G = 0; G < NGR; G++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) isum[G][i] = 0;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        Q6Half qa, qb;
+        q6r_load_half(ua, h, lane, qa);
+        q6r_load_half(ub, h, lane, qb);
+#pragma unroll
+        for (int sl8 = 0; sl8 < 8; sl8++) {
+            const uint32_t va = q6_vals(qa, sl8), vb = q6_vals(qb, sl8);
+            const int ca = sbyte(qa.sc[sl8 >> 2], sl8 & 3), cb = sbyte(qb.sc[sl8 >> 2], sl8 & 3);
+#pragma unroll
+            for (int G = 0; G < NGR; G++) {
+                int d[4];
+                mma_k16_u8s8(d, va, vb, x[G].w[8 * h + sl8]);
+                isum[G][0] += ca * d[0];
+                isum[G][1] += ca * d[1];
+                isum[G][2] += cb * d[2];
+                isum[G][3] += cb * d[3];
+            }
+        }
+    }
+    // scale word t4 of each row: the scales of sub-blocks 4*t4 .. 4*t4+3
+    const uint32_t wa = *reinterpret_cast<const uint32_t *>(ua + 1536 + 16 * g + 4 * t4);
+    const uint32_t wb = *reinterpret_cast<const uint32_t *>(ub + 1536 + 16 * g + 4 * t4);
+    const float fa = h2f(*reinterpret_cast<const uint16_t *>(ua + 1664 + 2 * g));
+    const float fb = h2f(*reinterpret_cast<const uint16_t *>(ub + 1664 + 2 * g));
 #pragma unroll
     for (int G = 0; G < NGR; G++) {
         int cl[4], ch[4];
@@ -539,7 +606,11 @@ __device__ __forceinline__ void fill(const GemvArgs &a, const GemvMaps &tm, Feed
             rec->item = -1;
             mbar_arrive_expect_tx(bar, 0u);
         } else {
-            uint32_t tx = WT == TMOE_WT_Q4K ? 16u * (uint32_t)a.chunk_blocks * TMOE_Q4K_BYTES : 16u * (uint32_t)a.nb1_0;
+            const int nb = a.K / TMOE_QK, kb0 = f.chunk * a.chunk_blocks;
+            const uint32_t r_bytes = (uint32_t)min(a.chunk_blocks, nb - kb0) * TMOE_Q6R_UNIT;  // Q6KR: per 8-row group
+            uint32_t tx = WT == TMOE_WT_Q4K    ? 16u * (uint32_t)a.chunk_blocks * TMOE_Q4K_BYTES
+                          : WT == TMOE_WT_Q6KR ? 2u * r_bytes
+                                               : 16u * (uint32_t)a.nb1_0;
             uintptr_t ps = 0;
             uint32_t pbytes = 0;
             int poff = 0;
@@ -561,6 +632,19 @@ __device__ __forceinline__ void fill(const GemvArgs &a, const GemvMaps &tm, Feed
                     tma_load_3d(slot + 8 * a.chunk_blocks * TMOE_Q4K_BYTES, &tm.m[1], x, f.tile * 8, f.e, bar);
                 } else {
                     tma_load_3d(slot, &tm.m[0], x, f.tile * 16, f.e, bar);
+                }
+            } else if constexpr (WT == TMOE_WT_Q6KR) {
+                // gate/up: 8-row group `tile` of each matrix; down: groups 2 tile and 2 tile + 1.  The
+                // second copy lands a full chunk after the first (compute indexes by chunk_blocks).
+                const size_t gs = (size_t)nb * TMOE_Q6R_UNIT, k0 = (size_t)kb0 * TMOE_Q6R_UNIT;
+                uint8_t *slot_b = slot + (size_t)a.chunk_blocks * TMOE_Q6R_UNIT;
+                if constexpr (GATEUP) {
+                    bulk_g2s(slot, a.w0 + (size_t)f.e * a.nb2_0 + (size_t)f.tile * gs + k0, r_bytes, bar);
+                    bulk_g2s(slot_b, a.w1 + (size_t)f.e * a.nb2_1 + (size_t)f.tile * gs + k0, r_bytes, bar);
+                } else {
+                    const uint8_t *src = a.w0 + (size_t)f.e * a.nb2_0 + (size_t)(2 * f.tile) * gs + k0;
+                    bulk_g2s(slot, src, r_bytes, bar);
+                    bulk_g2s(slot_b, src + gs, r_bytes, bar);
                 }
             } else {
                 const uint32_t rb = (uint32_t)a.nb1_0;
@@ -713,7 +797,26 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
             for (int G = 0; G < NG; G++) acc[G][0] = acc[G][1] = acc[G][2] = acc[G][3] = 0.0f;
         }
         const int S = a.row_stride;
-        if constexpr (NG == 1) {
+        if constexpr (WT == TMOE_WT_Q6KR) {  // MMA rows g: unit a's row g, g+8: unit b's row g
+            const uint8_t *ua = sl, *ub = sl + (size_t)a.chunk_blocks * TMOE_Q6R_UNIT;
+            for (int bi = 0; bi < nblk; bi++) {
+                const int kb = b0 + bi;
+                if constexpr (NG == 1) {
+                    XQ6 x[1];
+                    load_xq6(xb0, kb, x[0]);
+                    q6r_block<1>(ua + bi * TMOE_Q6R_UNIT, ub + bi * TMOE_Q6R_UNIT, x, acc);
+                } else if (ng == 1) {
+                    XQ6 x[1];
+                    load_xq6(a, tc[0], kb, nb, x[0]);
+                    q6r_block<1>(ua + bi * TMOE_Q6R_UNIT, ub + bi * TMOE_Q6R_UNIT, x, acc);
+                } else {
+                    XQ6 x[2];
+                    load_xq6(a, tc[0], kb, nb, x[0]);
+                    load_xq6(a, tc[NG - 1], kb, nb, x[1]);
+                    q6r_block<2>(ua + bi * TMOE_Q6R_UNIT, ub + bi * TMOE_Q6R_UNIT, x, acc);
+                }
+            }
+        } else if constexpr (NG == 1) {
             if constexpr (WT == TMOE_WT_Q4K) {
                 const uint8_t *ra = sl + (size_t)g * S, *rb = sl + (size_t)(g + 8) * S;
                 const bool lo = t4 < 2;
@@ -809,7 +912,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB)
             int row_a, row_b;
             if constexpr (GATEUP) {
                 row_a = row_b = tile * 8 + g;
-            } else if constexpr (WT == TMOE_WT_Q4K) {
+            } else if constexpr (WT != TMOE_WT_Q6K) {
                 row_a = tile * 16 + g;
                 row_b = row_a + 8;
             } else {
@@ -852,12 +955,15 @@ struct GemvPlan {
 // was slower (C2 decode T = 64: gate/up 61.7 us against 60.5, the layer 129.7 against 126.4 us),
 // the 36 KB it takes per CTA being worth more as L1 for the activation rows.  Q6_K: all of K; two
 // CTAs per SM if a slot per warp fits, else one (one CTA with two slots per warp: down 71.6 us
-// against 56.7 with two CTAs of one slot).
+// against 56.7 with two CTAs of one slot).  The same for Q6_K in 8-row fragment order (fills of
+// one super-block into three slots per warp were slower: C2 T = 64 down 55.6 us against 50.4).
 template <int WT>
 static GemvPlan plan_for(int K) {
     const int nb = K / TMOE_QK;
     const int cb = WT == TMOE_WT_Q4K ? (nb >= 2 ? 2 : 1) : nb;
-    const int slot = (WT == TMOE_WT_Q4K ? ITEM_ROWS * TMOE_Q4K_BYTES * cb : ITEM_ROWS * TMOE_Q6K_BYTES * nb + 16) +
+    const int slot = (WT == TMOE_WT_Q4K    ? ITEM_ROWS * TMOE_Q4K_BYTES * cb
+                      : WT == TMOE_WT_Q6KR ? 2 * nb * TMOE_Q6R_UNIT
+                                           : ITEM_ROWS * TMOE_Q6K_BYTES * nb + 16) +
                      PERM_STAGE;
     const int d2 = (GEMV_SMEM_2CTA - GEMV_HDR) / (GEMV_NW * slot);
     if (WT == TMOE_WT_Q4K && d2 >= 2) return {cb, 2, 2};
@@ -915,7 +1021,10 @@ static cudaError_t launch_t(const GemvArgs &args_in, int max_items, int sm_count
     a.chunk_blocks = pl.cb;
     a.n_chunks = (nb + pl.cb - 1) / pl.cb;
     a.row_stride = (WT == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES) * pl.cb;
-    a.wbytes = WT == TMOE_WT_Q4K ? ITEM_ROWS * a.row_stride : ITEM_ROWS * a.row_stride + 16;
+    // (Q6_K: + one word that the realigning loads of the last row may touch)
+    a.wbytes = WT == TMOE_WT_Q4K    ? ITEM_ROWS * a.row_stride
+               : WT == TMOE_WT_Q6KR ? 2 * pl.cb * TMOE_Q6R_UNIT
+                                    : ITEM_ROWS * a.row_stride + 16;
     a.slot_bytes = a.wbytes + PERM_STAGE;
     if (WT == TMOE_WT_Q4K && a.slot_bytes % 128 != 0) return cudaErrorInvalidValue;
     a.d_slots = pl.d;
@@ -979,6 +1088,7 @@ cudaError_t launch_gemv(int wt, bool gateup, const GemvArgs &a, int max_items, i
         return cudaErrorInvalidValue;
     // Q6_K: contiguous rows (whole-row fills); Q4_K: rows at least a row apart on 16-byte strides
     // (tensor-map fills: a matrix's K slices as experts); 16-byte aligned expert strides
+    // (Q6_K in 8-row fragment order: dense matrices, nb1 the ggml row size)
     const size_t rb = (size_t)(wt == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES) * (a.K / TMOE_QK);
     auto rows_ok = [&](size_t nb1) { return wt == TMOE_WT_Q4K ? nb1 >= rb && nb1 % 16 == 0 : nb1 == rb; };
     if (!rows_ok(a.nb1_0) || (a.nb2_0 & 15u) || ((uintptr_t)a.w0 & 15u)) return cudaErrorInvalidValue;
@@ -986,6 +1096,12 @@ cudaError_t launch_gemv(int wt, bool gateup, const GemvArgs &a, int max_items, i
     if (wt == TMOE_WT_Q4K)
         return gateup ? launch_t<TMOE_WT_Q4K, true>(a, max_items, sm_count, st)
                       : launch_t<TMOE_WT_Q4K, false>(a, max_items, sm_count, st);
+    if (wt == TMOE_WT_Q6KR) {
+        if ((size_t)a.N * rb > a.nb2_0 || (gateup && (size_t)a.N * rb > a.nb2_1)) return cudaErrorInvalidValue;
+        return gateup ? launch_t<TMOE_WT_Q6KR, true>(a, max_items, sm_count, st)
+                      : launch_t<TMOE_WT_Q6KR, false>(a, max_items, sm_count, st);
+    }
+    if (wt != TMOE_WT_Q6K) return cudaErrorInvalidValue;
     return gateup ? launch_t<TMOE_WT_Q6K, true>(a, max_items, sm_count, st)
                   : launch_t<TMOE_WT_Q6K, false>(a, max_items, sm_count, st);
 }

@@ -8,6 +8,7 @@
 
 #define TMOE_WT_Q4K 0
 #define TMOE_WT_Q6K 1
+#define TMOE_WT_Q6KR 2  // Q6_K in 8-row fragment order (TMOE_Q6R_UNIT); Q8_K activations as for Q6_K
 
 struct tmoe_comm;
 
@@ -90,9 +91,19 @@ struct Q8Rows {
     int8_t *qs;
     float *d;
     uint32_t *bl, *bh;
-    int wt;  // the consumer's weight type: TMOE_WT_Q4K or TMOE_WT_Q6K
+    int wt;  // the consumer's weight type: TMOE_WT_Q4K, TMOE_WT_Q6K or TMOE_WT_Q6KR
 };
 inline int q8_nbw(int wt) { return wt == TMOE_WT_Q4K ? 2 : 4; }
+// Where element e (0..255) of a Q8_K block sits in the stored block.  Q6_K consumers: the MMA
+// fragment order (m16n8k16 per 16-element sub-block, thread t4 of a column holding elements
+// 4 t4 .. 4 t4 + 3 of each), e = 16 s + 4 t4 + c -> 64 t4 + 4 s + c, so that the thread's operand
+// bytes of the whole block are 64 contiguous bytes (four 16-byte loads instead of sixteen 4-byte
+// ones).  Q4_K consumers: element order (a thread's 8-byte operands are already contiguous; the
+// same reordering measured slower there: C2 T = 64 gate/up 64.8 us against 60.6).
+__host__ __device__ inline int q8_frag_pos(int wt, int e) {
+    if (wt == TMOE_WT_Q4K) return e;
+    return 64 * ((e >> 2) & 3) + 4 * (e >> 4) + (e & 3);
+}
 
 // route.cu
 cudaError_t launch_rms_norm(const float *x, const float *norm_w, float eps, int64_t T, int H, float *out,
@@ -146,6 +157,9 @@ cudaError_t launch_wait_flag(const int32_t *flag, int32_t value, uint64_t limit_
 // quant.cu
 cudaError_t launch_quantize(int wt, const float *x, int64_t nblocks, uint8_t *out, cudaStream_t st);
 cudaError_t launch_dequantize(int wt, const uint8_t *in, int64_t n, float *out, cudaStream_t st);
+// Q6_K matrices (n_mats x n_rows rows, nb1 / nb2 apart) into 8-row fragment order, contiguous at dst.
+cudaError_t launch_prepack_q6k(const uint8_t *src, size_t nb1, size_t nb2, int64_t n_rows, int K, int64_t n_mats,
+                               uint8_t *dst, cudaStream_t st);
 // out[i][:K] = row rows[i] of W (ggml type 0 F32, 1 F16, 12 Q4_K, 14 Q6_K; n_rows_w rows nb1 apart);
 // a row outside [0, n_rows_w) gives zeros and latches TMOE_DEV_ERR_BADID in err.
 cudaError_t launch_get_rows(int32_t type, const uint8_t *W, size_t nb1, int K, int64_t n_rows_w, const int32_t *rows,

@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(256) dequant_f16_kernel(const uint8_t *__restr
     extern __shared__ __align__(16) uint8_t dq_rows[];
     const int ai = blockIdx.y;
     if (ai >= min(n_active[0], max_active)) return;
-    constexpr int BB = WT == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES;
+    constexpr int BB = WT == TMOE_WT_Q4K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES;  // per row and super-block
     const int nb = K / TMOE_QK;
     const int row_bytes = nb * BB;
     const int e = active[ai].x;
@@ -171,7 +171,9 @@ __global__ void __launch_bounds__(256) dequant_f16_kernel(const uint8_t *__restr
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int u = warp; u < nr * nb; u += blockDim.x >> 5) {
         const int r = u / nb, b = u - r * nb;
-        const uint8_t *blk = dq_rows + r * row_bytes + b * BB;
+        // ggml layout: the row's block; 8-row fragment order: the block's unit, row r % 8 of it
+        const uint8_t *blk = WT == TMOE_WT_Q6KR ? dq_rows + (r >> 3) * (nb * TMOE_Q6R_UNIT) + b * TMOE_Q6R_UNIT
+                                                : dq_rows + r * row_bytes + b * BB;
         __align__(16) __half h[8];
         // Two elements per step: their quant bytes become the fp16 pair (1024 + q) by exponent magic
         // (one byte permute), an exact half2 subtraction leaves the integers, and the value is
@@ -206,11 +208,19 @@ __global__ void __launch_bounds__(256) dequant_f16_kernel(const uint8_t *__restr
             }
         } else {
             const int hh = lane >> 4, rr = 8 * (lane & 15);  // element k = 128 hh + rr + i
-            const uint2 lo = lds_u64_a2(blk + 64 * hh + (rr & 63));
-            const uint2 hi = lds_u64_a2(blk + 128 + 32 * hh + (rr & 31));
+            // byte `off` of the row's ggml block (words: off % 4 == 0)
+            const int g8 = r & 7;
+            auto at = [&](int off) { return WT == TMOE_WT_Q6KR ? blk + q6r_offset(g8, off) : blk + off; };
+            auto u64 = [&](int off) {
+                return WT == TMOE_WT_Q6KR ? make_uint2(*reinterpret_cast<const uint32_t *>(at(off)),
+                                                       *reinterpret_cast<const uint32_t *>(at(off + 4)))
+                                          : lds_u64_a2(blk + off);
+            };
+            const uint2 lo = u64(64 * hh + (rr & 63));
+            const uint2 hi = u64(128 + 32 * hh + (rr & 31));
             const int lsh = rr < 64 ? 0 : 4, hsh = 2 * (rr >> 5);
-            const float d = h2f((uint16_t)(blk[208] | (blk[209] << 8)));
-            const float ds = __fmul_rn(d, (float)reinterpret_cast<const int8_t *>(blk + 192)[(128 * hh + rr) >> 4]);
+            const float d = h2f((uint16_t)(*at(208) | (*at(209) << 8)));
+            const float ds = __fmul_rn(d, (float)*reinterpret_cast<const int8_t *>(at(192 + ((128 * hh + rr) >> 4))));
             // the 6-bit quants of elements 0-3 and 4-7, one per byte
             const uint32_t qw[2] = {((lo.x >> lsh) & 0x0f0f0f0fu) | (((hi.x >> hsh) & 0x03030303u) << 4),
                                     ((lo.y >> lsh) & 0x0f0f0f0fu) | (((hi.y >> hsh) & 0x03030303u) << 4)};
@@ -981,7 +991,10 @@ cudaError_t launch_dequant_f16(int wt, const uint8_t *w, size_t nb2, int N, int 
         smem > 200 * 1024 || max_active > 65535)
         return cudaErrorInvalidValue;
     const dim3 grid((unsigned)((N + DQ_ROWS - 1) / DQ_ROWS), (unsigned)max_active);
-    auto kern = wt == TMOE_WT_Q4K ? dequant_f16_kernel<TMOE_WT_Q4K> : dequant_f16_kernel<TMOE_WT_Q6K>;
+    if (wt == TMOE_WT_Q6KR && N % DQ_ROWS) return cudaErrorInvalidValue;  // whole 8-row groups per CTA
+    auto kern = wt == TMOE_WT_Q4K    ? dequant_f16_kernel<TMOE_WT_Q4K>
+                : wt == TMOE_WT_Q6KR ? dequant_f16_kernel<TMOE_WT_Q6KR>
+                                     : dequant_f16_kernel<TMOE_WT_Q6K>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;

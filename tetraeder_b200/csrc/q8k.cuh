@@ -65,15 +65,23 @@ __device__ __forceinline__ void q8k_block_warp(const float (&v)[8], uint2 &q, fl
 namespace tmoe {
 
 // Stores the warp's Q8_K block b of row `row` (from q8k_block_warp) in the Q8Rows layout, with the
-// sub-block sums of the consumer's weight type split into exact low / high bytes.
+// sub-block sums of the consumer's weight type split into exact low / high bytes.  The 256 values
+// of a block are stored in the consumer's order (q8_frag_pos): for Q6_K the fragment order, in
+// which the GEMV thread of MMA column t4 reads its operand bytes of the block as 64 contiguous bytes.
 __device__ __forceinline__ void q8k_store_warp(const Q8Rows &o, int64_t row, int K, int b, const uint2 &q, float d,
                                                int s16) {
     const int lane = threadIdx.x & 31;
     const int nb = K / TMOE_QK;
-    *reinterpret_cast<uint2 *>(o.qs + row * K + (int64_t)b * TMOE_QK + 8 * lane) = q;
+    int8_t *blk = o.qs + row * K + (int64_t)b * TMOE_QK;
+    if (o.wt == TMOE_WT_Q4K) {
+        *reinterpret_cast<uint2 *>(blk + q8_frag_pos(o.wt, 8 * lane)) = q;
+    } else {
+        *reinterpret_cast<uint32_t *>(blk + q8_frag_pos(o.wt, 8 * lane)) = q.x;
+        *reinterpret_cast<uint32_t *>(blk + q8_frag_pos(o.wt, 8 * lane + 4)) = q.y;
+    }
     if (lane == 0) o.d[row * nb + b] = d;
     uint32_t lo = 0, hi = 0;
-    if (o.wt == TMOE_WT_Q6K) {  // 16-element sums: lane 2g holds sum g; 4 sums per word
+    if (o.wt != TMOE_WT_Q4K) {  // Q6_K: 16-element sums: lane 2g holds sum g; 4 sums per word
         if ((lane & 1) == 0) {
             const int i = (lane >> 1) & 3;
             lo = (uint32_t)(s16 & 63) << (8 * i);

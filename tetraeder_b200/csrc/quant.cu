@@ -205,4 +205,61 @@ cudaError_t launch_dequantize(int wt, const uint8_t *in, int64_t n, float *out, 
     return cudaGetLastError();
 }
 
+// One CTA per (8-row group, matrix): the group's 8 ggml rows are staged in shared memory, then
+// every output unit is written in order as 16-byte words (each byte taken through q6r_offset's
+// inverse: the unit's byte o holds byte off of row g, found by search over the 210 offsets once
+// per CTA into a shared table).
+__global__ void __launch_bounds__(256) prepack_q6k_kernel(const uint8_t *__restrict__ src, size_t nb1, size_t nb2,
+                                                          int nb, uint8_t *__restrict__ dst, int64_t groups) {
+    extern __shared__ __align__(16) uint8_t pk_smem[];
+    uint16_t *inv = reinterpret_cast<uint16_t *>(pk_smem);  // unit byte -> g * 210 + off
+    uint8_t *rows = pk_smem + 2 * TMOE_Q6R_UNIT;
+    const int64_t grp = blockIdx.x, mat = blockIdx.y;
+    for (int i = threadIdx.x; i < 8 * TMOE_Q6K_BYTES; i += blockDim.x) {
+        const int g = i / TMOE_Q6K_BYTES, off = i - g * TMOE_Q6K_BYTES;
+        inv[q6r_offset(g, off)] = (uint16_t)i;
+    }
+    const int rb = nb * TMOE_Q6K_BYTES;
+    const uint8_t *s0 = src + (size_t)mat * nb2 + (size_t)grp * 8 * nb1;
+    if (nb1 == (size_t)rb && ((uintptr_t)s0 & 15) == 0) {  // the 8 rows are one span of 8 * rb = 16 * 105 nb bytes
+        for (int i = threadIdx.x; i < 8 * rb / 16; i += blockDim.x)
+            reinterpret_cast<uint4 *>(rows)[i] = __ldg(reinterpret_cast<const uint4 *>(s0) + i);
+    } else {
+        for (int i = threadIdx.x; i < 8 * rb; i += blockDim.x) {
+            const int g = i / rb, c = i - g * rb;
+            rows[i] = s0[(size_t)g * nb1 + c];
+        }
+    }
+    __syncthreads();
+    uint8_t *out = dst + ((size_t)mat * groups + (size_t)grp) * (size_t)nb * TMOE_Q6R_UNIT;
+    for (int w = threadIdx.x; w < nb * TMOE_Q6R_UNIT / 16; w += blockDim.x) {
+        const int b = (16 * w) / TMOE_Q6R_UNIT, o0 = 16 * w - b * TMOE_Q6R_UNIT;
+        __align__(16) uint8_t v[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const int i = inv[o0 + j], g = i / TMOE_Q6K_BYTES, off = i - g * TMOE_Q6K_BYTES;
+            v[j] = rows[g * rb + b * TMOE_Q6K_BYTES + off];
+        }
+        *reinterpret_cast<uint4 *>(out + 16 * (size_t)w) = *reinterpret_cast<const uint4 *>(v);
+    }
+}
+
+cudaError_t launch_prepack_q6k(const uint8_t *src, size_t nb1, size_t nb2, int64_t n_rows, int K, int64_t n_mats,
+                               uint8_t *dst, cudaStream_t st) {
+    if (n_rows <= 0 || n_mats <= 0) return cudaSuccess;
+    const int nb = K / TMOE_QK;
+    const size_t smem = 2 * TMOE_Q6R_UNIT + (size_t)8 * nb * TMOE_Q6K_BYTES;
+    if (K <= 0 || K % TMOE_QK || n_rows % 8 || ((uintptr_t)dst & 15) || smem > 200 * 1024 || n_mats > 65535 ||
+        n_rows / 8 > 0x7fffffff)
+        return cudaErrorInvalidValue;
+    if (smem > 48 * 1024) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(prepack_q6k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    const int64_t groups = n_rows / 8;
+    prepack_q6k_kernel<<<dim3((unsigned)groups, (unsigned)n_mats), 256, smem, st>>>(src, nb1, nb2, nb, dst, groups);
+    return cudaGetLastError();
+}
+
 }  // namespace tmoe

@@ -174,7 +174,12 @@ struct PhaseMark {
 bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
 bool is_kquant(int t) { return t == TMOE_TYPE_Q4_K || t == TMOE_TYPE_Q6_K; }
-int wt_of(int t) { return t == TMOE_TYPE_Q4_K ? TMOE_WT_Q4K : TMOE_WT_Q6K; }
+// The expert products also take Q6_K in 8-row fragment order (tmoe_prepack).
+bool is_expert_type(int t) { return is_kquant(t) || t == TMOE_TYPE_Q6_K_R8; }
+int wt_of(int t) {
+    return t == TMOE_TYPE_Q4_K ? TMOE_WT_Q4K : t == TMOE_TYPE_Q6_K_R8 ? TMOE_WT_Q6KR : TMOE_WT_Q6K;
+}
+// Bytes per row (for Q6_K_R8: per row of the ggml matrix it was made from; the matrix has as many)
 size_t row_size(int t, int64_t K) {
     return (size_t)(K / TMOE_QK) * (t == TMOE_TYPE_Q4_K ? TMOE_Q4K_BYTES : TMOE_Q6K_BYTES);
 }
@@ -413,7 +418,8 @@ struct MmidLayout {
 int check_mmid(tmoe_handle *h, int32_t type, const void *W, size_t nb1, size_t nb2, int64_t K, int64_t N,
                int64_t n_w, const float *b, int64_t b1, const int32_t *ids, int64_t n_used, int64_t T,
                const float *out) {
-    if (!is_kquant(type)) return fail(h, TMOE_E_UNSUPPORTED, "mul_mat_id type %d (need Q4_K or Q6_K)", type);
+    if (!is_expert_type(type))
+        return fail(h, TMOE_E_UNSUPPORTED, "mul_mat_id type %d (need Q4_K, Q6_K or Q6_K_R8)", type);
     if (K <= 0 || K % 256 || K > (1 << 20) || N <= 0 || N > (1 << 20) || n_w <= 0 || n_w > kMaxSlots ||
         n_used <= 0 || n_used > kMaxSlots || T < 0 || T > (1 << 24) || T * n_used > (1 << 30) ||
         (b1 != 1 && b1 != n_used))
@@ -581,8 +587,9 @@ int tmoe_create(const tmoe_config *cfg, tmoe_handle **out) {
         return fail(nullptr, TMOE_E_INVALID, "n_embd and n_ff must be multiples of 256 (K-quant super-blocks)");
     if (c.n_expert > 256 || c.n_expert_used > 32 || c.n_expert_used > c.n_expert)
         return fail(nullptr, TMOE_E_INVALID, "n_expert <= 256 and n_expert_used <= min(32, n_expert) required");
-    if (!is_kquant(c.gate_type) || !is_kquant(c.up_type) || !is_kquant(c.down_type))
-        return fail(nullptr, TMOE_E_UNSUPPORTED, "expert types must be Q4_K (12) or Q6_K (14)");
+    if (!is_expert_type(c.gate_type) || !is_expert_type(c.up_type) || !is_expert_type(c.down_type))
+        return fail(nullptr, TMOE_E_UNSUPPORTED, "expert types must be Q4_K (12), Q6_K (14) or Q6_K_R8 (%d)",
+                    TMOE_TYPE_Q6_K_R8);
     if (c.gate_type != c.up_type)
         return fail(nullptr, TMOE_E_UNSUPPORTED, "gate and up must share a type");
     if ((int64_t)c.max_tokens * c.n_expert_used > (1 << 30))
@@ -1270,6 +1277,28 @@ int tmoe_dequantize(int32_t type, const void *in, int64_t n, float *out, void *s
     if (!in || !out) return fail(nullptr, TMOE_E_INVALID, "null tensor");
     cudaError_t e = tmoe::launch_dequantize(wt_of(type), (const uint8_t *)in, n, out, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(nullptr, e, "dequantize");
+    return TMOE_OK;
+}
+
+int tmoe_prepack(int32_t type, const void *src, size_t nb1, size_t nb2, int64_t n_rows, int64_t K, int64_t n_mats,
+                 void *dst, void *stream) {
+    if (type != TMOE_TYPE_Q6_K)
+        return fail(nullptr, TMOE_E_UNSUPPORTED, "prepack type %d (only Q6_K has a packed layout)", type);
+    if (n_rows < 0 || n_mats < 0 || K <= 0 || K % 256 || K > (1 << 20) || n_rows % 8 || n_rows > (1ll << 30) ||
+        n_mats > 65535)
+        return fail(nullptr, TMOE_E_INVALID, "prepack needs K a multiple of 256, rows a multiple of 8, <= 65535 mats");
+    if (n_rows == 0 || n_mats == 0) return TMOE_OK;
+    if (!src || !dst) return fail(nullptr, TMOE_E_INVALID, "null tensor");
+    const size_t rb = row_size(type, K);
+    if (nb1 < rb || (n_mats > 1 && nb2 < (size_t)n_rows * nb1))
+        return fail(nullptr, TMOE_E_INVALID, "rows or matrices overlap (nb1 < row size or nb2 < rows * nb1)");
+    if (!aligned16(dst)) return fail(nullptr, TMOE_E_INVALID, "dst must be 16-byte aligned");
+    const uintptr_t s0 = (uintptr_t)src, s1 = s0 + (size_t)(n_mats - 1) * nb2 + (size_t)(n_rows - 1) * nb1 + rb;
+    const uintptr_t d0 = (uintptr_t)dst, d1 = d0 + (size_t)n_mats * n_rows * rb;
+    if (s0 < d1 && d0 < s1) return fail(nullptr, TMOE_E_INVALID, "src and dst overlap");
+    const cudaError_t e = tmoe::launch_prepack_q6k((const uint8_t *)src, nb1, nb2, n_rows, (int)K, n_mats,
+                                                   (uint8_t *)dst, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "prepack");
     return TMOE_OK;
 }
 

@@ -21,10 +21,10 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from ._lib import TYPE_Q4_K, TYPE_Q6_K, TmoeError
+from ._lib import TYPE_Q4_K, TYPE_Q6_K, TYPE_Q6_K_R8, TmoeError
 
 QK_K = 256
-BLOCK_BYTES = {TYPE_Q4_K: 144, TYPE_Q6_K: 210}
+BLOCK_BYTES = {TYPE_Q4_K: 144, TYPE_Q6_K: 210, TYPE_Q6_K_R8: 210}
 
 
 def row_size(qtype: int, ncols: int) -> int:
@@ -79,6 +79,23 @@ def dequantize(qtype: int, data: torch.Tensor, n: int, stream=None) -> torch.Ten
     lib = _lib.load()
     out = torch.empty(n, dtype=torch.float32, device=data.device)
     _lib.check(lib.tmoe_dequantize(qtype, _ptr(data.contiguous()), n, _ptr(out), _stream(stream)), None)
+    return out
+
+
+def prepack(W: torch.Tensor, stream=None) -> torch.Tensor:
+    """tmoe_prepack, the optional explicit repack: Q6_K expert matrices uint8 [n_mats, rows, row_size]
+    (rows % 8 == 0) -> a new tensor of the same shape and bytes in 8-row fragment order, to be used
+    as TYPE_Q6_K_R8 wherever the Q6_K tensor was (products bit for bit the same)."""
+    lib = _lib.load()
+    if W.dtype != torch.uint8 or W.dim() != 3 or not W.is_cuda:
+        raise ValueError("prepack takes a CUDA uint8 tensor [n_mats, rows, row_size]")
+    n_mats, rows, rs = W.shape
+    if rs % BLOCK_BYTES[TYPE_Q6_K]:
+        raise ValueError("row size is not a whole number of Q6_K super-blocks")
+    K = rs // BLOCK_BYTES[TYPE_Q6_K] * QK_K
+    out = torch.empty((n_mats, rows, rs), dtype=torch.uint8, device=W.device)
+    _lib.check(lib.tmoe_prepack(TYPE_Q6_K, _ptr(W), W.stride(1), W.stride(0), rows, K, n_mats, _ptr(out),
+                                _stream(stream)), None)
     return out
 
 
@@ -351,5 +368,6 @@ def ep_a2a_moe_ffn(layer: "MoeLayer", comm: EPComm, x: torch.Tensor, experts: Ex
     return out
 
 
-__all__ = ["MoeLayer", "ExpertWeights", "TmoeError", "TYPE_Q4_K", "TYPE_Q6_K", "row_size", "quantize", "dequantize",
+__all__ = ["MoeLayer", "ExpertWeights", "TmoeError", "TYPE_Q4_K", "TYPE_Q6_K", "TYPE_Q6_K_R8", "row_size", "quantize",
+           "dequantize", "prepack",
            "EPComm", "ep_moe_ffn", "ep_a2a_moe_ffn", "ep_id_map", "SlotCache"]
