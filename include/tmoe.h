@@ -299,7 +299,7 @@ TMOE_API int tmoe_dequantize(int32_t type, const void *in, int64_t n, float *out
 
 /* The optional, explicit repack that the boundary allows (weights are never repacked implicitly;
  * the reference keeps expert weights unrepacked, docs/adr/0039): n_mats Q6_K matrices of n_rows
- * rows (n_rows % 8 == 0) and K columns (K % 256 == 0), rows nb1 bytes apart and matrices nb2 apart,
+ * rows (n_rows % 8 == 0) and K columns (K % 256 == 0, K <= 16384), rows nb1 bytes apart and matrices nb2 apart,
  * are written to dst (16-byte aligned, n_mats * n_rows * row size bytes, not overlapping src) as
  * TMOE_TYPE_Q6_K_R8: per matrix, n_rows / 8 row groups of K / 256 units of 1680 bytes, the same
  * bytes rearranged so that the expert GEMV reads them with aligned, conflict-free vector loads and

@@ -58,7 +58,7 @@ def test_prepack_argument_checks_without_a_gpu():
 
     rc, msg = call(_lib.TYPE_Q4_K, src, 144, 144 * 8, 8, 256, 1, dst)
     assert rc == _lib.TMOE_E_UNSUPPORTED and "only Q6_K" in msg
-    for rows, K in ((8, 300), (12, 256)):  # K not a multiple of 256, rows not a multiple of 8
+    for rows, K in ((8, 300), (12, 256), (8, 16640)):  # K not a multiple of 256 or too large; rows % 8
         rc, msg = call(_lib.TYPE_Q6_K, src, 210, 210 * rows, rows, K, 1, dst)
         assert rc == _lib.TMOE_E_INVALID and "multiple" in msg
     rc, msg = call(_lib.TYPE_Q6_K, src, 200, 210 * 8, 8, 256, 1, dst)

@@ -1284,9 +1284,11 @@ int tmoe_prepack(int32_t type, const void *src, size_t nb1, size_t nb2, int64_t 
                  void *dst, void *stream) {
     if (type != TMOE_TYPE_Q6_K)
         return fail(nullptr, TMOE_E_UNSUPPORTED, "prepack type %d (only Q6_K has a packed layout)", type);
-    if (n_rows < 0 || n_mats < 0 || K <= 0 || K % 256 || K > (1 << 20) || n_rows % 8 || n_rows > (1ll << 30) ||
+    // (K <= 16384: a row group of 8 rows is staged in shared memory, 13,440 bytes per 1024 columns)
+    if (n_rows < 0 || n_mats < 0 || K <= 0 || K % 256 || K > 16384 || n_rows % 8 || n_rows > (1ll << 30) ||
         n_mats > 65535)
-        return fail(nullptr, TMOE_E_INVALID, "prepack needs K a multiple of 256, rows a multiple of 8, <= 65535 mats");
+        return fail(nullptr, TMOE_E_INVALID,
+                    "prepack needs K a multiple of 256 up to 16384, rows a multiple of 8, at most 65535 matrices");
     if (n_rows == 0 || n_mats == 0) return TMOE_OK;
     if (!src || !dst) return fail(nullptr, TMOE_E_INVALID, "null tensor");
     const size_t rb = row_size(type, K);
