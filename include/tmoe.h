@@ -178,10 +178,10 @@ TMOE_API int tmoe_layer(tmoe_handle *h, void *stream, const float *x, int64_t T,
                const float *norm_w, const float *router_w, const float *logits,
                const int32_t *id_map, const tmoe_expert_tensors *wts, float *out,
                int32_t *ids_out, float *w_out);
-/* tmoe_layer with bf16 activations x [T][H] (the x_dtype of the survey's boundary: a caller whose
- * hidden state is bf16).  The rows are widened to f32, which is exact, into the handle's workspace,
- * and then the layer runs as tmoe_layer on them, so the results equal tmoe_layer's on the f32
- * values bit for bit.  `out` stays f32. */
+/* tmoe_layer with bf16 activations x [T][H], for a caller whose hidden state is bf16.  The rows
+ * are widened to f32, which is exact, into the handle's workspace, and then the layer runs as
+ * tmoe_layer on them, so the results equal tmoe_layer's on the f32 values bit for bit.  `out`
+ * stays f32. */
 TMOE_API int tmoe_layer_bf16(tmoe_handle *h, void *stream, const uint16_t *x, int64_t T, int32_t use_norm,
                              const float *norm_w, const float *router_w, const float *logits,
                              const int32_t *id_map, const tmoe_expert_tensors *wts, float *out,
@@ -258,21 +258,20 @@ TMOE_API int tmoe_streamed_layer(tmoe_handle *h, void *stream, tmoe_slots *s, co
                                  int32_t use_norm, const float *norm_w, const float *router_w, const float *logits,
                                  float *out, int32_t *ids_out, float *w_out);
 
-/* Expert parallelism with token dispatch/combine over an all-to-all (the survey's mode B), for
- * ranks that hold different tokens: rank r holds experts [r*E/g, (r+1)*E/g) in `wts` (n_slots =
- * E/g) and its own T tokens (T <= max_tokens / g; create the handle with max_tokens = g x the
- * tokens per rank, since it computes the rows the other ranks send).  Each token is sent once to
- * every rank that holds one of its choices; that rank computes its experts' pairs and combines
- * them in choice order (the reference's per-rank partial, qwen3moe_shard.rs:1043-1056), sends the
- * partial row back, and the token's rank adds the partials in rank order.  Messages have a fixed
- * capacity of max_tokens / g rows per peer (no host readback).  Every rank must make the same
- * calls in the same order; a rank whose routing fails still takes both exchange steps.
- * Exchange: the first call with a communicator maps every rank's exchange buffers into every
- * rank (CUDA IPC; host-synchronous, so not under stream capture), and from then on the messages
- * are written straight into the peers' buffers over NVLink with counted arrivals (a wait that runs
- * out after 1 s latches TMOE_DEV_ERR_TIMEOUT, reported by tmoe_check).  With g > 8, or if any rank
- * cannot map a peer, the ranks exchange through NCCL instead.  A rank must not destroy its handle
- * while another rank is still inside a call with it. */
+/* Expert parallelism with token dispatch/combine over an all-to-all (the mode beside the reference's
+ * all-reduce), for ranks that hold different tokens: rank r holds experts [r*E/g, (r+1)*E/g) in `wts`
+ * (n_slots = E/g) and its own T tokens (T <= max_tokens / g; create the handle with max_tokens = g x the
+ * tokens per rank, since it computes the rows the other ranks send). Each token is sent once to every rank
+ * that holds one of its choices; that rank computes its experts' pairs and combines them in choice order
+ * (the reference's per-rank partial, qwen3moe_shard.rs:1043-1056), sends the partial row back, and the
+ * token's rank adds the partials in rank order. Messages have a fixed capacity of max_tokens / g rows per
+ * peer (no host readback). Every rank must make the same calls in the same order; a rank whose routing fails
+ * still takes both exchange steps. Exchange: the first call with a communicator maps every rank's exchange
+ * buffers into every rank (CUDA IPC; host-synchronous, so not under stream capture), and from then on the
+ * messages are written straight into the peers' buffers over NVLink with counted arrivals (a wait that runs
+ * out after 1 s latches TMOE_DEV_ERR_TIMEOUT, reported by tmoe_check). With g > 8, or if any rank cannot map
+ * a peer, the ranks exchange through NCCL instead. A rank must not destroy its handle while another rank is
+ * still inside a call with it. */
 TMOE_API int tmoe_ep_a2a_layer(tmoe_handle *h, void *stream, tmoe_comm *comm, const float *x, int64_t T,
                                int32_t use_norm, const float *norm_w, const float *router_w, const float *logits,
                                const tmoe_expert_tensors *wts, float *out, int32_t *ids_out, float *w_out);

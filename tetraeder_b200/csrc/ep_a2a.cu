@@ -1,15 +1,13 @@
-// Expert parallelism with token dispatch/combine over an all-to-all (the survey's mode B): each
-// rank holds its own tokens and a contiguous share of the experts (the reference's partition rule,
-// qwen3moe_shard.rs:617-626).  A token is sent once to every rank that holds at least one of its k
-// experts, with its k choices mapped to that rank's local expert ids (-1 for the others) and its
-// k weights; the receiving rank runs the layer's expert products and its choice-ordered combine
-// over the received rows -- exactly the partial sum of the reference's EP mode for that rank
-// (qwen3moe_shard.rs:1043-1056) -- and sends the partial row back; the source rank adds the
-// partials of its tokens in rank order.
-//
-// Messages have a fixed capacity (`cap` rows per peer, the handle's token capacity per rank), so
-// their sizes are known to the host without a readback and the step stays stream-ordered; rows
-// past a peer's count carry -1 ids and cost no expert work.
+// Expert parallelism with token dispatch/combine over an all-to-all (the mode beside the reference's
+// all-reduce): each rank holds its own tokens and a contiguous share of the experts (the reference's
+// partition rule, qwen3moe_shard.rs:617-626). A token is sent once to every rank that holds at least one of
+// its k experts, with its k choices mapped to that rank's local expert ids (-1 for the others) and its k
+// weights; the receiving rank runs the layer's expert products and its choice-ordered combine over the
+// received rows -- exactly the partial sum of the reference's EP mode for that rank
+// (qwen3moe_shard.rs:1043-1056) -- and sends the partial row back; the source rank adds the partials of its
+// tokens in rank order. Messages have a fixed capacity (`cap` rows per peer, the handle's token capacity per
+// rank), so their sizes are known to the host without a readback and the step stays stream-ordered; rows past
+// a peer's count carry -1 ids and cost no expert work.
 #include "common.cuh"
 #include "kernels.cuh"
 
