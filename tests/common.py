@@ -137,3 +137,20 @@ def q6r_pack(W: np.ndarray) -> np.ndarray:
     unit[..., 1536:1664] = blk[..., 192:208].reshape(lead + (128,))
     unit[..., 1664:1680] = blk[..., 208:210].reshape(lead + (16,))
     return np.ascontiguousarray(unit).reshape(n, rows, rb)
+
+
+def q6r_unpack(P: np.ndarray) -> np.ndarray:
+    """The inverse of q6r_pack: 8-row fragment-ordered Q6_K units back to ggml rows."""
+    n, rows, rb = P.shape
+    nb = rb // 210
+    unit = P.reshape(n, rows // 8, nb, 1680)
+    lead = unit.shape[:3]
+    blk = np.empty(lead + (8, 210), np.uint8)
+    for h in range(2):
+        ql = unit[..., 768 * h:768 * h + 512].reshape(lead + (8, 4, 4, 4))  # g, t4, i, j
+        blk[..., 64 * h:64 * h + 64] = ql.transpose(0, 1, 2, 3, 5, 4, 6).reshape(lead + (8, 64))
+        qh = unit[..., 768 * h + 512:768 * h + 768].reshape(lead + (8, 4, 2, 4))  # g, t4, i, j
+        blk[..., 128 + 32 * h:160 + 32 * h] = qh.transpose(0, 1, 2, 3, 5, 4, 6).reshape(lead + (8, 32))
+    blk[..., 192:208] = unit[..., 1536:1664].reshape(lead + (8, 16))
+    blk[..., 208:210] = unit[..., 1664:1680].reshape(lead + (8, 2))
+    return np.ascontiguousarray(blk.transpose(0, 1, 3, 2, 4)).reshape(n, rows, rb)

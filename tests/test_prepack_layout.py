@@ -7,7 +7,7 @@ import ctypes as C
 import numpy as np
 import pytest
 
-from tests.common import q6r_pack
+from tests.common import q6r_pack, q6r_unpack
 from tetraeder_b200 import _lib
 
 
@@ -44,6 +44,20 @@ def test_numpy_packer_follows_the_byte_map(nb):
                 u = units[m, r // 8, b]
                 idx = [byte_map(r % 8, o) for o in range(210)]
                 assert np.array_equal(u[idx], blk)
+
+
+@pytest.mark.parametrize("n,rows,nb", [(1, 8, 1), (3, 64, 3), (2, 2048, 3), (2, 4096, 6)])
+def test_pack_unpack_round_trip(n, rows, nb):
+    """Repacking is a pure permutation within each 8-row group: unpacking gives the ggml bytes back, and a
+    packed matrix differs from its source unless the group's bytes happen to be symmetric."""
+    rng = np.random.default_rng(rows * 10 + nb)
+    W = rng.integers(0, 256, (n, rows, nb * 210), dtype=np.uint8)
+    P = q6r_pack(W)
+    assert np.array_equal(q6r_unpack(P), W)
+    assert not np.array_equal(P, W)
+    # each 8-row group maps onto itself: the same multiset of bytes per (matrix, group)
+    g = W.reshape(n, rows // 8, -1)
+    assert np.array_equal(np.sort(P.reshape(n, rows // 8, -1), axis=-1), np.sort(g, axis=-1))
 
 
 def test_prepack_argument_checks_without_a_gpu():
