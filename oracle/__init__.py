@@ -63,6 +63,7 @@ def _declare(L):
     L.tmo_vec_dot_q6k_q8k.argtypes, L.tmo_vec_dot_q6k_q8k.restype = [I64, P, P], C.c_float
     L.tmo_vec_dot_q4k_q8k_simd.argtypes, L.tmo_vec_dot_q4k_q8k_simd.restype = [I64, P, P], C.c_float
     L.tmo_vec_dot_q6k_q8k_simd.argtypes, L.tmo_vec_dot_q6k_q8k_simd.restype = [I64, P, P], C.c_float
+    L.tmo_dot_cols.argtypes = [C.c_int, I64, P, P, C.c_int, P]
     L.tmo_exp_canon.argtypes, L.tmo_exp_canon.restype = [C.c_float], C.c_float
     L.tmo_router_dot.argtypes, L.tmo_router_dot.restype = [P, P, I64], C.c_float
     L.tmo_rms_norm.argtypes = [P, P, C.c_float, P, I64]

@@ -345,7 +345,8 @@ float tmo_vec_dot_q6k_q8k(int64_t ncols, const void *w, const tmo_block_q8k *x) 
 }
 
 /* ------------------------------------------------------------------------ */
-/* SIMD forms of the two dots (AVX2), used by mul_mat_id / experts            */
+/* SIMD forms of the two dots (AVX2); mul_mat_id / experts use the
+ * multi-column form (tmo_dot_cols) */
 /* ------------------------------------------------------------------------ */
 /* ggml's CPU path computes the same integer sub-block sums with byte multiply-adds (maddubs:
  * unsigned weight bytes times signed activation bytes, pairs summed to 16 bits, then to 32).  These
@@ -440,7 +441,99 @@ float tmo_vec_dot_q6k_q8k_simd(int64_t ncols, const void *w, const tmo_block_q8k
     }
     return acc;
 }
+
+/* One weight row against up to four activation rows, the organisation of ggml's CPU mat-mul
+ * kernels: the row's quants are unpacked once per super-block and serve every column, and the
+ * sub-block scales multiply the 16-bit pair sums in vector registers (madd), so a super-block takes
+ * one horizontal sum per column instead of one per sub-block.  The integer sums are the same
+ * integers in another order (no lane can overflow: a Q4_K pair sum is at most 2 * 15 * 127, a Q6_K
+ * one 2 * 63 * 127, times a scale below 2^7), and the float scaling is the scalar statement's, so
+ * out[c] equals tmo_vec_dot_q4k_q8k / tmo_vec_dot_q6k_q8k of column c bit for bit. */
+static void dot_cols_q4k(int64_t ncols, const uint8_t *blk, const tmo_block_q8k *const *xs, int nc, float *out) {
+    const __m256i low = _mm256_set1_epi8(0x0f);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int64_t b = 0; b < ncols / TMO_QK_K; b++, blk += TMO_Q4K_BYTES) {
+        int sc[8], mn[8];
+        for (int s = 0; s < 8; s++) q4k_scale_min(blk + 4, s, &sc[s], &mn[s]);
+        __m256i q[8], scv[8];
+        for (int j = 0; j < 4; j++) {
+            const __m256i qv = _mm256_loadu_si256((const __m256i *)(blk + 16 + 32 * j));
+            q[2 * j] = _mm256_and_si256(qv, low);
+            q[2 * j + 1] = _mm256_and_si256(_mm256_srli_epi16(qv, 4), low);
+        }
+        for (int s = 0; s < 8; s++) scv[s] = _mm256_set1_epi16((short)sc[s]);
+        const float dw = tmo_f16_to_f32(rd16(blk)), mw = tmo_f16_to_f32(rd16(blk + 2));
+        for (int c = 0; c < nc; c++) {
+            const tmo_block_q8k *x = xs[c] + b;
+            __m256i a = _mm256_setzero_si256();
+            for (int s = 0; s < 8; s++)
+                a = _mm256_add_epi32(a, _mm256_madd_epi16(_mm256_maddubs_epi16(q[s], _mm256_loadu_si256(
+                                                              (const __m256i *)(x->qs + 32 * s))), scv[s]));
+            const int32_t isum = hsum8(a);
+            int32_t msum = 0;
+            for (int j = 0; j < 4; j++)
+                msum += mn[2 * j] * (x->bsums[4 * j] + x->bsums[4 * j + 1]) +
+                        mn[2 * j + 1] * (x->bsums[4 * j + 2] + x->bsums[4 * j + 3]);
+            const float d = dw * x->d, dmin = mw * x->d;
+            acc[c] += d * (float)isum;
+            acc[c] -= dmin * (float)msum;
+        }
+    }
+    for (int c = 0; c < nc; c++) out[c] = acc[c];
+}
+
+static void dot_cols_q6k(int64_t ncols, const uint8_t *blk, const tmo_block_q8k *const *xs, int nc, float *out) {
+    const __m256i low = _mm256_set1_epi8(0x0f), two = _mm256_set1_epi8(0x03);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int64_t b = 0; b < ncols / TMO_QK_K; b++, blk += TMO_Q6K_BYTES) {
+        const uint8_t *ql = blk, *qh = blk + 128;
+        const int8_t *scp = (const int8_t *)(blk + 192);
+        __m256i q[8], scv[8];
+        for (int h = 0; h < 2; h++) {
+            const __m256i l0 = _mm256_loadu_si256((const __m256i *)(ql + 64 * h));
+            const __m256i l1 = _mm256_loadu_si256((const __m256i *)(ql + 64 * h + 32));
+            const __m256i hb = _mm256_loadu_si256((const __m256i *)(qh + 32 * h));
+            q[4 * h] = _mm256_or_si256(_mm256_and_si256(l0, low), _mm256_slli_epi16(_mm256_and_si256(hb, two), 4));
+            q[4 * h + 1] = _mm256_or_si256(_mm256_and_si256(l1, low),
+                                           _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(hb, 2), two), 4));
+            q[4 * h + 2] = _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(l0, 4), low),
+                                           _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(hb, 4), two), 4));
+            q[4 * h + 3] = _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(l1, 4), low),
+                                           _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(hb, 6), two), 4));
+        }
+        /* register v holds elements 32 v .. 32 v + 31: sub-blocks 2 v (low half) and 2 v + 1 */
+        for (int v = 0; v < 8; v++)
+            scv[v] = _mm256_set_m128i(_mm_set1_epi16(scp[2 * v + 1]), _mm_set1_epi16(scp[2 * v]));
+        const float dw = tmo_f16_to_f32(rd16(blk + 208));
+        for (int c = 0; c < nc; c++) {
+            const tmo_block_q8k *x = xs[c] + b;
+            __m256i a = _mm256_setzero_si256();
+            for (int v = 0; v < 8; v++)
+                a = _mm256_add_epi32(a, _mm256_madd_epi16(_mm256_maddubs_epi16(q[v], _mm256_loadu_si256(
+                                                              (const __m256i *)(x->qs + 32 * v))), scv[v]));
+            int32_t bias = 0;
+            for (int s = 0; s < 16; s++) bias += scp[s] * x->bsums[s];
+            const int32_t isum = hsum8(a) - 32 * bias;
+            const float d = dw * x->d;
+            acc[c] += d * (float)isum;
+        }
+    }
+    for (int c = 0; c < nc; c++) out[c] = acc[c];
+}
+#endif
+
+void tmo_dot_cols(int type, int64_t ncols, const void *w, const tmo_block_q8k *const *xs, int nc, float *out) {
+    if (nc < 1 || nc > 4) return;
+#if defined(__AVX2__)
+    if (type == TMO_TYPE_Q4_K) return dot_cols_q4k(ncols, (const uint8_t *)w, xs, nc, out);
+    if (type == TMO_TYPE_Q6_K) return dot_cols_q6k(ncols, (const uint8_t *)w, xs, nc, out);
 #else
+    for (int c = 0; c < nc; c++)
+        out[c] = type == TMO_TYPE_Q4_K ? tmo_vec_dot_q4k_q8k(ncols, w, xs[c]) : tmo_vec_dot_q6k_q8k(ncols, w, xs[c]);
+#endif
+}
+
+#if !defined(__AVX2__)
 float tmo_vec_dot_q4k_q8k_simd(int64_t ncols, const void *w, const tmo_block_q8k *x) {
     return tmo_vec_dot_q4k_q8k(ncols, w, x);
 }
@@ -653,8 +746,10 @@ int tmo_mul_mat_id(int type, const void *W, size_t nb1, size_t nb2, int64_t K, i
     int64_t ncol = T * b1;
     tmo_block_q8k *q = (tmo_block_q8k *)malloc(sizeof(tmo_block_q8k) * (size_t)(ncol * nb));
     float *deq = (float *)malloc(sizeof(float) * (size_t)(ncol * K));
+    /* the f32 view of the activations is read only by the f64 mode and the float types */
+    const int need_deq = !(mode == TMO_MODE_Q8K && (type == TMO_TYPE_Q4_K || type == TMO_TYPE_Q6_K));
 #pragma omp parallel for num_threads(nthreads) schedule(static)
-    for (int64_t c = 0; c < ncol; c++) prep_act(type, b + c * K, K, q + c * nb, deq + c * K);
+    for (int64_t c = 0; c < ncol; c++) prep_act(type, b + c * K, K, q + c * nb, need_deq ? deq + c * K : NULL);
     int32_t *counts = (int32_t *)malloc(sizeof(int32_t) * (size_t)E);
     int32_t *offs = (int32_t *)malloc(sizeof(int32_t) * (size_t)(E + 1));
     int32_t *perm = (int32_t *)malloc(sizeof(int32_t) * (size_t)(T * n_used + 1));
@@ -672,6 +767,20 @@ int tmo_mul_mat_id(int type, const void *W, size_t nb1, size_t nb2, int64_t K, i
             if (!counts[e]) continue;
             for (int64_t r = r0; r < r0 + RB && r < N; r++) {
                 const uint8_t *wrow = (const uint8_t *)W + e * nb2 + r * nb1;
+                if (mode == TMO_MODE_Q8K && (type == TMO_TYPE_Q4_K || type == TMO_TYPE_Q6_K)) {
+                    for (int32_t i = offs[e]; i < offs[e + 1]; i += 4) {
+                        const int nc = offs[e + 1] - i < 4 ? offs[e + 1] - i : 4;
+                        const tmo_block_q8k *xs[4];
+                        float res[4];
+                        for (int c = 0; c < nc; c++) {
+                            int64_t p = perm[i + c], t = p / n_used, j = p % n_used;
+                            xs[c] = q + (t * b1 + (b1 == 1 ? 0 : j)) * nb;
+                        }
+                        tmo_dot_cols(type, K, wrow, xs, nc, res);
+                        for (int c = 0; c < nc; c++) out[(int64_t)perm[i + c] * N + r] = res[c];
+                    }
+                    continue;
+                }
                 for (int32_t i = offs[e]; i < offs[e + 1]; i++) {
                     int64_t p = perm[i], t = p / n_used, j = p % n_used;
                     int64_t c = t * b1 + (b1 == 1 ? 0 : j);

@@ -110,6 +110,32 @@ def test_simd_dots_equal_the_scalar_restatement(qt):
                 assert a.view(np.uint32) == b.view(np.uint32), (r, float(a), float(b))
 
 
+@pytest.mark.parametrize("qt", [O.TYPE_Q4_K, O.TYPE_Q6_K])
+def test_multi_column_dots_equal_the_scalar_restatement(qt):
+    """The dots mul_mat_id runs now (one weight row against up to four activation rows, scales applied
+    to the 16-bit pair sums in vector registers) against the scalar restatement, column by column and bit
+    for bit, with 1 to 4 columns, random valid blocks and activations at the Q8_K extremes."""
+    import ctypes as C
+    from tests.common import random_kquant_bytes
+    rng = np.random.default_rng(100 + qt)
+    ncols = 1536
+    rows = np.concatenate([O.quantize(qt, rng.uniform(-1, 1, (8, ncols)).astype(np.float32)),
+                           random_kquant_bytes(rng, qt, 24, ncols, 1.0)])
+    cols = [O.quantize_q8k(np.asarray(x, np.float32)) for x in
+            (rng.uniform(-1, 1, ncols), rng.standard_normal(ncols) * 30,
+             np.where(rng.random(ncols) < 0.5, -1.0, 1.0) * 127, rng.standard_normal(ncols))]
+    scalar = O.lib().tmo_vec_dot_q4k_q8k if qt == O.TYPE_Q4_K else O.lib().tmo_vec_dot_q6k_q8k
+    for nc in (1, 2, 3, 4):
+        xs = (C.c_void_p * 4)(*[c.ctypes.data for c in cols])
+        for r in range(rows.shape[0]):
+            row = np.ascontiguousarray(rows[r])
+            out = np.zeros(4, np.float32)
+            O.lib().tmo_dot_cols(qt, ncols, row.ctypes.data, xs, nc, out.ctypes.data)
+            for c in range(nc):
+                want = np.float32(scalar(ncols, row.ctypes.data, cols[c].ctypes.data))
+                assert out[c].view(np.uint32) == want.view(np.uint32), (nc, r, c)
+
+
 TYPES = [O.TYPE_Q4_K, O.TYPE_Q6_K]
 
 
