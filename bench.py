@@ -112,7 +112,8 @@ def parse():
                         "allreduce = the reference's EP mode, the same tokens on every rank, outputs summed")
     a = p.parse_args()
     global PREPACK
-    PREPACK = a.prepack and a.mode == "decode"  # the large-batch modes keep ggml's layout
+    # the large-batch modes and the reference arm (the CPU oracle on ggml's bytes) keep ggml's layout
+    PREPACK = a.prepack and a.mode == "decode" and a.impl == "ours"
     set_shape(a.shape)
     if a.mode in ("prefill", "streamed") and a.tokens == 64:
         a.tokens = 8192
