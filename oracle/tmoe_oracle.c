@@ -453,15 +453,28 @@ static void dot_cols_q4k(int64_t ncols, const uint8_t *blk, const tmo_block_q8k 
     const __m256i low = _mm256_set1_epi8(0x0f);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int64_t b = 0; b < ncols / TMO_QK_K; b++, blk += TMO_Q4K_BYTES) {
-        int sc[8], mn[8];
-        for (int s = 0; s < 8; s++) q4k_scale_min(blk + 4, s, &sc[s], &mn[s]);
+        /* the 6-bit scales and mins of q4k_scale_min, four at a time as bytes of 32-bit words */
+        uint32_t w0, w1, w2;
+        memcpy(&w0, blk + 4, 4);
+        memcpy(&w1, blk + 8, 4);
+        memcpy(&w2, blk + 12, 4);
+        const uint64_t sc8 = (uint64_t)(w0 & 0x3f3f3f3fu) |
+                             ((uint64_t)((w2 & 0x0f0f0f0fu) | ((w0 >> 2) & 0x30303030u)) << 32);
+        const uint64_t mn8 = (uint64_t)(w1 & 0x3f3f3f3fu) |
+                             ((uint64_t)(((w2 >> 4) & 0x0f0f0f0fu) | ((w1 >> 2) & 0x30303030u)) << 32);
+        const __m128i sc16 = _mm_cvtepu8_epi16(_mm_cvtsi64_si128((long long)sc8)); /* lanes: scale 0..7 */
+        const __m128i mn16 = _mm_cvtepu8_epi16(_mm_cvtsi64_si128((long long)mn8));
+        const __m256i scb = _mm256_broadcastsi128_si256(sc16);
         __m256i q[8], scv[8];
         for (int j = 0; j < 4; j++) {
             const __m256i qv = _mm256_loadu_si256((const __m256i *)(blk + 16 + 32 * j));
             q[2 * j] = _mm256_and_si256(qv, low);
             q[2 * j + 1] = _mm256_and_si256(_mm256_srli_epi16(qv, 4), low);
         }
-        for (int s = 0; s < 8; s++) scv[s] = _mm256_set1_epi16((short)sc[s]);
+        for (int s = 0; s < 8; s++) /* every 16-bit lane: scale s (bytes 2s, 2s+1 of each half) */
+            scv[s] = _mm256_shuffle_epi8(scb, _mm256_set1_epi16((short)(0x0100 * (2 * s + 1) + 2 * s)));
+        /* 16-bit lane i: the min of sub-block i / 2 (bsums i is a 16-element half of it) */
+        const __m256i mnv = _mm256_set_m128i(_mm_unpackhi_epi16(mn16, mn16), _mm_unpacklo_epi16(mn16, mn16));
         const float dw = tmo_f16_to_f32(rd16(blk)), mw = tmo_f16_to_f32(rd16(blk + 2));
         for (int c = 0; c < nc; c++) {
             const tmo_block_q8k *x = xs[c] + b;
@@ -469,11 +482,12 @@ static void dot_cols_q4k(int64_t ncols, const uint8_t *blk, const tmo_block_q8k 
             for (int s = 0; s < 8; s++)
                 a = _mm256_add_epi32(a, _mm256_madd_epi16(_mm256_maddubs_epi16(q[s], _mm256_loadu_si256(
                                                               (const __m256i *)(x->qs + 32 * s))), scv[s]));
-            const int32_t isum = hsum8(a);
-            int32_t msum = 0;
-            for (int j = 0; j < 4; j++)
-                msum += mn[2 * j] * (x->bsums[4 * j] + x->bsums[4 * j + 1]) +
-                        mn[2 * j + 1] * (x->bsums[4 * j + 2] + x->bsums[4 * j + 3]);
+            const __m256i m = _mm256_madd_epi16(_mm256_loadu_si256((const __m256i *)x->bsums), mnv);
+            /* both horizontal sums at once: [a01 a23 m01 m23 | a45 a67 m45 m67] -> [isum, msum, ..] */
+            const __m256i h = _mm256_hadd_epi32(a, m);
+            __m128i hs = _mm_add_epi32(_mm256_castsi256_si128(h), _mm256_extracti128_si256(h, 1));
+            hs = _mm_hadd_epi32(hs, hs);
+            const int32_t isum = _mm_cvtsi128_si32(hs), msum = _mm_extract_epi32(hs, 1);
             const float d = dw * x->d, dmin = mw * x->d;
             acc[c] += d * (float)isum;
             acc[c] -= dmin * (float)msum;
@@ -501,9 +515,17 @@ static void dot_cols_q6k(int64_t ncols, const uint8_t *blk, const tmo_block_q8k 
             q[4 * h + 3] = _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(l1, 4), low),
                                            _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(hb, 6), two), 4));
         }
-        /* register v holds elements 32 v .. 32 v + 31: sub-blocks 2 v (low half) and 2 v + 1 */
-        for (int v = 0; v < 8; v++)
-            scv[v] = _mm256_set_m128i(_mm_set1_epi16(scp[2 * v + 1]), _mm_set1_epi16(scp[2 * v]));
+        /* the 16 scales as 16-bit lanes: the -32 bias is -32 * sum_s sc_s * bsums_s */
+        const __m256i sc16 = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i *)scp));
+        /* register v holds elements 32 v .. 32 v + 31: sub-blocks 2 v (low half, every lane scale 2 v)
+         * and 2 v + 1 (high half); scales 0-7 sit in sc16's low 128 bits, 8-15 in its high ones */
+        const __m256i slo = _mm256_permute2x128_si256(sc16, sc16, 0x00), shi = _mm256_permute2x128_si256(sc16, sc16, 0x11);
+        for (int v = 0; v < 8; v++) {
+            const int w = 2 * (v & 3); /* the pair's first scale within its 8 */
+            const __m256i m = _mm256_set_m128i(_mm_set1_epi16((short)(0x0100 * (2 * w + 3) + 2 * w + 2)),
+                                               _mm_set1_epi16((short)(0x0100 * (2 * w + 1) + 2 * w)));
+            scv[v] = _mm256_shuffle_epi8(v < 4 ? slo : shi, m);
+        }
         const float dw = tmo_f16_to_f32(rd16(blk + 208));
         for (int c = 0; c < nc; c++) {
             const tmo_block_q8k *x = xs[c] + b;
@@ -511,15 +533,15 @@ static void dot_cols_q6k(int64_t ncols, const uint8_t *blk, const tmo_block_q8k 
             for (int v = 0; v < 8; v++)
                 a = _mm256_add_epi32(a, _mm256_madd_epi16(_mm256_maddubs_epi16(q[v], _mm256_loadu_si256(
                                                               (const __m256i *)(x->qs + 32 * v))), scv[v]));
-            int32_t bias = 0;
-            for (int s = 0; s < 16; s++) bias += scp[s] * x->bsums[s];
-            const int32_t isum = hsum8(a) - 32 * bias;
+            const __m256i bias = _mm256_madd_epi16(_mm256_loadu_si256((const __m256i *)x->bsums), sc16);
+            const int32_t isum = hsum8(_mm256_sub_epi32(a, _mm256_slli_epi32(bias, 5)));
             const float d = dw * x->d;
             acc[c] += d * (float)isum;
         }
     }
     for (int c = 0; c < nc; c++) out[c] = acc[c];
 }
+
 #endif
 
 void tmo_dot_cols(int type, int64_t ncols, const void *w, const tmo_block_q8k *const *xs, int nc, float *out) {
