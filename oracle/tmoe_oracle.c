@@ -442,7 +442,7 @@ float tmo_vec_dot_q6k_q8k_simd(int64_t ncols, const void *w, const tmo_block_q8k
     return acc;
 }
 
-/* One weight row against up to four activation rows, the organisation of ggml's CPU mat-mul
+/* One weight row against up to TMO_COLS (8) activation rows, the organisation of ggml's CPU mat-mul
  * kernels: the row's quants are unpacked once per super-block and serve every column, and the
  * sub-block scales multiply the 16-bit pair sums in vector registers (madd), so a super-block takes
  * one horizontal sum per column instead of one per sub-block.  The integer sums are the same
@@ -451,7 +451,7 @@ float tmo_vec_dot_q6k_q8k_simd(int64_t ncols, const void *w, const tmo_block_q8k
  * out[c] equals tmo_vec_dot_q4k_q8k / tmo_vec_dot_q6k_q8k of column c bit for bit. */
 static void dot_cols_q4k(int64_t ncols, const uint8_t *blk, const tmo_block_q8k *const *xs, int nc, float *out) {
     const __m256i low = _mm256_set1_epi8(0x0f);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc[TMO_COLS] = {0.f};
     for (int64_t b = 0; b < ncols / TMO_QK_K; b++, blk += TMO_Q4K_BYTES) {
         /* the 6-bit scales and mins of q4k_scale_min, four at a time as bytes of 32-bit words */
         uint32_t w0, w1, w2;
@@ -498,7 +498,7 @@ static void dot_cols_q4k(int64_t ncols, const uint8_t *blk, const tmo_block_q8k 
 
 static void dot_cols_q6k(int64_t ncols, const uint8_t *blk, const tmo_block_q8k *const *xs, int nc, float *out) {
     const __m256i low = _mm256_set1_epi8(0x0f), two = _mm256_set1_epi8(0x03);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc[TMO_COLS] = {0.f};
     for (int64_t b = 0; b < ncols / TMO_QK_K; b++, blk += TMO_Q6K_BYTES) {
         const uint8_t *ql = blk, *qh = blk + 128;
         const int8_t *scp = (const int8_t *)(blk + 192);
@@ -545,7 +545,7 @@ static void dot_cols_q6k(int64_t ncols, const uint8_t *blk, const tmo_block_q8k 
 #endif
 
 void tmo_dot_cols(int type, int64_t ncols, const void *w, const tmo_block_q8k *const *xs, int nc, float *out) {
-    if (nc < 1 || nc > 4) return;
+    if (nc < 1 || nc > TMO_COLS) return;
 #if defined(__AVX2__)
     if (type == TMO_TYPE_Q4_K) return dot_cols_q4k(ncols, (const uint8_t *)w, xs, nc, out);
     if (type == TMO_TYPE_Q6_K) return dot_cols_q6k(ncols, (const uint8_t *)w, xs, nc, out);
@@ -790,10 +790,10 @@ int tmo_mul_mat_id(int type, const void *W, size_t nb1, size_t nb2, int64_t K, i
             for (int64_t r = r0; r < r0 + RB && r < N; r++) {
                 const uint8_t *wrow = (const uint8_t *)W + e * nb2 + r * nb1;
                 if (mode == TMO_MODE_Q8K && (type == TMO_TYPE_Q4_K || type == TMO_TYPE_Q6_K)) {
-                    for (int32_t i = offs[e]; i < offs[e + 1]; i += 4) {
-                        const int nc = offs[e + 1] - i < 4 ? offs[e + 1] - i : 4;
-                        const tmo_block_q8k *xs[4];
-                        float res[4];
+                    for (int32_t i = offs[e]; i < offs[e + 1]; i += TMO_COLS) {
+                        const int nc = offs[e + 1] - i < TMO_COLS ? offs[e + 1] - i : TMO_COLS;
+                        const tmo_block_q8k *xs[TMO_COLS];
+                        float res[TMO_COLS];
                         for (int c = 0; c < nc; c++) {
                             int64_t p = perm[i + c], t = p / n_used, j = p % n_used;
                             xs[c] = q + (t * b1 + (b1 == 1 ? 0 : j)) * nb;

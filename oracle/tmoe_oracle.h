@@ -103,7 +103,8 @@ float tmo_vec_dot_q6k_q8k(int64_t ncols, const void *w, const tmo_block_q8k *x);
 /* The same two dots with AVX2 byte multiply-adds (bit-identical results). */
 float tmo_vec_dot_q4k_q8k_simd(int64_t ncols, const void *w, const tmo_block_q8k *x);
 float tmo_vec_dot_q6k_q8k_simd(int64_t ncols, const void *w, const tmo_block_q8k *x);
-/* One Q4_K / Q6_K row against nc (1..4) Q8_K rows xs[c]: out[c] bit for bit the scalar dots'. */
+/* One Q4_K / Q6_K row against nc (1..TMO_COLS) Q8_K rows xs[c]: out[c] bit for bit the scalar dots'. */
+#define TMO_COLS 8
 void tmo_dot_cols(int type, int64_t ncols, const void *w, const tmo_block_q8k *const *xs, int nc, float *out);
 
 /* --- canonical router arithmetic (bit-exact with the CUDA path) --------- */

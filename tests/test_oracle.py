@@ -112,9 +112,9 @@ def test_simd_dots_equal_the_scalar_restatement(qt):
 
 @pytest.mark.parametrize("qt", [O.TYPE_Q4_K, O.TYPE_Q6_K])
 def test_multi_column_dots_equal_the_scalar_restatement(qt):
-    """The dots mul_mat_id runs now (one weight row against up to four activation rows, scales applied
-    to the 16-bit pair sums in vector registers) against the scalar restatement, column by column and bit
-    for bit, with 1 to 4 columns, random valid blocks and activations at the Q8_K extremes."""
+    """The dots mul_mat_id runs (one weight row against up to eight activation rows, scales applied to
+    the 16-bit pair sums in vector registers) against the scalar restatement, column by column and bit for
+    bit, with 1 to 8 columns, random valid blocks and activations at the Q8_K extremes."""
     import ctypes as C
     from tests.common import random_kquant_bytes
     rng = np.random.default_rng(100 + qt)
@@ -123,13 +123,15 @@ def test_multi_column_dots_equal_the_scalar_restatement(qt):
                            random_kquant_bytes(rng, qt, 24, ncols, 1.0)])
     cols = [O.quantize_q8k(np.asarray(x, np.float32)) for x in
             (rng.uniform(-1, 1, ncols), rng.standard_normal(ncols) * 30,
-             np.where(rng.random(ncols) < 0.5, -1.0, 1.0) * 127, rng.standard_normal(ncols))]
+             np.where(rng.random(ncols) < 0.5, -1.0, 1.0) * 127, rng.standard_normal(ncols),
+             rng.uniform(-1, 1, ncols) * 5, rng.standard_normal(ncols) * 0.01,
+             np.where(rng.random(ncols) < 0.5, 127.0, -127.0), rng.standard_normal(ncols) * 100)]
     scalar = O.lib().tmo_vec_dot_q4k_q8k if qt == O.TYPE_Q4_K else O.lib().tmo_vec_dot_q6k_q8k
-    for nc in (1, 2, 3, 4):
-        xs = (C.c_void_p * 4)(*[c.ctypes.data for c in cols])
+    for nc in range(1, 9):
+        xs = (C.c_void_p * 8)(*[c.ctypes.data for c in cols])
         for r in range(rows.shape[0]):
             row = np.ascontiguousarray(rows[r])
-            out = np.zeros(4, np.float32)
+            out = np.zeros(8, np.float32)
             O.lib().tmo_dot_cols(qt, ncols, row.ctypes.data, xs, nc, out.ctypes.data)
             for c in range(nc):
                 want = np.float32(scalar(ncols, row.ctypes.data, cols[c].ctypes.data))
