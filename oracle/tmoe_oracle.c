@@ -684,25 +684,66 @@ void tmo_router_logits(const float *xn, const float *router_w, int64_t T, int64_
             logits[t * E + e] = tmo_router_dot(router_w + e * H, xn + t * H, H);
 }
 
+/* The same dots with the 32 lanes in vector registers.  A row of n (a multiple of 128) is first
+ * stored lane-major: element 128 m + 4 l + c at 128 m + 32 c + l, so that step (m, c) of every
+ * lane is one contiguous 32-float run; each lane then takes the same fused multiply-adds in the same
+ * order as tmo_router_dot, and the same butterfly, so the logits are the same bits. */
+static void lane_major(const float *src, float *dst, int64_t n) {
+    for (int64_t m = 0; m < n / 128; m++)
+        for (int c = 0; c < 4; c++)
+            for (int l = 0; l < 32; l++) dst[128 * m + 32 * c + l] = src[128 * m + 4 * l + c];
+}
+#if defined(__AVX2__) && defined(__FMA__)
+static float router_dot_lanes(const float *wp, const float *xp, int64_t n) {
+    __m256 a[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps()};
+    for (int64_t i = 0; i < n; i += 32)
+        for (int v = 0; v < 4; v++)
+            a[v] = _mm256_fmadd_ps(_mm256_loadu_ps(wp + i + 8 * v), _mm256_loadu_ps(xp + i + 8 * v), a[v]);
+    float part[32];
+    for (int v = 0; v < 4; v++) _mm256_storeu_ps(part + 8 * v, a[v]);
+    return butterfly32(part);
+}
+#define TMO_ROUTER_LANES 1
+#else
+#define TMO_ROUTER_LANES 0
+#endif
+
 void tmo_route(const float *x, int64_t T, int64_t H, int64_t E, int k, int use_norm,
                const float *norm_w, float eps, const float *router_w, const float *logits_in,
                float *xn_out, float *logits_out, int32_t *ids, float *w) {
+    const int lanes = TMO_ROUTER_LANES && router_w && H % 128 == 0;
+    float *wp = lanes ? (float *)malloc(sizeof(float) * (size_t)(E * H)) : NULL;
+    if (wp) {
+#pragma omp parallel for schedule(static)
+        for (int64_t e = 0; e < E; e++) lane_major(router_w + e * H, wp + e * H, H);
+    }
 #pragma omp parallel for schedule(static)
     for (int64_t t = 0; t < T; t++) {
         float *xn = (float *)malloc(sizeof(float) * (size_t)H);
         float *lg = (float *)malloc(sizeof(float) * (size_t)E);
+        float *xp = wp ? (float *)malloc(sizeof(float) * (size_t)H) : NULL;
         if (use_norm)
             tmo_rms_norm(x + t * H, norm_w, eps, xn, H);
         else
             memcpy(xn, x + t * H, sizeof(float) * (size_t)H);
         if (xn_out) memcpy(xn_out + t * H, xn, sizeof(float) * (size_t)H);
-        for (int64_t e = 0; e < E; e++)
+        if (xp) lane_major(xn, xp, H);
+        for (int64_t e = 0; e < E; e++) {
+#if TMO_ROUTER_LANES
+            if (xp) {
+                lg[e] = router_dot_lanes(wp + e * H, xp, H);
+                continue;
+            }
+#endif
             lg[e] = router_w ? tmo_router_dot(router_w + e * H, xn, H) : logits_in[t * E + e];
+        }
+        free(xp);
         if (logits_out) memcpy(logits_out + t * E, lg, sizeof(float) * (size_t)E);
         tmo_softmax_topk(lg, (int)E, k, NULL, ids + t * k, w + t * k);
         free(lg);
         free(xn);
     }
+    free(wp);
 }
 
 void tmo_map_ids(const int32_t *ids, int64_t n, const int32_t *table, int64_t E, int32_t *out) {

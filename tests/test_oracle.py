@@ -138,6 +138,24 @@ def test_multi_column_dots_equal_the_scalar_restatement(qt):
                 assert out[c].view(np.uint32) == want.view(np.uint32), (nc, r, c)
 
 
+@pytest.mark.parametrize("T,H,E,norm", [(5, 128, 16, False), (9, 768, 40, True), (16, 2048, 128, False),
+                                       (3, 4096, 64, True), (4, 200, 8, False)])
+def test_route_logits_equal_the_scalar_router_dot(T, H, E, norm):
+    """tmo_route's logits (32 lanes in vector registers over lane-major copies when H % 128 == 0) are
+    tmo_router_dot's bits for every (token, expert), with and without the norm, over values of mixed scale."""
+    rng = np.random.default_rng(T * 1000 + H + E)
+    x = (rng.standard_normal((T, H)) * rng.choice([1e-3, 1.0, 30.0], (T, H))).astype(np.float32)
+    rw = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    nw = rng.uniform(0.5, 1.5, H).astype(np.float32)
+    _, _, xn, lg = O.route(x, min(4, E), router_w=rw, norm=norm, norm_w=nw if norm else None)
+    dot = O.lib().tmo_router_dot
+    for t in range(T):
+        row = np.ascontiguousarray(xn[t])
+        for e in range(E):
+            want = np.float32(dot(rw[e].ctypes.data, row.ctypes.data, H))
+            assert lg[t, e].view(np.uint32) == want.view(np.uint32), (t, e)
+
+
 TYPES = [O.TYPE_Q4_K, O.TYPE_Q6_K]
 
 
